@@ -1,0 +1,348 @@
+"""Benchmark of the B200 tension operator.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = forward + backward of the fused tension op (RoPE base 10000 on
+Q/K, local window, τ-mass normalisation — the model.py call-site semantics)
+on one synthetic batch B=8, H=12, T=2048, HD=64, W=64, bf16, Q/K/V/dOut ~
+N(0,1) from seed 0 (+rank).  Per-rank work is fixed (weak scaling: every
+rank runs its own batch, no data-path collective — the op shards by batch).
+
+Printed JSON (one line, rank 0):
+  value     algorithmic HBM GB/s of the whole job (bytes: N_rows·(24·HD+8)
+            per step), inputs resident in HBM, CUDA events on
+            the launching stream, max over ranks;
+  e2e       the same metric through the public API with pinned HOST inputs
+            copied in and (out, dq, dk, dv) copied back every step;
+  roofline  for the dominant phase (fwd or bwd kernels) vs MEASURED_PEAKS;
+  cpu_baseline  the reference algorithm (CPU oracle port, fp32, all host
+            threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+B, H, T, HD = 8, 12, 2048, 64
+W_HEAD = 64
+WINDOWS = (32, 64, 128, 256)
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return FALLBACK_HBM_GBS, 1590.0, "fallback"
+
+
+def bytes_fwd(b=B, h=H, t=T, hd=HD):
+    return b * h * t * (4 * hd * 2 + 4)
+
+
+def bytes_bwd(b=B, h=H, t=T, hd=HD):
+    return b * h * t * (8 * hd * 2 + 4)
+
+
+def pairs(b, h, t, w):
+    return b * h * (t * w - w * (w + 1) // 2) if t >= w else b * h * t * (t - 1) // 2
+
+
+def flops_fwd_bwd(b, h, t, hd, w):
+    return 12 * pairs(b, h, t, w) * hd
+
+
+class Clocks:
+    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), f[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, fl in rows for i, v in enumerate(fl)
+                          if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows),
+                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def make_inputs(device, seed, b=B, t=T, dtype=torch.bfloat16):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    mk = lambda: torch.randn(b, t, H, HD, generator=g).to(dtype)
+    return [mk() for _ in range(4)]  # q, k, v, d_out (host)
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch.distributed as dist
+    import bozo_b200
+    from bozo_b200 import ops as bops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    hq, hk, hv, hdo = make_inputs(dev, 1234 + rank)
+    q, k, v, d_out = [x.to(dev) for x in (hq, hk, hv, hdo)]
+    q.requires_grad_(True); k.requires_grad_(True); v.requires_grad_(True)
+
+    def step(W, qq=q, kk=k, vv=v, dd=d_out, ev=None):
+        if ev:
+            ev[0].record(stream)
+        out = bozo_b200.tension(qq, kk, vv, window=W, rope_base=10_000.0, normalize="mass")
+        fl = bops.last_launches()
+        if ev:
+            ev[1].record(stream)
+        gq, gk, gv = torch.autograd.grad(out, (qq, kk, vv), dd)
+        bl = bops.last_launches()
+        if ev:
+            ev[2].record(stream)
+        return out, gq, gk, gv, fl + bl
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def maxred(x):
+        if world > 1:
+            t_ = torch.tensor([x], device=dev, dtype=torch.float64)
+            dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+            return float(t_.item())
+        return x
+
+    results = {}
+    launches_per_step = 0
+    for W in WINDOWS:
+        steps = args.steps if W == W_HEAD else max(3, args.steps // 4)
+        for _ in range(args.warmup):
+            step(W)
+        torch.cuda.synchronize()
+        barrier()
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        clk = Clocks(local_rank) if W == W_HEAD else None
+        if clk:
+            clk.__enter__()
+        torch.cuda.synchronize()
+        barrier()
+        start.record(stream)
+        n_launch = 0
+        for i in range(steps):
+            *_, nl = step(W, ev=evs[i])
+            n_launch += nl
+        end.record(stream)
+        torch.cuda.synchronize()
+        if clk:
+            clk.__exit__(None, None, None)
+        barrier()
+        ms = maxred(start.elapsed_time(end)) / steps
+        fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+        bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+        results[W] = dict(ms=ms, fwd_ms=maxred(fwd_ms), bwd_ms=maxred(bwd_ms),
+                          launches=n_launch, steps=steps,
+                          clocks=clk.summary() if clk else None, path=bops.last_path())
+        if W == W_HEAD:
+            launches_per_step = n_launch // steps
+
+    # ── e2e: public API, pinned host buffers in, results out, every step ──
+    hq, hk, hv, hdo = [x.pin_memory() for x in (hq, hk, hv, hdo)]
+    outs_h = [torch.empty(B, T, H, HD, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+
+    def e2e_step():
+        qq, kk, vv, dd = [x.to(dev, non_blocking=True) for x in (hq, hk, hv, hdo)]
+        qq.requires_grad_(True); kk.requires_grad_(True); vv.requires_grad_(True)
+        out, gq, gk, gv, _ = step(W_HEAD, qq, kk, vv, dd)
+        for dst, src in zip(outs_h, (out, gq, gk, gv)):
+            dst.copy_(src.detach(), non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    s0 = torch.cuda.Event(enable_timing=True); s1 = torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = maxred(s0.elapsed_time(s1)) / args.steps
+    barrier()
+    return results, e2e_ms, launches_per_step
+
+
+def cpu_baseline(budget_s=12.0):
+    """The reference CPU algorithm (oracle port of ops.py:29-63 + model.py
+    τ-mass + RoPE, fp32 autograd) on B=1 slices of the workload."""
+    from oracle import tension_oracle as orc
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    orc.cpu_fwd_bwd_sample(B=1, T=256, W=W_HEAD)  # warm the allocator
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        orc.cpu_fwd_bwd_sample(B=1, H=H, T=T, HD=HD, W=W_HEAD, seed=reps)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or reps >= 8:
+            break
+    gbs = bytes_fwd(1) * reps / el / 1e9 + bytes_bwd(1) * reps / el / 1e9
+    return dict(value=round(gbs, 4), unit="GB/s", cores=threads, kind="port",
+                sample=f"{reps} x B=1 slices (1/{B} of the batch each) of B{B} H{H} T{T} "
+                       f"HD{HD} W{W_HEAD}, fp32 unfold+autograd, {el:.1f}s",
+                tokens_per_s=round(reps * T / el, 1))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    hbm, tfl, peak_kind = peaks()
+    per_step_bytes = bytes_fwd() + bytes_bwd()
+    cfg = {"workload": "isolated tension op fwd+bwd (BASELINE configs[1])",
+           "B": B, "H": H, "T": T, "HD": HD, "W": W_HEAD, "rope_base": 10000,
+           "normalize": "mass", "tau_export": False, "per_rank_batch": B,
+           "l2": "inputs+outputs 303.6 MB per step > 126 MB L2; no flush needed",
+           "parallelism": f"batch-sharded replicas x{args.gpus}"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        torch.set_num_threads(os.cpu_count() or 1)
+        from oracle import tension_oracle as orc
+        for _ in range(max(1, min(args.warmup, 1))):
+            orc.cpu_fwd_bwd_sample(B=1, H=H, T=T, HD=HD, W=W_HEAD)
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            orc.cpu_fwd_bwd_sample(B=1, H=H, T=T, HD=HD, W=W_HEAD, seed=i)
+        el = time.perf_counter() - t0
+        ms = el * 1e3 / args.steps
+        val = (bytes_fwd(1) + bytes_bwd(1)) / (ms * 1e-3) / 1e9
+        line = {"impl": "reference", "metric": "tension fwd+bwd algorithmic HBM GB/s",
+                "value": round(val, 4), "unit": "GB/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic N(0,1)", "config": cfg,
+                "cpu_baseline": {"value": round(val, 4), "unit": "GB/s",
+                                 "cores": torch.get_num_threads(), "kind": "port",
+                                 "sample": f"each step = one B=1 slice (1/{B} of the batch)"},
+                "e2e": {"value": round(val, 4), "unit": "GB/s",
+                        "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    results, e2e_ms, launches_per_step = run_ours(args, rank, world, local_rank)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    head = results[W_HEAD]
+    n = args.gpus
+    value = n * per_step_bytes / (head["ms"] * 1e-3) / 1e9
+    fwd_gbs = bytes_fwd() / (head["fwd_ms"] * 1e-3) / 1e9
+    bwd_gbs = bytes_bwd() / (head["bwd_ms"] * 1e-3) / 1e9
+    dom = "bwd" if head["bwd_ms"] >= head["fwd_ms"] else "fwd"
+    ach = bwd_gbs if dom == "bwd" else fwd_gbs
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get(f"{dom}_bytes_per_launch")
+    h2d = 4 * B * T * H * HD * 2
+    d2h = 4 * B * T * H * HD * 2
+    line = {
+        "metric": "tension fwd+bwd algorithmic HBM GB/s", "value": round(value, 2),
+        "unit": "GB/s", "n_gpus": n, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(head["ms"], 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seed 1234+rank",
+        "config": cfg,
+        "tflops": round(n * flops_fwd_bwd(B, H, T, HD, W_HEAD) / (head["ms"] * 1e-3) / 1e12, 3),
+        "kernel_path": head["path"],
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(ach, 1), "peak": hbm,
+                     "unit": "GB/s", "frac": round(ach / hbm, 4), "traffic": traffic,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "fwd_gbs": round(fwd_gbs, 1), "bwd_gbs": round(bwd_gbs, 1),
+                     "fwd_ms": round(head["fwd_ms"], 4), "bwd_ms": round(head["bwd_ms"], 4)},
+        "per_window": {str(W): {"ms_per_step": round(r["ms"], 4),
+                                "gbs": round(per_step_bytes / (r["ms"] * 1e-3) / 1e9, 1),
+                                "tflops": round(flops_fwd_bwd(B, H, T, HD, W) / (r["ms"] * 1e-3) / 1e12, 3),
+                                "frac_of_roofline": round(max(per_step_bytes / (hbm * 1e9),
+                                                              flops_fwd_bwd(B, H, T, HD, W) / (tfl * 1e12))
+                                                          / (r["ms"] * 1e-3), 4)}
+                       for W, r in results.items()},
+        "e2e": {"value": round(n * per_step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": head["launches"],
+        "launches_per_step": launches_per_step,
+        "clocks": head["clocks"],
+    }
+    if n == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,102 @@
+"""ctypes binding of the C ABI declared in ``include/bozo_tension.h``.
+
+The structures below mirror the header field by field; ``tests/test_abi.py``
+compiles a C probe with gcc and checks every size and offset, and checks
+that the library exports every function the header declares.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib",
+                        "libbozo_tension.so")
+
+OK = 0
+DT_F32, DT_BF16, DT_F16 = 0, 1, 2
+MODE_LOCAL, MODE_GLOBAL = 0, 1
+NORM_NONE, NORM_MASS, NORM_COUNT = 0, 1, 2
+PATH_AUTO, PATH_SIMT, PATH_TCGEN05 = 0, 1, 2
+
+EXPORTED = (
+    "bozo_tension_fwd", "bozo_tension_bwd", "bozo_tension_bwd_workspace",
+    "bozo_tension_poll_error", "bozo_tension_last_path",
+    "bozo_tension_last_launches", "bozo_status_string",
+    "bozo_tension_abi_version",
+)
+
+
+class Tensor4(C.Structure):
+    _fields_ = [("ptr", C.c_void_p), ("dtype", C.c_int32), ("_pad", C.c_int32),
+                ("stride", C.c_int64 * 4)]
+
+
+class FwdArgs(C.Structure):
+    _fields_ = [
+        ("B", C.c_int32), ("T", C.c_int32), ("H", C.c_int32), ("HD", C.c_int32),
+        ("mode", C.c_int32), ("window", C.c_int32), ("normalize", C.c_int32),
+        ("path", C.c_int32), ("scale", C.c_float), ("rope_len", C.c_int32),
+        ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
+        ("q", Tensor4), ("k", Tensor4), ("v", Tensor4),
+        ("bias", C.c_void_p), ("bias_stride", C.c_int64 * 3),
+        ("out", C.c_void_p), ("out_dtype", C.c_int32), ("tau_dtype", C.c_int32),
+        ("tau", C.c_void_p), ("row_mass", C.c_void_p),
+    ]
+
+
+class BwdArgs(C.Structure):
+    _fields_ = [
+        ("B", C.c_int32), ("T", C.c_int32), ("H", C.c_int32), ("HD", C.c_int32),
+        ("mode", C.c_int32), ("window", C.c_int32), ("normalize", C.c_int32),
+        ("path", C.c_int32), ("scale", C.c_float), ("rope_len", C.c_int32),
+        ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
+        ("q", Tensor4), ("k", Tensor4), ("v", Tensor4), ("d_out", Tensor4),
+        ("out", Tensor4), ("row_mass", C.c_void_p),
+        ("bias", C.c_void_p), ("bias_stride", C.c_int64 * 3),
+        ("d_tau", C.c_void_p), ("d_tau_dtype", C.c_int32),
+        ("grad_dtype", C.c_int32 * 3), ("_pad", C.c_int32),
+        ("dq", C.c_void_p), ("dk", C.c_void_p), ("dv", C.c_void_p),
+        ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+    ]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib():
+    """Load the in-tree shared library (raises if it was never built)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise ImportError(
+                        f"{LIB_PATH} is missing: build it with `python -m bozo_b200.build` "
+                        "(the operator has no CPU fallback)")
+                L = C.CDLL(LIB_PATH)
+                L.bozo_tension_fwd.argtypes = [C.POINTER(FwdArgs), C.c_void_p]
+                L.bozo_tension_fwd.restype = C.c_int
+                L.bozo_tension_bwd.argtypes = [C.POINTER(BwdArgs), C.c_void_p]
+                L.bozo_tension_bwd.restype = C.c_int
+                L.bozo_tension_bwd_workspace.argtypes = [C.POINTER(BwdArgs)]
+                L.bozo_tension_bwd_workspace.restype = C.c_size_t
+                L.bozo_tension_poll_error.argtypes = [C.c_void_p]
+                L.bozo_tension_poll_error.restype = C.c_int
+                L.bozo_tension_last_path.restype = C.c_int
+                L.bozo_tension_last_launches.restype = C.c_int
+                L.bozo_status_string.argtypes = [C.c_int]
+                L.bozo_status_string.restype = C.c_char_p
+                L.bozo_tension_abi_version.restype = C.c_int
+                _lib = L
+    return _lib
+
+
+def status_string(code: int) -> str:
+    return lib().bozo_status_string(code).decode()
+
+
+def check(code: int, what: str):
+    if code != OK:
+        raise RuntimeError(f"{what} failed: {status_string(code)} (status {code})")

@@ -1,0 +1,217 @@
+// abi.cu — the extern "C" boundary (include/bozo_tension.h): argument
+// validation, kernel-path selection and launch bookkeeping.
+//
+// Validation mirrors the reference's asserts: bias must be [B,T,W]
+// (triton_tension/ops.py:93-97), tensors are 4-D [B,T,H,HD] (ops.py:22-24).
+#include <atomic>
+#include <mutex>
+
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace bozo {
+namespace {
+
+__device__ int g_device_error;  // set by bounded device-side waits
+
+// Last path / launch count, process-wide (autograd may run the backward on
+// its own device thread, so these are not thread-local).
+std::atomic<int> t_last_path{0};
+std::atomic<int> t_last_launches{0};
+
+constexpr int kMaxDevices = 64;
+int* g_err_ptr[kMaxDevices] = {nullptr};
+std::mutex g_err_mu;
+
+// Device address of the error word for the current device (looked up once
+// per device; cudaGetSymbolAddress needs that device current).
+int* error_word(cudaError_t* e) {
+  int dev = 0;
+  *e = cudaGetDevice(&dev);
+  if (*e != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  if (!g_err_ptr[dev]) {
+    void* ptr = nullptr;
+    *e = cudaGetSymbolAddress(&ptr, g_device_error);
+    if (*e != cudaSuccess) return nullptr;
+    g_err_ptr[dev] = static_cast<int*>(ptr);
+  }
+  return g_err_ptr[dev];
+}
+
+bool dtype_ok(int dt) { return dt == BOZO_DT_F32 || dt == BOZO_DT_BF16 || dt == BOZO_DT_F16; }
+
+int check_common(int B, int T, int H, int HD, int mode, int W, int norm, float scale,
+                 int rope_len, const float* cos, const float* sin) {
+  if (B <= 0 || T <= 0 || H <= 0 || HD <= 0) return BOZO_ERR_BAD_SHAPE;
+  if (HD > 128) return BOZO_ERR_UNSUPPORTED;
+  if (mode != BOZO_MODE_LOCAL && mode != BOZO_MODE_GLOBAL) return BOZO_ERR_BAD_SHAPE;
+  if (mode == BOZO_MODE_LOCAL && W < 1) return BOZO_ERR_BAD_SHAPE;
+  if (mode == BOZO_MODE_GLOBAL && W < 0) return BOZO_ERR_BAD_SHAPE;
+  if (norm != BOZO_NORM_NONE && norm != BOZO_NORM_MASS && norm != BOZO_NORM_COUNT)
+    return BOZO_ERR_BAD_SHAPE;
+  if (mode == BOZO_MODE_GLOBAL && norm == BOZO_NORM_COUNT) return BOZO_ERR_UNSUPPORTED;
+  if (!(scale != 0.f)) return BOZO_ERR_BAD_SHAPE;
+  if (rope_len != 0) {
+    if (!cos || !sin) return BOZO_ERR_NULL;
+    if (HD % 2 != 0) return BOZO_ERR_UNSUPPORTED;
+    if (rope_len < T) return BOZO_ERR_BAD_SHAPE;
+  }
+  return BOZO_OK;
+}
+
+int check_t4(const bozo_tensor4& t) {
+  if (!t.ptr) return BOZO_ERR_NULL;
+  if (!dtype_ok(t.dtype)) return BOZO_ERR_BAD_DTYPE;
+  return BOZO_OK;
+}
+
+size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+
+}  // namespace
+}  // namespace bozo
+
+using namespace bozo;
+
+extern "C" {
+
+int bozo_tension_abi_version(void) { return BOZO_TENSION_ABI_VERSION; }
+
+const char* bozo_status_string(int s) {
+  switch (s) {
+    case BOZO_OK: return "ok";
+    case BOZO_ERR_BAD_SHAPE: return "bad shape or size argument";
+    case BOZO_ERR_BAD_DTYPE: return "unsupported dtype code";
+    case BOZO_ERR_UNSUPPORTED: return "unsupported configuration";
+    case BOZO_ERR_ALIGNMENT: return "tensor-core path needs 16-byte aligned rows with unit HD stride";
+    case BOZO_ERR_NULL: return "required pointer is NULL";
+    case BOZO_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait timed out";
+    case BOZO_ERR_CUDA: return "CUDA runtime error";
+    case BOZO_ERR_WORKSPACE: return "workspace missing or too small";
+    default: return "unknown status";
+  }
+}
+
+int bozo_tension_last_path(void) { return t_last_path.load(); }
+int bozo_tension_last_launches(void) { return t_last_launches.load(); }
+
+int bozo_tension_fwd(const bozo_tension_fwd_args* a, void* stream) {
+  if (!a) return BOZO_ERR_NULL;
+  int st = check_common(a->B, a->T, a->H, a->HD, a->mode, a->window, a->normalize, a->scale,
+                        a->rope_len, a->rope_cos, a->rope_sin);
+  if (st) return st;
+  if ((st = check_t4(a->q)) || (st = check_t4(a->k)) || (st = check_t4(a->v))) return st;
+  if (!a->out) return BOZO_ERR_NULL;
+  if (!dtype_ok(a->out_dtype)) return BOZO_ERR_BAD_DTYPE;
+  if (a->tau && !dtype_ok(a->tau_dtype)) return BOZO_ERR_BAD_DTYPE;
+  if (a->mode == BOZO_MODE_GLOBAL && a->tau && a->window > a->T) return BOZO_ERR_BAD_SHAPE;
+
+  cudaError_t e;
+  FwdP p{};
+  p.B = a->B; p.T = a->T; p.H = a->H; p.HD = a->HD; p.mode = a->mode; p.W = a->window;
+  p.norm = a->normalize; p.scale = a->scale; p.inv_scale = 1.0f / a->scale;
+  p.cos = a->rope_len ? a->rope_cos : nullptr;
+  p.sin = a->rope_len ? a->rope_sin : nullptr;
+  p.q = dev_t4(a->q); p.k = dev_t4(a->k); p.v = dev_t4(a->v);
+  p.bias = a->bias; p.bs0 = a->bias_stride[0]; p.bs1 = a->bias_stride[1]; p.bs2 = a->bias_stride[2];
+  p.out = a->out; p.out_dt = a->out_dtype; p.tau = a->tau; p.tau_dt = a->tau_dtype;
+  p.row_mass = a->row_mass;
+  p.err = error_word(&e);
+  if (!p.err) return BOZO_ERR_CUDA;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int launches = 0;
+  const bool tc_ok = tc_fwd_eligible(p);
+  if (a->path == BOZO_PATH_TCGEN05 && !tc_ok) return BOZO_ERR_ALIGNMENT;
+  int path;
+  if (tc_ok && a->path != BOZO_PATH_SIMT) {
+    e = launch_tc_fwd(p, s, &launches);
+    path = BOZO_PATH_TCGEN05;
+  } else {
+    e = launch_simt_fwd(p, s, &launches);
+    path = BOZO_PATH_SIMT;
+  }
+  if (e != cudaSuccess) return BOZO_ERR_CUDA;
+  t_last_path = path;
+  t_last_launches = launches;
+  return BOZO_OK;
+}
+
+size_t bozo_tension_bwd_workspace(const bozo_tension_bwd_args* a) {
+  if (!a || a->B <= 0 || a->T <= 0 || a->H <= 0) return 0;
+  const size_t rows = (size_t)a->B * a->H * a->T;
+  return round256(rows * sizeof(float)) * 2;  // alpha, beta
+}
+
+int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
+  if (!a) return BOZO_ERR_NULL;
+  int st = check_common(a->B, a->T, a->H, a->HD, a->mode, a->window, a->normalize, a->scale,
+                        a->rope_len, a->rope_cos, a->rope_sin);
+  if (st) return st;
+  if ((st = check_t4(a->q)) || (st = check_t4(a->k)) || (st = check_t4(a->v)) ||
+      (st = check_t4(a->d_out)))
+    return st;
+  if (a->normalize == BOZO_NORM_MASS) {
+    if ((st = check_t4(a->out))) return st;
+    if (!a->row_mass) return BOZO_ERR_NULL;
+  }
+  if (!a->dq || !a->dk || !a->dv) return BOZO_ERR_NULL;
+  for (int i = 0; i < 3; ++i)
+    if (!dtype_ok(a->grad_dtype[i])) return BOZO_ERR_BAD_DTYPE;
+  if (a->d_tau && !dtype_ok(a->d_tau_dtype)) return BOZO_ERR_BAD_DTYPE;
+  const size_t need = bozo_tension_bwd_workspace(a);
+  if (need && (!a->workspace || a->workspace_bytes < need)) return BOZO_ERR_WORKSPACE;
+
+  cudaError_t e;
+  BwdP p{};
+  p.B = a->B; p.T = a->T; p.H = a->H; p.HD = a->HD; p.mode = a->mode; p.W = a->window;
+  p.norm = a->normalize; p.scale = a->scale; p.inv_scale = 1.0f / a->scale;
+  p.cos = a->rope_len ? a->rope_cos : nullptr;
+  p.sin = a->rope_len ? a->rope_sin : nullptr;
+  p.q = dev_t4(a->q); p.k = dev_t4(a->k); p.v = dev_t4(a->v); p.dout = dev_t4(a->d_out);
+  p.out = dev_t4(a->out);
+  p.row_mass = a->row_mass;
+  p.bias = a->bias; p.bs0 = a->bias_stride[0]; p.bs1 = a->bias_stride[1]; p.bs2 = a->bias_stride[2];
+  p.dtau = a->d_tau; p.dtau_dt = a->d_tau_dtype;
+  p.dq = a->dq; p.dk = a->dk; p.dv = a->dv;
+  p.dq_dt = a->grad_dtype[0]; p.dk_dt = a->grad_dtype[1]; p.dv_dt = a->grad_dtype[2];
+  const size_t rows = (size_t)a->B * a->H * a->T;
+  p.alpha = static_cast<float*>(a->workspace);
+  p.beta = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + round256(rows * sizeof(float)));
+  p.err = error_word(&e);
+  if (!p.err) return BOZO_ERR_CUDA;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int launches = 0;
+  const bool tc_ok = tc_bwd_eligible(p);
+  if (a->path == BOZO_PATH_TCGEN05 && !tc_ok) return BOZO_ERR_ALIGNMENT;
+  int path;
+  if (tc_ok && a->path != BOZO_PATH_SIMT) {
+    e = launch_tc_bwd(p, s, &launches);
+    path = BOZO_PATH_TCGEN05;
+  } else {
+    e = launch_simt_bwd(p, s, &launches);
+    path = BOZO_PATH_SIMT;
+  }
+  if (e != cudaSuccess) return BOZO_ERR_CUDA;
+  t_last_path = path;
+  t_last_launches = launches;
+  return BOZO_OK;
+}
+
+int bozo_tension_poll_error(void* stream) {
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return BOZO_ERR_CUDA;
+  int* ptr = error_word(&e);
+  if (!ptr) return BOZO_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpy(&v, ptr, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return BOZO_ERR_CUDA;
+  if (v) {
+    const int zero = 0;
+    if (cudaMemcpy(ptr, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) return BOZO_ERR_CUDA;
+    return BOZO_ERR_DEVICE_TIMEOUT;
+  }
+  return BOZO_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,92 @@
+// common.cuh — shared device helpers and the internal parameter blocks that
+// the C ABI (abi.cu) hands to the kernel launchers.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "bozo_tension.h"
+
+namespace bozo {
+
+constexpr float kMassEps = 1e-6f;  // model.py:227/257/281 clamp(min=1e-6)
+
+struct DevT4 {
+  const void* p;
+  int dt;
+  long long sb, st, sh, sd;
+};
+
+inline DevT4 dev_t4(const bozo_tensor4& t) {
+  return DevT4{t.ptr, t.dtype, t.stride[0], t.stride[1], t.stride[2], t.stride[3]};
+}
+
+// Everything a forward kernel needs, in device-friendly form.
+struct FwdP {
+  int B, T, H, HD, mode, W, norm;
+  float scale, inv_scale;
+  const float* cos;
+  const float* sin;  // NULL when no RoPE
+  DevT4 q, k, v;
+  const float* bias;
+  long long bs0, bs1, bs2;
+  void* out;
+  int out_dt;
+  void* tau;
+  int tau_dt;
+  float* row_mass;
+  int* err;  // device error word
+};
+
+struct BwdP {
+  int B, T, H, HD, mode, W, norm;
+  float scale, inv_scale;
+  const float* cos;
+  const float* sin;
+  DevT4 q, k, v, dout, out;
+  const float* row_mass;
+  const float* bias;
+  long long bs0, bs1, bs2;
+  const void* dtau;
+  int dtau_dt;
+  void* dq;
+  void* dk;
+  void* dv;
+  int dq_dt, dk_dt, dv_dt;
+  float* alpha;  // [B,H,T] workspace
+  float* beta;   // [B,H,T] workspace
+  int* err;
+};
+
+__device__ __forceinline__ float ldf(const void* p, long long i, int dt) {
+  if (dt == BOZO_DT_F32) return static_cast<const float*>(p)[i];
+  if (dt == BOZO_DT_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(static_cast<const __half*>(p)[i]);
+}
+
+__device__ __forceinline__ void stf(void* p, long long i, int dt, float v) {
+  if (dt == BOZO_DT_F32) {
+    static_cast<float*>(p)[i] = v;
+  } else if (dt == BOZO_DT_BF16) {
+    static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  } else {
+    static_cast<__half*>(p)[i] = __float2half_rn(v);
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Exact logistic sigmoid in fp32 (the CUDA-core path's definition).
+__device__ __forceinline__ float sigmoid_exact(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// Launchers (simt.cu)
+cudaError_t launch_simt_fwd(const FwdP& p, cudaStream_t st, int* launches);
+cudaError_t launch_simt_bwd(const BwdP& p, cudaStream_t st, int* launches);
+
+}  // namespace bozo

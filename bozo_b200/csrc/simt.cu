@@ -1,0 +1,445 @@
+// simt.cu — exact-fp32 CUDA-core kernels for every flag combination of the
+// tension operator (any HD ≤ 128, any dtype mix, local or global, bias, τ
+// export, RoPE, all three normalisations).  This is the parity path for fp32
+// callers (rtol 1e-5) and the fallback for shapes the tcgen05 kernels do not
+// take.  Semantics follow triton_tension/kernel.py:41-126 (forward),
+// kernel.py:130-228 (dQ) and kernel.py:232-341 (dK/dV), widened by the
+// model.py normalisation (257-258, 261-264) and global path (217-237).
+//
+// Structure: a CTA owns 32 rows (queries for fwd/dQ, keys for dK/dV) of one
+// (b, h); 8 warps × 4 rows.  The partner rows are streamed through shared
+// memory in chunks of 32 with lane = partner index, so the score of a
+// (row, partner) pair lives in one lane and the HD-wide accumulations use
+// warp shuffles.  All arithmetic is fp32.
+#include "common.cuh"
+
+namespace bozo {
+namespace {
+
+constexpr int kRows = 32;     // rows owned by a CTA
+constexpr int kChunk = 32;    // partner rows per shared-memory chunk
+constexpr int kThreads = 256; // 8 warps × 4 rows
+
+// Stage rows [t_begin, t_begin + n) of x[b, :, h, :] into dst (row pitch ld),
+// applying the half-split rotation of model.py:75-81 when cos/sin are given.
+// Out-of-range rows read as zero.
+__device__ void stage_rows(float* dst, int ld, const DevT4& x, int b, int h,
+                           int t_begin, int n, int T, int HD, const float* cos,
+                           const float* sin) {
+  const int half = HD / 2;
+  const bool rope = cos != nullptr;
+  const int per_row = rope ? half : HD;
+  for (int idx = threadIdx.x; idx < n * per_row; idx += blockDim.x) {
+    const int r = idx / per_row, d = idx % per_row;
+    const int t = t_begin + r;
+    float* row = dst + r * ld;
+    if (t < 0 || t >= T) {
+      row[d] = 0.f;
+      if (rope) row[d + half] = 0.f;
+      continue;
+    }
+    const long long base = (long long)b * x.sb + (long long)t * x.st + (long long)h * x.sh;
+    if (rope) {
+      const float x1 = ldf(x.p, base + (long long)d * x.sd, x.dt);
+      const float x2 = ldf(x.p, base + (long long)(d + half) * x.sd, x.dt);
+      const float c = cos[(long long)t * half + d], s = sin[(long long)t * half + d];
+      row[d] = x1 * c - x2 * s;
+      row[d + half] = x1 * s + x2 * c;
+    } else {
+      row[d] = ldf(x.p, base + (long long)d * x.sd, x.dt);
+    }
+  }
+}
+
+// Stage per-row scalars alpha/beta for query rows [t_begin, t_begin+n).
+__device__ void stage_scalars(float* a_dst, float* b_dst, const float* alpha,
+                              const float* beta, long long row_base, int t_begin,
+                              int n, int T) {
+  for (int r = threadIdx.x; r < n; r += blockDim.x) {
+    const int t = t_begin + r;
+    const bool ok = t >= 0 && t < T;
+    a_dst[r] = ok ? alpha[row_base + t] : 0.f;
+    b_dst[r] = ok ? beta[row_base + t] : 0.f;
+  }
+}
+
+// Key validity and the bias / τ slot for the pair (query t, key s).
+struct Pair {
+  bool valid;
+  int slot;       // local: window slot w; global: key position s
+  int tau_slot;   // exported τ column, -1 if not exported
+};
+
+__device__ __forceinline__ Pair pair_of(int mode, int W, int T, int t, int s) {
+  Pair pr;
+  if (mode == BOZO_MODE_LOCAL) {
+    pr.slot = s - t + W;
+    pr.valid = s >= 0 && t < T && pr.slot >= 0 && pr.slot < W;
+    pr.tau_slot = pr.valid ? pr.slot : -1;
+  } else {
+    pr.slot = s;
+    pr.valid = s >= 0 && s <= t && t < T;
+    const int j = T - 1 - s;  // model.py:236 flip: column j holds key T-1-j
+    pr.tau_slot = (pr.valid && j < W) ? j : -1;
+  }
+  return pr;
+}
+
+__device__ __forceinline__ float row_dot(const float* a, const float* b, int HD) {
+  float acc = 0.f;
+  for (int d = 0; d < HD; ++d) acc = fmaf(a[d], b[d], acc);
+  return acc;
+}
+
+// ───────────────────────────── forward ─────────────────────────────
+template <int NJ>
+__global__ void __launch_bounds__(kThreads) simt_fwd_kernel(FwdP p) {
+  extern __shared__ float sm[];
+  constexpr int LD = 32 * NJ + 1;
+  float* Qs = sm;
+  float* Ks = Qs + kRows * LD;
+  float* Vs = Ks + kChunk * LD;
+  const int b = blockIdx.z, h = blockIdx.y, t0 = blockIdx.x * kRows;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T = p.T, HD = p.HD, W = p.W;
+  const bool local = p.mode == BOZO_MODE_LOCAL;
+
+  stage_rows(Qs, LD, p.q, b, h, t0, kRows, T, HD, p.cos, p.sin);
+  if (!local && p.tau != nullptr) {
+    // global export: zero the exported window for this tile first
+    for (int idx = threadIdx.x; idx < kRows * W; idx += blockDim.x) {
+      const int t = t0 + idx / W, j = idx % W;
+      if (t < T) stf(p.tau, (((long long)b * T + t) * p.H + h) * W + j, p.tau_dt, 0.f);
+    }
+  }
+  const int s_lo = local ? t0 - W : 0;
+  const int s_hi = local ? min(t0 + kRows - 1, T) : min(t0 + kRows, T);
+
+  float acc[4][NJ];
+  float mass[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    mass[i] = 0.f;
+#pragma unroll
+    for (int n = 0; n < NJ; ++n) acc[i][n] = 0.f;
+  }
+
+  for (int c0 = s_lo; c0 < s_hi; c0 += kChunk) {
+    __syncthreads();
+    stage_rows(Ks, LD, p.k, b, h, c0, kChunk, T, HD, p.cos, p.sin);
+    stage_rows(Vs, LD, p.v, b, h, c0, kChunk, T, HD, nullptr, nullptr);
+    __syncthreads();
+    const int s = c0 + lane;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = warp * 4 + i, t = t0 + r;
+      if (t >= T) continue;  // warp-uniform
+      const Pair pr = pair_of(p.mode, W, T, t, s);
+      float tau = 0.f;
+      if (pr.valid && s < s_hi) {
+        float x = row_dot(Qs + r * LD, Ks + lane * LD, HD) / p.scale;
+        if (p.bias) x += p.bias[(long long)b * p.bs0 + (long long)t * p.bs1 + (long long)pr.slot * p.bs2];
+        tau = sigmoid_exact(x);
+      }
+      if (p.tau != nullptr && s < s_hi) {
+        if (local) {
+          if (pr.slot >= 0 && pr.slot < W)
+            stf(p.tau, (((long long)b * T + t) * p.H + h) * W + pr.slot, p.tau_dt, tau);
+        } else if (pr.tau_slot >= 0) {
+          stf(p.tau, (((long long)b * T + t) * p.H + h) * W + pr.tau_slot, p.tau_dt, tau);
+        }
+      }
+      mass[i] += tau;
+      for (int jj = 0; jj < kChunk; ++jj) {
+        const float tj = __shfl_sync(0xffffffffu, tau, jj);
+        if (tj == 0.f) continue;  // uniform across the warp
+#pragma unroll
+        for (int n = 0; n < NJ; ++n) acc[i][n] = fmaf(tj, Vs[jj * LD + lane + 32 * n], acc[i][n]);
+      }
+    }
+  }
+
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = warp * 4 + i, t = t0 + r;
+    const float m = warp_sum(mass[i]);
+    if (t >= T) continue;
+    float denom = 1.f;
+    if (p.norm == BOZO_NORM_MASS) denom = fmaxf(m, kMassEps);
+    if (p.norm == BOZO_NORM_COUNT) denom = (float)max(min(t, W), 1);
+    const long long ob = (((long long)b * T + t) * p.H + h) * HD;
+#pragma unroll
+    for (int n = 0; n < NJ; ++n) {
+      const int d = lane + 32 * n;
+      if (d < HD) stf(p.out, ob + d, p.out_dt, p.norm == BOZO_NORM_NONE ? acc[i][n] : acc[i][n] / denom);
+    }
+    if (lane == 0 && p.row_mass) p.row_mass[((long long)b * p.H + h) * T + t] = m;
+  }
+}
+
+// ───────────────────────── backward: dQ (+α, β) ─────────────────────────
+// dτ(t,s) = α_t·(dO_t·V_s) + β_t + dTau(t,slot);  ds = dτ·τ(1−τ)/scale
+//   NONE : α = 1,            β = 0
+//   COUNT: α = 1/count_t,    β = 0
+//   MASS : α = 1/max(m,ε),   β = −(dO_t·out_t)/max(m,ε) if m ≥ ε else 0
+template <int NJ>
+__global__ void __launch_bounds__(kThreads) simt_bwd_dq_kernel(BwdP p) {
+  extern __shared__ float sm[];
+  constexpr int LD = 32 * NJ + 1;
+  float* Qs = sm;
+  float* dOs = Qs + kRows * LD;
+  float* Ks = dOs + kRows * LD;
+  float* Vs = Ks + kChunk * LD;
+  const int b = blockIdx.z, h = blockIdx.y, t0 = blockIdx.x * kRows;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T = p.T, HD = p.HD, W = p.W;
+  const bool local = p.mode == BOZO_MODE_LOCAL;
+  const long long row_base = ((long long)b * p.H + h) * T;
+
+  stage_rows(Qs, LD, p.q, b, h, t0, kRows, T, HD, p.cos, p.sin);
+  stage_rows(dOs, LD, p.dout, b, h, t0, kRows, T, HD, nullptr, nullptr);
+  __syncthreads();
+
+  float alpha[4], beta[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = warp * 4 + i, t = t0 + r;
+    alpha[i] = 1.f;
+    beta[i] = 0.f;
+    if (t >= T) continue;
+    if (p.norm == BOZO_NORM_MASS) {
+      const float m = p.row_mass[row_base + t];
+      const float denom = fmaxf(m, kMassEps);
+      float dd = 0.f;
+      const long long ob = (long long)b * p.out.sb + (long long)t * p.out.st + (long long)h * p.out.sh;
+      for (int d = lane; d < HD; d += 32) dd = fmaf(dOs[r * LD + d], ldf(p.out.p, ob + (long long)d * p.out.sd, p.out.dt), dd);
+      dd = warp_sum(dd);
+      alpha[i] = 1.f / denom;
+      beta[i] = (m >= kMassEps) ? -dd / denom : 0.f;
+    } else if (p.norm == BOZO_NORM_COUNT) {
+      alpha[i] = 1.f / (float)max(min(t, W), 1);
+    }
+    if (lane == 0) {
+      p.alpha[row_base + t] = alpha[i];
+      p.beta[row_base + t] = beta[i];
+    }
+  }
+
+  const int s_lo = local ? t0 - W : 0;
+  const int s_hi = local ? min(t0 + kRows - 1, T) : min(t0 + kRows, T);
+  float acc[4][NJ];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int n = 0; n < NJ; ++n) acc[i][n] = 0.f;
+
+  for (int c0 = s_lo; c0 < s_hi; c0 += kChunk) {
+    __syncthreads();
+    stage_rows(Ks, LD, p.k, b, h, c0, kChunk, T, HD, p.cos, p.sin);
+    stage_rows(Vs, LD, p.v, b, h, c0, kChunk, T, HD, nullptr, nullptr);
+    __syncthreads();
+    const int s = c0 + lane;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = warp * 4 + i, t = t0 + r;
+      if (t >= T) continue;
+      const Pair pr = pair_of(p.mode, W, T, t, s);
+      float ds = 0.f;
+      if (pr.valid && s < s_hi) {
+        float x = row_dot(Qs + r * LD, Ks + lane * LD, HD) / p.scale;
+        if (p.bias) x += p.bias[(long long)b * p.bs0 + (long long)t * p.bs1 + (long long)pr.slot * p.bs2];
+        const float tau = sigmoid_exact(x);
+        float dtau = fmaf(alpha[i], row_dot(dOs + r * LD, Vs + lane * LD, HD), beta[i]);
+        if (p.dtau && pr.tau_slot >= 0)
+          dtau += ldf(p.dtau, (((long long)b * T + t) * p.H + h) * W + pr.tau_slot, p.dtau_dt);
+        ds = dtau * tau * (1.f - tau) / p.scale;
+      }
+      for (int jj = 0; jj < kChunk; ++jj) {
+        const float dj = __shfl_sync(0xffffffffu, ds, jj);
+        if (dj == 0.f) continue;
+#pragma unroll
+        for (int n = 0; n < NJ; ++n) acc[i][n] = fmaf(dj, Ks[jj * LD + lane + 32 * n], acc[i][n]);
+      }
+    }
+  }
+
+  // inverse RoPE (transpose rotation) through a shared-memory row, then store
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = warp * 4 + i;
+#pragma unroll
+    for (int n = 0; n < NJ; ++n) {
+      const int d = lane + 32 * n;
+      if (d < HD) Qs[r * LD + d] = acc[i][n];
+    }
+  }
+  __syncwarp();
+  const int half = HD / 2;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = warp * 4 + i, t = t0 + r;
+    if (t >= T) continue;
+    const long long ob = (((long long)b * T + t) * p.H + h) * HD;
+    for (int d = lane; d < HD; d += 32) {
+      float g = Qs[r * LD + d];
+      if (p.cos) {
+        const int dd = d < half ? d : d - half;
+        const float c = p.cos[(long long)t * half + dd], sn = p.sin[(long long)t * half + dd];
+        const float g1 = Qs[r * LD + dd], g2 = Qs[r * LD + dd + half];
+        g = d < half ? (g1 * c + g2 * sn) : (g2 * c - g1 * sn);
+      }
+      stf(p.dq, ob + d, p.dq_dt, g);
+    }
+  }
+}
+
+// ─────────────────────── backward: dK, dV (key-centric) ───────────────────────
+template <int NJ>
+__global__ void __launch_bounds__(kThreads) simt_bwd_dkv_kernel(BwdP p) {
+  extern __shared__ float sm[];
+  constexpr int LD = 32 * NJ + 1;
+  float* Ks = sm;
+  float* Vs = Ks + kRows * LD;
+  float* Qc = Vs + kRows * LD;
+  float* dOc = Qc + kChunk * LD;
+  float* Ac = dOc + kChunk * LD;
+  float* Bc = Ac + kChunk;
+  const int b = blockIdx.z, h = blockIdx.y, s0 = blockIdx.x * kRows;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T = p.T, HD = p.HD, W = p.W;
+  const bool local = p.mode == BOZO_MODE_LOCAL;
+  const long long row_base = ((long long)b * p.H + h) * T;
+
+  stage_rows(Ks, LD, p.k, b, h, s0, kRows, T, HD, p.cos, p.sin);
+  stage_rows(Vs, LD, p.v, b, h, s0, kRows, T, HD, nullptr, nullptr);
+
+  const int t_lo = local ? s0 + 1 : s0;
+  const int t_hi = local ? min(s0 + kRows - 1 + W + 1, T) : T;
+
+  float dk[4][NJ], dv[4][NJ];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int n = 0; n < NJ; ++n) dk[i][n] = dv[i][n] = 0.f;
+
+  for (int c0 = t_lo; c0 < t_hi; c0 += kChunk) {
+    __syncthreads();
+    stage_rows(Qc, LD, p.q, b, h, c0, kChunk, T, HD, p.cos, p.sin);
+    stage_rows(dOc, LD, p.dout, b, h, c0, kChunk, T, HD, nullptr, nullptr);
+    stage_scalars(Ac, Bc, p.alpha, p.beta, row_base, c0, kChunk, T);
+    __syncthreads();
+    const int t = c0 + lane;
+    const float a_t = Ac[lane], b_t = Bc[lane];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = warp * 4 + i, s = s0 + r;
+      if (s >= T) continue;
+      const Pair pr = pair_of(p.mode, W, T, t, s);
+      float ds = 0.f, pa = 0.f;
+      if (pr.valid && t < t_hi) {
+        float x = row_dot(Qc + lane * LD, Ks + r * LD, HD) / p.scale;
+        if (p.bias) x += p.bias[(long long)b * p.bs0 + (long long)t * p.bs1 + (long long)pr.slot * p.bs2];
+        const float tau = sigmoid_exact(x);
+        float dtau = fmaf(a_t, row_dot(dOc + lane * LD, Vs + r * LD, HD), b_t);
+        if (p.dtau && pr.tau_slot >= 0)
+          dtau += ldf(p.dtau, (((long long)b * T + t) * p.H + h) * W + pr.tau_slot, p.dtau_dt);
+        ds = dtau * tau * (1.f - tau) / p.scale;
+        pa = tau * a_t;
+      }
+      for (int jj = 0; jj < kChunk; ++jj) {
+        const float dj = __shfl_sync(0xffffffffu, ds, jj);
+        const float pj = __shfl_sync(0xffffffffu, pa, jj);
+        if (dj == 0.f && pj == 0.f) continue;
+#pragma unroll
+        for (int n = 0; n < NJ; ++n) {
+          dk[i][n] = fmaf(dj, Qc[jj * LD + lane + 32 * n], dk[i][n]);
+          dv[i][n] = fmaf(pj, dOc[jj * LD + lane + 32 * n], dv[i][n]);
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = warp * 4 + i;
+#pragma unroll
+    for (int n = 0; n < NJ; ++n) {
+      const int d = lane + 32 * n;
+      if (d < HD) Ks[r * LD + d] = dk[i][n];
+    }
+  }
+  __syncwarp();
+  const int half = HD / 2;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = warp * 4 + i, s = s0 + r;
+    if (s >= T) continue;
+    const long long ob = (((long long)b * T + s) * p.H + h) * HD;
+#pragma unroll
+    for (int n = 0; n < NJ; ++n) {
+      const int d = lane + 32 * n;
+      if (d < HD) stf(p.dv, ob + d, p.dv_dt, dv[i][n]);
+    }
+    for (int d = lane; d < HD; d += 32) {
+      float g = Ks[r * LD + d];
+      if (p.cos) {
+        const int dd = d < half ? d : d - half;
+        const float c = p.cos[(long long)s * half + dd], sn = p.sin[(long long)s * half + dd];
+        const float g1 = Ks[r * LD + dd], g2 = Ks[r * LD + dd + half];
+        g = d < half ? (g1 * c + g2 * sn) : (g2 * c - g1 * sn);
+      }
+      stf(p.dk, ob + d, p.dk_dt, g);
+    }
+  }
+}
+
+template <int NJ>
+cudaError_t fwd_nj(const FwdP& p, cudaStream_t st) {
+  constexpr int LD = 32 * NJ + 1;
+  const size_t smem = sizeof(float) * (kRows * LD + 2 * kChunk * LD);
+  cudaError_t e = cudaFuncSetAttribute(simt_fwd_kernel<NJ>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((p.T + kRows - 1) / kRows, p.H, p.B);
+  simt_fwd_kernel<NJ><<<grid, kThreads, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <int NJ>
+cudaError_t bwd_nj(const BwdP& p, cudaStream_t st) {
+  constexpr int LD = 32 * NJ + 1;
+  const size_t smem_dq = sizeof(float) * (2 * kRows * LD + 2 * kChunk * LD);
+  const size_t smem_dkv = sizeof(float) * (2 * kRows * LD + 2 * kChunk * LD + 2 * kChunk);
+  cudaError_t e = cudaFuncSetAttribute(simt_bwd_dq_kernel<NJ>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dq);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(simt_bwd_dkv_kernel<NJ>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dkv);
+  if (e != cudaSuccess) return e;
+  dim3 grid((p.T + kRows - 1) / kRows, p.H, p.B);
+  simt_bwd_dq_kernel<NJ><<<grid, kThreads, smem_dq, st>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  simt_bwd_dkv_kernel<NJ><<<grid, kThreads, smem_dkv, st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_simt_fwd(const FwdP& p, cudaStream_t st, int* launches) {
+  *launches = 1;
+  if (p.HD <= 32) return fwd_nj<1>(p, st);
+  if (p.HD <= 64) return fwd_nj<2>(p, st);
+  return fwd_nj<4>(p, st);
+}
+
+cudaError_t launch_simt_bwd(const BwdP& p, cudaStream_t st, int* launches) {
+  *launches = 2;
+  if (p.HD <= 32) return bwd_nj<1>(p, st);
+  if (p.HD <= 64) return bwd_nj<2>(p, st);
+  return bwd_nj<4>(p, st);
+}
+
+}  // namespace bozo

@@ -1,0 +1,333 @@
+"""Autograd front-ends of the B200 tension operator.
+
+* ``causal_tension`` — drop-in for ``triton_tension.causal_tension``
+  (reference triton_tension/ops.py:192-224): same signature, same raw
+  (unnormalised) Σ τ·V output, same optional ``[B,T,H,W]`` τ, same bias
+  contract (``[B,T,W]``, fp32, no gradient; ops.py:90-100, 184-187), outputs
+  in ``Q.dtype`` and gradients in each input's dtype (ops.py:122-124,
+  186-187).  Unlike the reference there is no CPU/float64 branch
+  (ops.py:217-219): such inputs raise.
+* ``tension`` — the fused entry point: RoPE on Q/K (model.py:200-204), local
+  window or global full-causal mode (model.py:217-237), the model's τ-mass
+  (model.py:257-258) or position-count (model.py:261-264) normalisation and
+  optional τ export, in one forward and one backward kernel family.
+
+Both call the C ABI (``include/bozo_tension.h``) through ``_capi`` on the
+caller's current CUDA stream.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from . import _capi
+
+_DT = {torch.float32: _capi.DT_F32, torch.bfloat16: _capi.DT_BF16,
+       torch.float16: _capi.DT_F16}
+_NORM = {None: _capi.NORM_NONE, "none": _capi.NORM_NONE, "mass": _capi.NORM_MASS,
+         "count": _capi.NORM_COUNT}
+_PATH = {"auto": _capi.PATH_AUTO, "simt": _capi.PATH_SIMT, "tcgen05": _capi.PATH_TCGEN05}
+
+# Kernel-path override for tests and benchmarks ("auto", "simt", "tcgen05").
+_path_override = "auto"
+
+
+def set_kernel_path(path: str) -> None:
+    """Select the kernel family: "auto" (default), "simt" or "tcgen05"."""
+    global _path_override
+    if path not in _PATH:
+        raise ValueError(f"unknown kernel path {path!r}")
+    _path_override = path
+
+
+def _dt(t: Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"bozo tension: unsupported dtype {t.dtype} "
+                        "(float32, bfloat16 and float16 are supported)") from None
+
+
+def _t4(t: Optional[Tensor]) -> _capi.Tensor4:
+    s = _capi.Tensor4()
+    if t is None:
+        return s
+    s.ptr = t.data_ptr()
+    s.dtype = _dt(t)
+    for i in range(4):
+        s.stride[i] = t.stride(i)
+    return s
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _require_cuda(*ts: Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError("bozo tension runs on CUDA only (no CPU fallback); "
+                               f"got a tensor on {t.device}")
+        if t.dim() != 4:
+            raise ValueError(f"expected a 4-D [B,T,H,HD] tensor, got shape {tuple(t.shape)}")
+    dev = ts[0].device
+    for t in ts[1:]:
+        if t.device != dev:
+            raise RuntimeError("bozo tension: all tensors must be on one device")
+
+
+_rope_cache: dict = {}
+
+
+def rope_tables(head_dim: int, length: int, base: float, device) -> tuple[Tensor, Tensor]:
+    """fp32 cos/sin ``[length, HD/2]`` built exactly as model.py:66-73 does."""
+    key = (head_dim, length, float(base), str(device))
+    tab = _rope_cache.get(key)
+    if tab is None:
+        half = head_dim // 2
+        theta = 1.0 / (base ** (torch.arange(0, half).float() / half))
+        freqs = torch.outer(torch.arange(length).float(), theta)
+        tab = (freqs.cos().contiguous().to(device), freqs.sin().contiguous().to(device))
+        _rope_cache[key] = tab
+    return tab
+
+
+def _fill_common(a, B, T, H, HD, mode, window, norm, scale, rope):
+    a.B, a.T, a.H, a.HD = B, T, H, HD
+    a.mode, a.window, a.normalize = mode, window, norm
+    a.path = _PATH[_path_override]
+    a.scale = float(scale)
+    if rope is not None:
+        cos, sin = rope
+        a.rope_len = cos.shape[0]
+        a.rope_cos, a.rope_sin = cos.data_ptr(), sin.data_ptr()
+    else:
+        a.rope_len = 0
+
+
+def _bias_arg(a, bias: Optional[Tensor]):
+    if bias is not None:
+        a.bias = bias.data_ptr()
+        for i in range(3):
+            a.bias_stride[i] = bias.stride(i)
+
+
+def _launch_fwd(q, k, v, *, mode, window, norm, scale, rope, bias, tau_width,
+                out_dtype, tau_dtype, want_mass):
+    B, T, H, HD = q.shape
+    out = torch.empty(B, T, H, HD, dtype=out_dtype, device=q.device)
+    tau = (torch.empty(B, T, H, tau_width, dtype=tau_dtype, device=q.device)
+           if tau_width is not None else None)
+    mass = (torch.empty(B, H, T, dtype=torch.float32, device=q.device)
+            if want_mass else None)
+    a = _capi.FwdArgs()
+    _fill_common(a, B, T, H, HD, mode, window, norm, scale, rope)
+    a.q, a.k, a.v = _t4(q), _t4(k), _t4(v)
+    _bias_arg(a, bias)
+    a.out, a.out_dtype = out.data_ptr(), _DT[out_dtype]
+    if tau is not None:
+        a.tau, a.tau_dtype = tau.data_ptr(), _DT[tau_dtype]
+    if mass is not None:
+        a.row_mass = mass.data_ptr()
+    _capi.check(_capi.lib().bozo_tension_fwd(C.byref(a), _stream(q.device)),
+                "bozo_tension_fwd")
+    return out, tau, mass
+
+
+def _launch_bwd(q, k, v, d_out, *, mode, window, norm, scale, rope, bias, out,
+                mass, d_tau):
+    B, T, H, HD = q.shape
+    dq = torch.empty(B, T, H, HD, dtype=q.dtype, device=q.device)
+    dk = torch.empty(B, T, H, HD, dtype=k.dtype, device=q.device)
+    dv = torch.empty(B, T, H, HD, dtype=v.dtype, device=q.device)
+    a = _capi.BwdArgs()
+    _fill_common(a, B, T, H, HD, mode, window, norm, scale, rope)
+    a.q, a.k, a.v, a.d_out = _t4(q), _t4(k), _t4(v), _t4(d_out)
+    if out is not None:
+        a.out = _t4(out)
+    if mass is not None:
+        a.row_mass = mass.data_ptr()
+    _bias_arg(a, bias)
+    if d_tau is not None:
+        a.d_tau, a.d_tau_dtype = d_tau.data_ptr(), _dt(d_tau)
+    a.grad_dtype[0], a.grad_dtype[1], a.grad_dtype[2] = _dt(q), _dt(k), _dt(v)
+    a.dq, a.dk, a.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
+    L = _capi.lib()
+    ws_bytes = L.bozo_tension_bwd_workspace(C.byref(a))
+    ws = None
+    if ws_bytes:
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws_bytes
+    _capi.check(L.bozo_tension_bwd(C.byref(a), _stream(q.device)), "bozo_tension_bwd")
+    return dq, dk, dv
+
+
+def _prep_bias(bias: Optional[Tensor], shape: tuple) -> Optional[Tensor]:
+    if bias is None:
+        return None
+    b = bias.to(torch.float32)
+    # same contract and message as triton_tension/ops.py:93-97
+    assert b.ndim == 3 and tuple(b.shape) == shape, (
+        f"bias must be [B, T, W]=[{shape[0]}, {shape[1]}, {shape[2]}], got {tuple(b.shape)}")
+    return b
+
+
+# ───────────────────────── drop-in raw operator ─────────────────────────
+
+class _CausalTensionFn(torch.autograd.Function):
+    """Mirror of triton_tension/ops.py:73-187 over the C ABI."""
+
+    @staticmethod
+    def forward(ctx, Q, K, V, W: int, scale: float, return_tau: bool, bias):
+        B, T, H, HD = Q.shape
+        Bias = _prep_bias(bias, (B, T, W))
+        out, tau, _ = _launch_fwd(Q, K, V, mode=_capi.MODE_LOCAL, window=W,
+                                  norm=_capi.NORM_NONE, scale=scale, rope=None,
+                                  bias=Bias, tau_width=W if return_tau else None,
+                                  out_dtype=Q.dtype, tau_dtype=Q.dtype, want_mass=False)
+        ctx.save_for_backward(Q, K, V, Bias)
+        ctx.W, ctx.scale, ctx.return_tau = W, scale, return_tau
+        if return_tau:
+            return out, tau
+        return out
+
+    @staticmethod
+    def backward(ctx, *grads):
+        Q, K, V, Bias = ctx.saved_tensors
+        d_out = grads[0]
+        d_tau = grads[1] if ctx.return_tau else None
+        if d_out is None:
+            d_out = torch.zeros_like(Q)
+        if d_tau is not None:
+            d_tau = d_tau.contiguous()
+        dq, dk, dv = _launch_bwd(Q, K, V, d_out, mode=_capi.MODE_LOCAL, window=ctx.W,
+                                 norm=_capi.NORM_NONE, scale=ctx.scale, rope=None,
+                                 bias=Bias, out=None, mass=None, d_tau=d_tau)
+        return dq, dk, dv, None, None, None, None
+
+
+@torch._dynamo.disable
+def causal_tension(Q: Tensor, K: Tensor, V: Tensor, window: int, scale: float,
+                   return_tau: bool = False, bias: Tensor | None = None):
+    """Fused causal sigmoid tension — drop-in for triton_tension.causal_tension.
+
+    Q, K, V : [B, T, H, HD] CUDA tensors (float32 / bfloat16 / float16, any
+              strides, dtypes may differ).
+    window  : causal look-back W (self excluded).
+    scale   : dot-product divisor (√HD in model.py).
+    return_tau : also return τ [B, T, H, W] (dtype of Q).
+    bias    : optional [B, T, W] pre-sigmoid bias, broadcast over heads.
+
+    Returns raw out [B, T, H, HD] = Σ τ·V (dtype of Q) or (out, tau).
+    """
+    _require_cuda(Q, K, V)
+    if int(window) < 1:
+        raise ValueError("window must be >= 1")
+    return _CausalTensionFn.apply(Q, K, V, int(window), float(scale), bool(return_tau), bias)
+
+
+# ───────────────────────── fused entry point ─────────────────────────
+
+class _TensionFn(torch.autograd.Function):
+
+    @staticmethod
+    def forward(ctx, q, k, v, mode, window, tau_width, norm, scale, rope_base,
+                rope_len, bias, return_tau):
+        B, T, H, HD = q.shape
+        rope = (rope_tables(HD, rope_len, rope_base, q.device)
+                if rope_base is not None else None)
+        if bias is not None:
+            shape = (B, T, T) if mode == _capi.MODE_GLOBAL else (B, T, window)
+            bias = _prep_bias(bias, shape)
+        w_arg = window if mode == _capi.MODE_LOCAL else (tau_width or 0)
+        out, tau, mass = _launch_fwd(
+            q, k, v, mode=mode, window=w_arg, norm=norm, scale=scale, rope=rope,
+            bias=bias, tau_width=(w_arg if return_tau else None), out_dtype=q.dtype,
+            tau_dtype=q.dtype, want_mass=True)
+        ctx.save_for_backward(q, k, v, out, mass, bias)
+        ctx.cfg = (mode, w_arg, norm, scale, rope_base, rope_len, return_tau)
+        ctx.mark_non_differentiable(mass)
+        if return_tau:
+            return out, tau
+        return out
+
+    @staticmethod
+    def backward(ctx, *grads):
+        q, k, v, out, mass, bias = ctx.saved_tensors
+        mode, w_arg, norm, scale, rope_base, rope_len, return_tau = ctx.cfg
+        d_out = grads[0]
+        if d_out is None:
+            d_out = torch.zeros_like(out)
+        d_tau = grads[1] if return_tau else None
+        if d_tau is not None:
+            d_tau = d_tau.contiguous()
+        rope = (rope_tables(q.shape[3], rope_len, rope_base, q.device)
+                if rope_base is not None else None)
+        dq, dk, dv = _launch_bwd(q, k, v, d_out, mode=mode, window=w_arg, norm=norm,
+                                 scale=scale, rope=rope, bias=bias, out=out, mass=mass,
+                                 d_tau=d_tau)
+        return dq, dk, dv, None, None, None, None, None, None, None, None, None
+
+
+@torch._dynamo.disable
+def tension(q: Tensor, k: Tensor, v: Tensor, *, window: Optional[int],
+            scale: Optional[float] = None, rope_base: Optional[float] = 10_000.0,
+            rope_len: Optional[int] = None, bias: Optional[Tensor] = None,
+            return_tau: bool = False, normalize: Optional[str] = "mass",
+            tau_window: Optional[int] = None):
+    """Fused tension layer core: RoPE → tension → normalisation (+ τ export).
+
+    q, k, v    : [B, T, H, HD] pre-RoPE projections (CUDA).
+    window     : local look-back W, or ``None`` for the global full-causal mode
+                 (self included, model.py:217-237).
+    scale      : dot divisor, default √HD (model.py:122).
+    rope_base  : RoPE base (model.py:66) or ``None`` for no rotation.
+    rope_len   : rows of the RoPE table (model.py uses max_seq_len; only rows
+                 < T are read), default T.
+    bias       : [B, T, W] (local) / [B, T, T] (global) pre-sigmoid bias.
+    normalize  : "mass" (model.py:257-258), "count" (model.py:261-264, local
+                 only) or None (raw Σ τ·V).
+    return_tau : also return τ; local → [B,T,H,W], global → the reference's
+                 exported window [B,T,H,min(tau_window,T)] (model.py:235-236).
+    tau_window : global mode only — the model's local W that sizes the
+                 exported τ window (required with return_tau).
+    """
+    _require_cuda(q, k, v)
+    B, T, H, HD = q.shape
+    if scale is None:
+        scale = math.sqrt(HD)
+    if window is None:
+        mode = _capi.MODE_GLOBAL
+        if normalize == "count":
+            raise ValueError("normalize='count' is defined for local windows only")
+        if return_tau and not tau_window:
+            raise ValueError("global mode exports τ over the model's local window: "
+                             "pass tau_window (model.py:235 uses min(window, T))")
+        tw = min(int(tau_window), T) if tau_window else 0
+        win = 0
+    else:
+        mode, win, tw = _capi.MODE_LOCAL, int(window), None
+        if win < 1:
+            raise ValueError("window must be >= 1")
+    return _TensionFn.apply(q, k, v, mode, win, tw, _NORM[normalize], float(scale),
+                            rope_base, int(rope_len or T), bias, bool(return_tau))
+
+
+def last_path() -> str:
+    """Kernel family of the last call on this thread ("simt"/"tcgen05")."""
+    return {0: "none", 1: "simt", 2: "tcgen05"}[_capi.lib().bozo_tension_last_path()]
+
+
+def last_launches() -> int:
+    return _capi.lib().bozo_tension_last_launches()
+
+
+def poll_device_error(device=None) -> None:
+    """Synchronise and raise if a bounded device-side wait timed out."""
+    dev = torch.device(device) if device is not None else torch.device("cuda")
+    code = _capi.lib().bozo_tension_poll_error(_stream(dev))
+    _capi.check(code, "device error poll")

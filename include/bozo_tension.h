@@ -1,0 +1,154 @@
+/*
+ * bozo_tension.h — C ABI of the B200 (sm_100a) sigmoid-tension operator.
+ *
+ * Plain pointers, sizes and strides only: no framework types cross this
+ * boundary.  Every call is asynchronous on the caller's CUDA stream, borrows
+ * its inputs, writes caller-allocated outputs, keeps no state between calls
+ * and is safe to call concurrently from several host threads (one stream
+ * each).
+ *
+ * Semantics (Q,K,V,dO are [B,T,H,HD]; σ = logistic sigmoid; scale = √HD in
+ * the reference model):
+ *
+ *   LOCAL  (window W ≥ 1): key slot w ∈ [0,W) of query t is position
+ *          s = t − (W − w); valid iff s ≥ 0 (self excluded).
+ *   GLOBAL (full causal):  keys s ∈ [0, t] (self included).
+ *
+ *   τ[t,s] = σ( Rq_t·Rk_s / scale + bias ) · valid     (R = optional RoPE)
+ *   S_t    = Σ_s τ[t,s] · V_s
+ *   out_t  = S_t                          (BOZO_NORM_NONE  — raw op)
+ *          = S_t / max(Σ_s τ[t,s], 1e-6)  (BOZO_NORM_MASS  — τ-mass)
+ *          = S_t / max(#valid slots, 1)   (BOZO_NORM_COUNT — position count)
+ *
+ * Reference interfaces replaced (BoggersTheFish/bozo):
+ *   bozo_tension_fwd  ← triton_tension/ops.py:75-124 (_CausalTensionFn.forward,
+ *                       the _fwd_kernel launch at ops.py:104) and, with
+ *                       NORM_MASS / NORM_COUNT / rope / GLOBAL, the
+ *                       surrounding model.py:200-237, 257-258, 261-264 code.
+ *   bozo_tension_bwd  ← triton_tension/ops.py:126-187 (_CausalTensionFn.backward,
+ *                       the _bwd_dq_kernel / _bwd_dkv_kernel launches at
+ *                       ops.py:165 and ops.py:174) plus autograd of the
+ *                       model.py normalisation and RoPE.
+ */
+#ifndef BOZO_TENSION_H
+#define BOZO_TENSION_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BOZO_TENSION_ABI_VERSION 1
+
+typedef enum {
+  BOZO_OK = 0,
+  BOZO_ERR_BAD_SHAPE = 1,      /* non-positive sizes, W < 1, bad bias/tau shape */
+  BOZO_ERR_BAD_DTYPE = 2,      /* dtype code not in bozo_dtype */
+  BOZO_ERR_UNSUPPORTED = 3,    /* e.g. HD > 128, odd HD with RoPE */
+  BOZO_ERR_ALIGNMENT = 4,      /* a forced tensor-core path got unaligned data */
+  BOZO_ERR_NULL = 5,           /* a required pointer is NULL */
+  BOZO_ERR_DEVICE_TIMEOUT = 6, /* a bounded device-side wait gave up */
+  BOZO_ERR_CUDA = 7,           /* a CUDA runtime call failed */
+  BOZO_ERR_WORKSPACE = 8       /* workspace NULL or smaller than required */
+} bozo_status;
+
+typedef enum { BOZO_DT_F32 = 0, BOZO_DT_BF16 = 1, BOZO_DT_F16 = 2 } bozo_dtype;
+typedef enum { BOZO_MODE_LOCAL = 0, BOZO_MODE_GLOBAL = 1 } bozo_mode;
+typedef enum { BOZO_NORM_NONE = 0, BOZO_NORM_MASS = 1, BOZO_NORM_COUNT = 2 } bozo_norm;
+
+/* Kernel-path selection (flags). AUTO picks the tcgen05 path whenever the
+ * inputs qualify (bf16 Q/K/V with unit HD stride, 16-byte aligned rows,
+ * HD = 64, LOCAL, W ≤ 128), else the exact-fp32 SIMT path. */
+enum {
+  BOZO_PATH_AUTO = 0,
+  BOZO_PATH_SIMT = 1,     /* force the fp32 CUDA-core path */
+  BOZO_PATH_TCGEN05 = 2   /* force the tensor-core path; error if ineligible */
+};
+
+/* A strided 4-D view [B,T,H,HD] (element strides). */
+typedef struct {
+  const void* ptr;
+  int32_t dtype;          /* bozo_dtype */
+  int32_t _pad;
+  int64_t stride[4];      /* b, t, h, d — in elements */
+} bozo_tensor4;
+
+typedef struct {
+  int32_t B, T, H, HD;
+  int32_t mode;           /* bozo_mode */
+  int32_t window;         /* LOCAL: W. GLOBAL: width of the exported τ window
+                             (min(local W, T) as model.py:235 takes it). */
+  int32_t normalize;      /* bozo_norm */
+  int32_t path;           /* BOZO_PATH_* */
+  float scale;            /* divisor of the dot product (√HD in model.py:122) */
+  int32_t rope_len;       /* rows of the RoPE tables (≥ T) or 0 for no RoPE */
+  const float* rope_cos;  /* [rope_len, HD/2] fp32 contiguous, or NULL */
+  const float* rope_sin;
+  bozo_tensor4 q, k, v;
+  const float* bias;      /* LOCAL [B,T,W] / GLOBAL [B,T,T] fp32, or NULL */
+  int64_t bias_stride[3];
+  /* outputs */
+  void* out;              /* [B,T,H,HD] contiguous, dtype out_dtype */
+  int32_t out_dtype;
+  int32_t tau_dtype;
+  void* tau;              /* [B,T,H,window] contiguous or NULL (no export) */
+  float* row_mass;        /* [B,H,T] fp32 Σ_s τ (unclamped) or NULL */
+} bozo_tension_fwd_args;
+
+typedef struct {
+  int32_t B, T, H, HD;
+  int32_t mode, window, normalize, path;
+  float scale;
+  int32_t rope_len;
+  const float* rope_cos;
+  const float* rope_sin;
+  bozo_tensor4 q, k, v;   /* the forward inputs (pre-RoPE when RoPE is on) */
+  bozo_tensor4 d_out;     /* cotangent of out */
+  bozo_tensor4 out;       /* forward output — read only for NORM_MASS */
+  const float* row_mass;  /* forward Σ τ [B,H,T] — required for NORM_MASS */
+  const float* bias;
+  int64_t bias_stride[3];
+  const void* d_tau;      /* [B,T,H,window] contiguous cotangent of τ, or NULL */
+  int32_t d_tau_dtype;
+  int32_t grad_dtype[3];  /* dtypes of dq, dk, dv */
+  int32_t _pad;
+  void* dq;               /* [B,T,H,HD] contiguous (gradient w.r.t. pre-RoPE q) */
+  void* dk;
+  void* dv;
+  void* workspace;        /* device scratch of bozo_tension_bwd_workspace() bytes */
+  size_t workspace_bytes;
+} bozo_tension_bwd_args;
+
+/* Forward. Returns bozo_status; launches are asynchronous on `stream`
+ * (a cudaStream_t, NULL = legacy default stream). */
+int bozo_tension_fwd(const bozo_tension_fwd_args* args, void* stream);
+
+/* Device scratch the backward needs for these arguments (bytes, 256-aligned
+ * size; 0 is possible). */
+size_t bozo_tension_bwd_workspace(const bozo_tension_bwd_args* args);
+
+/* Backward: writes dq, dk, dv. */
+int bozo_tension_bwd(const bozo_tension_bwd_args* args, void* stream);
+
+/* Synchronise `stream`, then read and clear the device error word that
+ * bounded waits inside the tensor-core kernels set when they give up.
+ * Returns BOZO_OK or BOZO_ERR_DEVICE_TIMEOUT (or BOZO_ERR_CUDA). */
+int bozo_tension_poll_error(void* stream);
+
+/* Which kernel path the last successful call in this process ran:
+ * BOZO_PATH_SIMT or BOZO_PATH_TCGEN05 (0 before any call). */
+int bozo_tension_last_path(void);
+
+/* Number of kernels the last successful call in this process launched. */
+int bozo_tension_last_launches(void);
+
+const char* bozo_status_string(int status);
+int bozo_tension_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BOZO_TENSION_H */

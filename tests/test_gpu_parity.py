@@ -1,0 +1,262 @@
+"""GPU parity of the tension operator against the reference (golden fixtures
+made by the reference's own code) and the float64 CPU oracle.
+
+Ports the intent of the reference's script tests — triton_tension/test.py
+(forward, manual grads, bias variants, large bf16 spot check) and
+triton_tension/test_tau.py (τ parity, Out bit-identical with/without τ,
+backward through τ, τ-unused parity, memory bound) — with the stricter
+tolerances of ``tests/_tol.py``.  Every call goes through the C ABI.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import tension_oracle as orc
+from tests._tol import TOL, assert_close
+
+pytestmark = pytest.mark.gpu
+
+cuda = pytest.mark.skipif(not torch.cuda.is_available(), reason="needs CUDA")
+
+
+@pytest.fixture(scope="module")
+def bz():
+    import bozo_b200
+    bozo_b200.set_kernel_path("auto")
+    return bozo_b200
+
+
+def _cu(a, dtype):
+    return torch.from_numpy(np.asarray(a)).to("cuda").to(dtype)
+
+
+def _run_raw(bz, c, dtype, with_tau=True):
+    B, T, H, HD, W = [int(x) for x in c["meta"]]
+    q, k, v = [_cu(c[n], dtype).requires_grad_(True) for n in ("q", "k", "v")]
+    bias = _cu(c["bias"], torch.float32) if "bias" in c else None
+    out, tau = bz.causal_tension(q, k, v, W, float(c["scale"]), return_tau=True, bias=bias)
+    loss = (out.float() * _cu(c["d_out"], torch.float32)).sum()
+    if "d_tau" in c:
+        loss = loss + (tau.float() * _cu(c["d_tau"], torch.float32)).sum()
+    loss.backward()
+    return out, tau, q.grad, k.grad, v.grad
+
+
+def _oracle_raw(c, dtype):
+    """float64 oracle on the dtype-rounded inputs (exact golden for fp32)."""
+    B, T, H, HD, W = [int(x) for x in c["meta"]]
+    rd = lambda a: torch.from_numpy(np.asarray(a)).to(dtype).double()
+    bias = torch.from_numpy(np.asarray(c["bias"], np.float64)) if "bias" in c else None
+    d_tau = rd(c["d_tau"]) if "d_tau" in c else None
+
+    def fn(q, k, v):
+        return orc.local_tension_raw(q, k, v, W, float(c["scale"]), bias, return_tau=True)
+
+    (o, t), (dq, dk, dv) = orc.tension_with_grads(
+        fn, [rd(c["q"]), rd(c["k"]), rd(c["v"])],
+        [torch.from_numpy(np.asarray(c["d_out"], np.float64)),
+         torch.from_numpy(np.asarray(c["d_tau"], np.float64)) if "d_tau" in c else None])
+    return o, t, dq, dk, dv
+
+
+@cuda
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_raw_op_matches_reference_golden(bz, golden_op, dtype):
+    for name, c in sorted(golden_op.items()):
+        got = _run_raw(bz, c, dtype)
+        if dtype == torch.float32:
+            ref = [c["out"], c["tau"], c["dq"], c["dk"], c["dv"]]
+        else:
+            ref = _oracle_raw(c, dtype)
+        for g, r, what in zip(got, ref, ("out", "tau", "dq", "dk", "dv")):
+            assert_close(g, r, dtype, f"{name}/{dtype}/{what}")
+
+
+@cuda
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fused_layer_matches_reference_golden(bz, golden_layer, dtype):
+    """RoPE + local/global tension + τ-mass normalisation + τ export vs
+    model.py's own layer (golden), forward and backward."""
+    for name, c in sorted(golden_layer.items()):
+        B, T, H, HD, W, Wl, msl = [int(x) for x in c["meta"]]
+        if dtype == torch.float32:
+            qa, ka, va = c["q_raw"], c["k_raw"], c["v"]
+        else:
+            qa, ka, va = [torch.from_numpy(c[n]).to(dtype).double().numpy()
+                          for n in ("q_raw", "k_raw", "v")]
+        q, k, v = [_cu(a, dtype).requires_grad_(True) for a in (qa, ka, va)]
+        bias = _cu(c["bias"], torch.float32) if "bias" in c else None
+        out, tau = bz.tension(q, k, v, window=None if W < 0 else W,
+                              scale=float(c["scale"]), rope_base=10_000.0, rope_len=msl,
+                              bias=bias, return_tau=True, normalize="mass", tau_window=Wl)
+        d_out = _cu(c["d_out"], torch.float32)
+        d_tau = _cu(c["d_tau"], torch.float32)
+        ((out.float() * d_out).sum() + (tau.float() * d_tau).sum()).backward()
+        if dtype == torch.float32:
+            ref = [c["out"], c["tau"], c["dq_raw"], c["dk_raw"], c["dv"]]
+        else:
+            bias64 = torch.from_numpy(c["bias"]) if "bias" in c else None
+
+            def fn(q_, k_, v_):
+                return orc.fused_reference(q_, k_, v_, window=None if W < 0 else W,
+                                           scale=float(c["scale"]), bias=bias64,
+                                           local_window=Wl, max_seq_len=msl)
+            (o, t), grads = orc.tension_with_grads(
+                fn, [torch.from_numpy(a) for a in (qa, ka, va)],
+                [torch.from_numpy(c["d_out"]), torch.from_numpy(c["d_tau"])])
+            ref = [o, t, *grads]
+        for g, r, what in zip((out, tau, q.grad, k.grad, v.grad), ref,
+                              ("out", "tau", "dq", "dk", "dv")):
+            assert_close(g, r, dtype, f"{name}/{dtype}/{what}")
+
+
+@cuda
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_out_identical_with_and_without_tau(bz, dtype):
+    """test_tau.py:47-60 — requesting τ must not change Out (bit-exact)."""
+    torch.manual_seed(1)
+    for (B, T, H, HD, W) in ((2, 16, 2, 16, 6), (2, 300, 3, 64, 64)):
+        q, k, v = [torch.randn(B, T, H, HD, device="cuda", dtype=dtype) for _ in range(3)]
+        a = bz.causal_tension(q, k, v, W, math.sqrt(HD))
+        b, _ = bz.causal_tension(q, k, v, W, math.sqrt(HD), return_tau=True)
+        assert torch.equal(a, b)
+
+
+@cuda
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_backward_tau_unused_matches_no_tau(bz, dtype):
+    """test_tau.py:102-127 — τ returned but unused gives the same grads."""
+    torch.manual_seed(3)
+    B, T, H, HD, W = 2, 200, 2, 64, 32
+    base = [torch.randn(B, T, H, HD, device="cuda", dtype=dtype) for _ in range(3)]
+    d_out = torch.randn(B, T, H, HD, device="cuda", dtype=dtype)
+    qa, ka, va = [x.clone().requires_grad_(True) for x in base]
+    (bz.causal_tension(qa, ka, va, W, 8.0) * d_out).sum().backward()
+    qb, kb, vb = [x.clone().requires_grad_(True) for x in base]
+    out_b, _ = bz.causal_tension(qb, kb, vb, W, 8.0, return_tau=True)
+    (out_b * d_out).sum().backward()
+    for ga, gb in ((qa.grad, qb.grad), (ka.grad, kb.grad), (va.grad, vb.grad)):
+        assert (ga.float() - gb.float()).abs().max().item() <= 1e-5
+
+
+@cuda
+def test_zero_bias_equals_no_bias(bz):
+    """ts_bridge/bias_smoke.py:10-25 — a zero bias is the unbiased op."""
+    torch.manual_seed(5)
+    B, T, H, HD, W = 2, 130, 2, 64, 16
+    q, k, v = [torch.randn(B, T, H, HD, device="cuda", dtype=torch.bfloat16) for _ in range(3)]
+    a = bz.causal_tension(q, k, v, W, 8.0)
+    b = bz.causal_tension(q, k, v, W, 8.0, bias=torch.zeros(B, T, W, device="cuda"))
+    assert torch.equal(a, b)
+
+
+@cuda
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_prefix_rows_invariant_to_future(bz, dtype):
+    """ts_bridge/streaming_parity.py:20-24 — by causality the τ rows and
+    outputs of a prefix do not depend on later tokens (bit-identical)."""
+    torch.manual_seed(6)
+    B, T, H, HD, W = 1, 384, 2, 64, 64
+    q, k, v = [torch.randn(B, T, H, HD, device="cuda", dtype=dtype) for _ in range(3)]
+    full_o, full_t = bz.tension(q, k, v, window=W, return_tau=True)
+    for Tp in (128, 200):
+        o, t = bz.tension(q[:, :Tp].contiguous(), k[:, :Tp].contiguous(),
+                          v[:, :Tp].contiguous(), window=W, return_tau=True)
+        assert torch.equal(o, full_o[:, :Tp])
+        assert torch.equal(t, full_t[:, :Tp])
+
+
+@cuda
+@pytest.mark.parametrize("W", [8, 32, 64, 100, 128])
+@pytest.mark.parametrize("normalize", ["mass", "count", None])
+def test_fused_local_bf16_vs_oracle(bz, W, normalize):
+    """Fused local op at HD 64 (the tensor-core shape) across windows,
+    normalisations, bias and τ cotangent, ragged T."""
+    torch.manual_seed(100 + W)
+    B, T, H, HD = 2, 333, 3, 64
+    dt = torch.bfloat16
+    q, k, v, d_out = [torch.randn(B, T, H, HD, dtype=dt) for _ in range(4)]
+    bias = torch.randn(B, T, W) * 0.5
+    d_tau = (torch.randn(B, T, H, W) * 0.1).to(dt)
+    qg, kg, vg = [x.cuda().requires_grad_(True) for x in (q, k, v)]
+    out, tau = bz.tension(qg, kg, vg, window=W, bias=bias.cuda(), return_tau=True,
+                          normalize=normalize)
+    ((out.float() * d_out.cuda().float()).sum() + (tau.float() * d_tau.cuda().float()).sum()).backward()
+
+    def fn(q_, k_, v_):
+        return orc.fused_reference(q_, k_, v_, window=W, scale=8.0, bias=bias.double(),
+                                   normalize=normalize or "none")
+    (o, t), grads = orc.tension_with_grads(fn, [x.double() for x in (q, k, v)],
+                                           [d_out.double(), d_tau.double()])
+    for g, r, what in zip((out, tau, qg.grad, kg.grad, vg.grad), (o, t, *grads),
+                          ("out", "tau", "dq", "dk", "dv")):
+        assert_close(g, r, dt, f"W{W}/{normalize}/{what}")
+
+
+@cuda
+def test_large_bf16_spot_check(bz):
+    """triton_tension/test.py:212-227 at B4 T512 H12 HD64 W64 (bf16)."""
+    torch.manual_seed(3)
+    B, T, H, HD, W = 4, 512, 12, 64, 64
+    q, k, v = [torch.randn(B, T, H, HD, dtype=torch.bfloat16) for _ in range(3)]
+    out = bz.causal_tension(q.cuda(), k.cuda(), v.cuda(), W, 8.0).float().cpu()
+    ref = orc.local_tension_raw(q.double(), k.double(), v.double(), W, 8.0)
+    rel = (out.double() - ref).abs() / (ref.abs() + 1e-6)
+    assert rel.mean().item() < 0.02
+    assert_close(out, ref, torch.bfloat16, "large")
+
+
+@cuda
+def test_memory_vs_unfold(bz):
+    """test_tau.py:130-159 — peak memory of the τ-returning op stays far
+    below the unfold gather (B4 T1024 H16 HD64 W256 bf16)."""
+    B, T, H, HD, W = 4, 1024, 16, 64, 256
+    torch.manual_seed(4)
+    q, k, v = [torch.randn(B, T, H, HD, device="cuda", dtype=torch.bfloat16) for _ in range(3)]
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    before = torch.cuda.memory_allocated()
+    out, tau = bz.causal_tension(q, k, v, W, 8.0, return_tau=True)
+    torch.cuda.synchronize()
+    peak = torch.cuda.max_memory_allocated()
+    unfold_bytes = B * T * H * W * HD * 2
+    assert peak - before < unfold_bytes / 4
+
+
+@cuda
+def test_cpu_and_float64_inputs_raise(bz):
+    q = torch.randn(1, 8, 1, 16)
+    with pytest.raises(RuntimeError):
+        bz.causal_tension(q, q, q, 4, 4.0)
+    qd = q.double().cuda()
+    with pytest.raises(TypeError):
+        bz.causal_tension(qd, qd, qd, 4, 4.0)
+
+
+@cuda
+def test_bias_shape_assertion(bz):
+    q = torch.randn(1, 8, 1, 16, device="cuda")
+    with pytest.raises(AssertionError):
+        bz.causal_tension(q, q, q, 4, 4.0, bias=torch.zeros(1, 8, 5, device="cuda"))
+
+
+@cuda
+def test_mixed_dtype_model_call_site(bz):
+    """model.py under bf16 autocast feeds fp32 (RoPE-promoted) Q/K with bf16 V;
+    the op returns Q.dtype and grads in each input's dtype (ops.py:122-124,
+    186-187)."""
+    torch.manual_seed(9)
+    B, T, H, HD, W = 2, 96, 2, 64, 16
+    q = torch.randn(B, T, H, HD, device="cuda", requires_grad=True)
+    k = torch.randn(B, T, H, HD, device="cuda", requires_grad=True)
+    v = torch.randn(B, T, H, HD, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    out, tau = bz.causal_tension(q, k, v, W, 8.0, return_tau=True)
+    assert out.dtype == torch.float32 and tau.dtype == torch.float32
+    (out.sum() + tau.sum()).backward()
+    assert q.grad.dtype == torch.float32 and v.grad.dtype == torch.bfloat16
+    ref_o, ref_t = orc.local_tension_raw(q.detach().double().cpu(), k.detach().double().cpu(),
+                                         v.detach().double().cpu(), W, 8.0, return_tau=True)
+    assert_close(out, ref_o, torch.float32, "mixed/out")
+    assert_close(tau, ref_t, torch.float32, "mixed/tau")

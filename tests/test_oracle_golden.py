@@ -1,0 +1,80 @@
+"""Pin the CPU oracle against fixtures produced by the reference itself.
+
+The fixtures (``tests/golden/*.npz``) come from running the reference's own
+``triton_tension/ops.py::_ref_forward`` and ``model.py`` layer on the CPU
+(``tests/golden/make_golden.py``).  Here the oracle restatement must
+reproduce them to float64 round-off, forward and backward.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import tension_oracle as orc
+
+TOL = dict(rtol=1e-10, atol=1e-11)
+
+
+def _t(a):
+    return torch.from_numpy(np.asarray(a, dtype=np.float64))
+
+
+def _op_names():
+    import os
+    from tests.conftest import _load
+    return sorted(_load("golden_op.npz"))
+
+
+def _layer_names():
+    from tests.conftest import _load
+    return sorted(_load("golden_layer.npz"))
+
+
+@pytest.mark.parametrize("name", _op_names())
+def test_oracle_raw_op_matches_reference(golden_op, name):
+    c = golden_op[name]
+    B, T, H, HD, W = [int(x) for x in c["meta"]]
+    scale = float(c["scale"])
+    bias = _t(c["bias"]) if "bias" in c else None
+    d_tau = _t(c["d_tau"]) if "d_tau" in c else None
+
+    def fn(q, k, v):
+        return orc.local_tension_raw(q, k, v, W, scale, bias, return_tau=True)
+
+    (out, tau), (dq, dk, dv) = orc.tension_with_grads(
+        fn, [_t(c["q"]), _t(c["k"]), _t(c["v"])], [_t(c["d_out"]), d_tau])
+    for got, key in ((out, "out"), (tau, "tau"), (dq, "dq"), (dk, "dk"), (dv, "dv")):
+        np.testing.assert_allclose(got.numpy(), c[key], err_msg=f"{name}:{key}", **TOL)
+
+
+@pytest.mark.parametrize("name", _layer_names())
+def test_oracle_layer_matches_reference(golden_layer, name):
+    c = golden_layer[name]
+    B, T, H, HD, W, Wl, msl = [int(x) for x in c["meta"]]
+    scale = float(c["scale"])
+    bias = _t(c["bias"]) if "bias" in c else None
+    cos, sin = orc.rope_tables(HD, msl, 10_000.0, torch.float64)
+    # the reference builds its tables in float32 then widens (model.py:69-73)
+    np.testing.assert_allclose(cos.numpy(), c["rope_cos"], rtol=0, atol=0)
+    np.testing.assert_allclose(sin.numpy(), c["rope_sin"], rtol=0, atol=0)
+
+    def fn(q, k, v):
+        out, tau = orc.fused_reference(q, k, v, window=None if W < 0 else W,
+                                       scale=scale, bias=bias, local_window=Wl,
+                                       max_seq_len=msl)
+        return out, tau
+
+    (out, tau), (dq, dk, dv) = orc.tension_with_grads(
+        fn, [_t(c["q_raw"]), _t(c["k_raw"]), _t(c["v"])],
+        [_t(c["d_out"]), _t(c["d_tau"])])
+    for got, key in ((out, "out"), (tau, "tau"), (dq, "dq_raw"), (dk, "dk_raw"),
+                     (dv, "dv")):
+        np.testing.assert_allclose(got.numpy(), c[key], err_msg=f"{name}:{key}", **TOL)
+    if "valid_count" in c:
+        np.testing.assert_array_equal(orc.valid_count(msl, W).numpy(), c["valid_count"])
+
+
+def test_algorithmic_pairs_matches_mask():
+    for T, W in ((2048, 64), (5, 8), (100, 100), (300, 128), (1, 1)):
+        m = orc.window_mask(T, W)
+        assert int(m.sum()) == orc.algorithmic_pairs(1, 1, T, W)
+    assert orc.algorithmic_pairs(1, 1, 7, None) == 28
