@@ -534,8 +534,4 @@ cudaError_t launch_tc_fwd(const FwdP& p, cudaStream_t st, int* launches) {
   return launch_variant<false, false>(mq, mk, mv, mo, a, smem, grid, st);
 }
 
-// The backward still runs on the exact-fp32 CUDA-core kernels.
-bool tc_bwd_eligible(const BwdP&) { return false; }
-cudaError_t launch_tc_bwd(const BwdP&, cudaStream_t, int*) { return cudaErrorNotSupported; }
-
 }  // namespace bozo
