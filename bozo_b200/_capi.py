@@ -23,7 +23,7 @@ EXPORTED = (
     "bozo_tension_fwd", "bozo_tension_bwd", "bozo_tension_bwd_workspace",
     "bozo_tension_poll_error", "bozo_tension_last_path",
     "bozo_tension_last_launches", "bozo_status_string",
-    "bozo_tension_abi_version",
+    "bozo_tension_abi_version", "bozo_tension_last_cuda_error",
 )
 
 
@@ -89,6 +89,7 @@ def lib():
                 L.bozo_status_string.argtypes = [C.c_int]
                 L.bozo_status_string.restype = C.c_char_p
                 L.bozo_tension_abi_version.restype = C.c_int
+                L.bozo_tension_last_cuda_error.restype = C.c_char_p
                 _lib = L
     return _lib
 
@@ -99,4 +100,7 @@ def status_string(code: int) -> str:
 
 def check(code: int, what: str):
     if code != OK:
-        raise RuntimeError(f"{what} failed: {status_string(code)} (status {code})")
+        detail = ""
+        if code == 7:  # BOZO_ERR_CUDA
+            detail = f" [{lib().bozo_tension_last_cuda_error().decode()}]"
+        raise RuntimeError(f"{what} failed: {status_string(code)} (status {code}){detail}")

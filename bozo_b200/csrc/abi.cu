@@ -18,6 +18,12 @@ __device__ int g_device_error;  // set by bounded device-side waits
 // its own device thread, so these are not thread-local).
 std::atomic<int> t_last_path{0};
 std::atomic<int> t_last_launches{0};
+std::atomic<int> t_last_cuda_error{0};
+
+int cuda_fail(cudaError_t e) {
+  t_last_cuda_error = (int)e;
+  return BOZO_ERR_CUDA;
+}
 
 constexpr int kMaxDevices = 64;
 int* g_err_ptr[kMaxDevices] = {nullptr};
@@ -37,6 +43,20 @@ int* error_word(cudaError_t* e) {
     g_err_ptr[dev] = static_cast<int*>(ptr);
   }
   return g_err_ptr[dev];
+}
+
+// Make the device that owns `ptr` current on the calling thread, with its
+// primary context bound.  Calls may arrive on threads that never touched CUDA
+// through this library (e.g. an autograd worker thread); without this the
+// driver-level tensor-map encoder sees no context and kernels would go to the
+// runtime's default device.
+cudaError_t bind_device(const void* ptr) {
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, ptr);
+  if (e != cudaSuccess) return e;
+  if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)
+    return cudaErrorInvalidDevicePointer;
+  return cudaSetDevice(attr.device);
 }
 
 bool dtype_ok(int dt) { return dt == BOZO_DT_F32 || dt == BOZO_DT_BF16 || dt == BOZO_DT_F16; }
@@ -93,6 +113,9 @@ const char* bozo_status_string(int s) {
 }
 
 int bozo_tension_last_path(void) { return t_last_path.load(); }
+const char* bozo_tension_last_cuda_error(void) {
+  return cudaGetErrorName((cudaError_t)t_last_cuda_error.load());
+}
 int bozo_tension_last_launches(void) { return t_last_launches.load(); }
 
 int bozo_tension_fwd(const bozo_tension_fwd_args* a, void* stream) {
@@ -106,7 +129,8 @@ int bozo_tension_fwd(const bozo_tension_fwd_args* a, void* stream) {
   if (a->tau && !dtype_ok(a->tau_dtype)) return BOZO_ERR_BAD_DTYPE;
   if (a->mode == BOZO_MODE_GLOBAL && a->tau && a->window > a->T) return BOZO_ERR_BAD_SHAPE;
 
-  cudaError_t e;
+  cudaError_t e = bind_device(a->q.ptr);
+  if (e != cudaSuccess) return cuda_fail(e);
   FwdP p{};
   p.B = a->B; p.T = a->T; p.H = a->H; p.HD = a->HD; p.mode = a->mode; p.W = a->window;
   p.norm = a->normalize; p.scale = a->scale; p.inv_scale = 1.0f / a->scale;
@@ -117,7 +141,7 @@ int bozo_tension_fwd(const bozo_tension_fwd_args* a, void* stream) {
   p.out = a->out; p.out_dt = a->out_dtype; p.tau = a->tau; p.tau_dt = a->tau_dtype;
   p.row_mass = a->row_mass;
   p.err = error_word(&e);
-  if (!p.err) return BOZO_ERR_CUDA;
+  if (!p.err) return cuda_fail(e);
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int launches = 0;
@@ -131,7 +155,7 @@ int bozo_tension_fwd(const bozo_tension_fwd_args* a, void* stream) {
     e = launch_simt_fwd(p, s, &launches);
     path = BOZO_PATH_SIMT;
   }
-  if (e != cudaSuccess) return BOZO_ERR_CUDA;
+  if (e != cudaSuccess) return cuda_fail(e);
   t_last_path = path;
   t_last_launches = launches;
   return BOZO_OK;
@@ -162,7 +186,8 @@ int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
   const size_t need = bozo_tension_bwd_workspace(a);
   if (need && (!a->workspace || a->workspace_bytes < need)) return BOZO_ERR_WORKSPACE;
 
-  cudaError_t e;
+  cudaError_t e = bind_device(a->q.ptr);
+  if (e != cudaSuccess) return cuda_fail(e);
   BwdP p{};
   p.B = a->B; p.T = a->T; p.H = a->H; p.HD = a->HD; p.mode = a->mode; p.W = a->window;
   p.norm = a->normalize; p.scale = a->scale; p.inv_scale = 1.0f / a->scale;
@@ -179,7 +204,7 @@ int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
   p.alpha = static_cast<float*>(a->workspace);
   p.beta = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + round256(rows * sizeof(float)));
   p.err = error_word(&e);
-  if (!p.err) return BOZO_ERR_CUDA;
+  if (!p.err) return cuda_fail(e);
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int launches = 0;
@@ -193,7 +218,7 @@ int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
     e = launch_simt_bwd(p, s, &launches);
     path = BOZO_PATH_SIMT;
   }
-  if (e != cudaSuccess) return BOZO_ERR_CUDA;
+  if (e != cudaSuccess) return cuda_fail(e);
   t_last_path = path;
   t_last_launches = launches;
   return BOZO_OK;

@@ -147,6 +147,10 @@ int bozo_tension_last_launches(void);
 const char* bozo_status_string(int status);
 int bozo_tension_abi_version(void);
 
+/* Name of the CUDA runtime error behind the last BOZO_ERR_CUDA returned in
+ * this process ("cudaSuccess" if none). */
+const char* bozo_tension_last_cuda_error(void);
+
 #ifdef __cplusplus
 }
 #endif

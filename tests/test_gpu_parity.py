@@ -270,3 +270,24 @@ def test_mixed_dtype_model_call_site(bz):
                                          v.detach().double().cpu(), W, 8.0, return_tau=True)
     assert_close(out, ref_o, torch.float32, "mixed/out")
     assert_close(tau, ref_t, torch.float32, "mixed/tau")
+
+
+@cuda
+@pytest.mark.parametrize("shape", [(1, 128, 1), (2, 128, 1), (1, 256, 2), (2, 130, 3)])
+def test_backward_on_autograd_thread_small_shapes(bz, shape):
+    """grad_outputs passed straight to autograd.grad: the backward runs on the
+    autograd device thread, which must get the data's device and context
+    bound before tensor maps are encoded."""
+    B, T, H = shape
+    torch.manual_seed(11)
+    q, k, v, d = [torch.randn(B, T, H, 64, device="cuda", dtype=torch.bfloat16) for _ in range(4)]
+    qg, kg, vg = [x.clone().requires_grad_(True) for x in (q, k, v)]
+    out = bz.tension(qg, kg, vg, window=64)
+    gq, gk, gv = torch.autograd.grad(out, (qg, kg, vg), d)
+
+    def fn(a, b, c):
+        return orc.fused_reference(a, b, c, window=64, scale=8.0)[0]
+    (o,), grads = orc.tension_with_grads(fn, [x.double().cpu() for x in (q, k, v)],
+                                         [d.double().cpu()])
+    for g, r, what in zip((out, gq, gk, gv), (o, *grads), ("out", "dq", "dk", "dv")):
+        assert_close(g, r, torch.bfloat16, f"{shape}/{what}")
