@@ -37,11 +37,12 @@ class FwdArgs(C.Structure):
         ("B", C.c_int32), ("T", C.c_int32), ("H", C.c_int32), ("HD", C.c_int32),
         ("mode", C.c_int32), ("window", C.c_int32), ("normalize", C.c_int32),
         ("path", C.c_int32), ("scale", C.c_float), ("rope_len", C.c_int32),
-        ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
+        ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p), ("rope_theta", C.c_void_p),
         ("q", Tensor4), ("k", Tensor4), ("v", Tensor4),
         ("bias", C.c_void_p), ("bias_stride", C.c_int64 * 3),
         ("out", C.c_void_p), ("out_dtype", C.c_int32), ("tau_dtype", C.c_int32),
         ("tau", C.c_void_p), ("row_mass", C.c_void_p),
+        ("q_rot", C.c_void_p), ("k_rot", C.c_void_p),
     ]
 
 
@@ -50,12 +51,12 @@ class BwdArgs(C.Structure):
         ("B", C.c_int32), ("T", C.c_int32), ("H", C.c_int32), ("HD", C.c_int32),
         ("mode", C.c_int32), ("window", C.c_int32), ("normalize", C.c_int32),
         ("path", C.c_int32), ("scale", C.c_float), ("rope_len", C.c_int32),
-        ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
+        ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p), ("rope_theta", C.c_void_p),
         ("q", Tensor4), ("k", Tensor4), ("v", Tensor4), ("d_out", Tensor4),
         ("out", Tensor4), ("row_mass", C.c_void_p),
         ("bias", C.c_void_p), ("bias_stride", C.c_int64 * 3),
         ("d_tau", C.c_void_p), ("d_tau_dtype", C.c_int32),
-        ("grad_dtype", C.c_int32 * 3), ("_pad", C.c_int32),
+        ("grad_dtype", C.c_int32 * 3), ("qk_rotated", C.c_int32),
         ("dq", C.c_void_p), ("dk", C.c_void_p), ("dv", C.c_void_p),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
     ]

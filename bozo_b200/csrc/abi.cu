@@ -136,10 +136,13 @@ int bozo_tension_fwd(const bozo_tension_fwd_args* a, void* stream) {
   p.norm = a->normalize; p.scale = a->scale; p.inv_scale = 1.0f / a->scale;
   p.cos = a->rope_len ? a->rope_cos : nullptr;
   p.sin = a->rope_len ? a->rope_sin : nullptr;
+  p.theta = a->rope_len ? a->rope_theta : nullptr;
   p.q = dev_t4(a->q); p.k = dev_t4(a->k); p.v = dev_t4(a->v);
   p.bias = a->bias; p.bs0 = a->bias_stride[0]; p.bs1 = a->bias_stride[1]; p.bs2 = a->bias_stride[2];
   p.out = a->out; p.out_dt = a->out_dtype; p.tau = a->tau; p.tau_dt = a->tau_dtype;
   p.row_mass = a->row_mass;
+  p.q_rot = p.cos ? a->q_rot : nullptr;
+  p.k_rot = p.cos ? a->k_rot : nullptr;
   p.err = error_word(&e);
   if (!p.err) return cuda_fail(e);
 
@@ -153,6 +156,9 @@ int bozo_tension_fwd(const bozo_tension_fwd_args* a, void* stream) {
     path = BOZO_PATH_TCGEN05;
   } else {
     e = launch_simt_fwd(p, s, &launches);
+    // the CUDA-core forward does not stage whole tiles: rotated copies
+    // come from a separate elementwise pass
+    if (e == cudaSuccess && (p.q_rot || p.k_rot)) e = launch_rope_copy(p, s, &launches);
     path = BOZO_PATH_SIMT;
   }
   if (e != cudaSuccess) return cuda_fail(e);
@@ -163,8 +169,11 @@ int bozo_tension_fwd(const bozo_tension_fwd_args* a, void* stream) {
 
 size_t bozo_tension_bwd_workspace(const bozo_tension_bwd_args* a) {
   if (!a || a->B <= 0 || a->T <= 0 || a->H <= 0) return 0;
-  const size_t rows = (size_t)a->B * a->H * a->T;
-  return round256(rows * sizeof(float)) * 2;  // alpha, beta
+  // three per-query-row coefficient planes; rows padded to a multiple of
+  // 128 so a 128-row slice starts 16-byte aligned (tensor-core bulk copies)
+  const size_t tpad = ((size_t)a->T + 127) / 128 * 128;
+  const size_t rows = (size_t)a->B * a->H * tpad;
+  return round256(rows * sizeof(float)) * 3;
 }
 
 int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
@@ -193,6 +202,7 @@ int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
   p.norm = a->normalize; p.scale = a->scale; p.inv_scale = 1.0f / a->scale;
   p.cos = a->rope_len ? a->rope_cos : nullptr;
   p.sin = a->rope_len ? a->rope_sin : nullptr;
+  p.theta = a->rope_len ? a->rope_theta : nullptr;
   p.q = dev_t4(a->q); p.k = dev_t4(a->k); p.v = dev_t4(a->v); p.dout = dev_t4(a->d_out);
   p.out = dev_t4(a->out);
   p.row_mass = a->row_mass;
@@ -200,9 +210,13 @@ int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
   p.dtau = a->d_tau; p.dtau_dt = a->d_tau_dtype;
   p.dq = a->dq; p.dk = a->dk; p.dv = a->dv;
   p.dq_dt = a->grad_dtype[0]; p.dk_dt = a->grad_dtype[1]; p.dv_dt = a->grad_dtype[2];
-  const size_t rows = (size_t)a->B * a->H * a->T;
+  p.qk_rotated = (a->qk_rotated && p.cos) ? 1 : 0;
+  const size_t tpad = ((size_t)a->T + 127) / 128 * 128;
+  const size_t rows = (size_t)a->B * a->H * tpad;
   p.alpha = static_cast<float*>(a->workspace);
   p.beta = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + round256(rows * sizeof(float)));
+  // the tensor-core path uses the same bytes as three contiguous planes
+  p.coef = static_cast<float*>(a->workspace);
   p.err = error_word(&e);
   if (!p.err) return cuda_fail(e);
 

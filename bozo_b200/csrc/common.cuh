@@ -28,7 +28,8 @@ struct FwdP {
   int B, T, H, HD, mode, W, norm;
   float scale, inv_scale;
   const float* cos;
-  const float* sin;  // NULL when no RoPE
+  const float* sin;    // NULL when no RoPE
+  const float* theta;  // [HD/2] frequencies of cos/sin, NULL if not supplied
   DevT4 q, k, v;
   const float* bias;
   long long bs0, bs1, bs2;
@@ -37,6 +38,8 @@ struct FwdP {
   void* tau;
   int tau_dt;
   float* row_mass;
+  void* q_rot;  // optional rotated copies (dtype of q / k)
+  void* k_rot;
   int* err;  // device error word
 };
 
@@ -45,6 +48,7 @@ struct BwdP {
   float scale, inv_scale;
   const float* cos;
   const float* sin;
+  const float* theta;
   DevT4 q, k, v, dout, out;
   const float* row_mass;
   const float* bias;
@@ -55,8 +59,10 @@ struct BwdP {
   void* dk;
   void* dv;
   int dq_dt, dk_dt, dv_dt;
-  float* alpha;  // [B,H,T] workspace
+  float* alpha;  // [B,H,T] workspace (CUDA-core path)
   float* beta;   // [B,H,T] workspace
+  float* coef;   // [3][B·H, Tpad] workspace (tensor-core path)
+  int qk_rotated;  // q, k are RoPE-rotated already
   int* err;
 };
 
@@ -88,5 +94,7 @@ __device__ __forceinline__ float sigmoid_exact(float x) { return 1.0f / (1.0f + 
 // Launchers (simt.cu)
 cudaError_t launch_simt_fwd(const FwdP& p, cudaStream_t st, int* launches);
 cudaError_t launch_simt_bwd(const BwdP& p, cudaStream_t st, int* launches);
+// Write RoPE(q), RoPE(k) into p.q_rot / p.k_rot (dtype of q / k).
+cudaError_t launch_rope_copy(const FwdP& p, cudaStream_t st, int* launches);
 
 }  // namespace bozo

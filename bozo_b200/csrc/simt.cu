@@ -11,6 +11,8 @@
 // memory in chunks of 32 with lane = partner index, so the score of a
 // (row, partner) pair lives in one lane and the HD-wide accumulations use
 // warp shuffles.  All arithmetic is fp32.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace bozo {
@@ -196,7 +198,10 @@ __global__ void __launch_bounds__(kThreads) simt_bwd_dq_kernel(BwdP p) {
   const bool local = p.mode == BOZO_MODE_LOCAL;
   const long long row_base = ((long long)b * p.H + h) * T;
 
-  stage_rows(Qs, LD, p.q, b, h, t0, kRows, T, HD, p.cos, p.sin);
+  // inputs already rotated by the forward need no rotation here
+  const float* rc = p.qk_rotated ? nullptr : p.cos;
+  const float* rs = p.qk_rotated ? nullptr : p.sin;
+  stage_rows(Qs, LD, p.q, b, h, t0, kRows, T, HD, rc, rs);
   stage_rows(dOs, LD, p.dout, b, h, t0, kRows, T, HD, nullptr, nullptr);
   __syncthreads();
 
@@ -235,7 +240,7 @@ __global__ void __launch_bounds__(kThreads) simt_bwd_dq_kernel(BwdP p) {
 
   for (int c0 = s_lo; c0 < s_hi; c0 += kChunk) {
     __syncthreads();
-    stage_rows(Ks, LD, p.k, b, h, c0, kChunk, T, HD, p.cos, p.sin);
+    stage_rows(Ks, LD, p.k, b, h, c0, kChunk, T, HD, rc, rs);
     stage_rows(Vs, LD, p.v, b, h, c0, kChunk, T, HD, nullptr, nullptr);
     __syncthreads();
     const int s = c0 + lane;
@@ -311,7 +316,9 @@ __global__ void __launch_bounds__(kThreads) simt_bwd_dkv_kernel(BwdP p) {
   const bool local = p.mode == BOZO_MODE_LOCAL;
   const long long row_base = ((long long)b * p.H + h) * T;
 
-  stage_rows(Ks, LD, p.k, b, h, s0, kRows, T, HD, p.cos, p.sin);
+  const float* rc = p.qk_rotated ? nullptr : p.cos;
+  const float* rs = p.qk_rotated ? nullptr : p.sin;
+  stage_rows(Ks, LD, p.k, b, h, s0, kRows, T, HD, rc, rs);
   stage_rows(Vs, LD, p.v, b, h, s0, kRows, T, HD, nullptr, nullptr);
 
   const int t_lo = local ? s0 + 1 : s0;
@@ -325,7 +332,7 @@ __global__ void __launch_bounds__(kThreads) simt_bwd_dkv_kernel(BwdP p) {
 
   for (int c0 = t_lo; c0 < t_hi; c0 += kChunk) {
     __syncthreads();
-    stage_rows(Qc, LD, p.q, b, h, c0, kChunk, T, HD, p.cos, p.sin);
+    stage_rows(Qc, LD, p.q, b, h, c0, kChunk, T, HD, rc, rs);
     stage_rows(dOc, LD, p.dout, b, h, c0, kChunk, T, HD, nullptr, nullptr);
     stage_scalars(Ac, Bc, p.alpha, p.beta, row_base, c0, kChunk, T);
     __syncthreads();
@@ -395,6 +402,34 @@ __global__ void __launch_bounds__(kThreads) simt_bwd_dkv_kernel(BwdP p) {
   }
 }
 
+// RoPE(q) → q_rot, RoPE(k) → k_rot (half-split rotation, model.py:75-81),
+// one thread per (row, pair), output contiguous in the input's dtype.
+__global__ void rope_copy_kernel(FwdP p) {
+  const int half = p.HD / 2;
+  const long long n = (long long)p.B * p.T * p.H * half;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < n;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(idx % half);
+    const long long row = idx / half;  // (b·T + t)·H + h
+    const int h = (int)(row % p.H);
+    const long long bt = row / p.H;
+    const int t = (int)(bt % p.T), b = (int)(bt / p.T);
+    const float c = p.cos[(long long)t * half + d], s = p.sin[(long long)t * half + d];
+    const DevT4* src[2] = {&p.q, &p.k};
+    void* dst[2] = {p.q_rot, p.k_rot};
+#pragma unroll
+    for (int z = 0; z < 2; ++z) {
+      if (!dst[z]) continue;
+      const DevT4& x = *src[z];
+      const long long base = (long long)b * x.sb + (long long)t * x.st + (long long)h * x.sh;
+      const float x1 = ldf(x.p, base + (long long)d * x.sd, x.dt);
+      const float x2 = ldf(x.p, base + (long long)(d + half) * x.sd, x.dt);
+      stf(dst[z], row * p.HD + d, x.dt, x1 * c - x2 * s);
+      stf(dst[z], row * p.HD + d + half, x.dt, x1 * s + x2 * c);
+    }
+  }
+}
+
 template <int NJ>
 cudaError_t fwd_nj(const FwdP& p, cudaStream_t st) {
   constexpr int LD = 32 * NJ + 1;
@@ -427,6 +462,14 @@ cudaError_t bwd_nj(const BwdP& p, cudaStream_t st) {
 }
 
 }  // namespace
+
+cudaError_t launch_rope_copy(const FwdP& p, cudaStream_t st, int* launches) {
+  const long long n = (long long)p.B * p.T * p.H * (p.HD / 2);
+  const int grid = (int)std::min<long long>((n + 255) / 256, 148 * 16);
+  rope_copy_kernel<<<grid, 256, 0, st>>>(p);
+  *launches += 1;
+  return cudaGetLastError();
+}
 
 cudaError_t launch_simt_fwd(const FwdP& p, cudaStream_t st, int* launches) {
   *launches = 1;

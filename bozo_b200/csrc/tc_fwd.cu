@@ -47,12 +47,12 @@ struct FwdTC {
   int B, T, H, W, Wr, nT, total;
   int norm, nbuf, ncols, pblocks;
   float half_inv_scale;
-  const float* cos;
-  const float* sin;
+  const float* theta;  // RoPE frequencies [32] or null (no RoPE)
   const float* bias;
   long long bs0, bs1, bs2;
   __nv_bfloat16* tau;
   float* row_mass;
+  int store_rot;  // also TMA-store the rotated Q/K tiles (q_rot, k_rot)
   int* err;
 };
 
@@ -104,37 +104,21 @@ __device__ __forceinline__ void rope_chunk(uint32_t base, int r, int c, const fl
   st_shared_v4(base + sw128_off(r, c + 4), rb[0], rb[1], rb[2], rb[3]);
 }
 
-__device__ __forceinline__ void load_cs(const float* cos, const float* sin, int t, int c,
-                                        float (&cs)[8], float (&sn)[8]) {
-  const float4* cp = reinterpret_cast<const float4*>(cos + (long long)t * 32 + c * 8);
-  const float4* sp = reinterpret_cast<const float4*>(sin + (long long)t * 32 + c * 8);
-  const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
-  cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
-  cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
-  sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
-  sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
-}
-
 // Rotate rows [0,128) of tiles a (and b, if non-null) — same positions t0+r.
-// Items are processed two at a time so their cos/sin fetches overlap.
-__device__ void rope_tiles(uint8_t* ta, uint8_t* tb, int t0, int T, const float* cos,
-                           const float* sin, int tid) {
+// Thread tid always handles 16-byte chunk c = tid & 3, so it keeps the eight
+// frequencies θ[8c..8c+7] in registers and evaluates cos/sin on the fly.
+__device__ void rope_tiles(uint8_t* ta, uint8_t* tb, int t0, int T, const float (&th)[8], int tid) {
   const uint32_t ba = smem_u32(ta), bb = tb ? smem_u32(tb) : 0u;
-  for (int item = tid; item < kTile * 4; item += 2 * kRotThreads) {
-    const int i0 = item, i1 = item + kRotThreads;
-    const int r0 = i0 >> 2, c0 = i0 & 3, r1 = i1 >> 2, c1 = i1 & 3;
-    const bool ok0 = t0 + r0 < T, ok1 = i1 < kTile * 4 && t0 + r1 < T;
-    float cs0[8], sn0[8], cs1[8], sn1[8];
-    load_cs(cos, sin, ok0 ? t0 + r0 : 0, c0, cs0, sn0);
-    load_cs(cos, sin, ok1 ? t0 + r1 : 0, c1, cs1, sn1);
-    if (ok0) {
-      rope_chunk(ba, r0, c0, cs0, sn0);
-      if (tb) rope_chunk(bb, r0, c0, cs0, sn0);
-    }
-    if (ok1) {
-      rope_chunk(ba, r1, c1, cs1, sn1);
-      if (tb) rope_chunk(bb, r1, c1, cs1, sn1);
-    }
+  const int c = tid & 3;
+  for (int item = tid; item < kTile * 4; item += kRotThreads) {
+    const int r = item >> 2;
+    const int t = t0 + r;
+    if (t >= T) continue;
+    float cs[8], sn[8];
+#pragma unroll
+    for (int z = 0; z < 8; ++z) rope_cs(t, th[z], cs[z], sn[z]);
+    rope_chunk(ba, r, c, cs, sn);
+    if (tb) rope_chunk(bb, r, c, cs, sn);
   }
 }
 
@@ -142,6 +126,7 @@ template <bool kBias, bool kTau>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmo,
+                  const __grid_constant__ CUtensorMap tmqr, const __grid_constant__ CUtensorMap tmkr,
                   const FwdTC p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -202,30 +187,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tmk);
       prefetch_tmap(&tmv);
       prefetch_tmap(&tmo);
-      int n = 0;
-      bool ok = true;
+      if (p.store_rot) {
+        prefetch_tmap(&tmqr);
+        prefetch_tmap(&tmkr);
+      }
+      int n = 0, n_cur = 0;
+      bool ok = true, pending_stores = false;
+      // rotated tiles are stored from the ring slots: a slot is refilled only
+      // after every store issued so far has finished reading shared memory
+      auto before_refill = [&]() {
+        if (pending_stores) {
+          bulk_wait_group_read0();
+          pending_stores = false;
+        }
+      };
       auto load_key = [&](int bh, int jj) {
         const int s = n % kKVSlots;
         if (n >= kKVSlots)
           ok = ok && mbar_wait(&bar->kv_empty[s], ((n / kKVSlots) - 1) & 1, err, kErrFwd | 1);
         if (!ok) return;
+        before_refill();
         mbar_arrive_expect_tx(&bar->kv_full[s], 2 * kTileBytes);
         const int b = bh / p.H, h = bh % p.H;
         tma_load_4d(sK + s * kTileBytes, &tmk, &bar->kv_full[s], 0, h, jj * kTile, b);
         tma_load_4d(sV + s * kTileBytes, &tmv, &bar->kv_full[s], 0, h, jj * kTile, b);
         ++n;
       };
+      // store RoPE(Q), RoPE(K) of tile (bh, j) once the rotators are done
+      auto store_rot = [&](int it_s, int bh, int j, int nk) {
+        const int qs = it_s % kQSlots, ks = nk % kKVSlots;
+        ok = ok && mbar_wait(&bar->q_ready[qs], (it_s / kQSlots) & 1, err, kErrFwd | 15);
+        ok = ok && mbar_wait(&bar->k_ready[ks], (nk / kKVSlots) & 1, err, kErrFwd | 16);
+        if (!ok) return;
+        tma_store_4d(&tmqr, sQ + qs * kTileBytes, 0, bh % p.H, j * kTile, bh / p.H);
+        tma_store_4d(&tmkr, sK + ks * kTileBytes, 0, bh % p.H, j * kTile, bh / p.H);
+        bulk_commit_group();
+        pending_stores = true;
+      };
+      int prev_bh = 0, prev_j = 0, prev_n = 0;
       for (int u = u0, it = 0; u < u1 && ok; ++u, ++it) {
         const int bh = u / nT, j = u % nT;
         const int qs = it % kQSlots;
         if (it >= kQSlots)
           ok = mbar_wait(&bar->q_empty[qs], ((it / kQSlots) - 1) & 1, err, kErrFwd | 2);
         if (!ok) break;
+        before_refill();
         mbar_arrive_expect_tx(&bar->q_full[qs], kTileBytes);
         tma_load_4d(sQ + qs * kTileBytes, &tmq, &bar->q_full[qs], 0, bh % p.H, j * kTile, bh / p.H);
         if (j >= 1 && u == u0) load_key(bh, j - 1);
+        n_cur = n;
         load_key(bh, j);
+        if (p.store_rot && it >= 1) store_rot(it - 1, prev_bh, prev_j, prev_n);
+        prev_bh = bh; prev_j = j; prev_n = n_cur;
       }
+      if (ok && p.store_rot && u1 > u0) store_rot(u1 - u0 - 1, prev_bh, prev_j, prev_n);
+      if (pending_stores) bulk_wait_group0();
     }
   } else if (warp == 1) {
     // ─────────────── MMA issuer ───────────────
@@ -308,6 +324,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp < 4 || warp >= 12) {
     // ─────────────── RoPE rotators (4 warps) ───────────────
     const int tid = (warp < 4 ? warp - 2 : warp - 10) * 32 + lane;
+    float th[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (p.theta)
+#pragma unroll
+      for (int z = 0; z < 8; ++z) th[z] = __ldg(p.theta + (tid & 3) * 8 + z);
     int n = 0;
     bool ok = true;
     for (int u = u0, it = 0; u < u1 && ok; ++u, ++it) {
@@ -317,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = n % kKVSlots;
         ok = mbar_wait(&bar->kv_full[s], (n / kKVSlots) & 1, err, kErrFwd | 8);
         if (!ok) break;
-        if (p.cos) rope_tiles(sK + s * kTileBytes, nullptr, (j - 1) * kTile, p.T, p.cos, p.sin, tid);
+        if (p.theta) rope_tiles(sK + s * kTileBytes, nullptr, (j - 1) * kTile, p.T, th, tid);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar->k_ready[s]);
@@ -327,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = mbar_wait(&bar->q_full[qs], (it / kQSlots) & 1, err, kErrFwd | 9);
       ok = ok && mbar_wait(&bar->kv_full[s], (n / kKVSlots) & 1, err, kErrFwd | 8);
       if (!ok) break;
-      if (p.cos) rope_tiles(sQ + qs * kTileBytes, sK + s * kTileBytes, j * kTile, p.T, p.cos, p.sin, tid);
+      if (p.theta) rope_tiles(sQ + qs * kTileBytes, sK + s * kTileBytes, j * kTile, p.T, th, tid);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -475,13 +495,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <bool kBias, bool kTau>
-cudaError_t launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                           const CUtensorMap& mo, const FwdTC& a, size_t smem, int grid,
+cudaError_t launch_variant(const CUtensorMap* m, const FwdTC& a, size_t smem, int grid,
                            cudaStream_t st) {
   auto kern = tc_fwd_kernel<kBias, kTau>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kThreads, smem, st>>>(mq, mk, mv, mo, a);
+  kern<<<grid, kThreads, smem, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], a);
   return cudaGetLastError();
 }
 
@@ -495,8 +514,9 @@ bool tc_fwd_eligible(const FwdP& p) {
       !tma_view_ok(p.v, p.B, p.T, p.H))
     return false;
   if ((reinterpret_cast<uintptr_t>(p.out) & 15) != 0) return false;
-  if (p.cos && ((reinterpret_cast<uintptr_t>(p.cos) & 15) || (reinterpret_cast<uintptr_t>(p.sin) & 15)))
-    return false;
+  for (const void* r : {p.q_rot, p.k_rot})
+    if (r && (reinterpret_cast<uintptr_t>(r) & 15) != 0) return false;
+  if (p.cos && !p.theta) return false;  // on-the-fly RoPE needs θ
   return tmap_encoder_available();
 }
 
@@ -511,27 +531,36 @@ cudaError_t launch_tc_fwd(const FwdP& p, cudaStream_t st, int* launches) {
   a.nbuf = (a.ncols + kHD <= 256) ? 2 : 1;
   a.pblocks = (a.ncols + 63) / 64;
   a.half_inv_scale = 0.5f / p.scale;
-  a.cos = p.cos; a.sin = p.sin;
+  a.theta = p.cos ? p.theta : nullptr;
   a.bias = p.bias; a.bs0 = p.bs0; a.bs1 = p.bs1; a.bs2 = p.bs2;
   a.tau = static_cast<__nv_bfloat16*>(p.tau);
   a.row_mass = p.row_mass;
+  a.store_rot = (a.theta && p.q_rot && p.k_rot) ? 1 : 0;
   a.err = p.err;
-  CUtensorMap mq, mk, mv, mo;
+  CUtensorMap m[6];
   const long long ob = (long long)p.T * p.H * kHD, ot = (long long)p.H * kHD, oh = kHD;
-  if (!make_tmap_bthd(&mq, p.q.p, p.q.sb, p.q.st, p.q.sh, p.B, p.T, p.H, kTile) ||
-      !make_tmap_bthd(&mk, p.k.p, p.k.sb, p.k.st, p.k.sh, p.B, p.T, p.H, kTile) ||
-      !make_tmap_bthd(&mv, p.v.p, p.v.sb, p.v.st, p.v.sh, p.B, p.T, p.H, kTile) ||
-      !make_tmap_bthd(&mo, p.out, ob, ot, oh, p.B, p.T, p.H, kTile))
+  if (!make_tmap_bthd(&m[0], p.q.p, p.q.sb, p.q.st, p.q.sh, p.B, p.T, p.H, kTile) ||
+      !make_tmap_bthd(&m[1], p.k.p, p.k.sb, p.k.st, p.k.sh, p.B, p.T, p.H, kTile) ||
+      !make_tmap_bthd(&m[2], p.v.p, p.v.sb, p.v.st, p.v.sh, p.B, p.T, p.H, kTile) ||
+      !make_tmap_bthd(&m[3], p.out, ob, ot, oh, p.B, p.T, p.H, kTile))
     return cudaErrorInvalidValue;
+  if (a.store_rot) {
+    if (!make_tmap_bthd(&m[4], p.q_rot, ob, ot, oh, p.B, p.T, p.H, kTile) ||
+        !make_tmap_bthd(&m[5], p.k_rot, ob, ot, oh, p.B, p.T, p.H, kTile))
+      return cudaErrorInvalidValue;
+  } else {
+    m[4] = m[3];  // unused
+    m[5] = m[3];
+  }
   const Layout L = fwd_layout(a.pblocks);
   const size_t smem = L.total + 1024;
   const int grid = std::min(num_sms(), a.total);
   *launches = 1;
   const bool has_bias = p.bias != nullptr, has_tau = p.tau != nullptr;
-  if (has_bias && has_tau) return launch_variant<true, true>(mq, mk, mv, mo, a, smem, grid, st);
-  if (has_bias) return launch_variant<true, false>(mq, mk, mv, mo, a, smem, grid, st);
-  if (has_tau) return launch_variant<false, true>(mq, mk, mv, mo, a, smem, grid, st);
-  return launch_variant<false, false>(mq, mk, mv, mo, a, smem, grid, st);
+  if (has_bias && has_tau) return launch_variant<true, true>(m, a, smem, grid, st);
+  if (has_bias) return launch_variant<true, false>(m, a, smem, grid, st);
+  if (has_tau) return launch_variant<false, true>(m, a, smem, grid, st);
+  return launch_variant<false, false>(m, a, smem, grid, st);
 }
 
 }  // namespace bozo

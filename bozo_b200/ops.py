@@ -83,15 +83,17 @@ def _require_cuda(*ts: Tensor) -> None:
 _rope_cache: dict = {}
 
 
-def rope_tables(head_dim: int, length: int, base: float, device) -> tuple[Tensor, Tensor]:
-    """fp32 cos/sin ``[length, HD/2]`` built exactly as model.py:66-73 does."""
+def rope_tables(head_dim: int, length: int, base: float, device):
+    """fp32 (cos, sin) ``[length, HD/2]`` and θ ``[HD/2]`` built exactly as
+    model.py:66-73 does (cos[t][i] = cos(fl(t·θ_i)))."""
     key = (head_dim, length, float(base), str(device))
     tab = _rope_cache.get(key)
     if tab is None:
         half = head_dim // 2
         theta = 1.0 / (base ** (torch.arange(0, half).float() / half))
         freqs = torch.outer(torch.arange(length).float(), theta)
-        tab = (freqs.cos().contiguous().to(device), freqs.sin().contiguous().to(device))
+        tab = (freqs.cos().contiguous().to(device), freqs.sin().contiguous().to(device),
+               theta.contiguous().to(device))
         _rope_cache[key] = tab
     return tab
 
@@ -102,9 +104,9 @@ def _fill_common(a, B, T, H, HD, mode, window, norm, scale, rope):
     a.path = _PATH[_path_override]
     a.scale = float(scale)
     if rope is not None:
-        cos, sin = rope
+        cos, sin, theta = rope
         a.rope_len = cos.shape[0]
-        a.rope_cos, a.rope_sin = cos.data_ptr(), sin.data_ptr()
+        a.rope_cos, a.rope_sin, a.rope_theta = cos.data_ptr(), sin.data_ptr(), theta.data_ptr()
     else:
         a.rope_len = 0
 
@@ -117,9 +119,13 @@ def _bias_arg(a, bias: Optional[Tensor]):
 
 
 def _launch_fwd(q, k, v, *, mode, window, norm, scale, rope, bias, tau_width,
-                out_dtype, tau_dtype, want_mass):
+                out_dtype, tau_dtype, want_mass, want_rotated=False):
     B, T, H, HD = q.shape
     out = torch.empty(B, T, H, HD, dtype=out_dtype, device=q.device)
+    q_rot = k_rot = None
+    if want_rotated and rope is not None:
+        q_rot = torch.empty(B, T, H, HD, dtype=q.dtype, device=q.device)
+        k_rot = torch.empty(B, T, H, HD, dtype=k.dtype, device=q.device)
     tau = (torch.empty(B, T, H, tau_width, dtype=tau_dtype, device=q.device)
            if tau_width is not None else None)
     mass = (torch.empty(B, H, T, dtype=torch.float32, device=q.device)
@@ -133,13 +139,15 @@ def _launch_fwd(q, k, v, *, mode, window, norm, scale, rope, bias, tau_width,
         a.tau, a.tau_dtype = tau.data_ptr(), _DT[tau_dtype]
     if mass is not None:
         a.row_mass = mass.data_ptr()
+    if q_rot is not None:
+        a.q_rot, a.k_rot = q_rot.data_ptr(), k_rot.data_ptr()
     _capi.check(_capi.lib().bozo_tension_fwd(C.byref(a), _stream(q.device)),
                 "bozo_tension_fwd")
-    return out, tau, mass
+    return out, tau, mass, q_rot, k_rot
 
 
 def _launch_bwd(q, k, v, d_out, *, mode, window, norm, scale, rope, bias, out,
-                mass, d_tau):
+                mass, d_tau, qk_rotated=False):
     B, T, H, HD = q.shape
     dq = torch.empty(B, T, H, HD, dtype=q.dtype, device=q.device)
     dk = torch.empty(B, T, H, HD, dtype=k.dtype, device=q.device)
@@ -155,6 +163,7 @@ def _launch_bwd(q, k, v, d_out, *, mode, window, norm, scale, rope, bias, out,
     if d_tau is not None:
         a.d_tau, a.d_tau_dtype = d_tau.data_ptr(), _dt(d_tau)
     a.grad_dtype[0], a.grad_dtype[1], a.grad_dtype[2] = _dt(q), _dt(k), _dt(v)
+    a.qk_rotated = 1 if qk_rotated else 0
     a.dq, a.dk, a.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
     L = _capi.lib()
     ws_bytes = L.bozo_tension_bwd_workspace(C.byref(a))
@@ -185,7 +194,7 @@ class _CausalTensionFn(torch.autograd.Function):
     def forward(ctx, Q, K, V, W: int, scale: float, return_tau: bool, bias):
         B, T, H, HD = Q.shape
         Bias = _prep_bias(bias, (B, T, W))
-        out, tau, _ = _launch_fwd(Q, K, V, mode=_capi.MODE_LOCAL, window=W,
+        out, tau, _, _, _ = _launch_fwd(Q, K, V, mode=_capi.MODE_LOCAL, window=W,
                                   norm=_capi.NORM_NONE, scale=scale, rope=None,
                                   bias=Bias, tau_width=W if return_tau else None,
                                   out_dtype=Q.dtype, tau_dtype=Q.dtype, want_mass=False)
@@ -244,11 +253,18 @@ class _TensionFn(torch.autograd.Function):
             shape = (B, T, T) if mode == _capi.MODE_GLOBAL else (B, T, window)
             bias = _prep_bias(bias, shape)
         w_arg = window if mode == _capi.MODE_LOCAL else (tau_width or 0)
-        out, tau, mass = _launch_fwd(
+        # for training the forward also writes RoPE(q), RoPE(k); the backward
+        # then reads the rotated tiles instead of rotating them again
+        rotated = rope is not None and any(ctx.needs_input_grad[:3])
+        out, tau, mass, q_rot, k_rot = _launch_fwd(
             q, k, v, mode=mode, window=w_arg, norm=norm, scale=scale, rope=rope,
             bias=bias, tau_width=(w_arg if return_tau else None), out_dtype=q.dtype,
-            tau_dtype=q.dtype, want_mass=True)
-        ctx.save_for_backward(q, k, v, out, mass, bias)
+            tau_dtype=q.dtype, want_mass=True, want_rotated=rotated)
+        if q_rot is not None:
+            ctx.save_for_backward(q_rot, k_rot, v, out, mass, bias)
+        else:
+            ctx.save_for_backward(q, k, v, out, mass, bias)
+        ctx.qk_rotated = q_rot is not None
         ctx.cfg = (mode, w_arg, norm, scale, rope_base, rope_len, return_tau)
         ctx.mark_non_differentiable(mass)
         if return_tau:
@@ -269,7 +285,7 @@ class _TensionFn(torch.autograd.Function):
                 if rope_base is not None else None)
         dq, dk, dv = _launch_bwd(q, k, v, d_out, mode=mode, window=w_arg, norm=norm,
                                  scale=scale, rope=rope, bias=bias, out=out, mass=mass,
-                                 d_tau=d_tau)
+                                 d_tau=d_tau, qk_rotated=ctx.qk_rotated)
         return dq, dk, dv, None, None, None, None, None, None, None, None, None
 
 

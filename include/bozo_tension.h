@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define BOZO_TENSION_ABI_VERSION 1
+#define BOZO_TENSION_ABI_VERSION 3
 
 typedef enum {
   BOZO_OK = 0,
@@ -60,7 +60,8 @@ typedef enum { BOZO_NORM_NONE = 0, BOZO_NORM_MASS = 1, BOZO_NORM_COUNT = 2 } boz
 
 /* Kernel-path selection (flags). AUTO picks the tcgen05 path whenever the
  * inputs qualify (bf16 Q/K/V with unit HD stride, 16-byte aligned rows,
- * HD = 64, LOCAL, W ≤ 128), else the exact-fp32 SIMT path. */
+ * HD = 64, LOCAL, W ≤ 128, RoPE given with rope_theta), else the
+ * exact-fp32 SIMT path. */
 enum {
   BOZO_PATH_AUTO = 0,
   BOZO_PATH_SIMT = 1,     /* force the fp32 CUDA-core path */
@@ -86,6 +87,10 @@ typedef struct {
   int32_t rope_len;       /* rows of the RoPE tables (≥ T) or 0 for no RoPE */
   const float* rope_cos;  /* [rope_len, HD/2] fp32 contiguous, or NULL */
   const float* rope_sin;
+  const float* rope_theta; /* [HD/2] fp32 frequencies θ_i of those tables
+                              (cos[t][i] = cos(t·θ_i)); lets the tensor-core
+                              kernels evaluate the rotation on the fly.
+                              Optional: NULL keeps table lookups only. */
   bozo_tensor4 q, k, v;
   const float* bias;      /* LOCAL [B,T,W] / GLOBAL [B,T,T] fp32, or NULL */
   int64_t bias_stride[3];
@@ -95,6 +100,8 @@ typedef struct {
   int32_t tau_dtype;
   void* tau;              /* [B,T,H,window] contiguous or NULL (no export) */
   float* row_mass;        /* [B,H,T] fp32 Σ_s τ (unclamped) or NULL */
+  void* q_rot;            /* optional [B,T,H,HD] contiguous copies of RoPE(q), */
+  void* k_rot;            /* RoPE(k) in q/k's dtype (for a later backward)    */
 } bozo_tension_fwd_args;
 
 typedef struct {
@@ -104,6 +111,7 @@ typedef struct {
   int32_t rope_len;
   const float* rope_cos;
   const float* rope_sin;
+  const float* rope_theta;
   bozo_tensor4 q, k, v;   /* the forward inputs (pre-RoPE when RoPE is on) */
   bozo_tensor4 d_out;     /* cotangent of out */
   bozo_tensor4 out;       /* forward output — read only for NORM_MASS */
@@ -113,7 +121,9 @@ typedef struct {
   const void* d_tau;      /* [B,T,H,window] contiguous cotangent of τ, or NULL */
   int32_t d_tau_dtype;
   int32_t grad_dtype[3];  /* dtypes of dq, dk, dv */
-  int32_t _pad;
+  int32_t qk_rotated;     /* 1: q, k above are already RoPE-rotated (the
+                             forward's q_rot/k_rot); dq, dk are still
+                             returned w.r.t. the pre-RoPE inputs */
   void* dq;               /* [B,T,H,HD] contiguous (gradient w.r.t. pre-RoPE q) */
   void* dk;
   void* dv;

@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
     assert set(declared) == set(_capi.EXPORTED)
     for name in declared:
         assert hasattr(lib, name), name
-    assert lib.bozo_tension_abi_version() == 1
+    assert lib.bozo_tension_abi_version() == 3
     assert _capi.status_string(0) == "ok"
 
 
@@ -43,10 +43,12 @@ int main(void) {
   S(bozo_tensor4); O(bozo_tensor4, dtype); O(bozo_tensor4, stride);
   S(bozo_tension_fwd_args);
   O(bozo_tension_fwd_args, scale); O(bozo_tension_fwd_args, rope_cos);
+  O(bozo_tension_fwd_args, rope_theta); O(bozo_tension_bwd_args, rope_theta);
   O(bozo_tension_fwd_args, q); O(bozo_tension_fwd_args, v); O(bozo_tension_fwd_args, bias);
   O(bozo_tension_fwd_args, bias_stride); O(bozo_tension_fwd_args, out);
   O(bozo_tension_fwd_args, out_dtype); O(bozo_tension_fwd_args, tau);
-  O(bozo_tension_fwd_args, row_mass);
+  O(bozo_tension_fwd_args, row_mass); O(bozo_tension_fwd_args, q_rot);
+  O(bozo_tension_fwd_args, k_rot); O(bozo_tension_bwd_args, qk_rotated);
   S(bozo_tension_bwd_args);
   O(bozo_tension_bwd_args, d_out); O(bozo_tension_bwd_args, out);
   O(bozo_tension_bwd_args, row_mass); O(bozo_tension_bwd_args, bias_stride);
