@@ -14,6 +14,8 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib",
                         "libbozo_tension.so")
 
 OK = 0
+ERR_SCRATCH_LIMIT = 9
+NOALLOC_SCRATCH_BYTES = 8 << 20  # BOZO_NOALLOC_SCRATCH_BYTES
 DT_F32, DT_BF16, DT_F16 = 0, 1, 2
 MODE_LOCAL, MODE_GLOBAL = 0, 1
 NORM_NONE, NORM_MASS, NORM_COUNT = 0, 1, 2
@@ -24,6 +26,7 @@ EXPORTED = (
     "bozo_tension_poll_error", "bozo_tension_last_path",
     "bozo_tension_last_launches", "bozo_status_string",
     "bozo_tension_abi_version", "bozo_tension_last_cuda_error",
+    "bozo_tension_bwd_noalloc",
 )
 
 
@@ -81,6 +84,8 @@ def lib():
                 L.bozo_tension_fwd.restype = C.c_int
                 L.bozo_tension_bwd.argtypes = [C.POINTER(BwdArgs), C.c_void_p]
                 L.bozo_tension_bwd.restype = C.c_int
+                L.bozo_tension_bwd_noalloc.argtypes = [C.POINTER(BwdArgs), C.c_void_p]
+                L.bozo_tension_bwd_noalloc.restype = C.c_int
                 L.bozo_tension_bwd_workspace.argtypes = [C.POINTER(BwdArgs)]
                 L.bozo_tension_bwd_workspace.restype = C.c_size_t
                 L.bozo_tension_poll_error.argtypes = [C.c_void_p]

@@ -45,6 +45,38 @@ int* error_word(cudaError_t* e) {
   return g_err_ptr[dev];
 }
 
+// Fixed backward scratch for bozo_tension_bwd_noalloc, for callers that may
+// not allocate device memory per call (a C/cgo/ctypes host without a caching
+// allocator, where cudaMalloc/cudaFree would synchronise the device every
+// step, or a service that reserves its memory once at start-up).  The array
+// is part of the module image, so using it allocates nothing.  No byte of it
+// has to start at zero: the first kernel of either backward path writes every
+// coefficient the later one reads.  Overlapping calls on one device share it
+// and race; it keeps the last call's contents.
+__device__ __align__(256) unsigned char g_noalloc_scratch[BOZO_NOALLOC_SCRATCH_BYTES];
+void* g_scratch_ptr[kMaxDevices] = {nullptr};
+
+// Device address of the scratch array on the current device, looked up once
+// per device with that device current (the first call should come before any
+// stream capture begins).
+void* noalloc_scratch(cudaError_t* e) {
+  int dev = 0;
+  *e = cudaGetDevice(&dev);
+  if (*e != cudaSuccess) return nullptr;
+  if (dev < 0 || dev >= kMaxDevices) {
+    *e = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* ptr = nullptr;
+    *e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_scratch);
+    if (*e != cudaSuccess) return nullptr;
+    g_scratch_ptr[dev] = ptr;
+  }
+  return g_scratch_ptr[dev];
+}
+
 // Make the device that owns `ptr` current on the calling thread, with its
 // primary context bound.  Calls may arrive on threads that never touched CUDA
 // through this library (e.g. an autograd worker thread); without this the
@@ -108,6 +140,8 @@ const char* bozo_status_string(int s) {
     case BOZO_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait timed out";
     case BOZO_ERR_CUDA: return "CUDA runtime error";
     case BOZO_ERR_WORKSPACE: return "workspace missing or too small";
+    case BOZO_ERR_SCRATCH_LIMIT:
+      return "problem needs more than the fixed 8 MiB no-alloc scratch; use bozo_tension_bwd";
     default: return "unknown status";
   }
 }
@@ -236,6 +270,22 @@ int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
   t_last_path = path;
   t_last_launches = launches;
   return BOZO_OK;
+}
+
+int bozo_tension_bwd_noalloc(const bozo_tension_bwd_args* a, void* stream) {
+  if (!a) return BOZO_ERR_NULL;
+  if (!a->q.ptr) return BOZO_ERR_NULL;
+  if (bozo_tension_bwd_workspace(a) > (size_t)BOZO_NOALLOC_SCRATCH_BYTES)
+    return BOZO_ERR_SCRATCH_LIMIT;
+  // the scratch address is per device: take it with the data's device current
+  cudaError_t e = bind_device(a->q.ptr);
+  if (e != cudaSuccess) return cuda_fail(e);
+  void* scratch = noalloc_scratch(&e);
+  if (!scratch) return cuda_fail(e);
+  bozo_tension_bwd_args local = *a;
+  local.workspace = scratch;
+  local.workspace_bytes = BOZO_NOALLOC_SCRATCH_BYTES;
+  return bozo_tension_bwd(&local, stream);
 }
 
 int bozo_tension_poll_error(void* stream) {

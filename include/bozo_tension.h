@@ -51,8 +51,14 @@ typedef enum {
   BOZO_ERR_NULL = 5,           /* a required pointer is NULL */
   BOZO_ERR_DEVICE_TIMEOUT = 6, /* a bounded device-side wait gave up */
   BOZO_ERR_CUDA = 7,           /* a CUDA runtime call failed */
-  BOZO_ERR_WORKSPACE = 8       /* workspace NULL or smaller than required */
+  BOZO_ERR_WORKSPACE = 8,      /* workspace NULL or smaller than required */
+  BOZO_ERR_SCRATCH_LIMIT = 9   /* bozo_tension_bwd_noalloc: problem needs more
+                                  than BOZO_NOALLOC_SCRATCH_BYTES of scratch */
 } bozo_status;
+
+/* Size of the library's fixed device scratch array used by
+ * bozo_tension_bwd_noalloc (8 MiB per device). */
+#define BOZO_NOALLOC_SCRATCH_BYTES (8u << 20)
 
 typedef enum { BOZO_DT_F32 = 0, BOZO_DT_BF16 = 1, BOZO_DT_F16 = 2 } bozo_dtype;
 typedef enum { BOZO_MODE_LOCAL = 0, BOZO_MODE_GLOBAL = 1 } bozo_mode;
@@ -141,6 +147,24 @@ size_t bozo_tension_bwd_workspace(const bozo_tension_bwd_args* args);
 
 /* Backward: writes dq, dk, dv. */
 int bozo_tension_bwd(const bozo_tension_bwd_args* args, void* stream);
+
+/* Backward that allocates nothing. This entry point has no counterpart in the
+ * reference (triton_tension/ops.py:126-187 lets torch allocate its scratch).
+ * It is for callers that cannot allocate device memory per call: a plain C,
+ * cgo or ctypes host with no caching allocator (a cudaMalloc/cudaFree pair per
+ * backward would synchronise the device each step), or a service that reserves
+ * all device memory at start-up and may not allocate afterwards.
+ * Same arguments and results as bozo_tension_bwd, except that `workspace` and
+ * `workspace_bytes` are ignored: the scratch is a fixed array of
+ * BOZO_NOALLOC_SCRATCH_BYTES inside the library, one per device. Problems whose
+ * bozo_tension_bwd_workspace() exceeds that size return
+ * BOZO_ERR_SCRATCH_LIMIT before anything is launched.
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any stream
+ * capture begins. Calls that overlap in time on one device (two streams, two
+ * threads) share the array and race; the array keeps the last call's contents
+ * after it returns. */
+int bozo_tension_bwd_noalloc(const bozo_tension_bwd_args* args, void* stream);
 
 /* Synchronise `stream`, then read and clear the device error word that
  * bounded waits inside the tensor-core kernels set when they give up.
