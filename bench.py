@@ -159,7 +159,7 @@ def run_ours(args, rank, world, local_rank):
 
     results = {}
     launches_per_step = 0
-    for W in WINDOWS:
+    for W in args.windows:
         steps = args.steps if W == W_HEAD else max(3, args.steps // 4)
         for _ in range(args.warmup):
             step(W)
@@ -191,6 +191,9 @@ def run_ours(args, rank, world, local_rank):
                           clocks=clk.summary() if clk else None, path=bops.last_path())
         if W == W_HEAD:
             launches_per_step = n_launch // steps
+
+    if args.no_e2e:
+        return results, None, launches_per_step
 
     # ── e2e: public API, pinned host buffers in, results out, every step ──
     hq, hk, hv, hdo = [x.pin_memory() for x in (hq, hk, hv, hdo)]
@@ -246,7 +249,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--windows", type=int, nargs="+", default=list(WINDOWS),
+                    help="windows to time; the headline window is always included")
     args = ap.parse_args()
+    if W_HEAD not in args.windows:
+        args.windows = [W_HEAD] + args.windows
     args.warmup = max(3, args.warmup)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -332,9 +341,10 @@ def main():
                                                               flops_fwd_bwd(B, H, T, HD, W) / (tfl * 1e12))
                                                           / (r["ms"] * 1e-3), 4)}
                        for W, r in results.items()},
-        "e2e": {"value": round(n * per_step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+        "e2e": None if e2e_ms is None else {
+            "value": round(n * per_step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h},
         "gpu_launches": head["launches"],
         "launches_per_step": launches_per_step,
         "clocks": head["clocks"],

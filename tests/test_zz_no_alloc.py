@@ -41,7 +41,7 @@ def _problem(seed, B, T, H, HD, dtype, *, mode, window, norm, rope_base, tau):
     dev = torch.device("cuda:0")
     q, k, v, d_out = (torch.randn(B, T, H, HD, generator=g).to(dev, dtype) for _ in range(4))
     rope = ops.rope_tables(HD, T, rope_base, dev) if rope_base else None
-    scale = HD ** -0.5
+    scale = HD ** 0.5  # the divisor of Q·K (model.py:122)
     width = window if mode == _capi.MODE_LOCAL else T
     out, _, mass, q_rot, k_rot = ops._launch_fwd(
         q, k, v, mode=mode, window=window, norm=norm, scale=scale, rope=rope, bias=None,
