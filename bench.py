@@ -48,6 +48,17 @@ def peaks():
     return FALLBACK_HBM_GBS, 1590.0, "fallback"
 
 
+def sustained_tflops():
+    """Dense bf16 peak for work timed inside a long step (MEASURED_PEAKS.json
+    bf16_tflops_sustained; the fallback's sustained figure otherwise)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        if "bf16_tflops_sustained" in d:
+            return float(d["bf16_tflops_sustained"]), "measured sustained"
+    return 1400.0, "fallback sustained"
+
+
 def bytes_fwd(b=B, h=H, t=T, hd=HD):
     return b * h * t * (4 * hd * 2 + 4)
 
@@ -159,6 +170,18 @@ def run_ours(args, rank, world, local_rank):
 
     results = {}
     launches_per_step = 0
+    # Process-level warm-up before any timed block: the first timed block of a
+    # fresh process otherwise runs slow (clock and power ramp, allocator and
+    # module first use); at least the requested warm-up steps, and ~1 s of work.
+    t_w = time.perf_counter()
+    n_w = 0
+    while n_w < args.warmup or time.perf_counter() - t_w < 1.0:
+        step(W_HEAD)
+        n_w += 1
+        if n_w % 8 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    barrier()
     for W in args.windows:
         steps = args.steps if W == W_HEAD else max(3, args.steps // 4)
         for _ in range(args.warmup):
@@ -221,6 +244,80 @@ def run_ours(args, rank, world, local_rank):
     return results, e2e_ms, launches_per_step
 
 
+TRAIN_B, TRAIN_T = 16, 1024  # per-GPU batch 16, seq 1024
+
+
+def run_train(args, rank, world, local_rank):
+    """117M TensionLM training steps through the
+    harness bozo_b200.lm: bf16 autocast, the operator in every tension layer,
+    CE + train.py's default aux losses (w_closure 0.01, w_diversity 0.02,
+    which put τ export and its cotangent in the loop), global-norm clip,
+    fused AdamW; DDP over NCCL when world > 1.  Per-GPU batch 16 × 1024
+    tokens, uniform random token ids from a per-rank seed, random init.
+    Returns {variant: (ms_per_step max over ranks, e2e ms_per_step)}."""
+    import torch.distributed as dist
+    from bozo_b200 import lm
+    dev = torch.device("cuda", local_rank)
+    torch.manual_seed(0)  # identical init on every rank (DDP also broadcasts rank 0's)
+    cfg = lm.preset_117m()
+    base = lm.TensionLM(cfg).to(dev)
+    model = lm.wrap_ddp(base) if world > 1 else base
+    opt = lm.make_optimizer(base, fused=True)
+    g = torch.Generator().manual_seed(4242 + rank)
+    ids_h = torch.randint(0, cfg.vocab_size, (TRAIN_B, TRAIN_T + 1), generator=g).pin_memory()
+    ids = ids_h.to(dev)
+    inputs, targets = ids[:, :-1], ids[:, 1:]
+    loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+
+    def maxred(x):
+        if world > 1:
+            t_ = torch.tensor([x], device=dev, dtype=torch.float64)
+            dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+            return float(t_.item())
+        return x
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    out = {}
+    variants = (("aux_on", lm.TrainWeights()),
+                ("aux_off", lm.TrainWeights(0.0, 0.0, 0.0, 0.0)))
+    for name, w in variants:
+        for _ in range(args.train_warmup):
+            lm.train_step(model, base, opt, inputs, targets, weights=w)
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.train_steps):
+            lm.train_step(model, base, opt, inputs, targets, weights=w)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = maxred(e0.elapsed_time(e1)) / args.train_steps
+        e2e = None
+        if name == "aux_on":
+            # end to end: token ids copied in from pinned host memory and the
+            # loss read back every step
+            barrier()
+            e0.record(stream)
+            for _ in range(args.train_steps):
+                idd = ids_h.to(dev, non_blocking=True)
+                loss = lm.train_step(model, base, opt, idd[:, :-1], idd[:, 1:], weights=w)
+                loss_h.copy_(loss, non_blocking=True)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            e2e = maxred(e0.elapsed_time(e1)) / args.train_steps
+        out[name] = (ms, e2e)
+        barrier()
+    params = base.num_params
+    del model, base, opt
+    torch.cuda.empty_cache()
+    return out, params
+
+
 def cpu_baseline(budget_s=12.0):
     """The reference CPU algorithm (oracle port of ops.py:29-63 + model.py
     τ-mass + RoPE, fp32 autograd) on B=1 slices of the workload."""
@@ -245,17 +342,21 @@ def cpu_baseline(budget_s=12.0):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--workload", default="all", choices=["all", "op", "train"],
+                    help="op: isolated operator (headline); train: 117M training step")
+    ap.add_argument("--train-steps", type=int, default=10)
+    ap.add_argument("--train-warmup", type=int, default=3)
     ap.add_argument("--windows", type=int, nargs="+", default=list(WINDOWS),
                     help="windows to time; the headline window is always included")
     args = ap.parse_args()
-    if W_HEAD not in args.windows:
-        args.windows = [W_HEAD] + args.windows
+    # the headline window is timed first, the others follow
+    args.windows = [W_HEAD] + [w for w in args.windows if w != W_HEAD]
     args.warmup = max(3, args.warmup)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -301,11 +402,55 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    results, e2e_ms, launches_per_step = run_ours(args, rank, world, local_rank)
+    results = train = None
+    if args.workload in ("all", "op"):
+        results, e2e_ms, launches_per_step = run_ours(args, rank, world, local_rank)
+    if args.workload in ("all", "train"):
+        torch.cuda.empty_cache()
+        train, n_params = run_train(args, rank, world, local_rank)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
     if rank != 0:
+        return
+    train_obj = None
+    if train is not None:
+        n = args.gpus
+        tok = n * TRAIN_B * TRAIN_T
+        ms_on, e2e_on = train["aux_on"]
+        ms_off, _ = train["aux_off"]
+        flop_tok = 6 * n_params + 12 * 64 * 12 * (9 * 64 + 3 * (TRAIN_T + 1) / 2)
+        tflops = tok * flop_tok / (ms_on * 1e-3) / 1e12
+        train_obj = {
+            "metric": "117M TensionLM train tokens/s (whole job)",
+            "value": round(tok / (ms_on * 1e-3), 1), "unit": "tokens/s",
+            "ms_per_step": round(ms_on, 3), "steps": args.train_steps,
+            "warmup": args.train_warmup, "n_gpus": n,
+            "aux_losses": "on (train.py defaults w_closure 0.01, w_diversity 0.02)",
+            "aux_off": {"value": round(tok / (ms_off * 1e-3), 1), "unit": "tokens/s",
+                        "ms_per_step": round(ms_off, 3)},
+            "model_tflops": round(tflops, 1),
+            "mfu": round(tflops / sustained_tflops()[0], 4),
+            "mfu_peak": f"{sustained_tflops()[0]} TFLOP/s bf16 ({sustained_tflops()[1]})",
+            "flops_per_token": int(flop_tok),
+            "e2e": {"value": round(tok / (e2e_on * 1e-3), 1), "unit": "tokens/s",
+                    "ms_per_step": round(e2e_on, 3),
+                    "h2d_bytes_per_step": TRAIN_B * (TRAIN_T + 1) * 8,
+                    "d2h_bytes_per_step": 4},
+            "config": {"workload": "TensionLM 117M training step (BASELINE configs[3])",
+                       "params": n_params, "dim": 768, "layers": 12, "heads": 12,
+                       "vocab": 32768, "W": 64, "global_every": 4, "seq_len": TRAIN_T,
+                       "per_gpu_batch": TRAIN_B, "global_batch": TRAIN_B * n,
+                       "dtype": "bf16 autocast, fp32 master weights", "optimizer": "AdamW (fused)",
+                       "parallelism": f"ddp{n}" if n > 1 else "single GPU",
+                       "data": "uniform random token ids, random init"},
+        }
+    if results is None:
+        line = dict(train_obj)
+        line.update({"higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                     "dtype": "bf16", "data": "synthetic"})
+        line["config"] = train_obj["config"]
+        print(json.dumps(line))
         return
 
     head = results[W_HEAD]
@@ -349,6 +494,8 @@ def main():
         "launches_per_step": launches_per_step,
         "clocks": head["clocks"],
     }
+    if train_obj is not None:
+        line["train_117m"] = train_obj
     if n == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     print(json.dumps(line))

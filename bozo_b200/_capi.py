@@ -66,6 +66,7 @@ class BwdArgs(C.Structure):
 
 
 _lib = None
+_ext = None
 _lock = threading.Lock()
 
 
@@ -98,6 +99,27 @@ def lib():
                 L.bozo_tension_last_cuda_error.restype = C.c_char_p
                 _lib = L
     return _lib
+
+
+def ext():
+    """The PyTorch C++ extension (``_torch_ext``) that calls the C ABI for the
+    autograd functions; built beside the library by ``bozo_b200.build``."""
+    global _ext
+    if _ext is None:
+        lib()  # the extension links against the library: fail with its message first
+        with _lock:
+            if _ext is None:
+                import glob
+                import importlib.util
+                found = glob.glob(os.path.join(os.path.dirname(LIB_PATH), "_torch_ext*.so"))
+                if not found:
+                    raise ImportError("the bozo_b200 torch extension is missing: build it with "
+                                      "`python -m bozo_b200.build`")
+                spec = importlib.util.spec_from_file_location("_torch_ext", found[0])
+                mod = importlib.util.module_from_spec(spec)
+                spec.loader.exec_module(mod)
+                _ext = mod
+    return _ext
 
 
 def status_string(code: int) -> str:

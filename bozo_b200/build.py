@@ -85,12 +85,49 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return lib
 
 
+EXT_SRC = os.path.join(CSRC, "host", "torch_ext.cpp")
+EXT_NAME = "_torch_ext"
+
+
+def ext_path() -> str:
+    import sysconfig
+    return os.path.join(OUT_DIR, EXT_NAME + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_ext(force: bool = False) -> str:
+    """Compile the PyTorch C++ extension (csrc/host/torch_ext.cpp) against the
+    installed torch and link it to the C-ABI library beside it ($ORIGIN)."""
+    import sysconfig
+    import torch
+    from torch.utils import cpp_extension as ce
+    lib = os.path.join(OUT_DIR, LIB_NAME)
+    out = ext_path()
+    if not force and not _newer([EXT_SRC, lib] + headers(), out):
+        return out
+    torch_lib = ce.library_paths()[0]
+    cuda_inc = os.path.join(os.path.dirname(os.path.dirname(nvcc())), "include")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-w",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", f"-DTORCH_EXTENSION_NAME={EXT_NAME}",
+           "-DTORCH_API_INCLUDE_EXTENSION_H",
+           *[f"-I{p}" for p in ce.include_paths()], f"-I{sysconfig.get_paths()['include']}",
+           f"-I{cuda_inc}", f"-I{INCLUDE}", EXT_SRC, "-o", out,
+           f"-L{torch_lib}", "-lc10", "-ltorch", "-ltorch_cpu", "-ltorch_python", "-lc10_cuda",
+           "-ltorch_cuda", f"-L{OUT_DIR}", "-lbozo_tension",
+           "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"torch extension build failed:\n{r.stdout}\n{r.stderr}")
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true", help="print ptxas resource usage")
     a = ap.parse_args()
     print(build(force=a.force, verbose=a.verbose))
+    print(build_ext(force=a.force))
 
 
 if __name__ == "__main__":

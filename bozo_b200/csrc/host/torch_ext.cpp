@@ -1,0 +1,184 @@
+// torch_ext.cpp — PyTorch C++ extension over the C ABI (include/bozo_tension.h).
+//
+// The autograd functions in bozo_b200/ops.py call these two entry points for
+// every forward / backward.  They fill the ABI argument blocks straight from
+// at::Tensor metadata, allocate the outputs (and the backward's coefficient
+// workspace) with the caching allocator on the tensors' device, and launch on
+// the caller's current stream — the same work the reference's
+// _CausalTensionFn.forward/backward do around their Triton launches
+// (triton_tension/ops.py:75-124, 126-187), in C++ so a call costs a few
+// microseconds of host time instead of a Python-level struct build.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "bozo_tension.h"
+
+namespace {
+
+int dtype_code(at::ScalarType t) {
+  switch (t) {
+    case at::kFloat: return BOZO_DT_F32;
+    case at::kBFloat16: return BOZO_DT_BF16;
+    case at::kHalf: return BOZO_DT_F16;
+    default:
+      throw pybind11::type_error(std::string("bozo tension: unsupported dtype ") +
+                                  c10::toString(t) +
+                                  " (float32, bfloat16 and float16 are supported)");
+  }
+}
+
+at::ScalarType scalar_type(int64_t code) {
+  switch (code) {
+    case BOZO_DT_F32: return at::kFloat;
+    case BOZO_DT_BF16: return at::kBFloat16;
+    case BOZO_DT_F16: return at::kHalf;
+    default: throw pybind11::type_error("bozo tension: bad dtype code");
+  }
+}
+
+bozo_tensor4 t4(const at::Tensor& t) {
+  bozo_tensor4 s{};
+  if (!t.defined()) return s;
+  s.ptr = t.data_ptr();
+  s.dtype = dtype_code(t.scalar_type());
+  for (int i = 0; i < 4; ++i) s.stride[i] = t.stride(i);
+  return s;
+}
+
+void check(int status, const char* what) {
+  if (status == BOZO_OK) return;
+  std::string msg = std::string(what) + " failed: " + bozo_status_string(status) +
+                    " (status " + std::to_string(status) + ")";
+  if (status == BOZO_ERR_CUDA) msg += std::string(" [") + bozo_tension_last_cuda_error() + "]";
+  throw std::runtime_error(msg);
+}
+
+template <typename A>
+void fill_common(A& a, const at::Tensor& q, int64_t mode, int64_t window, int64_t norm,
+                 double scale, int64_t path, const c10::optional<at::Tensor>& cos,
+                 const c10::optional<at::Tensor>& sin, const c10::optional<at::Tensor>& theta) {
+  a.B = (int32_t)q.size(0);
+  a.T = (int32_t)q.size(1);
+  a.H = (int32_t)q.size(2);
+  a.HD = (int32_t)q.size(3);
+  a.mode = (int32_t)mode;
+  a.window = (int32_t)window;
+  a.normalize = (int32_t)norm;
+  a.path = (int32_t)path;
+  a.scale = (float)scale;
+  if (cos && cos->defined()) {
+    a.rope_len = (int32_t)cos->size(0);
+    a.rope_cos = cos->data_ptr<float>();
+    a.rope_sin = sin->data_ptr<float>();
+    a.rope_theta = (theta && theta->defined()) ? theta->data_ptr<float>() : nullptr;
+  }
+}
+
+void fill_bias(const c10::optional<at::Tensor>& bias, const float** ptr, int64_t* stride) {
+  if (bias && bias->defined()) {
+    *ptr = bias->data_ptr<float>();
+    for (int i = 0; i < 3; ++i) stride[i] = bias->stride(i);
+  }
+}
+
+// Returns [out, tau, row_mass, q_rot, k_rot]; absent ones are None.
+std::vector<at::Tensor> tension_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                    int64_t mode, int64_t window, int64_t norm, double scale,
+                                    int64_t path, const c10::optional<at::Tensor>& cos,
+                                    const c10::optional<at::Tensor>& sin,
+                                    const c10::optional<at::Tensor>& theta,
+                                    const c10::optional<at::Tensor>& bias, int64_t tau_width,
+                                    int64_t out_dtype, int64_t tau_dtype, bool want_mass,
+                                    bool want_rotated) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int64_t B = q.size(0), T = q.size(1), H = q.size(2), HD = q.size(3);
+  auto opts = q.options();
+  at::Tensor out = at::empty({B, T, H, HD}, opts.dtype(scalar_type(out_dtype)));
+  at::Tensor tau, mass, q_rot, k_rot;
+  if (tau_width > 0) tau = at::empty({B, T, H, tau_width}, opts.dtype(scalar_type(tau_dtype)));
+  if (want_mass) mass = at::empty({B, H, T}, opts.dtype(at::kFloat));
+  if (want_rotated && cos && cos->defined()) {
+    q_rot = at::empty({B, T, H, HD}, opts);
+    k_rot = at::empty({B, T, H, HD}, k.options());
+  }
+  bozo_tension_fwd_args a{};
+  fill_common(a, q, mode, window, norm, scale, path, cos, sin, theta);
+  a.q = t4(q);
+  a.k = t4(k);
+  a.v = t4(v);
+  fill_bias(bias, &a.bias, a.bias_stride);
+  a.out = out.data_ptr();
+  a.out_dtype = (int32_t)out_dtype;
+  if (tau.defined()) {
+    a.tau = tau.data_ptr();
+    a.tau_dtype = (int32_t)tau_dtype;
+  }
+  if (mass.defined()) a.row_mass = mass.data_ptr<float>();
+  if (q_rot.defined()) {
+    a.q_rot = q_rot.data_ptr();
+    a.k_rot = k_rot.data_ptr();
+  }
+  check(bozo_tension_fwd(&a, at::cuda::getCurrentCUDAStream(q.device().index()).stream()),
+        "bozo_tension_fwd");
+  return {out, tau, mass, q_rot, k_rot};
+}
+
+// Returns [dq, dk, dv] in the dtypes of q, k, v.
+std::vector<at::Tensor> tension_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                    const at::Tensor& d_out, int64_t mode, int64_t window,
+                                    int64_t norm, double scale, int64_t path,
+                                    const c10::optional<at::Tensor>& cos,
+                                    const c10::optional<at::Tensor>& sin,
+                                    const c10::optional<at::Tensor>& theta,
+                                    const c10::optional<at::Tensor>& bias,
+                                    const c10::optional<at::Tensor>& out,
+                                    const c10::optional<at::Tensor>& mass,
+                                    const c10::optional<at::Tensor>& d_tau, bool qk_rotated) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int64_t B = q.size(0), T = q.size(1), H = q.size(2), HD = q.size(3);
+  at::Tensor dq = at::empty({B, T, H, HD}, q.options());
+  at::Tensor dk = at::empty({B, T, H, HD}, k.options());
+  at::Tensor dv = at::empty({B, T, H, HD}, v.options());
+  bozo_tension_bwd_args a{};
+  fill_common(a, q, mode, window, norm, scale, path, cos, sin, theta);
+  a.q = t4(q);
+  a.k = t4(k);
+  a.v = t4(v);
+  a.d_out = t4(d_out);
+  if (out && out->defined()) a.out = t4(*out);
+  if (mass && mass->defined()) a.row_mass = mass->data_ptr<float>();
+  fill_bias(bias, &a.bias, a.bias_stride);
+  if (d_tau && d_tau->defined()) {
+    a.d_tau = d_tau->data_ptr();
+    a.d_tau_dtype = dtype_code(d_tau->scalar_type());
+  }
+  a.grad_dtype[0] = dtype_code(q.scalar_type());
+  a.grad_dtype[1] = dtype_code(k.scalar_type());
+  a.grad_dtype[2] = dtype_code(v.scalar_type());
+  a.qk_rotated = qk_rotated ? 1 : 0;
+  a.dq = dq.data_ptr();
+  a.dk = dk.data_ptr();
+  a.dv = dv.data_ptr();
+  const size_t ws_bytes = bozo_tension_bwd_workspace(&a);
+  at::Tensor ws;
+  if (ws_bytes) {
+    ws = at::empty({(int64_t)ws_bytes}, q.options().dtype(at::kByte));
+    a.workspace = ws.data_ptr();
+    a.workspace_bytes = ws_bytes;
+  }
+  check(bozo_tension_bwd(&a, at::cuda::getCurrentCUDAStream(q.device().index()).stream()),
+        "bozo_tension_bwd");
+  return {dq, dk, dv};
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "PyTorch binding of the bozo tension C ABI";
+  m.def("tension_fwd", &tension_fwd, "forward through bozo_tension_fwd");
+  m.def("tension_bwd", &tension_bwd, "backward through bozo_tension_bwd");
+}

@@ -94,44 +94,51 @@ __host__ __device__ inline Layout bwd_layout() {
 
 // Per query row: the epilogue's coefficients α/2, α·c and β·c (c = 1/(4·scale))
 // of the normalisation, into padded rows [B·H, tpad] (rows t ≥ T are 0).
-// τ-mass needs dO·out, read as 128-bit loads from bf16 rows of 64.
+// τ-mass needs D = dO·out per row: eight threads share one 128-byte bf16 row
+// (one 16-byte chunk each) and rows are walked in memory order (b, t, h), so
+// every warp load is four whole rows.  The grid-stride step is a multiple of
+// 32 threads, so the 8-lane shuffle groups stay whole and warp-uniform.
 __global__ void alpha_beta_kernel(int B, int T, int H, int W, int tpad, int norm, float ds_scale,
                                   const float* __restrict__ row_mass, DevT4 dout, DevT4 out,
                                   float* __restrict__ a_half, float* __restrict__ a_ds,
                                   float* __restrict__ b_ds) {
-  const long long n = (long long)B * H * tpad;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < n;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const int t = (int)(idx % tpad);
-    const int bh = (int)(idx / tpad);
-    float a = 0.f, b = 0.f;
-    if (t < T) {
+  const long long rows = (long long)B * T * H;
+  const long long n8 = rows * 8;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const int c = threadIdx.x & 7;
+  for (long long base = (long long)blockIdx.x * blockDim.x; base < n8; base += stride) {
+    const long long idx = base + threadIdx.x;
+    const bool live = idx < n8;
+    const long long r = live ? idx >> 3 : 0;
+    const int h = (int)(r % H);
+    const long long bt = r / H;
+    const int t = (int)(bt % T), bb = (int)(bt / T);
+    float dd = 0.f;
+    if (norm == BOZO_NORM_MASS && live) {
+      const uint4 x = __ldg(reinterpret_cast<const uint4*>(
+          static_cast<const __nv_bfloat16*>(dout.p) + bb * dout.sb + (long long)t * dout.st + h * dout.sh) + c);
+      const uint4 y = __ldg(reinterpret_cast<const uint4*>(
+          static_cast<const __nv_bfloat16*>(out.p) + bb * out.sb + (long long)t * out.st + h * out.sh) + c);
+      const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+      const uint32_t ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 u = *reinterpret_cast<const __nv_bfloat162*>(&xs[e]);
+        const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&ys[e]);
+        dd = fmaf(__low2float(u), __low2float(v), dd);
+        dd = fmaf(__high2float(u), __high2float(v), dd);
+      }
+    }
+    if (norm == BOZO_NORM_MASS) {
+      dd += __shfl_xor_sync(0xffffffffu, dd, 4);
+      dd += __shfl_xor_sync(0xffffffffu, dd, 2);
+      dd += __shfl_xor_sync(0xffffffffu, dd, 1);
+    }
+    if (live && c == 0) {
+      const long long bh = (long long)bb * H + h;
+      float a, b = 0.f;
       if (norm == BOZO_NORM_MASS) {
-        const int bb = bh / H, h = bh % H;
-        const uint4* dr = reinterpret_cast<const uint4*>(
-            static_cast<const __nv_bfloat16*>(dout.p) + bb * dout.sb + (long long)t * dout.st + h * dout.sh);
-        const uint4* orow = reinterpret_cast<const uint4*>(
-            static_cast<const __nv_bfloat16*>(out.p) + bb * out.sb + (long long)t * out.st + h * out.sh);
-        uint4 x[8], y[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          x[c] = __ldg(dr + c);
-          y[c] = __ldg(orow + c);
-        }
-        float dd = 0.f;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t xs[4] = {x[c].x, x[c].y, x[c].z, x[c].w};
-          const uint32_t ys[4] = {y[c].x, y[c].y, y[c].z, y[c].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const __nv_bfloat162 u = *reinterpret_cast<const __nv_bfloat162*>(&xs[e]);
-            const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&ys[e]);
-            dd = fmaf(__low2float(u), __low2float(v), dd);
-            dd = fmaf(__high2float(u), __high2float(v), dd);
-          }
-        }
-        const float m = row_mass[(long long)bh * T + t];
+        const float m = row_mass[bh * T + t];
         a = 1.f / fmaxf(m, kMassEps);
         b = m >= kMassEps ? -dd * a : 0.f;
       } else if (norm == BOZO_NORM_COUNT) {
@@ -139,10 +146,20 @@ __global__ void alpha_beta_kernel(int B, int T, int H, int W, int tpad, int norm
       } else {
         a = 1.f;
       }
+      const long long o = bh * tpad + t;
+      a_half[o] = 0.5f * a;
+      a_ds[o] = a * ds_scale;
+      b_ds[o] = b * ds_scale;
     }
-    a_half[idx] = 0.5f * a;
-    a_ds[idx] = a * ds_scale;
-    b_ds[idx] = b * ds_scale;
+  }
+  // padding rows t ∈ [T, tpad)
+  const int pad = tpad - T;
+  const long long npad = (long long)B * H * pad;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < npad; i += stride) {
+    const long long o = (i / pad) * tpad + T + (i % pad);
+    a_half[o] = 0.f;
+    a_ds[o] = 0.f;
+    b_ds[o] = 0.f;
   }
 }
 
@@ -716,7 +733,8 @@ cudaError_t launch_tc_bwd(const BwdP& p, cudaStream_t st, int* launches) {
   a.err = p.err;
   {  // coefficient pre-pass into the (padded) workspace rows
     const long long n = (long long)p.B * p.H * a.tpad;
-    const int g = (int)std::min<long long>((n + 255) / 256, (long long)num_sms() * 8);
+    const int g = (int)std::min<long long>(((long long)p.B * p.T * p.H * 8 + 255) / 256,
+                                           (long long)num_sms() * 16);
     alpha_beta_kernel<<<g, 256, 0, st>>>(p.B, p.T, p.H, p.W, a.tpad, p.norm, a.ds_scale,
                                          p.row_mass, p.dout, p.out, p.coef, p.coef + n,
                                          p.coef + 2 * n);

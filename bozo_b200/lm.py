@@ -1,0 +1,387 @@
+"""TensionLM on the B200 operator — the model the 117M training workload runs.
+
+A restatement of the reference model (model.py:25-480) and of one training
+step of train.py (train.py:1040-1150) with every tension layer on
+``bozo_b200.tension``: RoPE, the local window or the global full-causal
+block, the normalisation and the optional τ export happen inside the
+operator's kernels instead of around ``causal_tension``.  Parameters, module
+names and initialisation follow model.py, so a reference ``state_dict``
+loads into it unchanged.
+
+Where model.py has two local-layer branches (model.py:247-264), this one
+keeps both: with ``return_tensions`` the τ-mass normalisation and τ export
+(model.py:250-258), without it the position-count normalisation
+(model.py:261-264).  Global layers use τ-mass and export the reference's
+flipped τ window (model.py:217-237).
+"""
+from __future__ import annotations
+
+import math
+from collections import defaultdict
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+
+
+@dataclass
+class TensionConfig:
+    """model.py:25-52 (same fields and defaults)."""
+    vocab_size: int = 2048
+    dim: int = 128
+    num_layers: int = 4
+    num_heads: int = 4
+    window: int = 8
+    ffn_mult: int = 3
+    max_seq_len: int = 256
+    dropout: float = 0.10
+    use_grad_checkpoint: bool = False
+    use_oscillation: bool = True
+    use_rope: bool = False
+    use_triton: bool = True  # kept for state compatibility; the operator is always used
+    global_every: int = 0
+
+    @property
+    def head_dim(self) -> int:
+        assert self.dim % self.num_heads == 0, "dim must be divisible by num_heads"
+        return self.dim // self.num_heads
+
+
+def preset_117m(**over) -> TensionConfig:
+    """train.py:226-234 ``--preset large`` with the benchmark's
+    ``--seq_len 1024 --max_seq_len 1024`` (117.2M parameters)."""
+    cfg = dict(vocab_size=32768, dim=768, num_layers=12, num_heads=12, window=64, ffn_mult=3,
+               max_seq_len=1024, dropout=0.0, use_oscillation=False, use_rope=True,
+               global_every=4)
+    cfg.update(over)
+    return TensionConfig(**cfg)
+
+
+class RMSNorm(nn.Module):
+    """model.py:86-98."""
+
+    def __init__(self, dim: int, eps: float = 1e-6):
+        super().__init__()
+        self.eps = eps
+        self.scale = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x):
+        return F.rms_norm(x, x.shape[-1:], self.scale, self.eps)
+
+
+class MultiHeadCausalTensionLayer(nn.Module):
+    """model.py:103-283 with the tension core on the fused operator."""
+
+    def __init__(self, cfg: TensionConfig, global_layer: bool = False):
+        super().__init__()
+        self.window = cfg.max_seq_len if global_layer else cfg.window
+        self.local_window = cfg.window
+        self.global_layer = global_layer
+        self.num_heads = cfg.num_heads
+        self.head_dim = cfg.head_dim
+        self.scale = math.sqrt(self.head_dim)
+        self.max_seq_len = cfg.max_seq_len
+        D = cfg.dim
+        self.wq = nn.Linear(D, D, bias=False)
+        self.rope_enabled = cfg.use_rope
+        if cfg.use_rope:
+            self.wk = nn.Linear(D, D, bias=False)
+            self.wv = nn.Linear(D, D, bias=False)
+            self.wkv = None
+        else:
+            self.wkv = nn.Linear(D, 2 * D, bias=False)
+            self.wk = self.wv = None
+        self.wo = nn.Linear(D, D, bias=False)
+        self.norm = RMSNorm(D)
+        self.dropout = nn.Dropout(cfg.dropout)
+        # the operator; tests may substitute a CPU restatement with the same keywords
+        self.tension_fn: Callable = ops.tension
+
+    def forward(self, x, return_tensions: bool = False, tau_bias=None):
+        B, T, D = x.shape
+        H, HD = self.num_heads, self.head_dim
+        q = self.wq(x).view(B, T, H, HD)
+        if self.rope_enabled:
+            k = self.wk(x).view(B, T, H, HD)
+            v = self.wv(x).view(B, T, H, HD)
+        else:
+            kv = self.wkv(x).view(B, T, H, 2 * HD)
+            k, v = kv.split(HD, dim=-1)
+        rope = 10_000.0 if self.rope_enabled else None
+        if self.global_layer:
+            res = self.tension_fn(q, k, v, window=None, scale=self.scale, rope_base=rope,
+                                  rope_len=self.max_seq_len, bias=tau_bias,
+                                  return_tau=return_tensions, normalize="mass",
+                                  tau_window=self.local_window)
+            msg, tau = res if return_tensions else (res, None)
+            out = self.norm(x + self.dropout(self.wo(msg.reshape(B, T, D))))
+            return (out, tau) if return_tensions else out
+        if return_tensions:
+            msg, tau = self.tension_fn(q, k, v, window=self.window, scale=self.scale,
+                                       rope_base=rope, rope_len=self.max_seq_len,
+                                       bias=tau_bias, return_tau=True, normalize="mass")
+            out = self.norm(x + self.dropout(self.wo(msg.reshape(B, T, D))))
+            return out, tau
+        msg = self.tension_fn(q, k, v, window=self.window, scale=self.scale, rope_base=rope,
+                              rope_len=self.max_seq_len, bias=tau_bias, normalize="count")
+        msg = self.dropout(msg)
+        return self.norm(x + self.wo(msg.reshape(B, T, D)))
+
+
+class OscillatoryModulation(nn.Module):
+    """model.py:288-310."""
+
+    def __init__(self, cfg: TensionConfig):
+        super().__init__()
+        self.freqs = nn.Parameter(torch.randn(cfg.dim) * 0.02)
+        self.phases = nn.Parameter(torch.zeros(cfg.dim))
+        self.amp = nn.Parameter(torch.full((1,), 0.1))
+        pos = torch.arange(cfg.max_seq_len, dtype=torch.float).unsqueeze(-1)
+        self.register_buffer("pos_buf", pos, persistent=False)
+
+    def forward(self, x):
+        T = x.shape[1]
+        mod = torch.sin(self.pos_buf[:T] * self.freqs + self.phases)
+        return x * (1.0 + self.amp * mod.unsqueeze(0))
+
+
+class TensionFFN(nn.Module):
+    """model.py:315-330 (SwiGLU)."""
+
+    def __init__(self, cfg: TensionConfig):
+        super().__init__()
+        hidden = cfg.dim * cfg.ffn_mult
+        self.gate = nn.Linear(cfg.dim, hidden, bias=False)
+        self.val = nn.Linear(cfg.dim, hidden, bias=False)
+        self.proj = nn.Linear(hidden, cfg.dim, bias=False)
+        self.norm = RMSNorm(cfg.dim)
+        self.dropout = nn.Dropout(cfg.dropout)
+
+    def forward(self, x):
+        h = F.silu(self.gate(x)) * self.val(x)
+        return self.norm(x + self.dropout(self.proj(h)))
+
+
+class TensionBlock(nn.Module):
+    """model.py:335-386 (gradient checkpointing left out: the operator keeps no
+    O(T·W·HD) intermediates, so there is nothing large to recompute)."""
+
+    def __init__(self, cfg: TensionConfig, global_layer: bool = False):
+        super().__init__()
+        self.pre_norm = RMSNorm(cfg.dim)
+        self.tension = MultiHeadCausalTensionLayer(cfg, global_layer=global_layer)
+        self.oscillate = OscillatoryModulation(cfg) if cfg.use_oscillation else None
+        self.ffn = TensionFFN(cfg)
+        self.global_layer = global_layer
+
+    def _osc(self, x):
+        return self.oscillate(x) if self.oscillate is not None else x
+
+    def forward(self, x, return_tensions: bool = False, tau_bias=None):
+        h = self.pre_norm(x)
+        if return_tensions:
+            h, tau = self.tension(h, return_tensions=True, tau_bias=tau_bias)
+            return self.ffn(self._osc(h)), tau
+        return self.ffn(self._osc(self.tension(h, tau_bias=tau_bias)))
+
+
+class TensionLM(nn.Module):
+    """model.py:391-480."""
+
+    def __init__(self, cfg: TensionConfig):
+        super().__init__()
+        self.cfg = cfg
+        self.embedding = nn.Embedding(cfg.vocab_size, cfg.dim)
+        self.emb_drop = nn.Dropout(cfg.dropout)
+        if not cfg.use_rope:
+            self.pos_embedding = nn.Embedding(cfg.max_seq_len, cfg.dim)
+            self.register_buffer("pos_buf", torch.arange(cfg.max_seq_len).unsqueeze(0),
+                                 persistent=False)
+        else:
+            self.pos_embedding = None
+        self.blocks = nn.ModuleList(
+            TensionBlock(cfg, global_layer=cfg.global_every > 0 and (i + 1) % cfg.global_every == 0)
+            for i in range(cfg.num_layers))
+        groups = defaultdict(list)
+        for i, b in enumerate(self.blocks):
+            groups[b.tension.window].append(i)
+        self.window_groups = dict(groups)
+        self.final_norm = RMSNorm(cfg.dim)
+        self.lm_head = nn.Linear(cfg.dim, cfg.vocab_size, bias=False)
+        self.lm_head.weight = self.embedding.weight
+        self._init_weights()
+
+    def _init_weights(self):
+        """model.py:412-424."""
+        std, depth = 0.02, self.cfg.num_layers
+        nn.init.normal_(self.embedding.weight, std=std)
+        if self.pos_embedding is not None:
+            nn.init.normal_(self.pos_embedding.weight, std=std)
+        for name, m in self.named_modules():
+            if isinstance(m, nn.Linear):
+                if name.endswith(("wo", "proj")):
+                    nn.init.normal_(m.weight, std=std / math.sqrt(2 * depth))
+                else:
+                    nn.init.normal_(m.weight, std=std / math.sqrt(depth))
+
+    def set_tension_fn(self, fn: Callable) -> None:
+        for b in self.blocks:
+            b.tension.tension_fn = fn
+
+    def forward(self, input_ids, return_all: bool = False, tau_bias=None, tau_bias_global=None):
+        B, T = input_ids.shape
+        assert T <= self.cfg.max_seq_len, \
+            f"Sequence length {T} exceeds max_seq_len {self.cfg.max_seq_len}"
+        x = self.embedding(input_ids)
+        if self.pos_embedding is not None:
+            x = x + self.pos_embedding(self.pos_buf[:, :T])
+        x = self.emb_drop(x)
+        tensions = []
+        for block in self.blocks:
+            bias = tau_bias_global if block.global_layer else tau_bias
+            if return_all:
+                x, tau = block(x, return_tensions=True, tau_bias=bias)
+                tensions.append(tau)
+            else:
+                x = block(x, tau_bias=bias)
+        hidden = self.final_norm(x)
+        logits = self.lm_head(hidden)
+        if return_all:
+            return logits, hidden, tensions
+        return logits
+
+    @property
+    def num_params(self) -> int:
+        return sum(p.numel() for p in self.parameters())
+
+
+# ── auxiliary losses (model.py:487-611) ──
+
+def manifold_closure_loss(hidden):
+    """model.py:487-494."""
+    return F.mse_loss(hidden[:, -1], hidden[:, 0].detach())
+
+
+def tension_diversity_loss(all_tensions, window_groups=None):
+    """model.py:497-532."""
+    if not all_tensions:
+        return torch.tensor(0.0)
+    if window_groups is not None:
+        groups = {W: [all_tensions[i] for i in idx] for W, idx in window_groups.items()}
+    else:
+        groups = defaultdict(list)
+        for t in all_tensions:
+            groups[t.shape[-1]].append(t)
+    total = torch.tensor(0.0, device=all_tensions[0].device)
+    n = 0
+    for W, ts in groups.items():
+        tau = torch.stack(ts)
+        p = tau / (tau.sum(-1, keepdim=True) + 1e-8)
+        ent = -(p * torch.log(p + 1e-8)).sum(-1)
+        total = total + F.relu(math.log(W) - ent.mean()).mean()
+        n += 1
+    return total / max(n, 1)
+
+
+def constraint_consistency_loss(all_tensions):
+    """model.py:535-577: tau[t,w1]·tau[t−w1,1] ≤ tau[t,w1+1] for w1 ∈ [1, min(W−2, 4)]."""
+    if not all_tensions:
+        return torch.tensor(0.0)
+    total = torch.tensor(0.0, device=all_tensions[0].device)
+    count = 0
+    for tau in all_tensions:
+        B, T, H, W = tau.shape
+        if W < 3 or T < 3:
+            continue
+        m = min(W - 2, 4)
+        last_start = m + 1
+        if last_start >= T:
+            continue
+        n = T - last_start
+        legs1 = torch.stack([tau[:, i + 2:i + 2 + n, :, i] for i in range(m)])
+        legs2 = torch.stack([tau[:, i + 1:i + 1 + n, :, 0] for i in range(m)])
+        comb = torch.stack([tau[:, i + 2:i + 2 + n, :, i + 1] for i in range(m)])
+        total = total + F.relu(legs1 * legs2 - comb).mean()
+        count += 1
+    return total / max(count, 1)
+
+
+def tension_entropy_loss(all_tensions):
+    """model.py:580-611."""
+    if not all_tensions:
+        return torch.tensor(0.0)
+    total = torch.tensor(0.0, device=all_tensions[0].device)
+    for tau in all_tensions:
+        mean_tau = tau.mean(-1)
+        total = total + F.relu(0.05 - mean_tau).mean() + F.relu(mean_tau - 0.80).mean()
+    return total / len(all_tensions)
+
+
+@dataclass
+class TrainWeights:
+    """train.py:135-141 defaults (the large preset leaves them unchanged)."""
+    w_closure: float = 0.01
+    w_diversity: float = 0.02
+    w_consistency: float = 0.0
+    w_entropy: float = 0.0
+
+    @property
+    def aux_enabled(self) -> bool:
+        return any(w > 0 for w in (self.w_closure, self.w_diversity, self.w_consistency,
+                                   self.w_entropy))
+
+
+def wrap_ddp(model: nn.Module):
+    """train.py:789-797: DDP with static graph, no buffer broadcast; gradients
+    are bucketed and all-reduced (NCCL on GPUs) while the backward runs."""
+    from torch.nn.parallel import DistributedDataParallel as DDP
+    dev = next(model.parameters()).device
+    return DDP(model, device_ids=[dev.index] if dev.type == "cuda" else None,
+               find_unused_parameters=False, broadcast_buffers=False, static_graph=True,
+               gradient_as_bucket_view=True)
+
+
+def make_optimizer(model: nn.Module, lr: float = 3e-4, weight_decay: float = 0.10,
+                   fused: Optional[bool] = None):
+    """train.py:893-901: AdamW, decay on ≥2-D parameters, betas (0.9, 0.95)."""
+    decay = [p for p in model.parameters() if p.requires_grad and p.dim() >= 2]
+    nodecay = [p for p in model.parameters() if p.requires_grad and p.dim() < 2]
+    return torch.optim.AdamW([{"params": decay, "weight_decay": weight_decay},
+                              {"params": nodecay, "weight_decay": 0.0}],
+                             lr=lr, betas=(0.9, 0.95), eps=1e-8, fused=fused)
+
+
+def train_step(model, base_model: TensionLM, optimizer, inputs, targets,
+               weights: Optional[TrainWeights] = None, clip_grad: float = 1.0,
+               amp: bool = True):
+    """One optimiser step of train.py:1040-1150 with grad_accum 1: bf16
+    autocast forward (τ returned when aux losses are on), CE + the four aux
+    losses, backward, global-norm clip, AdamW step.  Returns the loss tensor
+    (not synchronised)."""
+    weights = weights or TrainWeights()
+    V = base_model.cfg.vocab_size
+    dev_type = inputs.device.type
+    ctx = torch.autocast(device_type=dev_type, dtype=torch.bfloat16) if amp \
+        else torch.autocast(device_type=dev_type, enabled=False)
+    with ctx:
+        if weights.aux_enabled:
+            logits, hidden, tensions = model(inputs, return_all=True)
+        else:
+            logits, hidden, tensions = model(inputs), None, []
+        loss = F.cross_entropy(logits.reshape(-1, V), targets.reshape(-1))
+        if weights.aux_enabled and tensions:
+            loss = (loss
+                    + weights.w_closure * manifold_closure_loss(hidden)
+                    + weights.w_diversity * tension_diversity_loss(tensions,
+                                                                   base_model.window_groups)
+                    + weights.w_consistency * constraint_consistency_loss(tensions)
+                    + weights.w_entropy * tension_entropy_loss(tensions))
+    loss.backward()
+    nn.utils.clip_grad_norm_(base_model.parameters(), clip_grad)
+    optimizer.step()
+    optimizer.zero_grad(set_to_none=True)
+    return loss.detach()

@@ -44,11 +44,13 @@ def set_kernel_path(path: str) -> None:
     _path_override = path
 
 
-def _dt(t: Tensor) -> int:
+def _dt(t) -> int:
+    """ABI dtype code of a tensor or a torch.dtype (TypeError if unsupported)."""
+    dtype = t if isinstance(t, torch.dtype) else t.dtype
     try:
-        return _DT[t.dtype]
+        return _DT[dtype]
     except KeyError:
-        raise TypeError(f"bozo tension: unsupported dtype {t.dtype} "
+        raise TypeError(f"bozo tension: unsupported dtype {dtype} "
                         "(float32, bfloat16 and float16 are supported)") from None
 
 
@@ -118,60 +120,30 @@ def _bias_arg(a, bias: Optional[Tensor]):
             a.bias_stride[i] = bias.stride(i)
 
 
+def _rope_args(rope):
+    return rope if rope is not None else (None, None, None)
+
+
 def _launch_fwd(q, k, v, *, mode, window, norm, scale, rope, bias, tau_width,
                 out_dtype, tau_dtype, want_mass, want_rotated=False):
-    B, T, H, HD = q.shape
-    out = torch.empty(B, T, H, HD, dtype=out_dtype, device=q.device)
-    q_rot = k_rot = None
-    if want_rotated and rope is not None:
-        q_rot = torch.empty(B, T, H, HD, dtype=q.dtype, device=q.device)
-        k_rot = torch.empty(B, T, H, HD, dtype=k.dtype, device=q.device)
-    tau = (torch.empty(B, T, H, tau_width, dtype=tau_dtype, device=q.device)
-           if tau_width is not None else None)
-    mass = (torch.empty(B, H, T, dtype=torch.float32, device=q.device)
-            if want_mass else None)
-    a = _capi.FwdArgs()
-    _fill_common(a, B, T, H, HD, mode, window, norm, scale, rope)
-    a.q, a.k, a.v = _t4(q), _t4(k), _t4(v)
-    _bias_arg(a, bias)
-    a.out, a.out_dtype = out.data_ptr(), _DT[out_dtype]
-    if tau is not None:
-        a.tau, a.tau_dtype = tau.data_ptr(), _DT[tau_dtype]
-    if mass is not None:
-        a.row_mass = mass.data_ptr()
-    if q_rot is not None:
-        a.q_rot, a.k_rot = q_rot.data_ptr(), k_rot.data_ptr()
-    _capi.check(_capi.lib().bozo_tension_fwd(C.byref(a), _stream(q.device)),
-                "bozo_tension_fwd")
+    """One forward through the C ABI (via the C++ extension); returns
+    (out, tau, row_mass, q_rot, k_rot) with None for outputs not asked for."""
+    cos, sin, theta = _rope_args(rope)
+    out, tau, mass, q_rot, k_rot = _capi.ext().tension_fwd(
+        q, k, v, mode, window, norm, float(scale), _PATH[_path_override], cos, sin, theta,
+        bias, tau_width or 0, _dt(out_dtype), _dt(tau_dtype), bool(want_mass),
+        bool(want_rotated))
     return out, tau, mass, q_rot, k_rot
 
 
 def _launch_bwd(q, k, v, d_out, *, mode, window, norm, scale, rope, bias, out,
                 mass, d_tau, qk_rotated=False):
-    B, T, H, HD = q.shape
-    dq = torch.empty(B, T, H, HD, dtype=q.dtype, device=q.device)
-    dk = torch.empty(B, T, H, HD, dtype=k.dtype, device=q.device)
-    dv = torch.empty(B, T, H, HD, dtype=v.dtype, device=q.device)
-    a = _capi.BwdArgs()
-    _fill_common(a, B, T, H, HD, mode, window, norm, scale, rope)
-    a.q, a.k, a.v, a.d_out = _t4(q), _t4(k), _t4(v), _t4(d_out)
-    if out is not None:
-        a.out = _t4(out)
-    if mass is not None:
-        a.row_mass = mass.data_ptr()
-    _bias_arg(a, bias)
-    if d_tau is not None:
-        a.d_tau, a.d_tau_dtype = d_tau.data_ptr(), _dt(d_tau)
-    a.grad_dtype[0], a.grad_dtype[1], a.grad_dtype[2] = _dt(q), _dt(k), _dt(v)
-    a.qk_rotated = 1 if qk_rotated else 0
-    a.dq, a.dk, a.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
-    L = _capi.lib()
-    ws_bytes = L.bozo_tension_bwd_workspace(C.byref(a))
-    ws = None
-    if ws_bytes:
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
-        a.workspace, a.workspace_bytes = ws.data_ptr(), ws_bytes
-    _capi.check(L.bozo_tension_bwd(C.byref(a), _stream(q.device)), "bozo_tension_bwd")
+    """One backward through the C ABI (via the C++ extension); returns
+    (dq, dk, dv) in the dtypes of q, k, v."""
+    cos, sin, theta = _rope_args(rope)
+    dq, dk, dv = _capi.ext().tension_bwd(
+        q, k, v, d_out, mode, window, norm, float(scale), _PATH[_path_override], cos, sin,
+        theta, bias, out, mass, d_tau, bool(qk_rotated))
     return dq, dk, dv
 
 

@@ -1,0 +1,207 @@
+"""TensionLM harness (bozo_b200/lm.py) against the reference model.
+
+* CPU: the harness with the oracle in place of the operator reproduces the
+  reference model's aux-loss training forward and gradients
+  (``tests/golden/golden_lm.npz``, made by ``make_golden_lm.py``).
+* GPU: the same with the real operator — fp32 (exact CUDA-core path) and
+  bf16 autocast (tensor-core path for the local layers).
+* CPU, two gloo ranks: one DDP training step equals the single-process step
+  with the two half-batch gradients averaged.
+"""
+import math
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from bozo_b200 import lm
+from oracle import tension_oracle as orc
+from tests.conftest import _load
+
+CFGS = {
+    "rope_global": dict(vocab_size=97, dim=128, num_layers=4, num_heads=2, window=64, ffn_mult=3,
+                        max_seq_len=192, dropout=0.0, use_oscillation=False, use_rope=True,
+                        global_every=2),
+    "norope_osc": dict(vocab_size=97, dim=64, num_layers=2, num_heads=4, window=8, ffn_mult=3,
+                       max_seq_len=48, dropout=0.0, use_oscillation=True, use_rope=False,
+                       global_every=0),
+}
+WEIGHTS = lm.TrainWeights(w_closure=0.01, w_diversity=0.02, w_consistency=0.0, w_entropy=0.0)
+
+
+def oracle_tension(q, k, v, *, window, scale, rope_base=10_000.0, rope_len=None, bias=None,
+                   return_tau=False, normalize="mass", tau_window=None):
+    """The oracle with ``bozo_b200.tension``'s keywords (test-only stand-in)."""
+    out, tau = orc.fused_reference(q, k, v, window=window, scale=scale, rope_base=rope_base,
+                                   bias=bias, normalize=normalize or "none",
+                                   local_window=tau_window or 64, max_seq_len=rope_len)
+    out = out.to(q.dtype)
+    return (out, tau.to(q.dtype)) if return_tau else out
+
+
+@pytest.fixture(scope="module")
+def golden_lm():
+    return _load("golden_lm.npz")
+
+
+def _model(name, case, device):
+    torch.manual_seed(0)
+    m = lm.TensionLM(lm.TensionConfig(**CFGS[name]))
+    sd = {k[3:]: torch.from_numpy(v) for k, v in case.items() if k.startswith("sd.")}
+    missing, unexpected = m.load_state_dict(sd, strict=False)
+    # the reference keeps the same parameters and persistent buffers
+    assert not unexpected, unexpected
+    assert not [k for k in missing if not k.endswith("lm_head.weight")], missing
+    return m.to(device)
+
+
+def _forward_losses(m, case, device, amp=False):
+    inputs = torch.from_numpy(case["inputs"]).to(device)
+    targets = torch.from_numpy(case["targets"]).to(device)
+    V = m.cfg.vocab_size
+    ctx = (torch.autocast(device_type=device.type, dtype=torch.bfloat16) if amp
+           else torch.autocast(device_type=device.type, enabled=False))
+    with ctx:
+        logits, hidden, tensions = m(inputs, return_all=True)
+        ce = torch.nn.functional.cross_entropy(logits.reshape(-1, V), targets.reshape(-1))
+        parts = dict(ce=ce, closure=lm.manifold_closure_loss(hidden),
+                     diversity=lm.tension_diversity_loss(tensions, m.window_groups),
+                     consistency=lm.constraint_consistency_loss(tensions),
+                     entropy=lm.tension_entropy_loss(tensions))
+        loss = (ce + WEIGHTS.w_closure * parts["closure"] + WEIGHTS.w_diversity * parts["diversity"]
+                + WEIGHTS.w_consistency * parts["consistency"] + WEIGHTS.w_entropy * parts["entropy"])
+    loss.backward()
+    return logits, hidden, tensions, parts, loss
+
+
+def _check(m, case, logits, hidden, tensions, parts, loss, rtol, atol, grad_rtol, grad_atol):
+    def close(got, ref, what, rt=rtol, at=atol):
+        g = got.detach().float().cpu().numpy()
+        np.testing.assert_allclose(g, ref, rtol=rt, atol=at, err_msg=what)
+    close(logits, case["logits"], "logits")
+    close(hidden, case["hidden"], "hidden")
+    for i, t in enumerate(tensions):
+        close(t, case[f"tau{i}"], f"tau{i}")
+    for k, v in parts.items():
+        close(v, case[k], k)
+    close(loss, case["loss"], "loss")
+    params = dict(m.named_parameters())
+    for k in case:
+        if k.startswith("grad."):
+            close(params[k[5:]].grad, case[k], k, grad_rtol, grad_atol)
+
+
+@pytest.mark.parametrize("name", list(CFGS))
+def test_harness_matches_reference_model_cpu(golden_lm, name):
+    case = golden_lm[name]
+    m = _model(name, case, torch.device("cpu"))
+    m.set_tension_fn(oracle_tension)
+    out = _forward_losses(m, case, torch.device("cpu"))
+    _check(m, case, *out, rtol=1e-4, atol=1e-5, grad_rtol=1e-3, grad_atol=1e-6)
+
+
+def test_117m_preset_parameter_count():
+    m = lm.TensionLM(lm.preset_117m())
+    assert m.num_params == 117_206_784
+    assert m.window_groups == {64: [0, 1, 2, 4, 5, 6, 8, 9, 10], 1024: [3, 7, 11]}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", list(CFGS))
+def test_harness_matches_reference_model_gpu_fp32(golden_lm, name):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    case = golden_lm[name]
+    m = _model(name, case, torch.device("cuda:0"))
+    out = _forward_losses(m, case, torch.device("cuda:0"))
+    _check(m, case, *out, rtol=1e-4, atol=1e-5, grad_rtol=1e-3, grad_atol=1e-6)
+
+
+@pytest.mark.gpu
+def test_harness_bf16_autocast_tensor_core_path(golden_lm):
+    """bf16 autocast: local layers (HD 64, W 64) take the tcgen05 kernels."""
+    from bozo_b200 import ops
+    case = golden_lm["rope_global"]
+    m = _model("rope_global", case, torch.device("cuda:0"))
+    logits, hidden, tensions, parts, loss = _forward_losses(m, case, torch.device("cuda:0"),
+                                                            amp=True)
+    assert ops.last_path() in ("tcgen05", "simt")
+    ref = case["logits"]
+    g = logits.detach().float().cpu().numpy()
+    # bf16 activations through 4 layers: relative error of the logits ~1e-2
+    assert np.abs(g - ref).max() <= 3e-2 * max(1.0, np.abs(ref).max())
+    assert abs(float(loss) - float(case["loss"])) < 2e-2
+    for i, t in enumerate(tensions):
+        assert np.abs(t.detach().float().cpu().numpy() - case[f"tau{i}"]).max() < 3e-2
+
+
+# ───────────────────────── DDP over gloo (CPU) ─────────────────────────
+
+TINY = dict(vocab_size=53, dim=32, num_layers=2, num_heads=2, window=4, ffn_mult=2,
+            max_seq_len=24, dropout=0.0, use_oscillation=False, use_rope=True, global_every=2)
+
+
+def _tiny_batch():
+    g = torch.Generator().manual_seed(7)
+    ids = torch.randint(0, TINY["vocab_size"], (4, 17), generator=g)
+    return ids[:, :-1], ids[:, 1:]
+
+
+def _ddp_worker(rank, world, port, out_dir):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.manual_seed(0)
+        base = lm.TensionLM(lm.TensionConfig(**TINY))
+        base.set_tension_fn(oracle_tension)
+        model = lm.wrap_ddp(base)
+        opt = lm.make_optimizer(base, fused=False)
+        inputs, targets = _tiny_batch()
+        half = inputs.shape[0] // world
+        sl = slice(rank * half, (rank + 1) * half)
+        lm.train_step(model, base, opt, inputs[sl], targets[sl], weights=WEIGHTS, amp=False)
+        torch.save({k: v.detach().clone() for k, v in base.state_dict().items()},
+                   os.path.join(out_dir, f"rank{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_ddp_step_equals_averaged_half_batch_gradients(tmp_path):
+    world = 2
+    mp.start_processes(_ddp_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    r0 = torch.load(tmp_path / "rank0.pt")
+    r1 = torch.load(tmp_path / "rank1.pt")
+    for k in r0:
+        assert torch.equal(r0[k], r1[k]), f"ranks diverged at {k}"
+
+    # single process: mean of the two half-batch gradients, then clip + AdamW
+    torch.manual_seed(0)
+    base = lm.TensionLM(lm.TensionConfig(**TINY))
+    base.set_tension_fn(oracle_tension)
+    opt = lm.make_optimizer(base, fused=False)
+    inputs, targets = _tiny_batch()
+    V = TINY["vocab_size"]
+    for sl in (slice(0, 2), slice(2, 4)):
+        logits, hidden, tensions = base(inputs[sl], return_all=True)
+        loss = torch.nn.functional.cross_entropy(logits.reshape(-1, V), targets[sl].reshape(-1))
+        loss = (loss + WEIGHTS.w_closure * lm.manifold_closure_loss(hidden)
+                + WEIGHTS.w_diversity * lm.tension_diversity_loss(tensions, base.window_groups)
+                + WEIGHTS.w_consistency * lm.constraint_consistency_loss(tensions)
+                + WEIGHTS.w_entropy * lm.tension_entropy_loss(tensions))
+        (loss / 2).backward()
+    torch.nn.utils.clip_grad_norm_(base.parameters(), 1.0)
+    opt.step()
+    ref = base.state_dict()
+    for k in r0:
+        torch.testing.assert_close(r0[k], ref[k], rtol=1e-5, atol=1e-6, msg=k)
+    assert not math.isnan(float(sum(v.float().sum() for v in r0.values())))
