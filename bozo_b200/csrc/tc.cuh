@@ -11,4 +11,15 @@ cudaError_t launch_tc_fwd(const FwdP& p, cudaStream_t st, int* launches);
 bool tc_bwd_eligible(const BwdP& p);
 cudaError_t launch_tc_bwd(const BwdP& p, cudaStream_t st, int* launches);
 
+// Backward coefficient pre-pass: α/2, α·c, β·c (c = 1/(4·scale)) per query row
+// into three padded planes [B·H, tpad] at coef (tc_bwd.cu).
+cudaError_t launch_alpha_beta(const BwdP& p, int tpad, float ds_scale, float* coef,
+                              cudaStream_t st);
+
+// Global full-causal block (tc_global.cu).
+bool tc_global_fwd_eligible(const FwdP& p);
+cudaError_t launch_tc_global_fwd(const FwdP& p, cudaStream_t st, int* launches);
+bool tc_global_bwd_eligible(const BwdP& p);
+cudaError_t launch_tc_global_bwd(const BwdP& p, cudaStream_t st, int* launches);
+
 }  // namespace bozo

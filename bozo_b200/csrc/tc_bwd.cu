@@ -695,6 +695,16 @@ cudaError_t launch_bwd_variant(const CUtensorMap* m, const BwdTC& a, size_t smem
 
 }  // namespace
 
+cudaError_t launch_alpha_beta(const BwdP& p, int tpad, float ds_scale, float* coef,
+                              cudaStream_t st) {
+  const long long n = (long long)p.B * p.H * tpad;
+  const int g = (int)std::min<long long>(((long long)p.B * p.T * p.H * 8 + 255) / 256,
+                                         (long long)num_sms() * 16);
+  alpha_beta_kernel<<<g, 256, 0, st>>>(p.B, p.T, p.H, p.W, tpad, p.norm, ds_scale, p.row_mass,
+                                       p.dout, p.out, coef, coef + n, coef + 2 * n);
+  return cudaGetLastError();
+}
+
 bool tc_bwd_eligible(const BwdP& p) {
   if (p.mode != BOZO_MODE_LOCAL || p.HD != kHD || p.W < 1 || p.W > 128) return false;
   if (p.dq_dt != BOZO_DT_BF16 || p.dk_dt != BOZO_DT_BF16 || p.dv_dt != BOZO_DT_BF16) return false;
@@ -732,13 +742,7 @@ cudaError_t launch_tc_bwd(const BwdP& p, cudaStream_t st, int* launches) {
   a.coef = p.coef;
   a.err = p.err;
   {  // coefficient pre-pass into the (padded) workspace rows
-    const long long n = (long long)p.B * p.H * a.tpad;
-    const int g = (int)std::min<long long>(((long long)p.B * p.T * p.H * 8 + 255) / 256,
-                                           (long long)num_sms() * 16);
-    alpha_beta_kernel<<<g, 256, 0, st>>>(p.B, p.T, p.H, p.W, a.tpad, p.norm, a.ds_scale,
-                                         p.row_mass, p.dout, p.out, p.coef, p.coef + n,
-                                         p.coef + 2 * n);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_alpha_beta(p, a.tpad, a.ds_scale, p.coef, st);
     if (e != cudaSuccess) return e;
   }
   CUtensorMap m[7];

@@ -1,0 +1,695 @@
+// tc_global.cu — tcgen05 / TMA / TMEM kernels of the GLOBAL full-causal
+// tension block (model.py:217-237) for bf16 Q/K/V with HD = 64 (sm_100a).
+//
+// Semantics: τ[t,s] = σ(q_t·k_s/scale + bias[b,t,s]) for every key s ≤ t
+// (self included), out_t = Σ_s τ·v_s / max(Σ_s τ, 1e-6) (or the raw sum),
+// the reference's exported τ window τ_x[t,c] = τ[t, T−1−c], c < tw
+// (model.py:233-236), and the backward through all of it.  Q and K arrive
+// RoPE-rotated (the forward writes the rotated copies first); the backward
+// inverse-rotates dQ and dK.
+//
+// Three kernels share one pipeline skeleton.  A work unit is one 128-row
+// "outer" tile held in shared memory while 128-row "inner" tiles stream
+// through a TMA ring, each inner tile in two 64-row halves (sub-steps):
+//
+//   role  outer           inner (range)          producers (TMEM)        consumers (TMEM acc)
+//   FWD   Q_j             K_i,V_i   (i ≤ j)      S = Q·K_hᵀ              O  += P·V_h
+//   DKV   K_i,V_i         Q_j,dO_j  (j ≥ i)      Sᵀ = K·Q_hᵀ, dPᵀ=V·dO_hᵀ dV += (ατ)ᵀ·dO_h, dK += dSᵀ·Q_h
+//   DQ    Q_j,dO_j        K_i,V_i   (i ≤ j)      S = Q·K_hᵀ, dP = dO·V_hᵀ dQ += dS·K_h
+//
+// All MMAs are M = 128, N = 64, K = 64 (kind::f16, bf16 in, fp32 accumulate).
+// Producer results are double-buffered in TMEM, the epilogue's bf16 tiles
+// double-buffered in shared memory, and the accumulators double-buffered in
+// TMEM per unit, so the MMA of sub-step n+1 overlaps the epilogue of n and a
+// unit's output overlaps the next unit.  dQ is computed per query tile by its
+// own kernel (recomputing S and dP) so no partial sums leave an SM and no
+// atomics are needed.  Units are dealt to persistent CTAs heaviest first.
+//
+// Warps: 0 TMA; 1 MMA (one thread); 2,3,12,13 output (TMEM accumulators →
+// bf16 tile in the dead outer slot → TMA store); 4-11 epilogue.  Every
+// mbarrier wait is bounded (tc_ptx.cuh).
+#include <algorithm>
+
+#include "tc.cuh"
+#include "tc_host.cuh"
+#include "tc_ptx.cuh"
+
+namespace bozo {
+namespace {
+
+using namespace tc;
+
+constexpr int kTile = kTcTile;
+constexpr int kHD = kTcHD;
+constexpr int kTileBytes = kTile * kHD * 2;  // 16 KiB: [128 x 64] bf16, SW128
+constexpr int kCoefBytes = 3 * kTile * 4;   // α/2, α·c, β·c of 128 query rows
+constexpr int kThreads = 14 * 32;
+constexpr int kErrG = 0x300;
+
+enum Role : int { kFwd = 0, kDKV = 1, kDQ = 2 };
+
+template <int R>
+struct Traits {
+  static constexpr int kOuterTiles = R == kFwd ? 1 : 2;
+  static constexpr bool kOuterCoef = R == kDQ;
+  static constexpr bool kInnerCoef = R == kDKV;
+  static constexpr int kInnerStages = R == kDKV ? 2 : 3;
+  static constexpr int kEpiTiles = R == kDKV ? 2 : 1;  // bf16 tiles per sub-step
+  static constexpr int kAccCols = R == kDKV ? 128 : 64;
+};
+
+struct GlobTC {
+  int B, T, H, BH, nT, units, tpad, tw;
+  float half_inv_scale, ds_scale;
+  int norm;
+  const float* theta;  // RoPE frequencies [32] (inverse rotation of dQ/dK) or null
+  const float* bias;   // [B,T,T]
+  long long bs0, bs1, bs2;
+  __nv_bfloat16* tau;         // FWD: exported window [B,T,H,tw], zero-filled before
+  const __nv_bfloat16* dtau;  // DKV/DQ: its cotangent
+  float* row_mass;            // FWD: [B,H,T]
+  const float* coef;          // DKV/DQ: [3][B·H, tpad]
+  int* err;
+};
+
+struct __align__(8) GBars {
+  uint64_t outer_full[2], outer_empty[2];
+  uint64_t inner_full[3], inner_empty[3];
+  uint64_t s_full[2], s_free[2], p_full[2], p_free[2];
+  uint64_t acc_full[2], acc_free[2];
+  uint64_t mass_ready[2], staged;
+  uint32_t tmem_base;
+};
+
+struct GLayout {
+  uint32_t outer, ocoef, inner, icoef, epi, mass, bars, total;
+};
+
+template <int R>
+__host__ __device__ inline GLayout glayout() {
+  using Tr = Traits<R>;
+  GLayout L;
+  L.outer = 0;
+  L.ocoef = L.outer + 2 * Tr::kOuterTiles * kTileBytes;
+  L.inner = L.ocoef + (Tr::kOuterCoef ? 2 * kCoefBytes : 0);
+  L.inner = (L.inner + 1023) & ~1023u;
+  L.icoef = L.inner + Tr::kInnerStages * 2 * kTileBytes;
+  L.epi = L.icoef + (Tr::kInnerCoef ? Tr::kInnerStages * kCoefBytes : 0);
+  L.epi = (L.epi + 1023) & ~1023u;
+  L.mass = L.epi + 2 * Tr::kEpiTiles * kTileBytes;
+  L.bars = L.mass + (R == kFwd ? 2 * 2 * kTile * 4 : 0);
+  L.total = L.bars + (uint32_t)sizeof(GBars);
+  return L;
+}
+
+// Work unit k (heaviest first): FWD/DQ outer query tile j has j+1 key tiles,
+// DKV outer key tile i has nT−i query tiles.
+__device__ __forceinline__ void unit_of(int role, int k, int BH, int nT, int& bh, int& ot,
+                                        int& first_inner, int& n_inner) {
+  const int g = k / BH;
+  bh = k % BH;
+  if (role == kDKV) {
+    ot = g;
+    first_inner = g;
+    n_inner = nT - g;
+  } else {
+    ot = nT - 1 - g;
+    first_inner = 0;
+    n_inner = ot + 1;
+  }
+}
+
+template <int R, bool kBias, bool kExtra>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_global_kernel(const __grid_constant__ CUtensorMap tmo0, const __grid_constant__ CUtensorMap tmo1,
+                     const __grid_constant__ CUtensorMap tmi0, const __grid_constant__ CUtensorMap tmi1,
+                     const __grid_constant__ CUtensorMap tmout0, const __grid_constant__ CUtensorMap tmout1,
+                     const GlobTC p) {
+  using Tr = Traits<R>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const GLayout L = glayout<R>();
+  uint8_t* sOuter = smem + L.outer;  // [slot][tile] 16 KiB each
+  float* sOCoef = reinterpret_cast<float*>(smem + L.ocoef);
+  uint8_t* sInner = smem + L.inner;  // [stage][2 tiles]
+  float* sICoef = reinterpret_cast<float*>(smem + L.icoef);
+  uint8_t* sEpi = smem + L.epi;      // [buffer][tile]
+  float* sMass = reinterpret_cast<float*>(smem + L.mass);
+  GBars* bar = reinterpret_cast<GBars*>(smem + L.bars);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const int H = p.H, T = p.T, nT = p.nT, BH = p.BH;
+  constexpr int kStages = Tr::kInnerStages;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->outer_full[s], 1);
+      mbar_init(&bar->outer_empty[s], 1);
+      mbar_init(&bar->s_full[s], 1);
+      mbar_init(&bar->s_free[s], 8);
+      mbar_init(&bar->p_full[s], 8);
+      mbar_init(&bar->p_free[s], 1);
+      mbar_init(&bar->acc_full[s], 1);
+      mbar_init(&bar->acc_free[s], 4);
+      mbar_init(&bar->mass_ready[s], 8);
+    }
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bar->inner_full[s], 1);
+      mbar_init(&bar->inner_empty[s], 1);
+    }
+    mbar_init(&bar->staged, 4);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&bar->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bar->tmem_base;
+  int* err = p.err;
+
+  if (warp == 0) {
+    // ─────────────────────────── TMA producer ───────────────────────────
+    if (lane == 0) {
+      prefetch_tmap(&tmo0); prefetch_tmap(&tmi0); prefetch_tmap(&tmi1); prefetch_tmap(&tmout0);
+      if (Tr::kOuterTiles == 2) prefetch_tmap(&tmo1);
+      if (R == kDKV) prefetch_tmap(&tmout1);
+      const long long plane = (long long)BH * p.tpad;
+      bool ok = true;
+      int ni = 0;
+      for (int k = blockIdx.x, m = 0; k < p.units && ok; k += G, ++m) {
+        int bh, ot, fi, nin;
+        unit_of(R, k, BH, nT, bh, ot, fi, nin);
+        const int b = bh / H, h = bh % H;
+        const int os = m & 1;
+        if (m >= 2) ok = mbar_wait(&bar->outer_empty[os], ((m >> 1) - 1) & 1, err, kErrG | 1);
+        if (!ok) break;
+        uint8_t* o = sOuter + os * Tr::kOuterTiles * kTileBytes;
+        mbar_arrive_expect_tx(&bar->outer_full[os],
+                              Tr::kOuterTiles * kTileBytes + (Tr::kOuterCoef ? kCoefBytes : 0));
+        tma_load_4d(o, &tmo0, &bar->outer_full[os], 0, h, ot * kTile, b);
+        if (Tr::kOuterTiles == 2) tma_load_4d(o + kTileBytes, &tmo1, &bar->outer_full[os], 0, h, ot * kTile, b);
+        if (Tr::kOuterCoef) {
+          const long long off = (long long)bh * p.tpad + ot * kTile;
+#pragma unroll
+          for (int z = 0; z < 3; ++z)
+            bulk_load_1d(sOCoef + (os * 3 + z) * kTile, p.coef + z * plane + off, kTile * 4,
+                         &bar->outer_full[os]);
+        }
+        for (int x = 0; x < nin && ok; ++x) {
+          const int it = fi + x;
+          const int st = ni % kStages;
+          if (ni >= kStages) ok = mbar_wait(&bar->inner_empty[st], ((ni / kStages) - 1) & 1, err, kErrG | 2);
+          if (!ok) break;
+          uint8_t* in = sInner + st * 2 * kTileBytes;
+          mbar_arrive_expect_tx(&bar->inner_full[st], 2 * kTileBytes + (Tr::kInnerCoef ? kCoefBytes : 0));
+          tma_load_4d(in, &tmi0, &bar->inner_full[st], 0, h, it * kTile, b);
+          tma_load_4d(in + kTileBytes, &tmi1, &bar->inner_full[st], 0, h, it * kTile, b);
+          if (Tr::kInnerCoef) {
+            const long long off = (long long)bh * p.tpad + it * kTile;
+#pragma unroll
+            for (int z = 0; z < 3; ++z)
+              bulk_load_1d(sICoef + (st * 3 + z) * kTile, p.coef + z * plane + off, kTile * 4,
+                           &bar->inner_full[st]);
+          }
+          ++ni;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ─────────────────────────── MMA issuer ───────────────────────────
+    if (lane == 0) {
+      const uint32_t id_p = idesc_bf16(128, 64, false, false);    // producers: A, B K-major
+      const uint32_t id_c = idesc_bf16(128, kHD, false, true);    // consumers: B MN-major
+      constexpr uint64_t kTD = kTileBytes >> 4;                   // one tile, 16 B units
+      const uint64_t dOuter = sdesc_sw128(smem_u32(sOuter), 16, 1024);
+      const uint64_t dInner = sdesc_sw128(smem_u32(sInner), 16, 1024);
+      const uint64_t dEpi = sdesc_sw128(smem_u32(sEpi), 16, 1024);
+      bool ok = true;
+      int n = 0, ni = 0;
+      // the previous sub-step, whose consumers are still to be issued
+      bool have_prev = false;
+      int pn = 0, pm = 0, pst = 0, phh = 0;
+      bool pfirst = false, plast = false;
+
+      auto consumers = [&](int cn, int cm, int cst, int chh, bool cfirst, bool clast) {
+        const int b = cn & 1, ub = cm & 1;
+        ok = ok && mbar_wait(&bar->p_full[b], (cn >> 1) & 1, err, kErrG | 3);
+        if (ok && cfirst && cm >= 2) ok = mbar_wait(&bar->acc_free[ub], ((cm >> 1) - 1) & 1, err, kErrG | 4);
+        if (!ok) return;
+        tc_fence_after();
+        const uint64_t in0 = dInner + (uint64_t)(cst * 2) * kTD;   // K / Q / K
+        const uint64_t in1 = in0 + kTD;                             // V / dO / V
+        const uint64_t e0 = dEpi + (uint64_t)(b * Tr::kEpiTiles) * kTD;
+        const uint32_t acc_col = tbase + 256 + ub * Tr::kAccCols;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t rows = (uint64_t)(64 * chh + 16 * kk) * 8;  // 16 B units
+          const uint32_t acc = (cfirst && kk == 0) ? 0u : 1u;
+          if (R == kFwd) {
+            mma_bf16(acc_col, e0 + 2 * kk, in1 + rows, id_c, acc);            // O += P·V
+          } else if (R == kDKV) {
+            mma_bf16(acc_col + 64, e0 + 2 * kk, in1 + rows, id_c, acc);       // dV += (ατ)ᵀ·dO
+            mma_bf16(acc_col, e0 + kTD + 2 * kk, in0 + rows, id_c, acc);      // dK += dSᵀ·Q
+          } else {
+            mma_bf16(acc_col, e0 + 2 * kk, in0 + rows, id_c, acc);            // dQ += dS·K
+          }
+        }
+        mma_commit(&bar->p_free[b]);
+        if (chh == 1) mma_commit(&bar->inner_empty[cst]);
+        if (clast) mma_commit(&bar->acc_full[ub]);
+      };
+
+      for (int k = blockIdx.x, m = 0; k < p.units && ok; k += G, ++m) {
+        int bh, ot, fi, nin;
+        unit_of(R, k, BH, nT, bh, ot, fi, nin);
+        const int os = m & 1;
+        ok = mbar_wait(&bar->outer_full[os], (m >> 1) & 1, err, kErrG | 5);
+        const uint64_t o0 = dOuter + (uint64_t)(os * Tr::kOuterTiles) * kTD;
+        const uint64_t o1 = o0 + kTD;
+        for (int x = 0; x < nin && ok; ++x) {
+          const int st = ni % kStages;
+          ok = mbar_wait(&bar->inner_full[st], (ni / kStages) & 1, err, kErrG | 6);
+          const uint64_t in0 = dInner + (uint64_t)(st * 2) * kTD;
+          const uint64_t in1 = in0 + kTD;
+          for (int hh = 0; hh < 2 && ok; ++hh) {
+            const int b = n & 1;
+            if (n >= 2) ok = mbar_wait(&bar->s_free[b], ((n >> 1) - 1) & 1, err, kErrG | 7);
+            if (!ok) break;
+            tc_fence_after();
+            const uint64_t half = (uint64_t)(64 * hh) * 8;
+            const uint32_t sc = tbase + 128 * b;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              if (R == kFwd) {
+                mma_bf16(sc, o0 + 2 * kk, in0 + half + 2 * kk, id_p, kk > 0);        // S = Q·Kᵀ
+              } else if (R == kDKV) {
+                mma_bf16(sc, o0 + 2 * kk, in0 + half + 2 * kk, id_p, kk > 0);        // Sᵀ = K·Qᵀ
+                mma_bf16(sc + 64, o1 + 2 * kk, in1 + half + 2 * kk, id_p, kk > 0);   // dPᵀ = V·dOᵀ
+              } else {
+                mma_bf16(sc, o0 + 2 * kk, in0 + half + 2 * kk, id_p, kk > 0);        // S = Q·Kᵀ
+                mma_bf16(sc + 64, o1 + 2 * kk, in1 + half + 2 * kk, id_p, kk > 0);   // dP = dO·Vᵀ
+              }
+            }
+            mma_commit(&bar->s_full[b]);
+            if (have_prev) consumers(pn, pm, pst, phh, pfirst, plast);
+            have_prev = true;
+            pn = n; pm = m; pst = st; phh = hh;
+            pfirst = (x == 0 && hh == 0);
+            plast = (x == nin - 1 && hh == 1);
+            ++n;
+          }
+          ++ni;
+        }
+      }
+      if (ok && have_prev) consumers(pn, pm, pst, phh, pfirst, plast);
+    }
+  } else if (warp < 4 || warp >= 12) {
+    // ─────────── output warps: accumulators → bf16 → TMA store ───────────
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;  // TMEM lane = tile row
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    float th[32];
+#pragma unroll
+    for (int z = 0; z < 32; ++z) th[z] = p.theta ? __ldg(p.theta + z) : 0.f;
+    bool ok = true;
+    for (int k = blockIdx.x, m = 0; k < p.units && ok; k += G, ++m) {
+      int bh, ot, fi, nin;
+      unit_of(R, k, BH, nT, bh, ot, fi, nin);
+      const int b = bh / H, h = bh % H;
+      const int ub = m & 1, os = m & 1;
+      ok = mbar_wait(&bar->acc_full[ub], (m >> 1) & 1, err, kErrG | 8);
+      if (R == kFwd && ok) ok = mbar_wait(&bar->mass_ready[ub], (m >> 1) & 1, err, kErrG | 9);
+      if (!ok) break;
+      __syncwarp();
+      tc_fence_after();
+      const int pos = ot * kTile + r;
+      const uint32_t acc = tbase + lane_off + 256 + ub * Tr::kAccCols;
+      uint8_t* o = sOuter + os * Tr::kOuterTiles * kTileBytes;  // dead outer slot
+      const uint32_t st0 = smem_u32(o);
+      if (R == kFwd) {
+        uint32_t g[64];
+        tmem_ld32_wait(acc, g);
+        tmem_ld32_wait(acc + 32, g + 32);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->acc_free[ub]);
+        const float mass = sMass[(ub * 2 + 0) * kTile + r] + sMass[(ub * 2 + 1) * kTile + r];
+        const float inv = p.norm == BOZO_NORM_MASS ? 1.f / fmaxf(mass, kMassEps) : 1.f;
+#pragma unroll
+        for (int z = 0; z < 8; ++z) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int y = 0; y < 4; ++y)
+            w4[y] = pack_bf16(__uint_as_float(g[8 * z + 2 * y]) * inv,
+                              __uint_as_float(g[8 * z + 2 * y + 1]) * inv);
+          st_shared_v4(st0 + sw128_off(r, z), w4[0], w4[1], w4[2], w4[3]);
+        }
+        if (p.row_mass && pos < T) p.row_mass[(long long)bh * T + pos] = mass;
+      } else {
+        // dK (DKV) / dQ (DQ): inverse RoPE at this row's position
+        // dK (DKV) / dQ (DQ) in the accumulator's first 64 columns; frequency
+        // group c8 pairs columns [8c8, 8c8+8) with [32+8c8, 32+8c8+8)
+#pragma unroll
+        for (int c8 = 0; c8 < 4; c8 += 2) {
+          uint32_t g[32];
+          tmem_ld8x4_wait(acc + 8 * c8, acc + 32 + 8 * c8, acc + 8 * c8 + 8, acc + 40 + 8 * c8, g);
+#pragma unroll
+          for (int hg = 0; hg < 2; ++hg) {
+            const int grp = c8 + hg;
+            float o8[16];
+#pragma unroll
+            for (int z = 0; z < 8; ++z) {
+              float cs = 1.f, sn = 0.f;
+              if (p.theta && pos < T) rope_cs(pos, th[grp * 8 + z], cs, sn);
+              const float x1 = __uint_as_float(g[16 * hg + z]);
+              const float x2 = __uint_as_float(g[16 * hg + 8 + z]);
+              o8[z] = x1 * cs + x2 * sn;
+              o8[8 + z] = x2 * cs - x1 * sn;
+            }
+            st_shared_v4(st0 + sw128_off(r, grp), pack_bf16(o8[0], o8[1]), pack_bf16(o8[2], o8[3]),
+                         pack_bf16(o8[4], o8[5]), pack_bf16(o8[6], o8[7]));
+            st_shared_v4(st0 + sw128_off(r, 4 + grp), pack_bf16(o8[8], o8[9]),
+                         pack_bf16(o8[10], o8[11]), pack_bf16(o8[12], o8[13]),
+                         pack_bf16(o8[14], o8[15]));
+          }
+        }
+        if (R == kDKV) {
+          uint32_t g[64];
+          tmem_ld32_wait(acc + 64, g);
+          tmem_ld32_wait(acc + 96, g + 32);
+          const uint32_t st1 = st0 + kTileBytes;
+#pragma unroll
+          for (int z = 0; z < 8; ++z) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int y = 0; y < 4; ++y)
+              w4[y] = pack_bf16(__uint_as_float(g[8 * z + 2 * y]), __uint_as_float(g[8 * z + 2 * y + 1]));
+            st_shared_v4(st1 + sw128_off(r, z), w4[0], w4[1], w4[2], w4[3]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->acc_free[ub]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->staged);
+      if (warp == 2 && lane == 0) {
+        ok = mbar_wait(&bar->staged, m & 1, err, kErrG | 10);
+        if (ok) {
+          tma_store_4d(&tmout0, o, 0, h, ot * kTile, b);
+          if (R == kDKV) tma_store_4d(&tmout1, o + kTileBytes, 0, h, ot * kTile, b);
+          bulk_commit_group();
+          bulk_wait_group_read0();
+          mbar_arrive(&bar->outer_empty[os]);  // the TMA may refill this outer slot
+        }
+      }
+      __syncwarp();
+    }
+    if (warp == 2 && lane == 0) bulk_wait_group0();
+  } else {
+    // ─────────────────────────── epilogue (8 warps) ───────────────────────────
+    const int e = warp - 4;
+    const int qd = warp & 3;
+    const int hf = e >> 2;  // which 32 of the sub-step's 64 inner columns
+    const int r = qd * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
+    const uint32_t epi = smem_u32(sEpi);
+    bool ok = true;
+    int n = 0, ni = 0;
+    for (int k = blockIdx.x, m = 0; k < p.units && ok; k += G, ++m) {
+      int bh, ot, fi, nin;
+      unit_of(R, k, BH, nT, bh, ot, fi, nin);
+      const int b = bh / H, h = bh % H;
+      const int os = m & 1;
+      const int orow = ot * kTile + r;  // this thread's outer position
+      float mass = 0.f;
+      float row_ad = 0.f, row_bd = 0.f;
+      if (R == kDQ) {
+        ok = mbar_wait(&bar->outer_full[os], (m >> 1) & 1, err, kErrG | 11);
+        if (!ok) break;
+        row_ad = sOCoef[(os * 3 + 1) * kTile + r];
+        row_bd = sOCoef[(os * 3 + 2) * kTile + r];
+      }
+      for (int x = 0; x < nin && ok; ++x) {
+        const int it = fi + x;
+        const int st = ni % kStages;
+        if (R == kDKV) {
+          ok = mbar_wait(&bar->inner_full[st], (ni / kStages) & 1, err, kErrG | 12);
+          if (!ok) break;
+        }
+        const float* cf = sICoef + st * 3 * kTile;
+        for (int hh = 0; hh < 2 && ok; ++hh) {
+          const int bb = n & 1;
+          ok = mbar_wait(&bar->s_full[bb], (n >> 1) & 1, err, kErrG | 13);
+          if (!ok) break;
+          __syncwarp();
+          tc_fence_after();
+          uint32_t pk[2][8], dk[2][8];
+#pragma unroll
+          for (int ss = 0; ss < 2; ++ss) {
+            const int c0 = 64 * hh + 32 * hf + 16 * ss;  // first inner row (within tile) of the piece
+            const int ipos0 = it * kTile + c0;          // its position
+            // query / key positions of (row, column e): FWD/DQ row = query, DKV row = key
+            uint32_t Rg[32];
+            const uint32_t col = tbase + lane_off + 128 * bb + 32 * hf + 16 * ss;
+            if (R == kFwd) {
+              tmem_ld16_wait(col, Rg);
+            } else {
+              tmem_ld16x2_wait(col, col + 64, Rg);
+            }
+#pragma unroll
+            for (int e4 = 0; e4 < 16; e4 += 2) {
+              float pv[2], dv[2];
+#pragma unroll
+              for (int z = 0; z < 2; ++z) {
+                const int ee = e4 + z;
+                const int ipos = ipos0 + ee;
+                const int tq = (R == kDKV) ? ipos : orow;  // query position
+                const int sk = (R == kDKV) ? orow : ipos;  // key position
+                const bool valid = tq < T && sk <= tq;
+                float x = __uint_as_float(Rg[ee]) * p.half_inv_scale;
+                if constexpr (kBias) {
+                  const int tqc = min(tq, T - 1), skc = min(sk, T - 1);
+                  x = fmaf(0.5f, __ldg(p.bias + b * p.bs0 + (long long)tqc * p.bs1 + (long long)skc * p.bs2), x);
+                }
+                const float thv = tanh_approx(x);
+                if (R == kFwd) {
+                  const float tau = valid ? fmaf(0.5f, thv, 0.5f) : 0.f;
+                  mass += tau;
+                  pv[z] = tau;
+                  if constexpr (kExtra) {
+                    if (valid && sk >= T - p.tw)
+                      p.tau[((long long)(b * T + tq) * H + h) * p.tw + (T - 1 - sk)] = __float2bfloat16_rn(tau);
+                  }
+                } else {
+                  float ad, bd, ah = 0.f;
+                  if (R == kDKV) {
+                    const int qi = c0 + ee;  // query row within the inner tile
+                    ah = cf[qi];
+                    ad = cf[kTile + qi];
+                    bd = cf[2 * kTile + qi];
+                  } else {
+                    ad = row_ad;
+                    bd = row_bd;
+                  }
+                  float dt = fmaf(ad, __uint_as_float(Rg[16 + ee]), bd);
+                  if constexpr (kExtra) {
+                    if (valid && sk >= T - p.tw)
+                      dt = fmaf(__bfloat162float(p.dtau[((long long)(b * T + tq) * H + h) * p.tw + (T - 1 - sk)]),
+                                p.ds_scale, dt);
+                  }
+                  dv[z] = valid ? dt * fmaf(-thv, thv, 1.f) : 0.f;
+                  if (R == kDKV) pv[z] = valid ? fmaf(ah, thv, ah) : 0.f;
+                }
+              }
+              if (R == kFwd || R == kDKV) pk[ss][e4 >> 1] = pack_bf16(pv[0], pv[1]);
+              if (R != kFwd) dk[ss][e4 >> 1] = pack_bf16(dv[0], dv[1]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar->s_free[bb]);
+          if (n >= 2) ok = mbar_wait(&bar->p_free[bb], ((n >> 1) - 1) & 1, err, kErrG | 14);
+          if (!ok) break;
+          const uint32_t t0 = epi + (bb * Tr::kEpiTiles) * kTileBytes;
+#pragma unroll
+          for (int ss = 0; ss < 2; ++ss) {
+            const int c16 = (32 * hf + 16 * ss) >> 3;
+            if (R == kFwd || R == kDKV) {
+              st_shared_v4(t0 + sw128_off(r, c16), pk[ss][0], pk[ss][1], pk[ss][2], pk[ss][3]);
+              st_shared_v4(t0 + sw128_off(r, c16 + 1), pk[ss][4], pk[ss][5], pk[ss][6], pk[ss][7]);
+            }
+            if (R != kFwd) {
+              const uint32_t td = (R == kDKV) ? t0 + kTileBytes : t0;
+              st_shared_v4(td + sw128_off(r, c16), dk[ss][0], dk[ss][1], dk[ss][2], dk[ss][3]);
+              st_shared_v4(td + sw128_off(r, c16 + 1), dk[ss][4], dk[ss][5], dk[ss][6], dk[ss][7]);
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar->p_full[bb]);
+          ++n;
+        }
+        ++ni;
+      }
+      if (R == kFwd && ok) {
+        // the output warps wait for both halves' τ-mass of every row
+        const int ub = m & 1;
+        if (m >= 2) ok = mbar_wait(&bar->acc_free[ub], ((m >> 1) - 1) & 1, err, kErrG | 15);
+        if (!ok) break;
+        sMass[(ub * 2 + hf) * kTile + r] = mass;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->mass_ready[ub]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+template <int R, bool kBias, bool kExtra>
+cudaError_t launch_g(const CUtensorMap* m, const GlobTC& a, cudaStream_t st) {
+  auto kern = tc_global_kernel<R, kBias, kExtra>;
+  const size_t smem = glayout<R>().total + 1024;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int grid = std::min(num_sms(), a.units);
+  kern<<<grid, kThreads, smem, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], a);
+  return cudaGetLastError();
+}
+
+template <int R>
+cudaError_t launch_role(const CUtensorMap* m, const GlobTC& a, bool bias, bool extra, cudaStream_t st) {
+  if (bias && extra) return launch_g<R, true, true>(m, a, st);
+  if (bias) return launch_g<R, true, false>(m, a, st);
+  if (extra) return launch_g<R, false, true>(m, a, st);
+  return launch_g<R, false, false>(m, a, st);
+}
+
+bool out_ok(const void* ptr) { return ptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
+
+}  // namespace
+
+bool tc_global_fwd_eligible(const FwdP& p) {
+  if (p.mode != BOZO_MODE_GLOBAL || p.HD != kHD) return false;
+  if (p.norm != BOZO_NORM_MASS && p.norm != BOZO_NORM_NONE) return false;
+  if (p.out_dt != BOZO_DT_BF16 || !out_ok(p.out)) return false;
+  if (p.tau && p.tau_dt != BOZO_DT_BF16) return false;
+  if (!tma_view_ok(p.q, p.B, p.T, p.H) || !tma_view_ok(p.k, p.B, p.T, p.H) ||
+      !tma_view_ok(p.v, p.B, p.T, p.H))
+    return false;
+  // RoPE: the kernel reads the rotated copies, which the caller must request
+  if (p.cos && (!out_ok(p.q_rot) || !out_ok(p.k_rot))) return false;
+  return tmap_encoder_available();
+}
+
+cudaError_t launch_tc_global_fwd(const FwdP& p, cudaStream_t st, int* launches) {
+  *launches = 0;
+  GlobTC a{};
+  a.B = p.B; a.T = p.T; a.H = p.H; a.BH = p.B * p.H;
+  a.nT = (p.T + kTile - 1) / kTile;
+  a.units = a.BH * a.nT;
+  a.tw = p.tau ? p.W : 0;
+  a.half_inv_scale = 0.5f / p.scale;
+  a.norm = p.norm;
+  a.bias = p.bias; a.bs0 = p.bs0; a.bs1 = p.bs1; a.bs2 = p.bs2;
+  a.tau = static_cast<__nv_bfloat16*>(p.tau);
+  a.row_mass = p.row_mass;
+  a.err = p.err;
+  cudaError_t e;
+  const long long ob = (long long)p.T * p.H * kHD, ot = (long long)p.H * kHD, oh = kHD;
+  const void* qp = p.q.p;
+  const void* kp = p.k.p;
+  long long qs[3] = {p.q.sb, p.q.st, p.q.sh}, ks[3] = {p.k.sb, p.k.st, p.k.sh};
+  if (p.cos) {
+    if ((e = launch_rope_copy(p, st, launches)) != cudaSuccess) return e;
+    qp = p.q_rot;
+    kp = p.k_rot;
+    qs[0] = ks[0] = ob; qs[1] = ks[1] = ot; qs[2] = ks[2] = oh;
+  }
+  if (p.tau) {
+    e = cudaMemsetAsync(p.tau, 0, (size_t)p.B * p.T * p.H * p.W * sizeof(__nv_bfloat16), st);
+    if (e != cudaSuccess) return e;
+  }
+  CUtensorMap m[6];
+  if (!make_tmap_bthd(&m[0], qp, qs[0], qs[1], qs[2], p.B, p.T, p.H, kTile) ||
+      !make_tmap_bthd(&m[2], kp, ks[0], ks[1], ks[2], p.B, p.T, p.H, kTile) ||
+      !make_tmap_bthd(&m[3], p.v.p, p.v.sb, p.v.st, p.v.sh, p.B, p.T, p.H, kTile) ||
+      !make_tmap_bthd(&m[4], p.out, ob, ot, oh, p.B, p.T, p.H, kTile))
+    return cudaErrorInvalidValue;
+  m[1] = m[0];
+  m[5] = m[4];
+  *launches += 1;
+  return launch_role<kFwd>(m, a, p.bias != nullptr, p.tau != nullptr, st);
+}
+
+bool tc_global_bwd_eligible(const BwdP& p) {
+  if (p.mode != BOZO_MODE_GLOBAL || p.HD != kHD) return false;
+  if (p.norm != BOZO_NORM_MASS && p.norm != BOZO_NORM_NONE) return false;
+  if (p.dq_dt != BOZO_DT_BF16 || p.dk_dt != BOZO_DT_BF16 || p.dv_dt != BOZO_DT_BF16) return false;
+  if (!tma_view_ok(p.q, p.B, p.T, p.H) || !tma_view_ok(p.k, p.B, p.T, p.H) ||
+      !tma_view_ok(p.v, p.B, p.T, p.H) || !tma_view_ok(p.dout, p.B, p.T, p.H))
+    return false;
+  if (p.norm == BOZO_NORM_MASS) {
+    if (p.out.dt != BOZO_DT_BF16 || p.out.sd != 1 || (reinterpret_cast<uintptr_t>(p.out.p) & 15) ||
+        (p.out.sb % 8) || (p.out.st % 8) || (p.out.sh % 8))
+      return false;
+  }
+  if (p.dtau && p.dtau_dt != BOZO_DT_BF16) return false;
+  if (!out_ok(p.dq) || !out_ok(p.dk) || !out_ok(p.dv)) return false;
+  if (p.cos && (!p.theta || !p.qk_rotated)) return false;
+  if (!out_ok(p.coef)) return false;
+  return tmap_encoder_available();
+}
+
+cudaError_t launch_tc_global_bwd(const BwdP& p, cudaStream_t st, int* launches) {
+  GlobTC a{};
+  a.B = p.B; a.T = p.T; a.H = p.H; a.BH = p.B * p.H;
+  a.nT = (p.T + kTile - 1) / kTile;
+  a.units = a.BH * a.nT;
+  a.tpad = a.nT * kTile;
+  a.tw = p.dtau ? p.W : 0;
+  a.half_inv_scale = 0.5f / p.scale;
+  a.ds_scale = 0.25f / p.scale;
+  a.norm = p.norm;
+  a.theta = p.cos ? p.theta : nullptr;
+  a.bias = p.bias; a.bs0 = p.bs0; a.bs1 = p.bs1; a.bs2 = p.bs2;
+  a.dtau = static_cast<const __nv_bfloat16*>(p.dtau);
+  a.coef = p.coef;
+  a.err = p.err;
+  cudaError_t e = launch_alpha_beta(p, a.tpad, a.ds_scale, p.coef, st);
+  if (e != cudaSuccess) return e;
+  CUtensorMap mq, mk, mv, mdo, mdq, mdk, mdv;
+  const long long ob = (long long)p.T * p.H * kHD, ot = (long long)p.H * kHD, oh = kHD;
+  if (!make_tmap_bthd(&mq, p.q.p, p.q.sb, p.q.st, p.q.sh, p.B, p.T, p.H, kTile) ||
+      !make_tmap_bthd(&mk, p.k.p, p.k.sb, p.k.st, p.k.sh, p.B, p.T, p.H, kTile) ||
+      !make_tmap_bthd(&mv, p.v.p, p.v.sb, p.v.st, p.v.sh, p.B, p.T, p.H, kTile) ||
+      !make_tmap_bthd(&mdo, p.dout.p, p.dout.sb, p.dout.st, p.dout.sh, p.B, p.T, p.H, kTile) ||
+      !make_tmap_bthd(&mdq, p.dq, ob, ot, oh, p.B, p.T, p.H, kTile) ||
+      !make_tmap_bthd(&mdk, p.dk, ob, ot, oh, p.B, p.T, p.H, kTile) ||
+      !make_tmap_bthd(&mdv, p.dv, ob, ot, oh, p.B, p.T, p.H, kTile))
+    return cudaErrorInvalidValue;
+  const bool bias = p.bias != nullptr, dt = p.dtau != nullptr;
+  {
+    const CUtensorMap m[6] = {mk, mv, mq, mdo, mdk, mdv};
+    if ((e = launch_role<kDKV>(m, a, bias, dt, st)) != cudaSuccess) return e;
+  }
+  {
+    const CUtensorMap m[6] = {mq, mdo, mk, mv, mdq, mdq};
+    if ((e = launch_role<kDQ>(m, a, bias, dt, st)) != cudaSuccess) return e;
+  }
+  *launches = 3;
+  return cudaSuccess;
+}
+
+}  // namespace bozo

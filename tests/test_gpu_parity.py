@@ -205,6 +205,66 @@ def test_fused_local_bf16_vs_oracle(bz, W, normalize):
         assert_close(g, r, dt, f"W{W}/{normalize}/{what}")
 
 
+def _global_reference(q, k, v, scale, bias, tw, normalize):
+    """RoPE + the global block (model.py:200-204, 217-237) in float64; raw
+    Σ τ·V when ``normalize`` is None."""
+    def fn(q_, k_, v_):
+        T, HD = q_.shape[1], q_.shape[3]
+        cos, sin = orc.rope_tables(HD, T, 10_000.0, torch.float64)
+        out, tau_full, tau_local = orc.global_tension(orc.rope(q_, cos, sin), orc.rope(k_, cos, sin),
+                                                      v_, scale, bias, tw)
+        if normalize is None:
+            out = torch.einsum("bths,bshd->bthd", tau_full, v_)
+        return out, tau_local
+    return fn
+
+
+@cuda
+@pytest.mark.parametrize("T", [1, 100, 128, 300])
+@pytest.mark.parametrize("normalize", ["mass", None])
+def test_fused_global_bf16_vs_oracle(bz, T, normalize):
+    """Global full-causal block on the tensor-core path (bf16, HD 64): RoPE,
+    bias [B,T,T], the exported τ window and its cotangent, ragged T."""
+    torch.manual_seed(200 + T)
+    B, H, HD, tw = 2, 2, 64, min(64, T)
+    dt = torch.bfloat16
+    q, k, v, d_out = [torch.randn(B, T, H, HD, dtype=dt) for _ in range(4)]
+    bias = torch.randn(B, T, T) * 0.5
+    d_tau = (torch.randn(B, T, H, tw) * 0.1).to(dt)
+    qg, kg, vg = [x.cuda().requires_grad_(True) for x in (q, k, v)]
+    out, tau = bz.tension(qg, kg, vg, window=None, bias=bias.cuda(), return_tau=True,
+                          normalize=normalize, tau_window=tw)
+    assert bz.last_path() == "tcgen05"
+    ((out.float() * d_out.cuda().float()).sum() + (tau.float() * d_tau.cuda().float()).sum()).backward()
+    assert bz.last_path() == "tcgen05"
+    fn = _global_reference(None, None, None, 8.0, bias.double(), tw, normalize)
+    (o, t), grads = orc.tension_with_grads(fn, [x.double() for x in (q, k, v)],
+                                           [d_out.double(), d_tau.double()])
+    for g, r, what in zip((out, tau, qg.grad, kg.grad, vg.grad), (o, t, *grads),
+                          ("out", "tau", "dq", "dk", "dv")):
+        assert_close(g, r, dt, f"global T{T}/{normalize}/{what}")
+
+
+@cuda
+def test_global_bf16_large_spot_check(bz):
+    """Global block at T 1024 (the 117M layer's sequence), B1 H4: forward and
+    all gradients against the float64 oracle."""
+    torch.manual_seed(9)
+    B, T, H, HD = 1, 1024, 4, 64
+    dt = torch.bfloat16
+    q, k, v, d_out = [torch.randn(B, T, H, HD, dtype=dt) for _ in range(4)]
+    qg, kg, vg = [x.cuda().requires_grad_(True) for x in (q, k, v)]
+    out = bz.tension(qg, kg, vg, window=None)
+    assert bz.last_path() == "tcgen05"
+    (out.float() * d_out.cuda().float()).sum().backward()
+    fn = _global_reference(None, None, None, 8.0, None, 64, "mass")
+    outs, grads = orc.tension_with_grads(lambda a, b, c: (fn(a, b, c)[0],),
+                                         [x.double() for x in (q, k, v)], [d_out.double()])
+    o = outs[0]
+    for g, r, what in zip((out, qg.grad, kg.grad, vg.grad), (o, *grads), ("out", "dq", "dk", "dv")):
+        assert_close(g, r, dt, f"global T1024/{what}")
+
+
 @cuda
 def test_large_bf16_spot_check(bz):
     """triton_tension/test.py:212-227 at B4 T512 H12 HD64 W64 (bf16)."""
