@@ -25,12 +25,14 @@
 //   dQ_j += dS_j·K_i                   (A = both dSᵀ halves read MN-major)
 // into one of two TMEM accumulators: query tile i+1 starts in iteration i and
 // completes in i+1, so no partial sums leave the SM and no atomics are used.
-// The MMA issuer runs one sub-chunk ahead (Sᵀ/dPᵀ of n+1 before the
-// consumers of n) so tensor cores and the epilogue overlap.  A CTA whose range
+// Two threads issue MMAs — one the Sᵀ/dPᵀ of every sub-chunk, one the
+// consumers — so Sᵀ/dPᵀ run ahead of the consumers and tensor cores and the
+// epilogue overlap.  A CTA whose range
 // starts mid-sequence first runs a warm-up pass over key tile i−1 for dQ_i.
 //
-// Warps: 0 TMA; 1 MMA; 2/3/12/13 output (dQ/dK/dV from TMEM → inverse RoPE
-// → shared staging → TMA store); 4-11 epilogue.  All waits are bounded
+// Warps: 0 TMA; 1 MMA (Sᵀ/dPᵀ); 14 MMA (consumers); 2/3/12/13 output (dQ/dK/dV
+// from TMEM → inverse RoPE → shared staging → TMA store); 4-11 epilogue.
+// All waits are bounded
 // (tc_ptx.cuh).
 #include <algorithm>
 
@@ -47,7 +49,7 @@ constexpr int kTile = kTcTile;
 constexpr int kHD = kTcHD;
 constexpr int kTileBytes = kTile * kHD * 2;  // 16 KiB
 constexpr int kHalfBytes = kTileBytes;       // one [128 x 64] bf16 Pᵀ or dSᵀ buffer
-constexpr int kThreads = 14 * 32;
+constexpr int kThreads = 15 * 32;
 constexpr int kErrBwd = 0x200;
 
 // TMEM columns: Sᵀ/dPᵀ buffer b at 128b (Sᵀ) and 128b+64 (dPᵀ)
@@ -61,6 +63,9 @@ struct BwdTC {
   long long bs0, bs1, bs2;
   const __nv_bfloat16* dtau;       // [B,T,H,W] contiguous or null
   const float* coef;               // [3][B·H, tpad]: α/2, α·c, β·c
+  __nv_bfloat16* dq;               // [B,T,H,64] contiguous outputs
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
   int* err;
 };
 
@@ -191,9 +196,14 @@ struct Sub {
 struct SubGen {
   int u, u0, u1, nT, Wr, idx, it, n, nk, nq, qslot, kslot;
   bool c1h1_zero;
+  Step st;     // step of key tile u (recomputed only when u advances)
+  int st_u = -1;
   __device__ bool next(Sub& s) {
     while (u < u1) {
-      const Step st = step_of(u, u0, u1, nT);
+      if (st_u != u) {
+        st = step_of(u, u0, u1, nT);
+        st_u = u;
+      }
       const int kinds = (st.warm ? 2 : 0) + 2 + (st.has_c1 ? 2 : 0);
       if (idx >= kinds) {
         ++u;
@@ -283,10 +293,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar->p_free[s], 1);
       mbar_init(&bar->dq_free[s], 4);
     }
-    mbar_init(&bar->acc_full, 1);
-    mbar_init(&bar->dkv_free, 4);
     mbar_init(&bar->aux_staged, 4);
     mbar_init(&bar->aux_stored, 1);
+    mbar_init(&bar->acc_full, 1);
+    mbar_init(&bar->dkv_free, 4);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -337,8 +347,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (st.has_c1) load_query(st.bh, st.i + 1);
       }
     }
-  } else if (warp == 1) {
-    // ─────────────────────────── MMA issuer ───────────────────────────
+  } else if (warp == 1 || warp == 14) {
+    // ──────────── MMA issuers: warp 1 Sᵀ/dPᵀ, warp 14 consumers ────────────
+    // Two issuing threads: each walks the same sub-chunk sequence with a
+    // short, wait-only loop, so neither waits behind the other's MMAs.  Each
+    // commit covers only its own thread's MMAs; that suffices because the
+    // consumers of a sub-chunk start after the epilogue consumed its Sᵀ/dPᵀ
+    // (p_full), i.e. after every producer MMA that read the same tiles.
     if (lane == 0) {
       const uint32_t id_s = idesc_bf16(128, 64, false, false);   // Sᵀ/dPᵀ: A,B K-major
       const uint32_t id_kv = idesc_bf16(128, kHD, false, true);  // dV/dK: A K-major, B MN-major
@@ -354,7 +369,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dDSmn = sdesc_sw128(smem_u32(sPDS) + kHalfBytes, 2 * kHalfBytes, 1024);
       int dq_started[2] = {0, 0};
       bool ok = true;
-      const uint64_t kIdleLimitNs = kWaitLimitNs;
 
       auto issue_sdp = [&](const Sub& s) {
         const int b = s.n & 1;
@@ -399,60 +413,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (s.rel_k) mma_commit(&bar->kv_empty[s.ks]);
       };
 
-      // Event-driven issue: whichever of "Sᵀ/dPᵀ of the next sub-chunk" and
-      // "consumers of the oldest pending sub-chunk" is ready goes first, so a
-      // consumer waiting on the output warps never holds back the next Sᵀ/dPᵀ.
       SubGen gen{u0, u0, u1, nT, Wr, 0, 0, 0, 0, 0, 0, 0, c1h1_zero};
-      Sub nxt{};
-      bool have_next = gen.next(nxt);
-      Sub f0{}, f1{}, f2{};  // pending consumers, oldest first
-      int fn = 0;
-      uint64_t idle_since = 0;
-      uint32_t idle = 0;
-      while (ok && (have_next || fn > 0)) {
-        bool prog = false;
-        if (have_next && fn < 3) {
-          bool ready = true;
-          if (nxt.kidx >= 0) ready = mbar_test(&bar->kv_full[nxt.kidx & 1], (nxt.kidx >> 1) & 1);
-          if (ready && nxt.qidx >= 0) ready = mbar_test(&bar->q_full[nxt.qidx & 1], (nxt.qidx >> 1) & 1);
-          if (ready && nxt.n >= 2) ready = mbar_test(&bar->sdp_free[nxt.n & 1], ((nxt.n >> 1) - 1) & 1);
-          if (ready) {
-            tc_fence_after();
-            issue_sdp(nxt);
-            if (fn == 0) f0 = nxt; else if (fn == 1) f1 = nxt; else f2 = nxt;
-            ++fn;
-            have_next = gen.next(nxt);
-            prog = true;
-          }
+      Sub s{};
+      if (warp == 1) {
+        while (ok && gen.next(s)) {
+          if (s.kidx >= 0) ok = mbar_wait(&bar->kv_full[s.kidx & 1], (s.kidx >> 1) & 1, err, kErrBwd | 16);
+          if (ok && s.qidx >= 0) ok = mbar_wait(&bar->q_full[s.qidx & 1], (s.qidx >> 1) & 1, err, kErrBwd | 17);
+          if (ok && s.n >= 2) ok = mbar_wait(&bar->sdp_free[s.n & 1], ((s.n >> 1) - 1) & 1, err, kErrBwd | 18);
+          if (!ok) break;
+          tc_fence_after();
+          issue_sdp(s);
         }
-        if (fn > 0) {
-          const Sub& s = f0;
-          bool ready = mbar_test(&bar->p_full[s.n & 1], (s.n >> 1) & 1);
-          if (ready && s.kv_first && s.it >= 1) ready = mbar_test(&bar->dkv_free, (s.it - 1) & 1);
-          if (ready && s.hh == 1 && s.dq && !s.dq_acc && dq_started[s.bq] >= 1)
-            ready = mbar_test(&bar->dq_free[s.bq], (dq_started[s.bq] - 1) & 1);
-          if (ready) {
-            tc_fence_after();
-            issue_consumers(s);
-            f0 = f1;
-            f1 = f2;
-            --fn;
-            prog = true;
-          }
-        }
-        if (prog) {
-          idle = 0;
-        } else {
-          if (idle == 0) idle_since = globaltimer_ns();
-          if ((++idle & 63u) == 0 && globaltimer_ns() - idle_since > kIdleLimitNs) {
-            atomicCAS(err, 0, kErrBwd | 16);
-            ok = false;
-          }
-          __nanosleep(32);
+      } else {
+        while (ok && gen.next(s)) {
+          ok = mbar_wait(&bar->p_full[s.n & 1], (s.n >> 1) & 1, err, kErrBwd | 19);
+          if (ok && s.kv_first && s.it >= 1) ok = mbar_wait(&bar->dkv_free, (s.it - 1) & 1, err, kErrBwd | 20);
+          if (ok && s.hh == 1 && s.dq && !s.dq_acc && dq_started[s.bq] >= 1)
+            ok = mbar_wait(&bar->dq_free[s.bq], (dq_started[s.bq] - 1) & 1, err, kErrBwd | 21);
+          if (!ok) break;
+          tc_fence_after();
+          issue_consumers(s);
         }
       }
     }
-  } else if (warp < 4 || warp >= 12) {
+  } else if (warp < 4 || warp == 12 || warp == 13) {
     // ──────── output warps: dQ/dK/dV of each key tile ────────
     const int r = (warp & 3) * 32 + lane;  // == TMEM lane of this thread
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
@@ -470,8 +454,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Step st = step_of(u, u0, u1, nT);
       const int ks_cur = key_slot_of(u);
       ok = mbar_wait(&bar->acc_full, it & 1, err, kErrBwd | 25);
-      // the dQ staging tile must be read out by the previous store
-      if (ok && it >= 1) ok = mbar_wait(&bar->aux_stored, (it - 1) & 1, err, kErrBwd | 26);
       if (!ok) break;
       __syncwarp();
       tc_fence_after();
@@ -481,52 +463,59 @@ __global__ void __launch_bounds__(kThreads, 1)
       // K_i / V_i slots are dead once acc_full fired: stage dK and dV there
       const uint32_t kst = smem_u32(sK + ks_cur * kTileBytes), vst = smem_u32(sV + ks_cur * kTileBytes);
       const uint32_t qst = smem_u32(sStage);
-      {
-        uint32_t g[64];
-        tmem_ld32_wait(tbase + lane_off + kColDV, g);
-        tmem_ld32_wait(tbase + lane_off + kColDV + 32, g + 32);
+      uint32_t g[64];
+      // dV, then dK leave TMEM first: the next key tile's dV/dK MMAs wait only
+      // for that (dkv_free), not for the rotation and staging below
+      tmem_ld32_wait(tbase + lane_off + kColDV, g);
+      tmem_ld32_wait(tbase + lane_off + kColDV + 32, g + 32);
 #pragma unroll
-        for (int z = 0; z < 8; ++z) {
-          uint32_t w4[4];
+      for (int z = 0; z < 8; ++z) {
+        uint32_t w4[4];
 #pragma unroll
-          for (int y = 0; y < 4; ++y)
-            w4[y] = pack_bf16(__uint_as_float(g[8 * z + 2 * y]), __uint_as_float(g[8 * z + 2 * y + 1]));
-          st_shared_v4(vst + sw128_off(r, z), w4[0], w4[1], w4[2], w4[3]);
-        }
+        for (int y = 0; y < 4; ++y)
+          w4[y] = pack_bf16(__uint_as_float(g[8 * z + 2 * y]), __uint_as_float(g[8 * z + 2 * y + 1]));
+        st_shared_v4(vst + sw128_off(r, z), w4[0], w4[1], w4[2], w4[3]);
       }
-      // dK and dQ share the row position: one cos/sin per frequency for both
+      tmem_ld32_wait(tbase + lane_off + kColDK, g);
+      tmem_ld32_wait(tbase + lane_off + kColDK + 32, g + 32);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->dkv_free);
+      // dQ: the staging tile must have been read out by the previous store
+      if (it >= 1) ok = mbar_wait(&bar->aux_stored, (it - 1) & 1, err, kErrBwd | 26);
+      if (!ok) break;
+      // inverse RoPE of dK (registers) and dQ (TMEM, 8 frequencies at a time):
+      // frequency i pairs columns i and 32+i; one cos/sin serves both rows
+      const uint32_t qc = tbase + lane_off + kColDQ + 64 * bq;
 #pragma unroll
       for (int c8 = 0; c8 < 4; ++c8) {
-        uint32_t g[32];  // dK[lo], dK[hi], dQ[lo], dQ[hi] columns of this group
-        const uint32_t kc = tbase + lane_off + kColDK + 8 * c8;
-        const uint32_t qc = tbase + lane_off + kColDQ + 64 * bq + 8 * c8;
-        tmem_ld8x4_wait(kc, kc + 32, qc, qc + 32, g);
-        float o[32];
+        uint32_t gq[16];
+        tmem_ld8x2_wait(qc + 8 * c8, qc + 32 + 8 * c8, gq);  // columns [8c8, +8) and [32+8c8, +8)
+        float ok8[16], oq8[16];
 #pragma unroll
         for (int z = 0; z < 8; ++z) {
           float cs = 1.f, sn = 0.f;
           if (rope) rope_cs(pos, th[c8 * 8 + z], cs, sn);
-          const float k1 = __uint_as_float(g[z]), k2 = __uint_as_float(g[8 + z]);
-          const float q1 = __uint_as_float(g[16 + z]), q2 = __uint_as_float(g[24 + z]);
-          o[z] = k1 * cs + k2 * sn;
-          o[8 + z] = k2 * cs - k1 * sn;
-          o[16 + z] = q1 * cs + q2 * sn;
-          o[24 + z] = q2 * cs - q1 * sn;
+          const float k1 = __uint_as_float(g[8 * c8 + z]), k2 = __uint_as_float(g[32 + 8 * c8 + z]);
+          const float q1 = __uint_as_float(gq[z]), q2 = __uint_as_float(gq[8 + z]);
+          ok8[z] = k1 * cs + k2 * sn;
+          ok8[8 + z] = k2 * cs - k1 * sn;
+          oq8[z] = q1 * cs + q2 * sn;
+          oq8[8 + z] = q2 * cs - q1 * sn;
         }
-        st_shared_v4(kst + sw128_off(r, c8), pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]),
-                     pack_bf16(o[4], o[5]), pack_bf16(o[6], o[7]));
-        st_shared_v4(kst + sw128_off(r, 4 + c8), pack_bf16(o[8], o[9]), pack_bf16(o[10], o[11]),
-                     pack_bf16(o[12], o[13]), pack_bf16(o[14], o[15]));
-        st_shared_v4(qst + sw128_off(r, c8), pack_bf16(o[16], o[17]), pack_bf16(o[18], o[19]),
-                     pack_bf16(o[20], o[21]), pack_bf16(o[22], o[23]));
-        st_shared_v4(qst + sw128_off(r, 4 + c8), pack_bf16(o[24], o[25]), pack_bf16(o[26], o[27]),
-                     pack_bf16(o[28], o[29]), pack_bf16(o[30], o[31]));
+        st_shared_v4(kst + sw128_off(r, c8), pack_bf16(ok8[0], ok8[1]), pack_bf16(ok8[2], ok8[3]),
+                     pack_bf16(ok8[4], ok8[5]), pack_bf16(ok8[6], ok8[7]));
+        st_shared_v4(kst + sw128_off(r, 4 + c8), pack_bf16(ok8[8], ok8[9]), pack_bf16(ok8[10], ok8[11]),
+                     pack_bf16(ok8[12], ok8[13]), pack_bf16(ok8[14], ok8[15]));
+        st_shared_v4(qst + sw128_off(r, c8), pack_bf16(oq8[0], oq8[1]), pack_bf16(oq8[2], oq8[3]),
+                     pack_bf16(oq8[4], oq8[5]), pack_bf16(oq8[6], oq8[7]));
+        st_shared_v4(qst + sw128_off(r, 4 + c8), pack_bf16(oq8[8], oq8[9]), pack_bf16(oq8[10], oq8[11]),
+                     pack_bf16(oq8[12], oq8[13]), pack_bf16(oq8[14], oq8[15]));
       }
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&bar->dkv_free);
         mbar_arrive(&bar->dq_free[bq]);
         mbar_arrive(&bar->aux_staged);
       }
@@ -740,6 +729,9 @@ cudaError_t launch_tc_bwd(const BwdP& p, cudaStream_t st, int* launches) {
   a.bias = p.bias; a.bs0 = p.bs0; a.bs1 = p.bs1; a.bs2 = p.bs2;
   a.dtau = static_cast<const __nv_bfloat16*>(p.dtau);
   a.coef = p.coef;
+  a.dq = static_cast<__nv_bfloat16*>(p.dq);
+  a.dk = static_cast<__nv_bfloat16*>(p.dk);
+  a.dv = static_cast<__nv_bfloat16*>(p.dv);
   a.err = p.err;
   {  // coefficient pre-pass into the (padded) workspace rows
     cudaError_t e = launch_alpha_beta(p, a.tpad, a.ds_scale, p.coef, st);

@@ -231,6 +231,20 @@ __device__ __forceinline__ void tmem_ld8x4_wait(uint32_t a0, uint32_t a1, uint32
       : "memory");
 }
 
+// Two 8-column loads and one completion wait (16 registers: r[0..7] from a0,
+// r[8..15] from a1).
+__device__ __forceinline__ void tmem_ld8x2_wait(uint32_t a0, uint32_t a1, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%16];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%17];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(a0), "r"(a1)
+      : "memory");
+}
+
 // Two 16-column loads and one completion wait (32 registers).
 __device__ __forceinline__ void tmem_ld16x2_wait(uint32_t a0, uint32_t a1, uint32_t* r) {
   asm volatile(
