@@ -182,12 +182,14 @@ int bozo_tension_fwd(const bozo_tension_fwd_args* a, void* stream) {
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int launches = 0;
-  const bool global = p.mode == BOZO_MODE_GLOBAL;
-  const bool tc_ok = global ? tc_global_fwd_eligible(p) : tc_fwd_eligible(p);
+  // local windows up to 128 keys: the band kernel; global and wider local
+  // windows: the key-tile streaming kernel
+  const bool band = p.mode == BOZO_MODE_LOCAL && tc_fwd_eligible(p);
+  const bool tc_ok = band || tc_global_fwd_eligible(p);
   if (a->path == BOZO_PATH_TCGEN05 && !tc_ok) return BOZO_ERR_ALIGNMENT;
   int path;
   if (tc_ok && a->path != BOZO_PATH_SIMT) {
-    e = global ? launch_tc_global_fwd(p, s, &launches) : launch_tc_fwd(p, s, &launches);
+    e = band ? launch_tc_fwd(p, s, &launches) : launch_tc_global_fwd(p, s, &launches);
     path = BOZO_PATH_TCGEN05;
   } else {
     e = launch_simt_fwd(p, s, &launches);
@@ -257,12 +259,12 @@ int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int launches = 0;
-  const bool global = p.mode == BOZO_MODE_GLOBAL;
-  const bool tc_ok = global ? tc_global_bwd_eligible(p) : tc_bwd_eligible(p);
+  const bool band = p.mode == BOZO_MODE_LOCAL && tc_bwd_eligible(p);
+  const bool tc_ok = band || tc_global_bwd_eligible(p);
   if (a->path == BOZO_PATH_TCGEN05 && !tc_ok) return BOZO_ERR_ALIGNMENT;
   int path;
   if (tc_ok && a->path != BOZO_PATH_SIMT) {
-    e = global ? launch_tc_global_bwd(p, s, &launches) : launch_tc_bwd(p, s, &launches);
+    e = band ? launch_tc_bwd(p, s, &launches) : launch_tc_global_bwd(p, s, &launches);
     path = BOZO_PATH_TCGEN05;
   } else {
     e = launch_simt_bwd(p, s, &launches);

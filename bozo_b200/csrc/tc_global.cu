@@ -1,12 +1,15 @@
-// tc_global.cu — tcgen05 / TMA / TMEM kernels of the GLOBAL full-causal
-// tension block (model.py:217-237) for bf16 Q/K/V with HD = 64 (sm_100a).
+// tc_global.cu — tcgen05 / TMA / TMEM kernels that stream whole key tiles:
+// the GLOBAL full-causal tension block (model.py:217-237) and local windows
+// too wide for the band kernels (W > 128), for bf16 Q/K/V with HD = 64.
 //
-// Semantics: τ[t,s] = σ(q_t·k_s/scale + bias[b,t,s]) for every key s ≤ t
-// (self included), out_t = Σ_s τ·v_s / max(Σ_s τ, 1e-6) (or the raw sum),
-// the reference's exported τ window τ_x[t,c] = τ[t, T−1−c], c < tw
-// (model.py:233-236), and the backward through all of it.  Q and K arrive
-// RoPE-rotated (the forward writes the rotated copies first); the backward
-// inverse-rotates dQ and dK.
+// Semantics: τ[t,s] = σ(q_t·k_s/scale + bias) for every key s ≤ t (global,
+// self included, bias[b,t,s]) or 1 ≤ t − s ≤ W (local, bias[b,t,w] at window
+// slot w = W − (t − s), triton_tension/kernel.py:41-126); out_t = Σ_s τ·v_s
+// normalised by τ-mass (model.py:257-258), by the position count
+// (model.py:261-264) or raw; the exported τ (local [B,T,H,W]; global: the
+// reference's window τ_x[t,c] = τ[t, T−1−c], c < tw, model.py:233-236); and
+// the backward through all of it.  Q and K arrive RoPE-rotated (the forward
+// writes the rotated copies first); the backward inverse-rotates dQ and dK.
 //
 // Three kernels share one pipeline skeleton.  A work unit is one 128-row
 // "outer" tile held in shared memory while 128-row "inner" tiles stream
@@ -16,6 +19,7 @@
 //   FWD   Q_j             K_i,V_i   (i ≤ j)      S = Q·K_hᵀ              O  += P·V_h
 //   DKV   K_i,V_i         Q_j,dO_j  (j ≥ i)      Sᵀ = K·Q_hᵀ, dPᵀ=V·dO_hᵀ dV += (ατ)ᵀ·dO_h, dK += dSᵀ·Q_h
 //   DQ    Q_j,dO_j        K_i,V_i   (i ≤ j)      S = Q·K_hᵀ, dP = dO·V_hᵀ dQ += dS·K_h
+// (a local window limits the inner range to the tiles its band touches).
 //
 // All MMAs are M = 128, N = 64, K = 64 (kind::f16, bf16 in, fp32 accumulate).
 // Producer results are double-buffered in TMEM, the epilogue's bf16 tiles
@@ -60,12 +64,13 @@ struct Traits {
 
 struct GlobTC {
   int B, T, H, BH, nT, units, tpad, tw;
+  int local, W;  // local: sliding window of W keys before each query (self excluded)
   float half_inv_scale, ds_scale;
   int norm;
   const float* theta;  // RoPE frequencies [32] (inverse rotation of dQ/dK) or null
-  const float* bias;   // [B,T,T]
+  const float* bias;   // global [B,T,T] / local [B,T,W]
   long long bs0, bs1, bs2;
-  __nv_bfloat16* tau;         // FWD: exported window [B,T,H,tw], zero-filled before
+  __nv_bfloat16* tau;         // FWD: exported τ [B,T,H,tw], zero-filled before
   const __nv_bfloat16* dtau;  // DKV/DQ: its cotangent
   float* row_mass;            // FWD: [B,H,T]
   const float* coef;          // DKV/DQ: [3][B·H, tpad]
@@ -102,20 +107,22 @@ __host__ __device__ inline GLayout glayout() {
   return L;
 }
 
-// Work unit k (heaviest first): FWD/DQ outer query tile j has j+1 key tiles,
-// DKV outer key tile i has nT−i query tiles.
-__device__ __forceinline__ void unit_of(int role, int k, int BH, int nT, int& bh, int& ot,
-                                        int& first_inner, int& n_inner) {
+// Work unit k (heaviest first): FWD/DQ outer query tile j has key tiles
+// [first, j] (first = 0 globally, the window's first tile locally), DKV outer
+// key tile i has query tiles [i, last].
+__device__ __forceinline__ void unit_of(int role, int k, int BH, int nT, int local, int W, int& bh,
+                                        int& ot, int& first_inner, int& n_inner) {
   const int g = k / BH;
   bh = k % BH;
   if (role == kDKV) {
     ot = g;
     first_inner = g;
-    n_inner = nT - g;
+    const int last = local ? min(nT - 1, (g * kTile + kTile - 1 + W) / kTile) : nT - 1;
+    n_inner = last - g + 1;
   } else {
     ot = nT - 1 - g;
-    first_inner = 0;
-    n_inner = ot + 1;
+    first_inner = local ? max(0, ot * kTile - W) / kTile : 0;
+    n_inner = ot - first_inner + 1;
   }
 }
 
@@ -182,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int ni = 0;
       for (int k = blockIdx.x, m = 0; k < p.units && ok; k += G, ++m) {
         int bh, ot, fi, nin;
-        unit_of(R, k, BH, nT, bh, ot, fi, nin);
+        unit_of(R, k, BH, nT, p.local, p.W, bh, ot, fi, nin);
         const int b = bh / H, h = bh % H;
         const int os = m & 1;
         if (m >= 2) ok = mbar_wait(&bar->outer_empty[os], ((m >> 1) - 1) & 1, err, kErrG | 1);
@@ -265,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       for (int k = blockIdx.x, m = 0; k < p.units && ok; k += G, ++m) {
         int bh, ot, fi, nin;
-        unit_of(R, k, BH, nT, bh, ot, fi, nin);
+        unit_of(R, k, BH, nT, p.local, p.W, bh, ot, fi, nin);
         const int os = m & 1;
         ok = mbar_wait(&bar->outer_full[os], (m >> 1) & 1, err, kErrG | 5);
         const uint64_t o0 = dOuter + (uint64_t)(os * Tr::kOuterTiles) * kTD;
@@ -318,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int k = blockIdx.x, m = 0; k < p.units && ok; k += G, ++m) {
       int bh, ot, fi, nin;
-      unit_of(R, k, BH, nT, bh, ot, fi, nin);
+      unit_of(R, k, BH, nT, p.local, p.W, bh, ot, fi, nin);
       const int b = bh / H, h = bh % H;
       const int ub = m & 1, os = m & 1;
       ok = mbar_wait(&bar->acc_full[ub], (m >> 1) & 1, err, kErrG | 8);
@@ -338,7 +345,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar->acc_free[ub]);
         const float mass = sMass[(ub * 2 + 0) * kTile + r] + sMass[(ub * 2 + 1) * kTile + r];
-        const float inv = p.norm == BOZO_NORM_MASS ? 1.f / fmaxf(mass, kMassEps) : 1.f;
+        float inv = 1.f;
+        if (p.norm == BOZO_NORM_MASS) inv = 1.f / fmaxf(mass, kMassEps);
+        else if (p.norm == BOZO_NORM_COUNT) inv = 1.f / (float)max(min(pos, p.W), 1);  // model.py:261-264
 #pragma unroll
         for (int z = 0; z < 8; ++z) {
           uint32_t w4[4];
@@ -423,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int n = 0, ni = 0;
     for (int k = blockIdx.x, m = 0; k < p.units && ok; k += G, ++m) {
       int bh, ot, fi, nin;
-      unit_of(R, k, BH, nT, bh, ot, fi, nin);
+      unit_of(R, k, BH, nT, p.local, p.W, bh, ot, fi, nin);
       const int b = bh / H, h = bh % H;
       const int os = m & 1;
       const int orow = ot * kTile + r;  // this thread's outer position
@@ -471,11 +480,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int ipos = ipos0 + ee;
                 const int tq = (R == kDKV) ? ipos : orow;  // query position
                 const int sk = (R == kDKV) ? orow : ipos;  // key position
-                const bool valid = tq < T && sk <= tq;
+                // global: s ≤ t; local: 1 ≤ t − s ≤ W, window slot w = W − (t − s)
+                const int dts = tq - sk;
+                const bool valid = tq < T && (p.local ? (dts >= 1 && dts <= p.W) : dts >= 0);
                 float x = __uint_as_float(Rg[ee]) * p.half_inv_scale;
                 if constexpr (kBias) {
-                  const int tqc = min(tq, T - 1), skc = min(sk, T - 1);
-                  x = fmaf(0.5f, __ldg(p.bias + b * p.bs0 + (long long)tqc * p.bs1 + (long long)skc * p.bs2), x);
+                  const int tqc = min(tq, T - 1);
+                  const int col = p.local ? (valid ? p.W - dts : 0) : min(sk, T - 1);
+                  x = fmaf(0.5f, __ldg(p.bias + b * p.bs0 + (long long)tqc * p.bs1 + (long long)col * p.bs2), x);
                 }
                 const float thv = tanh_approx(x);
                 if (R == kFwd) {
@@ -483,8 +495,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                   mass += tau;
                   pv[z] = tau;
                   if constexpr (kExtra) {
-                    if (valid && sk >= T - p.tw)
-                      p.tau[((long long)(b * T + tq) * H + h) * p.tw + (T - 1 - sk)] = __float2bfloat16_rn(tau);
+                    // exported τ: local [B,T,H,W] at w; global window of the last
+                    // tw keys, column T−1−s (model.py:233-236)
+                    const int col = p.local ? p.W - dts : T - 1 - sk;
+                    if (valid && (unsigned)col < (unsigned)p.tw)
+                      p.tau[((long long)(b * T + tq) * H + h) * p.tw + col] = __float2bfloat16_rn(tau);
                   }
                 } else {
                   float ad, bd, ah = 0.f;
@@ -499,8 +514,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                   }
                   float dt = fmaf(ad, __uint_as_float(Rg[16 + ee]), bd);
                   if constexpr (kExtra) {
-                    if (valid && sk >= T - p.tw)
-                      dt = fmaf(__bfloat162float(p.dtau[((long long)(b * T + tq) * H + h) * p.tw + (T - 1 - sk)]),
+                    const int col = p.local ? p.W - dts : T - 1 - sk;
+                    if (valid && (unsigned)col < (unsigned)p.tw)
+                      dt = fmaf(__bfloat162float(p.dtau[((long long)(b * T + tq) * H + h) * p.tw + col]),
                                 p.ds_scale, dt);
                   }
                   dv[z] = valid ? dt * fmaf(-thv, thv, 1.f) : 0.f;
@@ -581,8 +597,8 @@ bool out_ok(const void* ptr) { return ptr && (reinterpret_cast<uintptr_t>(ptr) &
 }  // namespace
 
 bool tc_global_fwd_eligible(const FwdP& p) {
-  if (p.mode != BOZO_MODE_GLOBAL || p.HD != kHD) return false;
-  if (p.norm != BOZO_NORM_MASS && p.norm != BOZO_NORM_NONE) return false;
+  if (p.HD != kHD || (p.mode == BOZO_MODE_LOCAL && p.W < 1)) return false;
+  if (p.mode == BOZO_MODE_GLOBAL && p.norm == BOZO_NORM_COUNT) return false;
   if (p.out_dt != BOZO_DT_BF16 || !out_ok(p.out)) return false;
   if (p.tau && p.tau_dt != BOZO_DT_BF16) return false;
   if (!tma_view_ok(p.q, p.B, p.T, p.H) || !tma_view_ok(p.k, p.B, p.T, p.H) ||
@@ -600,6 +616,8 @@ cudaError_t launch_tc_global_fwd(const FwdP& p, cudaStream_t st, int* launches) 
   a.nT = (p.T + kTile - 1) / kTile;
   a.units = a.BH * a.nT;
   a.tw = p.tau ? p.W : 0;
+  a.local = p.mode == BOZO_MODE_LOCAL;
+  a.W = p.W;
   a.half_inv_scale = 0.5f / p.scale;
   a.norm = p.norm;
   a.bias = p.bias; a.bs0 = p.bs0; a.bs1 = p.bs1; a.bs2 = p.bs2;
@@ -634,8 +652,8 @@ cudaError_t launch_tc_global_fwd(const FwdP& p, cudaStream_t st, int* launches) 
 }
 
 bool tc_global_bwd_eligible(const BwdP& p) {
-  if (p.mode != BOZO_MODE_GLOBAL || p.HD != kHD) return false;
-  if (p.norm != BOZO_NORM_MASS && p.norm != BOZO_NORM_NONE) return false;
+  if (p.HD != kHD || (p.mode == BOZO_MODE_LOCAL && p.W < 1)) return false;
+  if (p.mode == BOZO_MODE_GLOBAL && p.norm == BOZO_NORM_COUNT) return false;
   if (p.dq_dt != BOZO_DT_BF16 || p.dk_dt != BOZO_DT_BF16 || p.dv_dt != BOZO_DT_BF16) return false;
   if (!tma_view_ok(p.q, p.B, p.T, p.H) || !tma_view_ok(p.k, p.B, p.T, p.H) ||
       !tma_view_ok(p.v, p.B, p.T, p.H) || !tma_view_ok(p.dout, p.B, p.T, p.H))
@@ -659,6 +677,8 @@ cudaError_t launch_tc_global_bwd(const BwdP& p, cudaStream_t st, int* launches) 
   a.units = a.BH * a.nT;
   a.tpad = a.nT * kTile;
   a.tw = p.dtau ? p.W : 0;
+  a.local = p.mode == BOZO_MODE_LOCAL;
+  a.W = p.W;
   a.half_inv_scale = 0.5f / p.scale;
   a.ds_scale = 0.25f / p.scale;
   a.norm = p.norm;

@@ -227,9 +227,10 @@ class _TensionFn(torch.autograd.Function):
         w_arg = window if mode == _capi.MODE_LOCAL else (tau_width or 0)
         # for training the forward also writes RoPE(q), RoPE(k); the backward
         # then reads the rotated tiles instead of rotating them again.  The
-        # global block's tensor-core forward always reads rotated copies.
+        # key-tile streaming forward (global block, windows over 128 keys)
+        # always reads rotated copies.
         rotated = rope is not None and (any(ctx.needs_input_grad[:3])
-                                        or mode == _capi.MODE_GLOBAL)
+                                        or mode == _capi.MODE_GLOBAL or window > 128)
         out, tau, mass, q_rot, k_rot = _launch_fwd(
             q, k, v, mode=mode, window=w_arg, norm=norm, scale=scale, rope=rope,
             bias=bias, tau_width=(w_arg if return_tau else None), out_dtype=q.dtype,

@@ -179,10 +179,11 @@ def test_prefix_rows_invariant_to_future(bz, dtype):
 
 
 @cuda
-@pytest.mark.parametrize("W", [8, 32, 64, 100, 128])
+@pytest.mark.parametrize("W", [8, 32, 64, 100, 128, 129, 256])
 @pytest.mark.parametrize("normalize", ["mass", "count", None])
 def test_fused_local_bf16_vs_oracle(bz, W, normalize):
-    """Fused local op at HD 64 (the tensor-core shape) across windows,
+    """Fused local op at HD 64 (the tensor-core shape) across windows —
+    the band kernels up to W 128, the key-tile streaming kernels above —
     normalisations, bias and τ cotangent, ragged T."""
     torch.manual_seed(100 + W)
     B, T, H, HD = 2, 333, 3, 64
@@ -193,7 +194,9 @@ def test_fused_local_bf16_vs_oracle(bz, W, normalize):
     qg, kg, vg = [x.cuda().requires_grad_(True) for x in (q, k, v)]
     out, tau = bz.tension(qg, kg, vg, window=W, bias=bias.cuda(), return_tau=True,
                           normalize=normalize)
+    assert bz.last_path() == "tcgen05"
     ((out.float() * d_out.cuda().float()).sum() + (tau.float() * d_tau.cuda().float()).sum()).backward()
+    assert bz.last_path() == "tcgen05"
 
     def fn(q_, k_, v_):
         return orc.fused_reference(q_, k_, v_, window=W, scale=8.0, bias=bias.double(),
