@@ -144,18 +144,13 @@ def run_ours(args, rank, world, local_rank):
     q, k, v, d_out = [x.to(dev) for x in (hq, hk, hv, hdo)]
     q.requires_grad_(True); k.requires_grad_(True); v.requires_grad_(True)
 
-    def step(W, qq=q, kk=k, vv=v, dd=d_out, ev=None):
-        if ev:
-            ev[0].record(stream)
-        out = bozo_b200.tension(qq, kk, vv, window=W, rope_base=10_000.0, normalize="mass")
-        fl = bops.last_launches()
-        if ev:
-            ev[1].record(stream)
+    def fwd(W, qq=q, kk=k, vv=v):
+        return bozo_b200.tension(qq, kk, vv, window=W, rope_base=10_000.0, normalize="mass")
+
+    def step(W, qq=q, kk=k, vv=v, dd=d_out):
+        out = fwd(W, qq, kk, vv)
         gq, gk, gv = torch.autograd.grad(out, (qq, kk, vv), dd)
-        bl = bops.last_launches()
-        if ev:
-            ev[2].record(stream)
-        return out, gq, gk, gv, fl + bl
+        return out, gq, gk, gv
 
     def barrier():
         if world > 1:
@@ -168,8 +163,44 @@ def run_ours(args, rank, world, local_rank):
             return float(t_.item())
         return x
 
+    def capture_fn(fn):
+        """fn (calls of the public API) as one CUDA graph: its kernel launches
+        replay without host work between them."""
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                fn()
+        stream.wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            keep = fn()
+        torch.cuda.synchronize()
+        return graph, keep
+
+    def capture(W):
+        return capture_fn(lambda: step(W))
+
+    def timed(run, n, clk=None):
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        if clk:
+            clk.__enter__()
+        torch.cuda.synchronize()
+        barrier()
+        e0.record(stream)
+        for _ in range(n):
+            run()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if clk:
+            clk.__exit__(None, None, None)
+        return maxred(e0.elapsed_time(e1)) / n
+
     results = {}
-    launches_per_step = 0
     # Process-level warm-up before any timed block: the first timed block of a
     # fresh process otherwise runs slow (clock and power ramp, allocator and
     # module first use); at least the requested warm-up steps, and ~1 s of work.
@@ -182,61 +213,98 @@ def run_ours(args, rank, world, local_rank):
             torch.cuda.synchronize()
     torch.cuda.synchronize()
     barrier()
+    # kernels of our library per step (forward call + backward call)
+    fwd(W_HEAD)
+    fl = bops.last_launches()
+    step(W_HEAD)
+    launches_per_step = fl + bops.last_launches()
+    # Device time of the forward alone (its own CUDA graph); the backward's is
+    # the step's minus the forward's.  (A backward is never captured alone:
+    # autograd would run it on the stream of a forward made outside the
+    # capture.)  After a failed capture every later block runs eagerly.
+    phase = {}
+    can_capture = True
+    try:
+        gf, kf = capture_fn(lambda: fwd(W_HEAD))
+        phase["fwd_ms"] = timed(gf.replay, args.steps)
+        del gf, kf
+    except Exception:
+        can_capture = False
+        phase["fwd_ms"] = timed(lambda: fwd(W_HEAD), args.steps)
     for W in args.windows:
         steps = args.steps if W == W_HEAD else max(3, args.steps // 4)
+        graph = keep = None
+        run, mode = (lambda W=W: step(W)), "eager (capture unavailable)"
+        if can_capture:
+            try:
+                graph, keep = capture(W)
+                run, mode = graph.replay, "cuda-graph replay of the fwd+bwd step"
+            except Exception as ex:  # time the eager calls from here on
+                can_capture = False
+                graph = keep = None
+                run, mode = (lambda W=W: step(W)), f"eager ({type(ex).__name__})"
         for _ in range(args.warmup):
-            step(W)
-        torch.cuda.synchronize()
-        barrier()
-        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
+            run()
         clk = Clocks(local_rank) if W == W_HEAD else None
-        if clk:
-            clk.__enter__()
-        torch.cuda.synchronize()
-        barrier()
-        start.record(stream)
-        n_launch = 0
-        for i in range(steps):
-            *_, nl = step(W, ev=evs[i])
-            n_launch += nl
-        end.record(stream)
-        torch.cuda.synchronize()
-        if clk:
-            clk.__exit__(None, None, None)
-        barrier()
-        ms = maxred(start.elapsed_time(end)) / steps
-        fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
-        bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
-        results[W] = dict(ms=ms, fwd_ms=maxred(fwd_ms), bwd_ms=maxred(bwd_ms),
-                          launches=n_launch, steps=steps,
+        ms = timed(run, steps, clk)
+        results[W] = dict(ms=ms, steps=steps, mode=mode, launches=launches_per_step * steps,
                           clocks=clk.summary() if clk else None, path=bops.last_path())
-        if W == W_HEAD:
-            launches_per_step = n_launch // steps
+        del graph, keep
+        barrier()
+    results[W_HEAD].update(phase)
+    results[W_HEAD]["bwd_ms"] = max(results[W_HEAD]["ms"] - phase["fwd_ms"], 1e-6)
 
     if args.no_e2e:
         return results, None, launches_per_step
 
     # ── e2e: public API, pinned host buffers in, results out, every step ──
+    # Step i copies its inputs in on a copy stream (into one of two device
+    # input sets), runs fwd+bwd on the compute stream and reads out, results
+    # back on a second copy stream; stream events order the three, so step
+    # i+1's upload overlaps step i's compute and read-out (PCIe is full duplex).
     hq, hk, hv, hdo = [x.pin_memory() for x in (hq, hk, hv, hdo)]
-    outs_h = [torch.empty(B, T, H, HD, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+    outs_h = [[torch.empty(B, T, H, HD, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+              for _ in range(2)]
+    ins_d = [[torch.empty(B, T, H, HD, dtype=torch.bfloat16, device=dev) for _ in range(4)]
+             for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]   # compute done reading input set
+    ev_done = [torch.cuda.Event() for _ in range(2)]   # compute results ready
+    ev_out = [torch.cuda.Event() for _ in range(2)]    # read-out of host set finished
 
-    def e2e_step():
-        qq, kk, vv, dd = [x.to(dev, non_blocking=True) for x in (hq, hk, hv, hdo)]
-        qq.requires_grad_(True); kk.requires_grad_(True); vv.requires_grad_(True)
-        out, gq, gk, gv, _ = step(W_HEAD, qq, kk, vv, dd)
-        for dst, src in zip(outs_h, (out, gq, gk, gv)):
-            dst.copy_(src.detach(), non_blocking=True)
+    def e2e_step(i):
+        sl = i & 1
+        with torch.cuda.stream(s_in):
+            if i >= 2:
+                s_in.wait_event(ev_used[sl])
+            for dst, src in zip(ins_d[sl], (hq, hk, hv, hdo)):
+                dst.copy_(src, non_blocking=True)
+            ev_in[sl].record(s_in)
+        stream.wait_event(ev_in[sl])
+        qq, kk, vv, dd = [x.detach().requires_grad_(j < 3) for j, x in enumerate(ins_d[sl])]
+        out, gq, gk, gv = step(W_HEAD, qq, kk, vv, dd)
+        ev_used[sl].record(stream)
+        ev_done[sl].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_done[sl])
+            if i >= 2:
+                s_out.wait_event(ev_out[sl])
+            for dst, src in zip(outs_h[sl], (out, gq, gk, gv)):
+                src.record_stream(s_out)
+                dst.copy_(src.detach(), non_blocking=True)
+            ev_out[sl].record(s_out)
 
-    for _ in range(args.warmup):
-        e2e_step()
+    for i in range(args.warmup):
+        e2e_step(i)
     torch.cuda.synchronize()
     barrier()
     s0 = torch.cuda.Event(enable_timing=True); s1 = torch.cuda.Event(enable_timing=True)
     s0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
+    s_in.wait_stream(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    stream.wait_stream(s_out)
     s1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = maxred(s0.elapsed_time(s1)) / args.steps
@@ -474,12 +542,13 @@ def main():
         "config": cfg,
         "tflops": round(n * flops_fwd_bwd(B, H, T, HD, W_HEAD) / (head["ms"] * 1e-3) / 1e12, 3),
         "kernel_path": head["path"],
+        "timing": head["mode"],
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(ach, 1), "peak": hbm,
                      "unit": "GB/s", "frac": round(ach / hbm, 4), "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                      "fwd_gbs": round(fwd_gbs, 1), "bwd_gbs": round(bwd_gbs, 1),
                      "fwd_ms": round(head["fwd_ms"], 4), "bwd_ms": round(head["bwd_ms"], 4)},
-        "per_window": {str(W): {"ms_per_step": round(r["ms"], 4),
+        "per_window": {str(W): {"ms_per_step": round(r["ms"], 4), "timing": r["mode"],
                                 "gbs": round(per_step_bytes / (r["ms"] * 1e-3) / 1e9, 1),
                                 "tflops": round(flops_fwd_bwd(B, H, T, HD, W) / (r["ms"] * 1e-3) / 1e12, 3),
                                 "frac_of_roofline": round(max(per_step_bytes / (hbm * 1e9),

@@ -100,30 +100,29 @@ __host__ __device__ inline Layout bwd_layout() {
 // Per query row: the epilogue's coefficients α/2, α·c and β·c (c = 1/(4·scale))
 // of the normalisation, into padded rows [B·H, tpad] (rows t ≥ T are 0).
 // τ-mass needs D = dO·out per row: eight threads share one 128-byte bf16 row
-// (one 16-byte chunk each) and rows are walked in memory order (b, t, h), so
-// every warp load is four whole rows.  The grid-stride step is a multiple of
+// (one 16-byte chunk each) and rows are walked in memory order (t, h) within
+// batch b = blockIdx.y, so every warp load is four whole rows and the index
+// math is one 32-bit division per row.  The grid-stride step is a multiple of
 // 32 threads, so the 8-lane shuffle groups stay whole and warp-uniform.
 __global__ void alpha_beta_kernel(int B, int T, int H, int W, int tpad, int norm, float ds_scale,
                                   const float* __restrict__ row_mass, DevT4 dout, DevT4 out,
                                   float* __restrict__ a_half, float* __restrict__ a_ds,
                                   float* __restrict__ b_ds) {
-  const long long rows = (long long)B * T * H;
-  const long long n8 = rows * 8;
-  const long long stride = (long long)gridDim.x * blockDim.x;
+  const int bb = blockIdx.y;
+  const int n8 = T * H * 8;  // threads needed for this batch row
+  const int stride = gridDim.x * blockDim.x;
   const int c = threadIdx.x & 7;
-  for (long long base = (long long)blockIdx.x * blockDim.x; base < n8; base += stride) {
-    const long long idx = base + threadIdx.x;
+  const __nv_bfloat16* dob = static_cast<const __nv_bfloat16*>(dout.p) + bb * dout.sb;
+  const __nv_bfloat16* oub = static_cast<const __nv_bfloat16*>(out.p) + bb * out.sb;
+  for (int base = blockIdx.x * blockDim.x; base < n8; base += stride) {
+    const int idx = base + threadIdx.x;
     const bool live = idx < n8;
-    const long long r = live ? idx >> 3 : 0;
-    const int h = (int)(r % H);
-    const long long bt = r / H;
-    const int t = (int)(bt % T), bb = (int)(bt / T);
+    const int rr = live ? idx >> 3 : 0;  // (t, h) row within the batch
+    const int t = rr / H, h = rr - t * H;
     float dd = 0.f;
     if (norm == BOZO_NORM_MASS && live) {
-      const uint4 x = __ldg(reinterpret_cast<const uint4*>(
-          static_cast<const __nv_bfloat16*>(dout.p) + bb * dout.sb + (long long)t * dout.st + h * dout.sh) + c);
-      const uint4 y = __ldg(reinterpret_cast<const uint4*>(
-          static_cast<const __nv_bfloat16*>(out.p) + bb * out.sb + (long long)t * out.st + h * out.sh) + c);
+      const uint4 x = __ldg(reinterpret_cast<const uint4*>(dob + (long long)t * dout.st + h * dout.sh) + c);
+      const uint4 y = __ldg(reinterpret_cast<const uint4*>(oub + (long long)t * out.st + h * out.sh) + c);
       const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
       const uint32_t ys[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
@@ -140,10 +139,10 @@ __global__ void alpha_beta_kernel(int B, int T, int H, int W, int tpad, int norm
       dd += __shfl_xor_sync(0xffffffffu, dd, 1);
     }
     if (live && c == 0) {
-      const long long bh = (long long)bb * H + h;
+      const int bh = bb * H + h;
       float a, b = 0.f;
       if (norm == BOZO_NORM_MASS) {
-        const float m = row_mass[bh * T + t];
+        const float m = row_mass[(long long)bh * T + t];
         a = 1.f / fmaxf(m, kMassEps);
         b = m >= kMassEps ? -dd * a : 0.f;
       } else if (norm == BOZO_NORM_COUNT) {
@@ -151,17 +150,16 @@ __global__ void alpha_beta_kernel(int B, int T, int H, int W, int tpad, int norm
       } else {
         a = 1.f;
       }
-      const long long o = bh * tpad + t;
+      const long long o = (long long)bh * tpad + t;
       a_half[o] = 0.5f * a;
       a_ds[o] = a * ds_scale;
       b_ds[o] = b * ds_scale;
     }
   }
-  // padding rows t ∈ [T, tpad)
+  // padding rows t ∈ [T, tpad) of this batch's heads
   const int pad = tpad - T;
-  const long long npad = (long long)B * H * pad;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < npad; i += stride) {
-    const long long o = (i / pad) * tpad + T + (i % pad);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H * pad; i += stride) {
+    const long long o = (long long)(bb * H + i / pad) * tpad + T + (i % pad);
     a_half[o] = 0.f;
     a_ds[o] = 0.f;
     b_ds[o] = 0.f;
@@ -687,15 +685,18 @@ cudaError_t launch_bwd_variant(const CUtensorMap* m, const BwdTC& a, size_t smem
 cudaError_t launch_alpha_beta(const BwdP& p, int tpad, float ds_scale, float* coef,
                               cudaStream_t st) {
   const long long n = (long long)p.B * p.H * tpad;
-  const int g = (int)std::min<long long>(((long long)p.B * p.T * p.H * 8 + 255) / 256,
-                                         (long long)num_sms() * 16);
-  alpha_beta_kernel<<<g, 256, 0, st>>>(p.B, p.T, p.H, p.W, tpad, p.norm, ds_scale, p.row_mass,
-                                       p.dout, p.out, coef, coef + n, coef + 2 * n);
+  // per batch row: T·H·8 threads; about 16 resident CTAs per SM over all rows
+  const long long per_b = ((long long)p.T * p.H * 8 + 255) / 256;
+  const int gx = (int)std::max<long long>(1, std::min<long long>(per_b, (num_sms() * 16LL + p.B - 1) / p.B));
+  alpha_beta_kernel<<<dim3(gx, p.B), 256, 0, st>>>(p.B, p.T, p.H, p.W, tpad, p.norm, ds_scale,
+                                                   p.row_mass, p.dout, p.out, coef, coef + n,
+                                                   coef + 2 * n);
   return cudaGetLastError();
 }
 
 bool tc_bwd_eligible(const BwdP& p) {
   if (p.mode != BOZO_MODE_LOCAL || p.HD != kHD || p.W < 1 || p.W > 128) return false;
+  if (p.B > 65535 || (long long)p.T * p.H * 8 > 0x7fffffffLL) return false;  // pre-pass grid
   if (p.dq_dt != BOZO_DT_BF16 || p.dk_dt != BOZO_DT_BF16 || p.dv_dt != BOZO_DT_BF16) return false;
   if (!tma_view_ok(p.q, p.B, p.T, p.H) || !tma_view_ok(p.k, p.B, p.T, p.H) ||
       !tma_view_ok(p.v, p.B, p.T, p.H) || !tma_view_ok(p.dout, p.B, p.T, p.H))

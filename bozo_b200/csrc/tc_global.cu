@@ -653,6 +653,7 @@ cudaError_t launch_tc_global_fwd(const FwdP& p, cudaStream_t st, int* launches) 
 
 bool tc_global_bwd_eligible(const BwdP& p) {
   if (p.HD != kHD || (p.mode == BOZO_MODE_LOCAL && p.W < 1)) return false;
+  if (p.B > 65535 || (long long)p.T * p.H * 8 > 0x7fffffffLL) return false;  // pre-pass grid
   if (p.mode == BOZO_MODE_GLOBAL && p.norm == BOZO_NORM_COUNT) return false;
   if (p.dq_dt != BOZO_DT_BF16 || p.dk_dt != BOZO_DT_BF16 || p.dv_dt != BOZO_DT_BF16) return false;
   if (!tma_view_ok(p.q, p.B, p.T, p.H) || !tma_view_ok(p.k, p.B, p.T, p.H) ||
