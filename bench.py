@@ -386,6 +386,72 @@ def run_train(args, rank, world, local_rank):
     return out, params
 
 
+PREFILL_B, PREFILL_T = 4, 2048  # batch 32 over 8 GPUs, seq 2048
+
+
+def run_prefill(args, rank, world, local_rank):
+    """350M TensionLM inference prefill with τ export:
+    bf16 weights, no grad, every layer returns τ (local [B,T,H,W], global
+    the exported window), batch 4 per GPU (32 over 8 GPUs), T 2048, random
+    init, uniform token ids.  Pure replicas: no collective.  Returns
+    (ms per forward max over ranks, e2e ms with token ids in and every
+    layer's τ read back to pinned host memory, params, τ bytes)."""
+    import torch.distributed as dist
+    from bozo_b200 import lm
+    dev = torch.device("cuda", local_rank)
+    torch.manual_seed(0)
+    cfg = lm.preset_350m_prefill()
+    model = lm.TensionLM(cfg).to(dev, torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(777 + rank)
+    ids_h = torch.randint(0, cfg.vocab_size, (PREFILL_B, PREFILL_T), generator=g).pin_memory()
+    ids = ids_h.to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def fwd(x):
+        with torch.no_grad():
+            return model(x, return_all=True)
+
+    def maxred(x):
+        if world > 1:
+            t_ = torch.tensor([x], device=dev, dtype=torch.float64)
+            dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+            return float(t_.item())
+        return x
+
+    _, _, taus = fwd(ids)
+    tau_bytes = sum(t.numel() * t.element_size() for t in taus)
+    taus_h = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in taus]
+    del taus
+    for _ in range(args.train_warmup):
+        fwd(ids)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.train_steps):
+        fwd(ids)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = maxred(e0.elapsed_time(e1)) / args.train_steps
+    if world > 1:
+        dist.barrier()
+    e0.record(stream)
+    for _ in range(args.train_steps):
+        x = ids_h.to(dev, non_blocking=True)
+        _, _, taus = fwd(x)
+        for dst, src in zip(taus_h, taus):
+            dst.copy_(src, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e = maxred(e0.elapsed_time(e1)) / args.train_steps
+    params = model.num_params
+    del model, taus
+    torch.cuda.empty_cache()
+    return ms, e2e, params, tau_bytes
+
+
 def cpu_baseline(budget_s=12.0):
     """The reference CPU algorithm (oracle port of ops.py:29-63 + model.py
     τ-mass + RoPE, fp32 autograd) on B=1 slices of the workload."""
@@ -416,8 +482,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end leg (profiling runs)")
-    ap.add_argument("--workload", default="all", choices=["all", "op", "train"],
-                    help="op: isolated operator (headline); train: 117M training step")
+    ap.add_argument("--workload", default="all", choices=["all", "op", "train", "prefill"],
+                    help="op: isolated operator (headline); train: 117M training step; "
+                         "prefill: 350M inference prefill with tau export")
     ap.add_argument("--train-steps", type=int, default=10)
     ap.add_argument("--train-warmup", type=int, default=3)
     ap.add_argument("--windows", type=int, nargs="+", default=list(WINDOWS),
@@ -470,12 +537,15 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    results = train = None
+    results = train = prefill = None
     if args.workload in ("all", "op"):
         results, e2e_ms, launches_per_step = run_ours(args, rank, world, local_rank)
     if args.workload in ("all", "train"):
         torch.cuda.empty_cache()
         train, n_params = run_train(args, rank, world, local_rank)
+    if args.workload in ("all", "prefill"):
+        torch.cuda.empty_cache()
+        prefill = run_prefill(args, rank, world, local_rank)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -498,8 +568,8 @@ def main():
             "aux_off": {"value": round(tok / (ms_off * 1e-3), 1), "unit": "tokens/s",
                         "ms_per_step": round(ms_off, 3)},
             "model_tflops": round(tflops, 1),
-            "mfu": round(tflops / sustained_tflops()[0], 4),
-            "mfu_peak": f"{sustained_tflops()[0]} TFLOP/s bf16 ({sustained_tflops()[1]})",
+            "mfu": round(tflops / (n * sustained_tflops()[0]), 4),
+            "mfu_peak": f"{sustained_tflops()[0]} TFLOP/s bf16 per GPU ({sustained_tflops()[1]})",
             "flops_per_token": int(flop_tok),
             "e2e": {"value": round(tok / (e2e_on * 1e-3), 1), "unit": "tokens/s",
                     "ms_per_step": round(e2e_on, 3),
@@ -513,11 +583,36 @@ def main():
                        "parallelism": f"ddp{n}" if n > 1 else "single GPU",
                        "data": "uniform random token ids, random init"},
         }
+    prefill_obj = None
+    if prefill is not None:
+        n = args.gpus
+        ms_p, e2e_p, p_params, tau_bytes = prefill
+        tok = n * PREFILL_B * PREFILL_T
+        prefill_obj = {
+            "metric": "350M TensionLM prefill tokens/s with tau export (whole job)",
+            "value": round(tok / (ms_p * 1e-3), 1), "unit": "tokens/s",
+            "ms_per_step": round(ms_p, 3), "steps": args.train_steps, "n_gpus": n,
+            "model_tflops": round(tok * 2 * p_params / (ms_p * 1e-3) / 1e12, 1),
+            "e2e": {"value": round(tok / (e2e_p * 1e-3), 1), "unit": "tokens/s",
+                    "ms_per_step": round(e2e_p, 3),
+                    "h2d_bytes_per_step": PREFILL_B * PREFILL_T * 8,
+                    "d2h_bytes_per_step": tau_bytes},
+            "config": {"workload": "TensionLM 350M prefill, every layer's tau exported "
+                                   "(BASELINE configs[4])",
+                       "params": p_params, "dim": 1024, "layers": 24, "heads": 16,
+                       "vocab": 32768, "W": 128, "global_every": 3, "seq_len": PREFILL_T,
+                       "per_gpu_batch": PREFILL_B, "global_batch": PREFILL_B * n,
+                       "dtype": "bf16 weights, no grad", "tau_bytes_per_gpu": tau_bytes,
+                       "parallelism": f"batch-sharded replicas x{n}",
+                       "data": "uniform random token ids, random init"},
+        }
     if results is None:
-        line = dict(train_obj)
+        line = dict(train_obj or prefill_obj)
         line.update({"higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                      "dtype": "bf16", "data": "synthetic"})
-        line["config"] = train_obj["config"]
+        line["config"] = (train_obj or prefill_obj)["config"]
+        if train_obj is not None and prefill_obj is not None:
+            line["prefill_350m"] = prefill_obj
         print(json.dumps(line))
         return
 
@@ -565,6 +660,8 @@ def main():
     }
     if train_obj is not None:
         line["train_117m"] = train_obj
+    if prefill_obj is not None:
+        line["prefill_350m"] = prefill_obj
     if n == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     print(json.dumps(line))

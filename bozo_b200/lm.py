@@ -61,6 +61,17 @@ def preset_117m(**over) -> TensionConfig:
     return TensionConfig(**cfg)
 
 
+def preset_350m_prefill(**over) -> TensionConfig:
+    """The 350M inference configuration: dim 1024, 24 layers, 16 heads,
+    vocab 32768, W 128, T 2048, global layer every 3rd block (train.py:246-256
+    ``--preset 350m`` with the benchmark's vocabulary and window)."""
+    cfg = dict(vocab_size=32768, dim=1024, num_layers=24, num_heads=16, window=128, ffn_mult=3,
+               max_seq_len=2048, dropout=0.0, use_oscillation=False, use_rope=True,
+               global_every=3)
+    cfg.update(over)
+    return TensionConfig(**cfg)
+
+
 class RMSNorm(nn.Module):
     """model.py:86-98."""
 
