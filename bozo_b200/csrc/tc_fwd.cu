@@ -38,14 +38,17 @@ constexpr int kTile = kTcTile;
 constexpr int kHD = kTcHD;
 constexpr int kTileBytes = kTile * kHD * 2;  // 16 KiB
 constexpr int kQSlots = 2;
-constexpr int kKVSlots = 3;
+constexpr int kKVSlots = 3;  // barrier array size; p.nkv ≤ this slots are used
 constexpr int kThreads = 14 * 32;
 constexpr int kRotThreads = 128;
 constexpr int kErrFwd = 0x100;  // device error codes (| site)
+constexpr size_t kMaxSmemPerBlock = 227 * 1024;  // sm_100 opt-in limit
 
 struct FwdTC {
   int B, T, H, W, Wr, nT, total;
   int norm, nbuf, ncols, pblocks;
+  int nkv;      // K/V ring slots (3, or 2 when the τ staging rows need the room)
+  int tstride;  // bytes per row of the τ staging buffer (0: no τ export)
   float half_inv_scale;
   const float* theta;  // RoPE frequencies [32] or null (no RoPE)
   const float* bias;
@@ -58,27 +61,32 @@ struct FwdTC {
 
 struct __align__(8) Bars {
   uint64_t q_full[kQSlots], q_ready[kQSlots], q_empty[kQSlots];
-  uint64_t kv_full[kKVSlots], k_ready[kKVSlots], kv_empty[kKVSlots];
+  // K and V have separate ring barriers: a K slot is free after its last
+  // QKᵀ, a V slot only after its last P·V
+  uint64_t k_full[kKVSlots], k_ready[kKVSlots], k_empty[kKVSlots];
+  uint64_t v_full[kKVSlots], v_empty[kKVSlots];
   uint64_t s_full[2], o_full[2], tmem_empty[2];
   uint64_t p_full;
   uint64_t mass_ready[2];  // the 8 epilogue warps have published their τ-mass halves
   uint64_t ostage_full, ostage_empty;
+  uint64_t tau_free;  // every epilogue warp has copied its τ rows out
   uint32_t tmem_base;
 };
 
 struct Layout {
-  uint32_t q, k, v, p, o, mass, bars, total;
+  uint32_t q, k, v, p, o, mass, tau, bars, total;
 };
 
-__host__ __device__ inline Layout fwd_layout(int pblocks) {
+__host__ __device__ inline Layout fwd_layout(int pblocks, int nkv, int tstride) {
   Layout L;
   L.q = 0;
   L.k = L.q + kQSlots * kTileBytes;
-  L.v = L.k + kKVSlots * kTileBytes;
-  L.p = L.v + kKVSlots * kTileBytes;
+  L.v = L.k + nkv * kTileBytes;
+  L.p = L.v + nkv * kTileBytes;
   L.o = L.p + pblocks * kTileBytes;
   L.mass = L.o + kTileBytes;  // float[2][2][128]
-  L.bars = L.mass + 2 * 2 * kTile * 4;
+  L.tau = L.mass + 2 * 2 * kTile * 4;  // τ rows [128][tstride bytes]
+  L.bars = L.tau + kTile * tstride;
   L.total = L.bars + (uint32_t)sizeof(Bars);
   return L;
 }
@@ -122,7 +130,7 @@ __device__ void rope_tiles(uint8_t* ta, uint8_t* tb, int t0, int T, const float 
   }
 }
 
-template <bool kBias, bool kTau>
+template <bool kBias, bool kTau, int kNKV>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmo,
@@ -130,7 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const FwdTC p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Layout L = fwd_layout(p.pblocks);
+  const Layout L = fwd_layout(p.pblocks, p.nkv, p.tstride);
   uint8_t* sQ = smem + L.q;
   uint8_t* sK = smem + L.k;
   uint8_t* sV = smem + L.v;
@@ -152,10 +160,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar->q_ready[i], 4);
       mbar_init(&bar->q_empty[i], 1);
     }
-    for (int i = 0; i < kKVSlots; ++i) {
-      mbar_init(&bar->kv_full[i], 1);
+    for (int i = 0; i < kNKV; ++i) {
+      mbar_init(&bar->k_full[i], 1);
       mbar_init(&bar->k_ready[i], 4);
-      mbar_init(&bar->kv_empty[i], 1);
+      mbar_init(&bar->k_empty[i], 1);
+      mbar_init(&bar->v_full[i], 1);
+      mbar_init(&bar->v_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar->s_full[i], 1);
@@ -166,6 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bar->p_full, 8);
     mbar_init(&bar->ostage_full, 8);
     mbar_init(&bar->ostage_empty, 1);
+    mbar_init(&bar->tau_free, 8);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -179,6 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tbase = bar->tmem_base;
   int* err = p.err;
   const int nT = p.nT, Wr = p.Wr;
+  constexpr int NKV = kNKV;  // K/V ring slots (compile time: cheap slot/phase math)
 
   if (warp == 0) {
     // ─────────────── TMA producer ───────────────
@@ -202,22 +214,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       auto load_key = [&](int bh, int jj) {
-        const int s = n % kKVSlots;
-        if (n >= kKVSlots)
-          ok = ok && mbar_wait(&bar->kv_empty[s], ((n / kKVSlots) - 1) & 1, err, kErrFwd | 1);
+        const int s = n % NKV;
+        const int b = bh / p.H, h = bh % p.H;
+        if (n >= NKV)
+          ok = ok && mbar_wait(&bar->k_empty[s], ((n / NKV) - 1) & 1, err, kErrFwd | 1);
         if (!ok) return;
         before_refill();
-        mbar_arrive_expect_tx(&bar->kv_full[s], 2 * kTileBytes);
-        const int b = bh / p.H, h = bh % p.H;
-        tma_load_4d(sK + s * kTileBytes, &tmk, &bar->kv_full[s], 0, h, jj * kTile, b);
-        tma_load_4d(sV + s * kTileBytes, &tmv, &bar->kv_full[s], 0, h, jj * kTile, b);
+        mbar_arrive_expect_tx(&bar->k_full[s], kTileBytes);
+        tma_load_4d(sK + s * kTileBytes, &tmk, &bar->k_full[s], 0, h, jj * kTile, b);
+        if (n >= NKV)
+          ok = ok && mbar_wait(&bar->v_empty[s], ((n / NKV) - 1) & 1, err, kErrFwd | 17);
+        if (!ok) return;
+        mbar_arrive_expect_tx(&bar->v_full[s], kTileBytes);
+        tma_load_4d(sV + s * kTileBytes, &tmv, &bar->v_full[s], 0, h, jj * kTile, b);
         ++n;
       };
       // store RoPE(Q), RoPE(K) of tile (bh, j) once the rotators are done
       auto store_rot = [&](int it_s, int bh, int j, int nk) {
-        const int qs = it_s % kQSlots, ks = nk % kKVSlots;
+        const int qs = it_s % kQSlots, ks = nk % NKV;
         ok = ok && mbar_wait(&bar->q_ready[qs], (it_s / kQSlots) & 1, err, kErrFwd | 15);
-        ok = ok && mbar_wait(&bar->k_ready[ks], (nk / kKVSlots) & 1, err, kErrFwd | 16);
+        ok = ok && mbar_wait(&bar->k_ready[ks], (nk / NKV) & 1, err, kErrFwd | 16);
         if (!ok) return;
         tma_store_4d(&tmqr, sQ + qs * kTileBytes, 0, bh % p.H, j * kTile, bh / p.H);
         tma_store_4d(&tmkr, sK + ks * kTileBytes, 0, bh % p.H, j * kTile, bh / p.H);
@@ -245,6 +261,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ─────────────── MMA issuer ───────────────
+    // With two TMEM buffers (nbuf 2) the QKᵀ of tile it+1 is issued before
+    // the P·V of tile it, so the epilogue finds S ready as soon as it is done
+    // with tile it.  The single shared P tile stays safe: the epilogue writes
+    // P(it+1) only after it has waited for P·V(it) (o_full) to normalise O(it).
     if (lane == 0) {
       const uint32_t id_s1 = idesc_bf16(128, Wr, false, false);
       const uint32_t id_s2 = idesc_bf16(128, 128, false, false);
@@ -255,54 +275,82 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dp0 = sdesc_sw128(smem_u32(sP), 16, 1024);
       constexpr uint64_t kTileD = kTileBytes >> 4;  // descriptor units (16 B)
       const uint64_t halo = (uint64_t)((kTile - Wr) * 128) >> 4;
-      int n = 0, prev = -1;
+      struct Rec {
+        int it, bi, qs, prev, cur, prev_idx, cur_idx;
+        bool has_prev, next_is_succ;
+      };
+      int n = 0, carry = -1, carry_idx = 0;  // K/V load index; halo slot carried over
       bool ok = true;
-      for (int u = u0, it = 0; u < u1 && ok; ++u, ++it) {
+      // slots of tile u (in load order) and its waits before QKᵀ
+      auto make = [&](int u, int it) {
+        Rec r;
         const int j = u % nT;
-        const int bi = p.nbuf == 2 ? (it & 1) : 0;
-        if (it >= p.nbuf)
-          ok = mbar_wait(&bar->tmem_empty[bi], ((it / p.nbuf) - 1) & 1, err, kErrFwd | 3);
-        if (ok && j >= 1 && u == u0) {
-          prev = n % kKVSlots;
-          ok = mbar_wait(&bar->k_ready[prev], (n / kKVSlots) & 1, err, kErrFwd | 4);
+        r.it = it;
+        r.bi = p.nbuf == 2 ? (it & 1) : 0;
+        r.qs = it % kQSlots;
+        r.has_prev = j >= 1;
+        r.prev = carry;
+        r.prev_idx = carry_idx;
+        if (r.has_prev && u == u0) {  // halo tile loaded only at the start of a range
+          r.prev = n % NKV;
+          r.prev_idx = n;
           ++n;
         }
-        const int cur = n % kKVSlots;
-        ok = ok && mbar_wait(&bar->k_ready[cur], (n / kKVSlots) & 1, err, kErrFwd | 5);
+        r.cur = n % NKV;
+        r.cur_idx = n;
         ++n;
-        const int qs = it % kQSlots;
-        ok = ok && mbar_wait(&bar->q_ready[qs], (it / kQSlots) & 1, err, kErrFwd | 6);
-        if (!ok) break;
+        r.next_is_succ = (u + 1 < u1) && ((u + 1) % nT != 0);
+        carry = r.next_is_succ ? r.cur : -1;
+        carry_idx = r.cur_idx;
+        return r;
+      };
+      auto issue_s = [&](const Rec& r) {
+        if (r.it >= p.nbuf)
+          ok = ok && mbar_wait(&bar->tmem_empty[r.bi], ((r.it / p.nbuf) - 1) & 1, err, kErrFwd | 3);
+        if (r.has_prev)
+          ok = ok && mbar_wait(&bar->k_ready[r.prev], (r.prev_idx / NKV) & 1, err, kErrFwd | 4);
+        ok = ok && mbar_wait(&bar->k_ready[r.cur], (r.cur_idx / NKV) & 1, err, kErrFwd | 5);
+        ok = ok && mbar_wait(&bar->q_ready[r.qs], (r.it / kQSlots) & 1, err, kErrFwd | 6);
+        if (!ok) return;
         tc_fence_after();
-        const bool has_prev = j >= 1;
-        const uint32_t s_col = tbase + bi * 256;
-        const uint32_t o_col = s_col + p.ncols;
-        const uint64_t dq = dq0 + qs * kTileD;
-        if (has_prev) {
-          const uint64_t dk = dk0 + prev * kTileD + halo;
+        const uint32_t s_col = tbase + r.bi * 256;
+        const uint64_t dq = dq0 + r.qs * kTileD;
+        if (r.has_prev) {
+          const uint64_t dk = dk0 + r.prev * kTileD + halo;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) mma_bf16(s_col, dq + 2 * kk, dk + 2 * kk, id_s1, kk > 0);
         }
         {
-          const uint64_t dk = dk0 + cur * kTileD;
+          const uint64_t dk = dk0 + r.cur * kTileD;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) mma_bf16(s_col + Wr, dq + 2 * kk, dk + 2 * kk, id_s2, kk > 0);
         }
-        mma_commit(&bar->s_full[bi]);
-        mma_commit(&bar->q_empty[qs]);
-        ok = mbar_wait(&bar->p_full, it & 1, err, kErrFwd | 7);
-        if (!ok) break;
+        mma_commit(&bar->s_full[r.bi]);
+        mma_commit(&bar->q_empty[r.qs]);
+        // K of the halo tile is done; the current tile's K still serves as
+        // the next tile's halo unless that tile starts a new sequence
+        if (r.has_prev) mma_commit(&bar->k_empty[r.prev]);
+        if (!r.next_is_succ) mma_commit(&bar->k_empty[r.cur]);
+      };
+      auto issue_o = [&](const Rec& r) {
+        // V first (loaded long before, so these waits overlap the epilogue)
+        if (r.has_prev)
+          ok = ok && mbar_wait(&bar->v_full[r.prev], (r.prev_idx / NKV) & 1, err, kErrFwd | 18);
+        ok = ok && mbar_wait(&bar->v_full[r.cur], (r.cur_idx / NKV) & 1, err, kErrFwd | 19);
+        ok = ok && mbar_wait(&bar->p_full, r.it & 1, err, kErrFwd | 7);
+        if (!ok) return;
         tc_fence_after();
+        const uint32_t o_col = tbase + r.bi * 256 + p.ncols;
         uint32_t acc = 0;
-        if (has_prev) {
-          const uint64_t dv = dv0 + prev * kTileD + halo;
+        if (r.has_prev) {
+          const uint64_t dv = dv0 + r.prev * kTileD + halo;
           for (int kk = 0; kk < Wr / 16; ++kk) {
             mma_bf16(o_col, dp0 + (kk >> 2) * kTileD + (kk & 3) * 2, dv + kk * 128, id_o, acc);
             acc = 1;
           }
         }
         {
-          const uint64_t dv = dv0 + cur * kTileD;
+          const uint64_t dv = dv0 + r.cur * kTileD;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const int pk = Wr / 16 + kk;
@@ -310,15 +358,41 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc = 1;
           }
         }
-        mma_commit(&bar->o_full[bi]);
-        if (has_prev) mma_commit(&bar->kv_empty[prev]);
-        const bool next_is_succ = (u + 1 < u1) && ((u + 1) % nT != 0);
-        if (next_is_succ) {
-          prev = cur;
-        } else {
-          mma_commit(&bar->kv_empty[cur]);
-          prev = -1;
+        mma_commit(&bar->o_full[r.bi]);
+        if (r.has_prev) mma_commit(&bar->v_empty[r.prev]);
+        if (!r.next_is_succ) mma_commit(&bar->v_empty[r.cur]);
+      };
+      // The output tile of tile it, staged by the epilogue, is stored from
+      // here (this thread would otherwise idle until the next P is ready):
+      // issued before the next P·V, the staging buffer handed back after it,
+      // by when the store has long finished reading it.
+      auto store_o = [&](int u, int it) {
+        ok = ok && mbar_wait(&bar->ostage_full, it & 1, err, kErrFwd | 14);
+        if (!ok) return;
+        const int bh = u / nT, j = u % nT;
+        tma_store_4d(&tmo, sO, 0, bh % p.H, j * kTile, bh / p.H);
+        bulk_commit_group();
+      };
+      auto release_o = [&]() {
+        bulk_wait_group_read0();
+        mbar_arrive(&bar->ostage_empty);
+      };
+      if (u0 < u1) {
+        Rec cur = make(u0, 0);
+        issue_s(cur);
+        for (int u = u0, it = 0; u < u1 && ok; ++u, ++it) {
+          Rec nxt{};
+          const bool more = u + 1 < u1;
+          if (more) nxt = make(u + 1, it + 1);
+          if (p.nbuf == 2 && more) issue_s(nxt);  // QKᵀ one tile ahead
+          if (it >= 1) store_o(u - 1, it - 1);     // staged while P(it) was formed
+          issue_o(cur);
+          if (it >= 1 && ok) release_o();
+          if (p.nbuf != 2 && more) issue_s(nxt);
+          cur = nxt;
         }
+        if (ok) store_o(u1 - 1, u1 - u0 - 1);
+        bulk_wait_group0();
       }
     }
   } else if (warp < 4 || warp >= 12) {
@@ -334,8 +408,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int j = u % nT;
       const int qs = it % kQSlots;
       if (j >= 1 && u == u0) {  // halo key tile loaded only at the start of a range
-        const int s = n % kKVSlots;
-        ok = mbar_wait(&bar->kv_full[s], (n / kKVSlots) & 1, err, kErrFwd | 8);
+        const int s = n % NKV;
+        ok = mbar_wait(&bar->k_full[s], (n / NKV) & 1, err, kErrFwd | 8);
         if (!ok) break;
         if (p.theta) rope_tiles(sK + s * kTileBytes, nullptr, (j - 1) * kTile, p.T, th, tid);
         fence_proxy_async_smem();
@@ -343,9 +417,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&bar->k_ready[s]);
         ++n;
       }
-      const int s = n % kKVSlots;
+      const int s = n % NKV;
       ok = mbar_wait(&bar->q_full[qs], (it / kQSlots) & 1, err, kErrFwd | 9);
-      ok = ok && mbar_wait(&bar->kv_full[s], (n / kKVSlots) & 1, err, kErrFwd | 8);
+      ok = ok && mbar_wait(&bar->k_full[s], (n / NKV) & 1, err, kErrFwd | 8);
       if (!ok) break;
       if (p.theta) rope_tiles(sQ + qs * kTileBytes, sK + s * kTileBytes, j * kTile, p.T, th, tid);
       fence_proxy_async_smem();
@@ -372,6 +446,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int my_hi = hf == 0 ? ch_lo + (nch + 1) / 2 : ch_hi + 1;
     const uint32_t p_base = smem_u32(sP);
     const uint32_t o_base = smem_u32(sO);
+    // τ staging rows (exported τ): row i holds τ[t, 0..W) as bf16
+    __nv_bfloat16* const tau_s = reinterpret_cast<__nv_bfloat16*>(smem + L.tau);
+    const int tau_pitch = p.tstride / 2;  // elements per staging row
     bool ok = true;
     for (int u = u0, it = 0; u < u1 && ok; ++u, ++it) {
       const int bh = u / nT, j = u % nT;
@@ -379,6 +456,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int bi = p.nbuf == 2 ? (it & 1) : 0;
       const uint32_t par = (it / p.nbuf) & 1;
       ok = mbar_wait(&bar->s_full[bi], par, err, kErrFwd | 10);
+      // the τ rows of the previous tile must have been copied out
+      if constexpr (kTau) {
+        if (ok && it >= 1) ok = mbar_wait(&bar->tau_free, (it - 1) & 1, err, kErrFwd | 20);
+      }
       if (!ok) break;
       __syncwarp();  // tcgen05.ld below is .sync.aligned
       tc_fence_after();
@@ -389,9 +470,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int c_min = Wr - j * kTile;  // s ≥ 0  ⇔  c ≥ c_min
       float mass = 0.f;
       const float* bias_row = nullptr;
-      __nv_bfloat16* tau_row = nullptr;
       if constexpr (kBias) bias_row = p.bias + b * p.bs0 + (long long)min(t, p.T - 1) * p.bs1;
-      if constexpr (kTau) tau_row = p.tau + ((long long)(b * p.T + min(t, p.T - 1)) * p.H + h) * W;
+      __nv_bfloat16* const tau_row = tau_s + i * tau_pitch;
 
       auto process16 = [&](int ch, const uint32_t* r) {
         uint32_t pk[8];
@@ -413,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mass += tau;
             tv[z] = tau;
             if constexpr (kTau) {
-              if (row_ok && in_win) tau_row[w] = __float2bfloat16_rn(tau);
+              if (in_win) tau_row[w] = __float2bfloat16_rn(tau);
             }
           }
           pk[e2 >> 1] = pack_bf16(tv[0], tv[1]);
@@ -443,6 +523,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->mass_ready[it & 1]);
       ok = mbar_wait(&bar->mass_ready[it & 1], (it >> 1) & 1, err, kErrFwd | 12);
+      if constexpr (kTau) {
+        // every warp is past its τ writes: copy 16 whole rows out, each row
+        // contiguous in [B,T,H,W] (16-byte stores when W is a multiple of 8)
+        if (ok) {
+          const int r0 = e * 16;
+          __nv_bfloat16* const gbase = p.tau + ((long long)b * p.T * p.H + h) * W;
+          const long long gpitch = (long long)p.H * W;  // elements between rows t, t+1
+          if ((W & 7) == 0) {
+            const int vpr = W / 8;
+            for (int idx = lane; idx < 16 * vpr; idx += 32) {
+              const int rr = r0 + idx / vpr, cc = idx - (idx / vpr) * vpr;
+              const int tt = j * kTile + rr;
+              if (tt < p.T) {
+                uint32_t a0, a1, a2, a3;
+                ld_shared_v4(smem_u32(tau_s + rr * tau_pitch) + cc * 16, a0, a1, a2, a3);
+                *reinterpret_cast<uint4*>(gbase + tt * gpitch + cc * 8) = make_uint4(a0, a1, a2, a3);
+              }
+            }
+          } else {
+            for (int idx = lane; idx < 16 * W; idx += 32) {
+              const int rr = r0 + idx / W, cc = idx - (idx / W) * W;
+              const int tt = j * kTile + rr;
+              if (tt < p.T) gbase[tt * gpitch + cc] = tau_s[rr * tau_pitch + cc];
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar->tau_free);
+        }
+      }
       ok = ok && mbar_wait(&bar->o_full[bi], par, err, kErrFwd | 11);
       if (!ok) break;
       __syncwarp();
@@ -456,8 +565,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->tmem_empty[bi]);
-      // stage the bf16 tile for one TMA store (the previous store must have
-      // finished reading the staging buffer)
+      // stage the bf16 tile for one TMA store (issued by the MMA thread); the
+      // previous store must have finished reading the staging buffer
       if (it > 0) ok = mbar_wait(&bar->ostage_empty, (it - 1) & 1, err, kErrFwd | 13);
       if (!ok) break;
 #pragma unroll
@@ -472,18 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->ostage_full);
-      if (warp == 4 && lane == 0) {
-        ok = mbar_wait(&bar->ostage_full, it & 1, err, kErrFwd | 14);
-        if (ok) {
-          tma_store_4d(&tmo, sO, 0, h, j * kTile, b);
-          bulk_commit_group();
-          bulk_wait_group_read0();
-          mbar_arrive(&bar->ostage_empty);
-        }
-      }
-      __syncwarp();
     }
-    if (warp == 4 && lane == 0) bulk_wait_group0();
   }
 
   tc_fence_before();
@@ -494,10 +592,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <bool kBias, bool kTau>
+template <bool kBias, bool kTau, int kNKV>
 cudaError_t launch_variant(const CUtensorMap* m, const FwdTC& a, size_t smem, int grid,
                            cudaStream_t st) {
-  auto kern = tc_fwd_kernel<kBias, kTau>;
+  auto kern = tc_fwd_kernel<kBias, kTau, kNKV>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, smem, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], a);
@@ -537,6 +635,12 @@ cudaError_t launch_tc_fwd(const FwdP& p, cudaStream_t st, int* launches) {
   a.row_mass = p.row_mass;
   a.store_rot = (a.theta && p.q_rot && p.k_rot) ? 1 : 0;
   a.err = p.err;
+  // τ export stages whole rows in shared memory (+16 bytes per row keeps the
+  // rows' 2-byte writes off one bank); the K/V ring drops to two slots when
+  // three would not leave room for them
+  a.tstride = p.tau ? p.W * 2 + 16 : 0;
+  a.nkv = 3;
+  if (fwd_layout(a.pblocks, 3, a.tstride).total + 1024 > kMaxSmemPerBlock) a.nkv = 2;
   CUtensorMap m[6];
   const long long ob = (long long)p.T * p.H * kHD, ot = (long long)p.H * kHD, oh = kHD;
   if (!make_tmap_bthd(&m[0], p.q.p, p.q.sb, p.q.st, p.q.sh, p.B, p.T, p.H, kTile) ||
@@ -552,15 +656,21 @@ cudaError_t launch_tc_fwd(const FwdP& p, cudaStream_t st, int* launches) {
     m[4] = m[3];  // unused
     m[5] = m[3];
   }
-  const Layout L = fwd_layout(a.pblocks);
+  const Layout L = fwd_layout(a.pblocks, a.nkv, a.tstride);
   const size_t smem = L.total + 1024;
+  if (smem > kMaxSmemPerBlock) return cudaErrorInvalidConfiguration;
   const int grid = std::min(num_sms(), a.total);
   *launches = 1;
   const bool has_bias = p.bias != nullptr, has_tau = p.tau != nullptr;
-  if (has_bias && has_tau) return launch_variant<true, true>(m, a, smem, grid, st);
-  if (has_bias) return launch_variant<true, false>(m, a, smem, grid, st);
-  if (has_tau) return launch_variant<false, true>(m, a, smem, grid, st);
-  return launch_variant<false, false>(m, a, smem, grid, st);
+  const bool two = a.nkv == 2;  // only τ export narrows the ring
+  if (has_bias && has_tau)
+    return two ? launch_variant<true, true, 2>(m, a, smem, grid, st)
+               : launch_variant<true, true, 3>(m, a, smem, grid, st);
+  if (has_tau)
+    return two ? launch_variant<false, true, 2>(m, a, smem, grid, st)
+               : launch_variant<false, true, 3>(m, a, smem, grid, st);
+  if (has_bias) return launch_variant<true, false, 3>(m, a, smem, grid, st);
+  return launch_variant<false, false, 3>(m, a, smem, grid, st);
 }
 
 }  // namespace bozo
