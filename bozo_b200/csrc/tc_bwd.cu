@@ -584,6 +584,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (band[ss]) {
           uint32_t R[32];  // Sᵀ | dPᵀ of this 16-column piece
           const uint32_t col = tbase + lane_off + 128 * b + 32 * hf + 16 * ss;
+          // optional per-element inputs (bias, τ cotangent) are gathered
+          // before the TMEM load so their global latency overlaps it (the
+          // TMEM load is a memory-clobbering asm the loads cannot move past);
+          // across the warp each load reads 32 consecutive window slots of
+          // one query row
+          // Element e of the piece is query t = tq0+cq0+e at window slot
+          // w = W − (128c + cq0 + e − r): one base address per piece, then a
+          // constant step per element; out-of-band elements load nothing.
+          float gb[16], gd[16];
+          if constexpr (kBias || kDTau) {
+            const int t0 = tq0 + cq0, w0 = W - (kTile * c + cq0 - r);
+            const float* b0 = nullptr;
+            const __nv_bfloat16* d0 = nullptr;
+            long long bstep = 0, dstep = 0;
+            if constexpr (kBias) {
+              b0 = p.bias + bb * p.bs0 + (long long)t0 * p.bs1 + (long long)w0 * p.bs2;
+              bstep = p.bs1 - p.bs2;
+            }
+            if constexpr (kDTau) {
+              d0 = p.dtau + (((long long)bb * p.T + t0) * H + h) * W + w0;
+              dstep = (long long)H * W - 1;
+            }
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const bool valid = (unsigned)(e - lo[ss]) < (unsigned)cnt[ss];
+              if constexpr (kBias) gb[e] = valid ? 0.5f * __ldg(b0 + e * bstep) : 0.f;
+              if constexpr (kDTau) gd[e] = valid ? p.ds_scale * __bfloat162float(d0[e * dstep]) : 0.f;
+            }
+          }
           tmem_ld16x2_wait(col, col + 64, R);
 #pragma unroll
           for (int e4 = 0; e4 < 16; e4 += 4) {
@@ -600,15 +629,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               const bool valid = (unsigned)(e - lo[ss]) < (unsigned)cnt[ss];
               float x = __uint_as_float(R[e]) * p.half_inv_scale;
               float dt = fmaf(ad[z], __uint_as_float(R[16 + e]), bd[z]);
-              if constexpr (kBias || kDTau) {
-                const int q = cq0 + e;
-                const int tc = valid ? tq0 + q : 0;
-                const int wc = valid ? W - (kTile * c + q - r) : 0;
-                if constexpr (kBias)
-                  x = fmaf(0.5f, __ldg(p.bias + bb * p.bs0 + (long long)tc * p.bs1 + (long long)wc * p.bs2), x);
-                if constexpr (kDTau)
-                  dt = fmaf(__bfloat162float(p.dtau[(((long long)bb * p.T + tc) * H + h) * W + wc]), p.ds_scale, dt);
-              }
+              if constexpr (kBias) x += gb[e];
+              if constexpr (kDTau) dt += gd[e];
               const float th = tanh_approx(x);
               pv[z] = valid ? fmaf(ah[z], th, ah[z]) : 0.f;
               dv[z] = valid ? dt * fmaf(-th, th, 1.f) : 0.f;
