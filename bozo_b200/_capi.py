@@ -1,4 +1,5 @@
-"""ctypes binding of the C ABI declared in ``include/bozo_tension.h``.
+"""ctypes binding of the C ABI declared in ``include/bozo_tension.h`` and
+``include/bozo_tau_aux.h``.
 
 The structures below mirror the header field by field; ``tests/test_abi.py``
 compiles a C probe with gcc and checks every size and offset, and checks
@@ -27,7 +28,9 @@ EXPORTED = (
     "bozo_tension_last_launches", "bozo_status_string",
     "bozo_tension_abi_version", "bozo_tension_last_cuda_error",
     "bozo_tension_bwd_noalloc",
+    "bozo_tau_aux_workspace", "bozo_tau_aux_fwd", "bozo_tau_aux_bwd",
 )
+TAU_AUX_MAX_LAYERS = 64  # BOZO_TAU_AUX_MAX_LAYERS
 
 
 class Tensor4(C.Structure):
@@ -65,6 +68,24 @@ class BwdArgs(C.Structure):
     ]
 
 
+class TauAuxFwdArgs(C.Structure):
+    _fields_ = [
+        ("n_layers", C.c_int32), ("dtype", C.c_int32),
+        ("B", C.c_int32), ("T", C.c_int32), ("H", C.c_int32), ("W", C.c_int32),
+        ("tau", C.c_void_p * TAU_AUX_MAX_LAYERS), ("stats", C.c_void_p),
+        ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+    ]
+
+
+class TauAuxBwdArgs(C.Structure):
+    _fields_ = [
+        ("n_layers", C.c_int32), ("dtype", C.c_int32),
+        ("B", C.c_int32), ("T", C.c_int32), ("H", C.c_int32), ("W", C.c_int32),
+        ("tau", C.c_void_p * TAU_AUX_MAX_LAYERS), ("d_stats", C.c_void_p),
+        ("d_tau", C.c_void_p * TAU_AUX_MAX_LAYERS),
+    ]
+
+
 _lib = None
 _ext = None
 _lock = threading.Lock()
@@ -97,6 +118,12 @@ def lib():
                 L.bozo_status_string.restype = C.c_char_p
                 L.bozo_tension_abi_version.restype = C.c_int
                 L.bozo_tension_last_cuda_error.restype = C.c_char_p
+                L.bozo_tau_aux_workspace.argtypes = [C.POINTER(TauAuxFwdArgs)]
+                L.bozo_tau_aux_workspace.restype = C.c_size_t
+                L.bozo_tau_aux_fwd.argtypes = [C.POINTER(TauAuxFwdArgs), C.c_void_p]
+                L.bozo_tau_aux_fwd.restype = C.c_int
+                L.bozo_tau_aux_bwd.argtypes = [C.POINTER(TauAuxBwdArgs), C.c_void_p]
+                L.bozo_tau_aux_bwd.restype = C.c_int
                 _lib = L
     return _lib
 

@@ -1,0 +1,108 @@
+"""Fused τ-field consumer: the reference's three τ regularisers from one pass
+over the exported τ fields.
+
+``tension_aux_losses(all_tensions, window_groups)`` returns the values of
+``tension_diversity_loss`` (model.py:498-532), ``constraint_consistency_loss``
+(model.py:535-577) and ``tension_entropy_loss`` (model.py:580-611) for the
+list of per-layer τ fields a ``return_all`` forward yields, with gradients
+w.r.t. every field.  The per-row work — row sums, entropies of the
+normalised rows, the transitivity hinges, the mean-τ band penalties — runs in
+``bozo_tau_aux_fwd`` (one read of every field, per-layer statistics) and
+its cotangent in ``bozo_tau_aux_bwd`` (one read and one write per field,
+``include/bozo_tau_aux.h``).  What remains here are the reference's scalar
+tails over those statistics (group means, ``relu(log W − ·)``, the averages),
+so their gradient flows back through ordinary autograd into the statistics'
+cotangent, which the backward kernel reads on the device.
+
+The statistics are accumulated in fp32/fp64 from the stored τ values; the
+reference's framework ops round some intermediates to bf16 under autocast,
+so bf16 results agree within bf16 rounding and fp32 results within fp32
+summation-order rounding.  CUDA tensors only: there is no CPU path here.
+"""
+from __future__ import annotations
+
+import math
+from collections import defaultdict
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+from torch import Tensor
+
+from . import _capi
+
+__all__ = ["tau_field_stats", "tension_aux_losses"]
+
+
+class _TauStatsFn(torch.autograd.Function):
+    """[L, 3] fp32 statistics of L equally shaped τ fields (see the header)."""
+
+    @staticmethod
+    def forward(ctx, *taus: Tensor) -> Tensor:
+        ctx.save_for_backward(*taus)
+        return _capi.ext().tau_aux_fwd(list(taus))
+
+    @staticmethod
+    def backward(ctx, d_stats: Tensor):
+        taus = ctx.saved_tensors
+        return tuple(_capi.ext().tau_aux_bwd(list(taus), d_stats.float().contiguous()))
+
+
+def tau_field_stats(taus: Sequence[Tensor]) -> Tensor:
+    """Per-layer statistics ``[L, 3]``: mean row entropy of ``τ/(Στ+1e-8)``,
+    mean transitivity hinge, mean-τ band penalty (``bozo_tau_aux_fwd``).
+    Fields of different shapes or dtypes are batched per shape."""
+    if not taus:
+        raise ValueError("tau_field_stats: no τ fields")
+    for t in taus:
+        if not t.is_cuda:
+            raise RuntimeError("tau_field_stats: τ fields must be CUDA tensors "
+                               "(the fused τ consumer has no CPU path)")
+    by_kind: Dict[tuple, List[int]] = defaultdict(list)
+    for i, t in enumerate(taus):
+        by_kind[(tuple(t.shape), t.dtype)].append(i)
+    if len(by_kind) == 1:
+        return _TauStatsFn.apply(*[t.contiguous() for t in taus])
+    rows: List[Optional[Tensor]] = [None] * len(taus)
+    for idx in by_kind.values():
+        st = _TauStatsFn.apply(*[taus[i].contiguous() for i in idx])
+        for j, i in enumerate(idx):
+            rows[i] = st[j]
+    return torch.stack(rows)
+
+
+def _consistency_applies(shape: torch.Size) -> bool:
+    """model.py:551-562: layers with W < 3, T < 3 or no live slot are skipped."""
+    _, T, _, W = shape
+    if W < 3 or T < 3:
+        return False
+    return min(W - 2, 4) + 1 < T
+
+
+def tension_aux_losses(all_tensions: Sequence[Tensor],
+                       window_groups: Optional[dict] = None) -> Tuple[Tensor, Tensor, Tensor]:
+    """(diversity, consistency, entropy) of model.py:498-611 for the per-layer
+    τ fields, as fp32 scalars with gradients w.r.t. every field."""
+    if not all_tensions:
+        z = torch.tensor(0.0)
+        return z, z, z
+    stats = tau_field_stats(all_tensions)
+    # diversity (model.py:511-532): per window group, relu(log W − mean entropy)
+    if window_groups is not None:
+        groups = {W: list(idx) for W, idx in window_groups.items()}
+    else:
+        groups = defaultdict(list)
+        for i, t in enumerate(all_tensions):
+            groups[t.shape[-1]].append(i)
+    div = stats.new_zeros(())
+    for W, idx in groups.items():
+        # every field of a group has N = B·T·H rows, so the mean of the
+        # per-layer means is the mean over the stacked rows
+        ent = stats[idx, 0].mean()
+        div = div + torch.relu(math.log(W) - ent)
+    div = div / max(len(groups), 1)
+    # consistency (model.py:548-577): average over the layers that apply
+    live = [i for i, t in enumerate(all_tensions) if _consistency_applies(t.shape)]
+    cons = stats[live, 1].sum() / max(len(live), 1) if live else stats.new_zeros(())
+    # entropy regulariser (model.py:597-611): average over all layers
+    ent_loss = stats[:, 2].sum() / len(all_tensions)
+    return div, cons, ent_loss

@@ -8,6 +8,7 @@
 
 #include "common.cuh"
 #include "tc.cuh"
+#include "tc_host.cuh"
 
 namespace bozo {
 namespace {
@@ -119,6 +120,19 @@ int check_t4(const bozo_tensor4& t) {
 }
 
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Shared checks of the two τ-consumer argument blocks.
+template <typename A>
+int check_aux(const A* a) {
+  if (!a) return BOZO_ERR_NULL;
+  if (a->n_layers < 1 || a->n_layers > BOZO_TAU_AUX_MAX_LAYERS) return BOZO_ERR_BAD_SHAPE;
+  if (a->B <= 0 || a->T <= 0 || a->H <= 0 || a->W <= 0) return BOZO_ERR_BAD_SHAPE;
+  if ((long long)a->B * a->T * a->H > 0x7fffffffLL) return BOZO_ERR_UNSUPPORTED;  // rows < 2^31
+  if (!dtype_ok(a->dtype)) return BOZO_ERR_BAD_DTYPE;
+  for (int i = 0; i < a->n_layers; ++i)
+    if (!a->tau[i]) return BOZO_ERR_NULL;
+  return BOZO_OK;
+}
 
 }  // namespace
 }  // namespace bozo
@@ -290,6 +304,39 @@ int bozo_tension_bwd_noalloc(const bozo_tension_bwd_args* a, void* stream) {
   local.workspace = scratch;
   local.workspace_bytes = BOZO_NOALLOC_SCRATCH_BYTES;
   return bozo_tension_bwd(&local, stream);
+}
+
+size_t bozo_tau_aux_workspace(const bozo_tau_aux_fwd_args* a) {
+  if (check_aux(a) != BOZO_OK) return 0;
+  const AuxShape s = aux_shape(a->B, a->T, a->H, a->W);
+  return round256((size_t)a->n_layers * aux_blocks(s, a->n_layers, num_sms()) * 3 * sizeof(float));
+}
+
+int bozo_tau_aux_fwd(const bozo_tau_aux_fwd_args* a, void* stream) {
+  int st = check_aux(a);
+  if (st) return st;
+  if (!a->stats) return BOZO_ERR_NULL;
+  cudaError_t e = bind_device(a->tau[0]);
+  if (e != cudaSuccess) return cuda_fail(e);
+  const size_t need = bozo_tau_aux_workspace(a);
+  if (!a->workspace || a->workspace_bytes < need) return BOZO_ERR_WORKSPACE;
+  const AuxShape s = aux_shape(a->B, a->T, a->H, a->W);
+  e = launch_tau_aux_fwd(*a, aux_blocks(s, a->n_layers, num_sms()), static_cast<float*>(a->workspace),
+                         static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
+}
+
+int bozo_tau_aux_bwd(const bozo_tau_aux_bwd_args* a, void* stream) {
+  int st = check_aux(a);
+  if (st) return st;
+  if (!a->d_stats) return BOZO_ERR_NULL;
+  for (int i = 0; i < a->n_layers; ++i)
+    if (!a->d_tau[i]) return BOZO_ERR_NULL;
+  cudaError_t e = bind_device(a->tau[0]);
+  if (e != cudaSuccess) return cuda_fail(e);
+  const AuxShape s = aux_shape(a->B, a->T, a->H, a->W);
+  e = launch_tau_aux_bwd(*a, aux_blocks(s, a->n_layers, num_sms()), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
 }
 
 int bozo_tension_poll_error(void* stream) {

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "bozo_tau_aux.h"
 #include "bozo_tension.h"
 
 namespace bozo {
@@ -96,5 +97,40 @@ cudaError_t launch_simt_fwd(const FwdP& p, cudaStream_t st, int* launches);
 cudaError_t launch_simt_bwd(const BwdP& p, cudaStream_t st, int* launches);
 // Write RoPE(q), RoPE(k) into p.q_rot / p.k_rot (dtype of q / k).
 cudaError_t launch_rope_copy(const FwdP& p, cudaStream_t st, int* launches);
+
+// Fused τ-field consumer (tau_aux.cu).  Shape of one call's fields and the
+// consistency extents: m = min(W−2, 4) slots (0: the layer is skipped),
+// t_out queries per slot.
+// Unsigned 32-bit division by an invariant divisor as a multiply-high and
+// two shifts (Granlund & Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994, Fig. 4.1): l = ⌈log2 d⌉,
+// m = ⌊2^32·(2^l − d)/d⌋ + 1, q = (t + ((n − t) >> min(l,1))) >> max(l−1,0)
+// with t = mulhi(m, n); exact for every 32-bit n.
+struct FastDiv {
+  uint32_t m, s1, s2;
+};
+inline FastDiv make_fastdiv(uint32_t d) {
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;
+  const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
+  return FastDiv{(uint32_t)m, l < 1 ? l : 1u, l > 1 ? l - 1 : 0u};
+}
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, FastDiv f) {
+  const uint32_t t = __umulhi(f.m, n);
+  return (t + ((n - t) >> f.s1)) >> f.s2;
+}
+
+struct AuxShape {
+  int B, T, H, W;
+  long long N;  // rows B·T·H (< 2^31)
+  int m, t_out;
+  float inv_n, inv_w, inv_cons;
+  FastDiv div_h, div_t;  // row → (b·T + t) → b
+};
+AuxShape aux_shape(int B, int T, int H, int W);
+int aux_blocks(const AuxShape& s, int n_layers, int sms);
+cudaError_t launch_tau_aux_fwd(const bozo_tau_aux_fwd_args& a, int nblk, float* partial,
+                               cudaStream_t st);
+cudaError_t launch_tau_aux_bwd(const bozo_tau_aux_bwd_args& a, int nblk, cudaStream_t st);
 
 }  // namespace bozo

@@ -12,9 +12,11 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <algorithm>
 #include <stdexcept>
 #include <string>
 
+#include "bozo_tau_aux.h"
 #include "bozo_tension.h"
 
 namespace {
@@ -175,10 +177,83 @@ std::vector<at::Tensor> tension_bwd(const at::Tensor& q, const at::Tensor& k, co
   return {dq, dk, dv};
 }
 
+// τ fields of one τ-consumer call: same shape, dtype and device, contiguous.
+void check_fields(const std::vector<at::Tensor>& taus) {
+  if (taus.empty()) throw std::invalid_argument("tau_aux: no τ fields");
+  const at::Tensor& t0 = taus[0];
+  for (const auto& t : taus) {
+    if (!t.is_cuda()) throw std::invalid_argument("tau_aux: τ fields must be CUDA tensors");
+    if (t.dim() != 4 || t.sizes() != t0.sizes() || t.scalar_type() != t0.scalar_type() ||
+        t.device() != t0.device())
+      throw std::invalid_argument("tau_aux: τ fields must share one [B,T,H,W] shape, dtype and device");
+    if (!t.is_contiguous()) throw std::invalid_argument("tau_aux: τ fields must be contiguous");
+  }
+}
+
+template <typename A>
+void fill_aux(A& a, const std::vector<at::Tensor>& taus, size_t i0, size_t n) {
+  const at::Tensor& t0 = taus[0];
+  a.n_layers = (int32_t)n;
+  a.dtype = dtype_code(t0.scalar_type());
+  a.B = (int32_t)t0.size(0);
+  a.T = (int32_t)t0.size(1);
+  a.H = (int32_t)t0.size(2);
+  a.W = (int32_t)t0.size(3);
+  for (size_t i = 0; i < n; ++i) a.tau[i] = taus[i0 + i].data_ptr();
+}
+
+// Per-layer statistics [L, 3] fp32 of the τ fields (bozo_tau_aux_fwd), in
+// chunks of BOZO_TAU_AUX_MAX_LAYERS fields.
+at::Tensor tau_aux_fwd(const std::vector<at::Tensor>& taus) {
+  check_fields(taus);
+  const c10::cuda::CUDAGuard guard(taus[0].device());
+  const auto stream = at::cuda::getCurrentCUDAStream(taus[0].device().index()).stream();
+  const int64_t L = (int64_t)taus.size();
+  at::Tensor stats = at::empty({L, 3}, taus[0].options().dtype(at::kFloat));
+  for (size_t i0 = 0; i0 < taus.size(); i0 += BOZO_TAU_AUX_MAX_LAYERS) {
+    const size_t n = std::min<size_t>(BOZO_TAU_AUX_MAX_LAYERS, taus.size() - i0);
+    bozo_tau_aux_fwd_args a{};
+    fill_aux(a, taus, i0, n);
+    a.stats = stats.data_ptr<float>() + 3 * i0;
+    const size_t ws_bytes = bozo_tau_aux_workspace(&a);
+    at::Tensor ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 1)},
+                              taus[0].options().dtype(at::kByte));
+    a.workspace = ws.data_ptr();
+    a.workspace_bytes = ws_bytes;
+    check(bozo_tau_aux_fwd(&a, stream), "bozo_tau_aux_fwd");
+  }
+  return stats;
+}
+
+// Cotangents of the τ fields from the cotangent [L, 3] of their statistics.
+std::vector<at::Tensor> tau_aux_bwd(const std::vector<at::Tensor>& taus, const at::Tensor& d_stats) {
+  check_fields(taus);
+  const int64_t L = (int64_t)taus.size();
+  if (d_stats.scalar_type() != at::kFloat || d_stats.numel() != 3 * L || !d_stats.is_contiguous() ||
+      d_stats.device() != taus[0].device())
+    throw std::invalid_argument("tau_aux: d_stats must be a contiguous fp32 [L,3] tensor on the fields' device");
+  const c10::cuda::CUDAGuard guard(taus[0].device());
+  const auto stream = at::cuda::getCurrentCUDAStream(taus[0].device().index()).stream();
+  std::vector<at::Tensor> out;
+  out.reserve(taus.size());
+  for (const auto& t : taus) out.push_back(at::empty_like(t));
+  for (size_t i0 = 0; i0 < taus.size(); i0 += BOZO_TAU_AUX_MAX_LAYERS) {
+    const size_t n = std::min<size_t>(BOZO_TAU_AUX_MAX_LAYERS, taus.size() - i0);
+    bozo_tau_aux_bwd_args a{};
+    fill_aux(a, taus, i0, n);
+    a.d_stats = d_stats.data_ptr<float>() + 3 * i0;
+    for (size_t i = 0; i < n; ++i) a.d_tau[i] = out[i0 + i].data_ptr();
+    check(bozo_tau_aux_bwd(&a, stream), "bozo_tau_aux_bwd");
+  }
+  return out;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "PyTorch binding of the bozo tension C ABI";
   m.def("tension_fwd", &tension_fwd, "forward through bozo_tension_fwd");
   m.def("tension_bwd", &tension_bwd, "backward through bozo_tension_bwd");
+  m.def("tau_aux_fwd", &tau_aux_fwd, "τ-field statistics through bozo_tau_aux_fwd");
+  m.def("tau_aux_bwd", &tau_aux_bwd, "τ-field cotangents through bozo_tau_aux_bwd");
 }

@@ -332,6 +332,18 @@ def tension_entropy_loss(all_tensions):
     return total / len(all_tensions)
 
 
+def aux_losses(all_tensions, window_groups=None):
+    """(diversity, consistency, entropy) as train.py:1083-1087 computes them.
+    CUDA τ fields go through the fused τ consumer (``bozo_b200.aux``: one
+    kernel pass over every field, one for the cotangent); the framework-op
+    formulas above serve the harness when it runs on CPU tensors."""
+    if all_tensions and all_tensions[0].is_cuda:
+        from .aux import tension_aux_losses
+        return tension_aux_losses(all_tensions, window_groups)
+    return (tension_diversity_loss(all_tensions, window_groups),
+            constraint_consistency_loss(all_tensions), tension_entropy_loss(all_tensions))
+
+
 @dataclass
 class TrainWeights:
     """train.py:135-141 defaults (the large preset leaves them unchanged)."""
@@ -371,7 +383,8 @@ def train_step(model, base_model: TensionLM, optimizer, inputs, targets,
                amp: bool = True):
     """One optimiser step of train.py:1040-1150 with grad_accum 1: bf16
     autocast forward (τ returned when aux losses are on), CE + the four aux
-    losses, backward, global-norm clip, AdamW step.  Returns the loss tensor
+    losses (the three τ terms through ``aux_losses``), backward, global-norm
+    clip, AdamW step.  Returns the loss tensor
     (not synchronised)."""
     weights = weights or TrainWeights()
     V = base_model.cfg.vocab_size
@@ -385,12 +398,12 @@ def train_step(model, base_model: TensionLM, optimizer, inputs, targets,
             logits, hidden, tensions = model(inputs), None, []
         loss = F.cross_entropy(logits.reshape(-1, V), targets.reshape(-1))
         if weights.aux_enabled and tensions:
+            div, cons, ent = aux_losses(tensions, base_model.window_groups)
             loss = (loss
                     + weights.w_closure * manifold_closure_loss(hidden)
-                    + weights.w_diversity * tension_diversity_loss(tensions,
-                                                                   base_model.window_groups)
-                    + weights.w_consistency * constraint_consistency_loss(tensions)
-                    + weights.w_entropy * tension_entropy_loss(tensions))
+                    + weights.w_diversity * div
+                    + weights.w_consistency * cons
+                    + weights.w_entropy * ent)
     loss.backward()
     nn.utils.clip_grad_norm_(base_model.parameters(), clip_grad)
     optimizer.step()

@@ -1,5 +1,5 @@
 """C-ABI checks that need no GPU: the library loads, exports every function
-``include/bozo_tension.h`` declares, and the ctypes mirror of every struct
+the headers under ``include/`` declare, and the ctypes mirror of every struct
 matches the C layout (sizes and offsets measured by a gcc-compiled probe)."""
 import ctypes as C
 import os
@@ -13,11 +13,19 @@ from bozo_b200 import _capi
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HEADER = os.path.join(ROOT, "include", "bozo_tension.h")
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("bozo_tension.h", "bozo_tau_aux.h")]
 
 
 def _declared_functions():
-    src = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(bozo_\w+)\s*\(", src, re.M)))
+    found = set()
+    for h in HEADERS:
+        src = open(h).read()
+        found |= set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(bozo_\w+)\s*\(", src, re.M))
+    return sorted(found)
+
+
+def test_every_header_is_covered():
+    assert sorted(os.listdir(os.path.join(ROOT, "include"))) == sorted(os.path.basename(h) for h in HEADERS)
 
 
 def test_library_exports_every_declared_symbol():
@@ -37,6 +45,7 @@ PROBE = r"""
 #include <stdio.h>
 #include <stddef.h>
 #include "bozo_tension.h"
+#include "bozo_tau_aux.h"
 #define O(T, f) printf(#T "." #f " %zu\n", offsetof(T, f))
 #define S(T) printf(#T " %zu\n", sizeof(T))
 int main(void) {
@@ -55,6 +64,11 @@ int main(void) {
   O(bozo_tension_bwd_args, d_tau); O(bozo_tension_bwd_args, grad_dtype);
   O(bozo_tension_bwd_args, dq); O(bozo_tension_bwd_args, workspace);
   O(bozo_tension_bwd_args, workspace_bytes);
+  S(bozo_tau_aux_fwd_args); O(bozo_tau_aux_fwd_args, W); O(bozo_tau_aux_fwd_args, tau);
+  O(bozo_tau_aux_fwd_args, stats); O(bozo_tau_aux_fwd_args, workspace);
+  O(bozo_tau_aux_fwd_args, workspace_bytes);
+  S(bozo_tau_aux_bwd_args); O(bozo_tau_aux_bwd_args, tau); O(bozo_tau_aux_bwd_args, d_stats);
+  O(bozo_tau_aux_bwd_args, d_tau);
   return 0;
 }
 """
@@ -68,7 +82,9 @@ def test_struct_layout_matches_header():
         subprocess.run(["gcc", "-I", os.path.dirname(HEADER), c, "-o", exe], check=True)
         lines = subprocess.run([exe], check=True, capture_output=True, text=True).stdout.split("\n")
     names = {"bozo_tensor4": _capi.Tensor4, "bozo_tension_fwd_args": _capi.FwdArgs,
-             "bozo_tension_bwd_args": _capi.BwdArgs}
+             "bozo_tension_bwd_args": _capi.BwdArgs,
+             "bozo_tau_aux_fwd_args": _capi.TauAuxFwdArgs,
+             "bozo_tau_aux_bwd_args": _capi.TauAuxBwdArgs}
     for line in filter(None, lines):
         key, val = line.split()
         if "." in key:

@@ -58,7 +58,7 @@ def _model(name, case, device):
     return m.to(device)
 
 
-def _forward_losses(m, case, device, amp=False):
+def _forward_losses(m, case, device, amp=False, fused_aux=False):
     inputs = torch.from_numpy(case["inputs"]).to(device)
     targets = torch.from_numpy(case["targets"]).to(device)
     V = m.cfg.vocab_size
@@ -67,10 +67,14 @@ def _forward_losses(m, case, device, amp=False):
     with ctx:
         logits, hidden, tensions = m(inputs, return_all=True)
         ce = torch.nn.functional.cross_entropy(logits.reshape(-1, V), targets.reshape(-1))
-        parts = dict(ce=ce, closure=lm.manifold_closure_loss(hidden),
-                     diversity=lm.tension_diversity_loss(tensions, m.window_groups),
-                     consistency=lm.constraint_consistency_loss(tensions),
-                     entropy=lm.tension_entropy_loss(tensions))
+        if fused_aux:
+            div, cons, ent = lm.aux_losses(tensions, m.window_groups)
+        else:
+            div = lm.tension_diversity_loss(tensions, m.window_groups)
+            cons = lm.constraint_consistency_loss(tensions)
+            ent = lm.tension_entropy_loss(tensions)
+        parts = dict(ce=ce, closure=lm.manifold_closure_loss(hidden), diversity=div,
+                     consistency=cons, entropy=ent)
         loss = (ce + WEIGHTS.w_closure * parts["closure"] + WEIGHTS.w_diversity * parts["diversity"]
                 + WEIGHTS.w_consistency * parts["consistency"] + WEIGHTS.w_entropy * parts["entropy"])
     loss.backward()
@@ -116,6 +120,18 @@ def test_harness_matches_reference_model_gpu_fp32(golden_lm, name):
     case = golden_lm[name]
     m = _model(name, case, torch.device("cuda:0"))
     out = _forward_losses(m, case, torch.device("cuda:0"))
+    _check(m, case, *out, rtol=1e-4, atol=1e-5, grad_rtol=1e-3, grad_atol=1e-6)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", list(CFGS))
+def test_harness_fused_aux_losses_match_reference_model_gpu_fp32(golden_lm, name):
+    """The fused τ consumer in the training loss: same losses and parameter
+    gradients as the reference model's framework-op losses."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    case = golden_lm[name]
+    m = _model(name, case, torch.device("cuda:0"))
+    out = _forward_losses(m, case, torch.device("cuda:0"), fused_aux=True)
     _check(m, case, *out, rtol=1e-4, atol=1e-5, grad_rtol=1e-3, grad_atol=1e-6)
 
 

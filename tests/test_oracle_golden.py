@@ -78,3 +78,37 @@ def test_algorithmic_pairs_matches_mask():
         m = orc.window_mask(T, W)
         assert int(m.sum()) == orc.algorithmic_pairs(1, 1, T, W)
     assert orc.algorithmic_pairs(1, 1, 7, None) == 28
+
+
+# ───────────── τ-field consumer (model.py:498-611) ─────────────
+
+def _aux_case(name):
+    import ast
+    from tests.conftest import _load
+    c = _load("golden_aux.npz")[name]
+    n = len([k for k in c if k.startswith("tau")])
+    taus = [torch.from_numpy(c[f"tau{i}"]) for i in range(n)]
+    grads = [c[f"grad{i}"] for i in range(n)]
+    groups = ast.literal_eval(str(c["groups"]))
+    vals = (float(c["diversity"]), float(c["consistency"]), float(c["entropy"]))
+    return taus, grads, groups, vals
+
+
+def _aux_names():
+    from tests.conftest import _load
+    return sorted(_load("golden_aux.npz"))
+
+
+AUX_WEIGHTS = (1.0, 0.7, 0.3)  # tests/golden/make_golden_aux.py W_DIV, W_CONS, W_ENT
+
+
+@pytest.mark.parametrize("name", _aux_names())
+def test_aux_oracle_matches_reference(name):
+    from oracle import aux_oracle
+    taus, grads, groups, vals = _aux_case(name)
+    got, got_grads = aux_oracle.losses_and_grads(taus, groups, AUX_WEIGHTS)
+    # the reference ran in fp32: agree to fp32 round-off
+    np.testing.assert_allclose(got, vals, rtol=2e-6, atol=1e-7)
+    for g, r in zip(got_grads, grads):
+        scale = float(np.abs(r).max()) or 1.0
+        np.testing.assert_allclose(g.numpy(), r, rtol=1e-5, atol=1e-6 * scale)

@@ -1,0 +1,123 @@
+"""Fused τ-field consumer (``bozo_b200.aux``, ``include/bozo_tau_aux.h``).
+
+* GPU, fp32: the three losses and the gradients of their weighted sum match
+  the reference functions' own outputs (``tests/golden/golden_aux.npz``).
+* GPU, bf16 / fp32 at training widths and odd widths (vector and scalar
+  kernel paths): against the float64 oracle on the same τ values.
+* GPU: the statistics are bit-identical run to run (fixed-order reduction).
+* CPU: CUDA-only — CPU fields raise instead of falling back.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import aux_oracle
+from tests.test_oracle_golden import AUX_WEIGHTS, _aux_case, _aux_names
+
+
+def _close(got, ref, rtol, atol_rel, what):
+    g = got.detach().double().cpu().numpy()
+    r = np.asarray(ref, dtype=np.float64)
+    scale = float(np.abs(r).max()) or 1.0
+    np.testing.assert_allclose(g, r, rtol=rtol, atol=atol_rel * scale, err_msg=what)
+
+
+def _fused(taus, groups, weights=AUX_WEIGHTS):
+    from bozo_b200 import aux
+    xs = [t.detach().clone().requires_grad_(True) for t in taus]
+    d, c, e = aux.tension_aux_losses(xs, groups)
+    total = weights[0] * d + weights[1] * c + weights[2] * e
+    grads = torch.autograd.grad(total, xs)
+    return (d, c, e), grads
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", _aux_names())
+def test_fused_matches_reference_golden_fp32(name):
+    taus, grads, groups, vals = _aux_case(name)
+    dev = torch.device("cuda:0")
+    (d, c, e), got = _fused([t.to(dev) for t in taus], groups)
+    _close(torch.stack([d, c, e]), vals, 1e-5, 1e-6, f"{name} losses")
+    for i, (g, r) in enumerate(zip(got, grads)):
+        assert g.dtype == torch.float32
+        _close(g, r, 1e-4, 1e-5, f"{name} dτ{i}")
+
+
+def _fields(shape, n, dtype, seed):
+    B, T, H, W = shape
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for _ in range(n):
+        x = torch.randn(B, T, H, W, generator=g) * 1.5
+        off = torch.randint(-1, 2, (B, T, H, 1), generator=g).float() * 4.0
+        tau = torch.sigmoid(x + off)
+        t = torch.arange(T).view(1, T, 1, 1)
+        w = torch.arange(W).view(1, 1, 1, W)
+        out.append((tau * ((t - (W - w)) >= 0).float()).to(dtype))
+    return out
+
+
+# (shape, layers): vector paths G = 1…32 for bf16 (W = 8…256) and fp32, the
+# scalar path for widths that are not whole 16-byte vectors of a power-of-two
+# lane count (W = 24, 37, 300)
+SHAPES = [((2, 300, 4, 64), 3), ((1, 257, 3, 128), 2), ((2, 64, 2, 8), 2), ((1, 96, 2, 256), 2),
+          ((2, 70, 3, 24), 2), ((1, 50, 2, 37), 2), ((1, 40, 2, 300), 1), ((3, 33, 2, 16), 3)]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("shape,n", SHAPES)
+def test_fused_matches_oracle(shape, n, dtype):
+    taus = _fields(shape, n, dtype, seed=shape[-1] * 7 + n)
+    groups = {shape[-1]: list(range(n - 1)), 4 * shape[-1]: [n - 1]} if n > 1 else None
+    w = (1.0, 0.5, 2.0)
+    vals, ref = aux_oracle.losses_and_grads(taus, groups, w)
+    dev = torch.device("cuda:0")
+    (d, c, e), got = _fused([t.to(dev) for t in taus], groups, w)
+    # statistics in fp32 from the stored values: fp32 round-off against float64
+    _close(torch.stack([d, c, e]), vals, 2e-5, 1e-6, f"{shape} {dtype} losses")
+    # dτ is stored in the fields' dtype: its rounding is the tolerance.  Rows
+    # with no live slot (t = 0) have Σ = 0, so the reference's +1e-8
+    # denominator gives their slots cotangents near −2e5, beyond fp16's range:
+    # compare with the oracle rounded to the field dtype (−inf there)
+    rtol = {torch.float32: 1e-4, torch.bfloat16: 1e-2, torch.float16: 2e-3}[dtype]
+    for i, (g, r) in enumerate(zip(got, ref)):
+        assert g.dtype == dtype and g.shape == taus[i].shape
+        r = r.to(dtype).double()
+        fin = torch.isfinite(r)
+        assert torch.equal(torch.isfinite(g.cpu()), fin), f"{shape} {dtype} dτ{i}: overflow pattern"
+        _close(g.cpu()[fin], r[fin].numpy(), rtol, rtol * 1e-1, f"{shape} {dtype} dτ{i}")
+
+
+@pytest.mark.gpu
+def test_fields_of_two_shapes_and_dtypes():
+    """Fields of different widths (local and a different exported window) are
+    batched per shape and still produce one statistics row each."""
+    from bozo_b200 import aux
+    a = _fields((2, 80, 3, 64), 2, torch.bfloat16, 5)
+    b = _fields((2, 80, 3, 16), 1, torch.bfloat16, 6)
+    taus = [a[0], b[0], a[1]]
+    groups = {64: [0, 2], 1024: [1]}
+    vals, ref = aux_oracle.losses_and_grads(taus, groups, (1.0, 1.0, 1.0))
+    dev = torch.device("cuda:0")
+    st = aux.tau_field_stats([t.to(dev) for t in taus])
+    assert st.shape == (3, 3)
+    (d, c, e), got = _fused([t.to(dev) for t in taus], groups, (1.0, 1.0, 1.0))
+    _close(torch.stack([d, c, e]), vals, 2e-5, 1e-6, "mixed losses")
+    for g, r in zip(got, ref):
+        _close(g, r.numpy(), 1e-2, 1e-3, "mixed dτ")
+
+
+@pytest.mark.gpu
+def test_statistics_are_deterministic():
+    from bozo_b200 import aux
+    taus = [t.cuda() for t in _fields((4, 512, 6, 64), 4, torch.bfloat16, 9)]
+    a = aux.tau_field_stats(taus)
+    b = aux.tau_field_stats(taus)
+    assert torch.equal(a, b)
+
+
+def test_cpu_fields_raise():
+    from bozo_b200 import aux
+    with pytest.raises(RuntimeError, match="CUDA"):
+        aux.tension_aux_losses([torch.rand(1, 8, 2, 4)], None)
