@@ -33,6 +33,7 @@
 // bf16 tile in the dead outer slot → TMA store); 4-11 epilogue.  Every
 // mbarrier wait is bounded (tc_ptx.cuh).
 #include <algorithm>
+#include <type_traits>
 
 #include "tc.cuh"
 #include "tc_host.cuh"
@@ -471,6 +472,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               tmem_ld16x2_wait(col, col + 64, Rg);
             }
+            // Does this piece touch the exported τ?  Local windows export every
+            // valid element; the global block only the last tw keys
+            // (model.py:233-236), i.e. pieces whose key positions reach T − tw
+            // — uniform over the warp for FWD/DQ (keys = inner positions), per
+            // thread for DKV (key = this row).  Only those pieces take the
+            // element loop with the τ store / cotangent read.
+            const bool pexp = kExtra && (p.local || (R == kDKV ? orow >= T - p.tw : ipos0 + 15 >= T - p.tw));
+            auto piece = [&](auto exp_tag) {
+              constexpr bool kExp = decltype(exp_tag)::value;
 #pragma unroll
             for (int e4 = 0; e4 < 16; e4 += 2) {
               float pv[2], dv[2];
@@ -494,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const float tau = valid ? fmaf(0.5f, thv, 0.5f) : 0.f;
                   mass += tau;
                   pv[z] = tau;
-                  if constexpr (kExtra) {
+                  if constexpr (kExp) {
                     // exported τ: local [B,T,H,W] at w; global window of the last
                     // tw keys, column T−1−s (model.py:233-236)
                     const int col = p.local ? p.W - dts : T - 1 - sk;
@@ -513,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     bd = row_bd;
                   }
                   float dt = fmaf(ad, __uint_as_float(Rg[16 + ee]), bd);
-                  if constexpr (kExtra) {
+                  if constexpr (kExp) {
                     const int col = p.local ? p.W - dts : T - 1 - sk;
                     if (valid && (unsigned)col < (unsigned)p.tw)
                       dt = fmaf(__bfloat162float(p.dtau[((long long)(b * T + tq) * H + h) * p.tw + col]),
@@ -526,6 +536,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (R == kFwd || R == kDKV) pk[ss][e4 >> 1] = pack_bf16(pv[0], pv[1]);
               if (R != kFwd) dk[ss][e4 >> 1] = pack_bf16(dv[0], dv[1]);
             }
+            };
+            if (pexp)
+              piece(std::true_type{});
+            else
+              piece(std::false_type{});
           }
           tc_fence_before();
           __syncwarp();
