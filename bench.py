@@ -386,6 +386,65 @@ def run_train(args, rank, world, local_rank):
     return out, params
 
 
+def run_tau_consumer(local_rank, iters=20):
+    """The fused τ consumer (bozo_b200.aux, csrc/tau_aux.cu) on the fields of
+    the 117M training step: 12 τ fields [16,1024,12,64] bf16 (302 MB).  Device
+    times (CUDA events over `iters` launches) of the statistics pass (one read
+    of every field) and the cotangent pass (one read, one write), the fused
+    losses fwd+bwd through autograd, and the framework-op formulation of the
+    same three losses (model.py:498-611 restated in bozo_b200.lm, autocast)."""
+    from bozo_b200 import _capi, aux, lm
+    dev = torch.device("cuda", local_rank)
+    g = torch.Generator(device=dev).manual_seed(77)
+    taus = [torch.rand(TRAIN_B, TRAIN_T, 12, 64, device=dev, generator=g).to(torch.bfloat16)
+            for _ in range(12)]
+    groups = {64: [0, 1, 2, 4, 5, 6, 8, 9, 10], 1024: [3, 7, 11]}
+    d_stats = torch.ones(12, 3, device=dev)
+    leaves = [t.clone().requires_grad_(True) for t in taus]
+
+    def fused_losses():
+        d, c, e = aux.tension_aux_losses(leaves, groups)
+        torch.autograd.grad(0.02 * d + 0.0 * c + 0.0 * e, leaves)
+
+    def framework_losses():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            d = lm.tension_diversity_loss(leaves, groups)
+            c = lm.constraint_consistency_loss(leaves)
+            e = lm.tension_entropy_loss(leaves)
+        torch.autograd.grad(0.02 * d + 0.0 * c + 0.0 * e, leaves)
+
+    def timed(fn, n):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / n
+
+    ms_stats = timed(lambda: aux.tau_field_stats(taus), iters)
+    ms_cot = timed(lambda: _capi.ext().tau_aux_bwd(taus, d_stats), iters)
+    ms_fused = timed(fused_losses, 10)
+    ms_fw = timed(framework_losses, 3)
+    field_bytes = 12 * TRAIN_B * TRAIN_T * 12 * 64 * 2
+    hbm = peaks()[0]
+    return {
+        "fields": "12 x [16,1024,12,64] bf16 (the 117M step's tau fields)",
+        "stats_us": round(ms_stats * 1e3, 1),
+        "stats_gbs": round(field_bytes / (ms_stats * 1e-3) / 1e9, 1),
+        "stats_frac_hbm": round(field_bytes / (ms_stats * 1e-3) / 1e9 / hbm, 4),
+        "cotangent_us": round(ms_cot * 1e3, 1),
+        "cotangent_gbs": round(2 * field_bytes / (ms_cot * 1e-3) / 1e9, 1),
+        "cotangent_frac_hbm": round(2 * field_bytes / (ms_cot * 1e-3) / 1e9 / hbm, 4),
+        "fused_losses_fwd_bwd_ms": round(ms_fused, 3),
+        "framework_ops_fwd_bwd_ms": round(ms_fw, 3),
+    }
+
+
 PREFILL_B, PREFILL_T = 4, 2048  # BASELINE configs[4]: batch 32 over 8 GPUs, seq 2048
 
 
@@ -540,9 +599,12 @@ def main():
     results = train = prefill = None
     if args.workload in ("all", "op"):
         results, e2e_ms, launches_per_step = run_ours(args, rank, world, local_rank)
+    tau_consumer = None
     if args.workload in ("all", "train"):
         torch.cuda.empty_cache()
         train, n_params = run_train(args, rank, world, local_rank)
+        torch.cuda.empty_cache()
+        tau_consumer = run_tau_consumer(local_rank)
     if args.workload in ("all", "prefill"):
         torch.cuda.empty_cache()
         prefill = run_prefill(args, rank, world, local_rank)
@@ -582,6 +644,7 @@ def main():
                        "dtype": "bf16 autocast, fp32 master weights", "optimizer": "AdamW (fused)",
                        "parallelism": f"ddp{n}" if n > 1 else "single GPU",
                        "data": "uniform random token ids, random init"},
+            "tau_consumer": tau_consumer,
         }
     prefill_obj = None
     if prefill is not None:

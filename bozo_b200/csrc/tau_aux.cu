@@ -12,9 +12,9 @@
 //   * scalar path (any other W): one warp per row, lanes strided over it,
 //     the row re-read from L1/L2 for each pass.
 // Per row (x = the row, S = Σx, D = S + 1e-8, p = x/D, model.py:527-528;
-// one reciprocal per row, log and the p/(p+1e-8) quotient by the fast
-// hardware approximations, whose error stays far below the fp32 tolerance of
-// the sums):
+// one reciprocal per row, logs in base 2 with the row scale and ln 2 applied
+// per row, log2 and 1/q by the fast hardware approximations, whose error
+// stays far below the fp32 tolerance of the sums):
 //   ent = −Σ p·log(p + 1e-8)                           diversity (model.py:528)
 //   pen = relu(0.05 − S/W) + relu(S/W − 0.8)           entropy   (model.py:602-608)
 //   hinge_i = relu(x[t,i]·x[t−1,0] − x[t,i+1]),  i < m  consistency (model.py:561-576)
@@ -88,6 +88,21 @@ __device__ __forceinline__ float group_sum(float v) {
 #pragma unroll
   for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+// The row entropy in base 2 with the row scale pulled out:
+//   −Σ_w p_w·ln(p_w + 1e-8) = −ln2·(1/D)·Σ_w x_w·log2(x_w/D + 1e-8),
+// so a value costs one FFMA, one MUFU lg2 and one FFMA.
+constexpr float kLn2 = 0.69314718f;
+constexpr float kInvLn2 = 1.44269504f;
+__device__ __forceinline__ float ent2_term(float x, float invD, float acc) {
+  return fmaf(x, __log2f(fmaf(x, invD, kAuxEps)), acc);
+}
+// ∂ent/∂p = −(ln q + p/q), q = p + 1e-8, as −ln2·h with
+// h = log2 q + (p/ln2)·(1/q)  (invDl = invD/ln2): two MUFU ops and two FFMAs.
+__device__ __forceinline__ float grad_h(float x, float invD, float invDl) {
+  const float q = fmaf(x, invD, kAuxEps);
+  return fmaf(x * invDl, __fdividef(1.f, q), __log2f(q));
 }
 
 // Consistency slot i is live for query t iff t ∈ [i+2, i+2+t_out) (model.py:561-571).
@@ -175,14 +190,11 @@ __global__ void __launch_bounds__(kAuxThreads)
 #pragma unroll
     for (int k = 0; k < NV; ++k) sum += cur.x[k];
     sum = group_sum<G>(sum);
-    const float invD = 1.f / (sum + kAuxEps);
+    const float invD = __fdividef(1.f, sum + kAuxEps);
     float e = 0.f;
 #pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      const float p = cur.x[k] * invD;
-      e -= p * __logf(p + kAuxEps);
-    }
-    e = group_sum<G>(e);
+    for (int k = 0; k < NV; ++k) e = ent2_term(cur.x[k], invD, e);
+    e = -kLn2 * invD * group_sum<G>(e);
     // slot 4 of a fp32 row sits in the group's second lane
     const float x4 = NV > 4 ? cur.x[NV > 4 ? 4 : 0] : __shfl_down_sync(0xffffffffu, cur.x[0], 1);
     if (cur.live && g == 0) {
@@ -225,21 +237,21 @@ __global__ void __launch_bounds__(kAuxThreads)
 #pragma unroll
     for (int k = 0; k < NV; ++k) sum += cur.x[k];
     sum = group_sum<G>(sum);
-    const float invD = 1.f / (sum + kAuxEps);
-    float gq[NV], a = 0.f;
+    const float invD = __fdividef(1.f, sum + kAuxEps), invDl = invD * kInvLn2;
+    float hq[NV], a = 0.f;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
-      const float p = cur.x[k] * invD, q = p + kAuxEps;
-      gq[k] = -(__logf(q) + __fdividef(p, q));
-      a = fmaf(gq[k], cur.x[k], a);
+      hq[k] = grad_h(cur.x[k], invD, invDl);
+      a = fmaf(hq[k], cur.x[k], a);
     }
     a = group_sum<G>(a);
     const float mu = sum * s.inv_w;
     const float dpen = gP * ((0.05f - mu > 0.f ? -1.f : 0.f) + (mu - 0.8f > 0.f ? 1.f : 0.f));
-    const float cA = gE * a * invD * invD;
+    // dx = gE·(g/D − (Σ g·x)/D²) + dpen with g = −ln2·h
+    const float c1 = -kLn2 * gE * invD, c0 = dpen + kLn2 * gE * a * invD * invD;
     float dx[NV];
 #pragma unroll
-    for (int k = 0; k < NV; ++k) dx[k] = fmaf(gE * invD, gq[k], dpen - cA);
+    for (int k = 0; k < NV; ++k) dx[k] = fmaf(c1, hq[k], c0);
     // consistency: slots 0..m of this row, from this row's terms and row t+1's
     const float x4 = NV > 4 ? cur.x[NV > 4 ? 4 : 0] : __shfl_down_sync(0xffffffffu, cur.x[0], 1);
     float dc[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
@@ -351,11 +363,10 @@ __global__ void __launch_bounds__(kAuxThreads)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 a = unpack2(word(cur.v[k], j), (E*)nullptr);
-        const float p0 = a.x * invD, p1 = a.y * invD;
-        e = fmaf(-p0, __logf(p0 + kAuxEps), e);
-        e = fmaf(-p1, __logf(p1 + kAuxEps), e);
+        e = ent2_term(a.x, invD, e);
+        e = ent2_term(a.y, invD, e);
       }
-    e = group_sum<G>(e);
+    e = -kLn2 * invD * group_sum<G>(e);
     if (cur.live && g == 0) {
       acc_ent += e;
       const float mu = sum * s.inv_w;
@@ -403,25 +414,23 @@ __global__ void __launch_bounds__(kAuxThreads)
         sum += a.x + a.y;
       }
     sum = group_sum<G>(sum);
-    const float invD = __fdividef(1.f, sum + kAuxEps);
-    // g_w = ∂ent/∂p_w, kept for the write pass (two MUFU ops per value)
+    const float invD = __fdividef(1.f, sum + kAuxEps), invDl = invD * kInvLn2;
+    // h_w (∂ent/∂p_w = −ln2·h_w), kept for the write pass
     float gq[32], a = 0.f;
 #pragma unroll
     for (int k = 0; k < 4; ++k)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 x = unpack2(word(cur.v[k], j), (E*)nullptr);
-        const float p0 = x.x * invD, q0 = p0 + kAuxEps;
-        const float p1 = x.y * invD, q1 = p1 + kAuxEps;
-        gq[8 * k + 2 * j] = -(__logf(q0) + __fdividef(p0, q0));
-        gq[8 * k + 2 * j + 1] = -(__logf(q1) + __fdividef(p1, q1));
+        gq[8 * k + 2 * j] = grad_h(x.x, invD, invDl);
+        gq[8 * k + 2 * j + 1] = grad_h(x.y, invD, invDl);
         a = fmaf(gq[8 * k + 2 * j], x.x, a);
         a = fmaf(gq[8 * k + 2 * j + 1], x.y, a);
       }
     a = group_sum<G>(a);
     const float mu = sum * s.inv_w;
     const float dpen = gP * ((0.05f - mu > 0.f ? -1.f : 0.f) + (mu - 0.8f > 0.f ? 1.f : 0.f));
-    const float c0 = dpen - gE * a * invD * invD, c1 = gE * invD;
+    const float c1 = -kLn2 * gE * invD, c0 = dpen + kLn2 * gE * a * invD * invD;
     // consistency: slots 0..m of this row, from this row's terms and row t+1's
     float dc[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
     if (cur.live && g == 0 && s.m > 0) {
@@ -482,13 +491,10 @@ __global__ void __launch_bounds__(kAuxThreads)
     float sum = 0.f;
     for (int w = lane; w < s.W; w += 32) sum += to_f(row[w]);
     sum = warp_sum(sum);
-    const float invD = 1.f / (sum + kAuxEps);
+    const float invD = __fdividef(1.f, sum + kAuxEps);
     float e = 0.f;
-    for (int w = lane; w < s.W; w += 32) {
-      const float p = to_f(row[w]) * invD;
-      e -= p * __logf(p + kAuxEps);
-    }
-    e = warp_sum(e);
+    for (int w = lane; w < s.W; w += 32) e = ent2_term(to_f(row[w]), invD, e);
+    e = -kLn2 * invD * warp_sum(e);
     if (lane == 0) {
       acc_ent += e;
       const float mu = sum * s.inv_w;
@@ -522,20 +528,20 @@ __global__ void __launch_bounds__(kAuxThreads)
     float sum = 0.f;
     for (int w = lane; w < s.W; w += 32) sum += to_f(row[w]);
     sum = warp_sum(sum);
-    const float invD = 1.f / (sum + kAuxEps);
+    const float invD = __fdividef(1.f, sum + kAuxEps), invDl = invD * kInvLn2;
     float a = 0.f;
     for (int w = lane; w < s.W; w += 32) {
-      const float x = to_f(row[w]), p = x * invD, q = p + kAuxEps;
-      a = fmaf(-(__logf(q) + __fdividef(p, q)), x, a);
+      const float x = to_f(row[w]);
+      a = fmaf(grad_h(x, invD, invDl), x, a);
     }
     a = warp_sum(a);
     const float mu = sum * s.inv_w;
     const float dpen = gP * ((0.05f - mu > 0.f ? -1.f : 0.f) + (mu - 0.8f > 0.f ? 1.f : 0.f));
-    const float cA = gE * a * invD * invD;
+    const float c1 = -kLn2 * gE * invD, c0 = dpen + kLn2 * gE * a * invD * invD;
     const int t = query_of(r, s);
     for (int w = lane; w < s.W; w += 32) {
-      const float x = to_f(row[w]), p = x * invD, q = p + kAuxEps;
-      float dx = fmaf(gE * invD, -(__logf(q) + __fdividef(p, q)), dpen - cA);
+      const float x = to_f(row[w]);
+      float dx = fmaf(c1, grad_h(x, invD, invDl), c0);
       if (s.m > 0 && w <= s.m) {  // consistency terms of slot w
         if (t >= 1) {
           const float prev0 = to_f(tau[(r - s.H) * s.W]);
