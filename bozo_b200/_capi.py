@@ -65,6 +65,7 @@ class BwdArgs(C.Structure):
         ("grad_dtype", C.c_int32 * 3), ("qk_rotated", C.c_int32),
         ("dq", C.c_void_p), ("dk", C.c_void_p), ("dv", C.c_void_p),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+        ("aux_row", C.c_void_p),
     ]
 
 
@@ -83,6 +84,7 @@ class TauAuxBwdArgs(C.Structure):
         ("B", C.c_int32), ("T", C.c_int32), ("H", C.c_int32), ("W", C.c_int32),
         ("tau", C.c_void_p * TAU_AUX_MAX_LAYERS), ("d_stats", C.c_void_p),
         ("d_tau", C.c_void_p * TAU_AUX_MAX_LAYERS),
+        ("row_coef", C.c_void_p * TAU_AUX_MAX_LAYERS),
     ]
 
 

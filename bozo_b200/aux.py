@@ -34,23 +34,47 @@ __all__ = ["tau_field_stats", "tension_aux_losses"]
 
 
 class _TauStatsFn(torch.autograd.Function):
-    """[L, 3] fp32 statistics of L equally shaped τ fields (see the header)."""
+    """[L, 3] fp32 statistics of L equally shaped τ fields (see the header).
+
+    Backward: fields that carry a ``_bozo_tau_slot`` (exported by a tension
+    call whose backward can form the cotangent itself, ``ops._TauSlot``) get
+    their cotangent as per-query-row coefficients in that slot — row mode of
+    ``bozo_tau_aux_bwd``, allowed only when the consistency statistic takes
+    no gradient (``row_ok``) — and ``None`` here; the others get a
+    materialised cotangent."""
 
     @staticmethod
-    def forward(ctx, *taus: Tensor) -> Tensor:
+    def forward(ctx, row_ok: bool, *taus: Tensor) -> Tensor:
         ctx.save_for_backward(*taus)
+        ctx.slots = [getattr(t, "_bozo_tau_slot", None) if row_ok else None for t in taus]
         return _capi.ext().tau_aux_fwd(list(taus))
 
     @staticmethod
     def backward(ctx, d_stats: Tensor):
         taus = ctx.saved_tensors
-        return tuple(_capi.ext().tau_aux_bwd(list(taus), d_stats.float().contiguous()))
+        d_stats = d_stats.float().contiguous()
+        grads: List[Optional[Tensor]] = [None] * len(taus)
+        rows = [i for i, sl in enumerate(ctx.slots) if sl is not None]
+        mats = [i for i, sl in enumerate(ctx.slots) if sl is None]
+        if rows:
+            coef = _capi.ext().tau_aux_rowcoef([taus[i] for i in rows], d_stats[rows].contiguous())
+            for j, i in enumerate(rows):
+                ctx.slots[i].add(coef[j])
+        if mats:
+            sub = mats if len(mats) < len(taus) else None
+            dts = _capi.ext().tau_aux_bwd([taus[i] for i in mats],
+                                          d_stats[sub].contiguous() if sub else d_stats)
+            for j, i in enumerate(mats):
+                grads[i] = dts[j]
+        return (None, *grads)
 
 
-def tau_field_stats(taus: Sequence[Tensor]) -> Tensor:
+def tau_field_stats(taus: Sequence[Tensor], row_ok: bool = False) -> Tensor:
     """Per-layer statistics ``[L, 3]``: mean row entropy of ``τ/(Στ+1e-8)``,
     mean transitivity hinge, mean-τ band penalty (``bozo_tau_aux_fwd``).
-    Fields of different shapes or dtypes are batched per shape."""
+    Fields of different shapes or dtypes are batched per shape.  ``row_ok``:
+    the caller takes no gradient through column 1 (consistency), so fields
+    exported with a slot may receive their cotangent per row."""
     if not taus:
         raise ValueError("tau_field_stats: no τ fields")
     for t in taus:
@@ -61,10 +85,10 @@ def tau_field_stats(taus: Sequence[Tensor]) -> Tensor:
     for i, t in enumerate(taus):
         by_kind[(tuple(t.shape), t.dtype)].append(i)
     if len(by_kind) == 1:
-        return _TauStatsFn.apply(*[t.contiguous() for t in taus])
+        return _TauStatsFn.apply(row_ok, *[t.contiguous() for t in taus])
     rows: List[Optional[Tensor]] = [None] * len(taus)
     for idx in by_kind.values():
-        st = _TauStatsFn.apply(*[taus[i].contiguous() for i in idx])
+        st = _TauStatsFn.apply(row_ok, *[taus[i].contiguous() for i in idx])
         for j, i in enumerate(idx):
             rows[i] = st[j]
     return torch.stack(rows)
@@ -78,14 +102,21 @@ def _consistency_applies(shape: torch.Size) -> bool:
     return min(W - 2, 4) + 1 < T
 
 
-def tension_aux_losses(all_tensions: Sequence[Tensor],
-                       window_groups: Optional[dict] = None) -> Tuple[Tensor, Tensor, Tensor]:
+def tension_aux_losses(all_tensions: Sequence[Tensor], window_groups: Optional[dict] = None,
+                       grad_consistency: bool = True) -> Tuple[Tensor, Tensor, Tensor]:
     """(diversity, consistency, entropy) of model.py:498-611 for the per-layer
-    τ fields, as fp32 scalars with gradients w.r.t. every field."""
+    τ fields, as fp32 scalars with gradients w.r.t. every field.
+
+    ``grad_consistency=False`` (a caller whose consistency weight is 0, as
+    train.py's default): the consistency value is returned without a
+    gradient, which is what a zero weight makes of it anyway, and fields
+    exported by the local tensor-core kernels then receive the diversity and
+    entropy cotangents per query row, formed inside the tension backward
+    instead of being written out and read back."""
     if not all_tensions:
         z = torch.tensor(0.0)
         return z, z, z
-    stats = tau_field_stats(all_tensions)
+    stats = tau_field_stats(all_tensions, row_ok=not grad_consistency)
     # diversity (model.py:511-532): per window group, relu(log W − mean entropy)
     if window_groups is not None:
         groups = {W: list(idx) for W, idx in window_groups.items()}
@@ -102,7 +133,8 @@ def tension_aux_losses(all_tensions: Sequence[Tensor],
     div = div / max(len(groups), 1)
     # consistency (model.py:548-577): average over the layers that apply
     live = [i for i, t in enumerate(all_tensions) if _consistency_applies(t.shape)]
-    cons = stats[live, 1].sum() / max(len(live), 1) if live else stats.new_zeros(())
+    cons_col = stats[:, 1] if grad_consistency else stats[:, 1].detach()
+    cons = cons_col[live].sum() / max(len(live), 1) if live else stats.new_zeros(())
     # entropy regulariser (model.py:597-611): average over all layers
     ent_loss = stats[:, 2].sum() / len(all_tensions)
     return div, cons, ent_loss

@@ -220,11 +220,12 @@ int bozo_tension_fwd(const bozo_tension_fwd_args* a, void* stream) {
 
 size_t bozo_tension_bwd_workspace(const bozo_tension_bwd_args* a) {
   if (!a || a->B <= 0 || a->T <= 0 || a->H <= 0) return 0;
-  // three per-query-row coefficient planes; rows padded to a multiple of
-  // 128 so a 128-row slice starts 16-byte aligned (tensor-core bulk copies)
+  // three per-query-row coefficient planes (five with a per-row τ
+  // cotangent); rows padded to a multiple of 128 so a 128-row slice starts
+  // 16-byte aligned (tensor-core bulk copies)
   const size_t tpad = ((size_t)a->T + 127) / 128 * 128;
   const size_t rows = (size_t)a->B * a->H * tpad;
-  return round256(rows * sizeof(float)) * 3;
+  return round256(rows * sizeof(float)) * (a->aux_row ? 5 : 3);
 }
 
 int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
@@ -262,6 +263,7 @@ int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
   p.dq = a->dq; p.dk = a->dk; p.dv = a->dv;
   p.dq_dt = a->grad_dtype[0]; p.dk_dt = a->grad_dtype[1]; p.dv_dt = a->grad_dtype[2];
   p.qk_rotated = (a->qk_rotated && p.cos) ? 1 : 0;
+  p.aux_row = a->aux_row;
   const size_t tpad = ((size_t)a->T + 127) / 128 * 128;
   const size_t rows = (size_t)a->B * a->H * tpad;
   p.alpha = static_cast<float*>(a->workspace);
@@ -276,6 +278,8 @@ int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
   const bool band = p.mode == BOZO_MODE_LOCAL && tc_bwd_eligible(p);
   const bool tc_ok = band || tc_global_bwd_eligible(p);
   if (a->path == BOZO_PATH_TCGEN05 && !tc_ok) return BOZO_ERR_ALIGNMENT;
+  // the per-row τ cotangent is formed by the local tensor-core kernel only
+  if (a->aux_row && (!band || a->path == BOZO_PATH_SIMT)) return BOZO_ERR_UNSUPPORTED;
   int path;
   if (tc_ok && a->path != BOZO_PATH_SIMT) {
     e = band ? launch_tc_bwd(p, s, &launches) : launch_tc_global_bwd(p, s, &launches);
@@ -330,8 +334,13 @@ int bozo_tau_aux_bwd(const bozo_tau_aux_bwd_args* a, void* stream) {
   int st = check_aux(a);
   if (st) return st;
   if (!a->d_stats) return BOZO_ERR_NULL;
-  for (int i = 0; i < a->n_layers; ++i)
-    if (!a->d_tau[i]) return BOZO_ERR_NULL;
+  // every layer in one mode: all d_tau (cotangent) or all row_coef (row mode)
+  const bool rows = a->row_coef[0] != nullptr;
+  for (int i = 0; i < a->n_layers; ++i) {
+    if (rows ? !a->row_coef[i] : !a->d_tau[i]) return BOZO_ERR_NULL;
+    if (rows && a->d_tau[i]) return BOZO_ERR_BAD_SHAPE;
+  }
+  if (rows && !tau_aux_row_mode_ok(*a)) return BOZO_ERR_UNSUPPORTED;
   cudaError_t e = bind_device(a->tau[0]);
   if (e != cudaSuccess) return cuda_fail(e);
   const AuxShape s = aux_shape(a->B, a->T, a->H, a->W);

@@ -64,6 +64,7 @@ struct BwdP {
   float* beta;   // [B,H,T] workspace
   float* coef;   // [3][B·H, Tpad] workspace (tensor-core path)
   int qk_rotated;  // q, k are RoPE-rotated already
+  const float* aux_row;  // [3][B·H·T] per-row τ cotangent (a1, a0, inv_d) or null
   int* err;
 };
 
@@ -132,5 +133,6 @@ int aux_blocks(const AuxShape& s, int n_layers, int sms);
 cudaError_t launch_tau_aux_fwd(const bozo_tau_aux_fwd_args& a, int nblk, float* partial,
                                cudaStream_t st);
 cudaError_t launch_tau_aux_bwd(const bozo_tau_aux_bwd_args& a, int nblk, cudaStream_t st);
+bool tau_aux_row_mode_ok(const bozo_tau_aux_bwd_args& a);
 
 }  // namespace bozo

@@ -139,7 +139,8 @@ std::vector<at::Tensor> tension_bwd(const at::Tensor& q, const at::Tensor& k, co
                                     const c10::optional<at::Tensor>& bias,
                                     const c10::optional<at::Tensor>& out,
                                     const c10::optional<at::Tensor>& mass,
-                                    const c10::optional<at::Tensor>& d_tau, bool qk_rotated) {
+                                    const c10::optional<at::Tensor>& d_tau, bool qk_rotated,
+                                    const c10::optional<at::Tensor>& aux_row) {
   const c10::cuda::CUDAGuard guard(q.device());
   const int64_t B = q.size(0), T = q.size(1), H = q.size(2), HD = q.size(3);
   at::Tensor dq = at::empty({B, T, H, HD}, q.options());
@@ -162,6 +163,12 @@ std::vector<at::Tensor> tension_bwd(const at::Tensor& q, const at::Tensor& k, co
   a.grad_dtype[1] = dtype_code(k.scalar_type());
   a.grad_dtype[2] = dtype_code(v.scalar_type());
   a.qk_rotated = qk_rotated ? 1 : 0;
+  if (aux_row && aux_row->defined()) {
+    if (aux_row->scalar_type() != at::kFloat || !aux_row->is_contiguous() ||
+        aux_row->numel() != 3 * B * T * H)
+      throw std::invalid_argument("tension_bwd: aux_row must be a contiguous fp32 [3, B·H·T] tensor");
+    a.aux_row = aux_row->data_ptr<float>();
+  }
   a.dq = dq.data_ptr();
   a.dk = dk.data_ptr();
   a.dv = dv.data_ptr();
@@ -248,6 +255,29 @@ std::vector<at::Tensor> tau_aux_bwd(const std::vector<at::Tensor>& taus, const a
   return out;
 }
 
+// Row mode of the τ consumer's cotangent: per field the per-query-row
+// coefficients [3, B·H·T] (a1, a0, 1/D) the tension backward takes as aux_row.
+at::Tensor tau_aux_rowcoef(const std::vector<at::Tensor>& taus, const at::Tensor& d_stats) {
+  check_fields(taus);
+  const int64_t L = (int64_t)taus.size();
+  if (d_stats.scalar_type() != at::kFloat || d_stats.numel() != 3 * L || !d_stats.is_contiguous() ||
+      d_stats.device() != taus[0].device())
+    throw std::invalid_argument("tau_aux: d_stats must be a contiguous fp32 [L,3] tensor on the fields' device");
+  const c10::cuda::CUDAGuard guard(taus[0].device());
+  const auto stream = at::cuda::getCurrentCUDAStream(taus[0].device().index()).stream();
+  const int64_t rows = taus[0].size(0) * taus[0].size(1) * taus[0].size(2);
+  at::Tensor out = at::empty({L, 3, rows}, taus[0].options().dtype(at::kFloat));
+  for (size_t i0 = 0; i0 < taus.size(); i0 += BOZO_TAU_AUX_MAX_LAYERS) {
+    const size_t n = std::min<size_t>(BOZO_TAU_AUX_MAX_LAYERS, taus.size() - i0);
+    bozo_tau_aux_bwd_args a{};
+    fill_aux(a, taus, i0, n);
+    a.d_stats = d_stats.data_ptr<float>() + 3 * i0;
+    for (size_t i = 0; i < n; ++i) a.row_coef[i] = out[i0 + i].data_ptr<float>();
+    check(bozo_tau_aux_bwd(&a, stream), "bozo_tau_aux_bwd (row mode)");
+  }
+  return out;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -256,4 +286,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tension_bwd", &tension_bwd, "backward through bozo_tension_bwd");
   m.def("tau_aux_fwd", &tau_aux_fwd, "τ-field statistics through bozo_tau_aux_fwd");
   m.def("tau_aux_bwd", &tau_aux_bwd, "τ-field cotangents through bozo_tau_aux_bwd");
+  m.def("tau_aux_rowcoef", &tau_aux_rowcoef,
+        "per-query-row τ cotangent coefficients through bozo_tau_aux_bwd (row mode)");
 }

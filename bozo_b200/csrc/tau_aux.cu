@@ -475,6 +475,67 @@ __global__ void __launch_bounds__(kAuxThreads)
   }
 }
 
+// Row mode of the cotangent: per query row the coefficients with which the
+// tension backward forms the diversity + entropy cotangent itself,
+//   dτ_w = c1·h_w + c0 = a1·(log2 q_w − 1e-8/(q_w·ln 2)) + a0,
+//   a1 = c1, a0 = c0 + c1/ln 2, q_w = τ_w/D + 1e-8,
+// written to [a1 | a0 | 1/D] planes at row (b·H + h)·T + t (the backward's
+// per-query-row order).  The consistency cotangent is not per-row: callers
+// use this mode only when it is zero.
+template <typename E, int G>
+__global__ void __launch_bounds__(kAuxThreads)
+    tau_aux_rowcoef_wide(AuxPtrs P, AuxShape s, const float* __restrict__ d_stats) {
+  constexpr int RPW = 32 / G;
+  const int layer = blockIdx.y;
+  const E* tau = static_cast<const E*>(P.tau[layer]);
+  float* coef = static_cast<float*>(P.dtau[layer]);
+  const float gE = d_stats[layer * 3 + 0] * s.inv_n;
+  const float gP = d_stats[layer * 3 + 2] * s.inv_n * s.inv_w;
+  const int lane = threadIdx.x & 31, g = lane % G, sub = lane / G;
+  const long long warp0 = (long long)blockIdx.x * kAuxWarps + (threadIdx.x >> 5);
+  const long long step = (long long)gridDim.x * kAuxWarps * RPW;
+  WideFetch<false> cur, nx;
+  fetch_wide<E, G, false>(tau, warp0 * RPW + sub, s, g, nx);
+  for (long long base = warp0 * RPW; base < s.N; base += step) {
+    cur = nx;
+    fetch_wide<E, G, false>(tau, base + step + sub, s, g, nx);
+    const long long r = base + sub;
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 a = unpack2(word(cur.v[k], j), (E*)nullptr);
+        sum += a.x + a.y;
+      }
+    sum = group_sum<G>(sum);
+    const float invD = __fdividef(1.f, sum + kAuxEps), invDl = invD * kInvLn2;
+    float a = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 x = unpack2(word(cur.v[k], j), (E*)nullptr);
+        a = fmaf(grad_h(x.x, invD, invDl), x.x, a);
+        a = fmaf(grad_h(x.y, invD, invDl), x.y, a);
+      }
+    a = group_sum<G>(a);
+    if (cur.live && g == 0) {
+      const float mu = sum * s.inv_w;
+      const float dpen = gP * ((0.05f - mu > 0.f ? -1.f : 0.f) + (mu - 0.8f > 0.f ? 1.f : 0.f));
+      const float c1 = -kLn2 * gE * invD, c0 = dpen + kLn2 * gE * a * invD * invD;
+      const uint32_t bt = fast_div((uint32_t)r, s.div_h);
+      const uint32_t h = (uint32_t)r - bt * (uint32_t)s.H;
+      const uint32_t b = fast_div(bt, s.div_t);
+      const uint32_t t = bt - b * (uint32_t)s.T;
+      const long long o = ((long long)b * s.H + h) * s.T + t;
+      coef[o] = c1;
+      coef[s.N + o] = fmaf(c1, kInvLn2, c0);
+      coef[2 * s.N + o] = invD;
+    }
+  }
+}
+
 // ───────────────────────────── scalar path ─────────────────────────────
 // One warp per row, any W; the row is re-read for every pass.
 template <typename E>
@@ -733,11 +794,39 @@ cudaError_t launch_tau_aux_fwd(const bozo_tau_aux_fwd_args& a, int nblk, float* 
   }
 }
 
+// Row mode is served by the wide kernels only.
+bool tau_aux_row_mode_ok(const bozo_tau_aux_bwd_args& a) {
+  if (a.dtype == BOZO_DT_BF16) return wide_lanes<__nv_bfloat16>(a.W, a.tau, a.n_layers) != 0;
+  if (a.dtype == BOZO_DT_F16) return wide_lanes<__half>(a.W, a.tau, a.n_layers) != 0;
+  return false;
+}
+
 cudaError_t launch_tau_aux_bwd(const bozo_tau_aux_bwd_args& a, int nblk, cudaStream_t st) {
   AuxPtrs P{};
+  const bool rows = a.row_coef[0] != nullptr;
   for (int i = 0; i < a.n_layers; ++i) {
     P.tau[i] = a.tau[i];
-    P.dtau[i] = a.d_tau[i];
+    P.dtau[i] = rows ? static_cast<void*>(a.row_coef[i]) : a.d_tau[i];
+  }
+  if (rows) {
+    const AuxShape s = aux_shape(a.B, a.T, a.H, a.W);
+    const dim3 grid(nblk, a.n_layers);
+    const int g = a.dtype == BOZO_DT_BF16 ? wide_lanes<__nv_bfloat16>(a.W, a.tau, a.n_layers)
+                                          : wide_lanes<__half>(a.W, a.tau, a.n_layers);
+#define BOZO_ROWCOEF(E)                                                                          \
+  switch (g) {                                                                                   \
+    case 1: tau_aux_rowcoef_wide<E, 1><<<grid, kAuxThreads, 0, st>>>(P, s, a.d_stats); break;   \
+    case 2: tau_aux_rowcoef_wide<E, 2><<<grid, kAuxThreads, 0, st>>>(P, s, a.d_stats); break;   \
+    case 4: tau_aux_rowcoef_wide<E, 4><<<grid, kAuxThreads, 0, st>>>(P, s, a.d_stats); break;   \
+    default: tau_aux_rowcoef_wide<E, 8><<<grid, kAuxThreads, 0, st>>>(P, s, a.d_stats); break;  \
+  }
+    if (a.dtype == BOZO_DT_BF16) {
+      BOZO_ROWCOEF(__nv_bfloat16)
+    } else {
+      BOZO_ROWCOEF(__half)
+    }
+#undef BOZO_ROWCOEF
+    return cudaGetLastError();
   }
   const AuxShape s = aux_shape(a.B, a.T, a.H, a.W);
   switch (a.dtype) {

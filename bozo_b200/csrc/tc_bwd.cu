@@ -51,6 +51,7 @@ constexpr int kTileBytes = kTile * kHD * 2;  // 16 KiB
 constexpr int kHalfBytes = kTileBytes;       // one [128 x 64] bf16 Pᵀ or dSᵀ buffer
 constexpr int kThreads = 15 * 32;
 constexpr int kErrBwd = 0x200;
+constexpr float kEpsOverLn2 = 1.44269504e-8f;  // 1e-8 / ln 2
 
 // TMEM columns: Sᵀ/dPᵀ buffer b at 128b (Sᵀ) and 128b+64 (dPᵀ)
 constexpr uint32_t kColDK = 256, kColDV = 320, kColDQ = 384;
@@ -82,7 +83,9 @@ struct Layout {
   uint32_t k, v, q, dout, pds, stage, ab, theta, bars, total;
 };
 
-__host__ __device__ inline Layout bwd_layout() {
+// nplanes per-query-row coefficient planes per query slot: α/2, α·c, β·c
+// (+ a1·c and 1/D of the per-row τ cotangent when kAux)
+__host__ __device__ inline Layout bwd_layout(int nplanes) {
   Layout L;
   L.k = 0;
   L.v = L.k + 2 * kTileBytes;
@@ -90,8 +93,8 @@ __host__ __device__ inline Layout bwd_layout() {
   L.dout = L.q + 2 * kTileBytes;
   L.pds = L.dout + 2 * kTileBytes;       // [P0][dS0][P1][dS1], 16 KiB each
   L.stage = L.pds + 4 * kHalfBytes;      // dQ output staging tile
-  L.ab = L.stage + kTileBytes;           // coefficients: float[2 slots][3][128]
-  L.theta = L.ab + 2 * 3 * kTile * 4;    // RoPE θ: float[32]
+  L.ab = L.stage + kTileBytes;           // coefficients: float[2 slots][nplanes][128]
+  L.theta = L.ab + 2 * nplanes * kTile * 4;  // RoPE θ: float[32]
   L.bars = L.theta + 32 * 4;
   L.total = L.bars + (uint32_t)sizeof(Bars);
   return L;
@@ -104,10 +107,13 @@ __host__ __device__ inline Layout bwd_layout() {
 // batch b = blockIdx.y, so every warp load is four whole rows and the index
 // math is one 32-bit division per row.  The grid-stride step is a multiple of
 // 32 threads, so the 8-lane shuffle groups stay whole and warp-uniform.
+// With a per-row τ cotangent (aux_row: a1 | a0 | 1/D planes over B·H·T rows)
+// its constant a0 joins β and a1·c, 1/D fill two more planes.
 __global__ void alpha_beta_kernel(int B, int T, int H, int W, int tpad, int norm, float ds_scale,
                                   const float* __restrict__ row_mass, DevT4 dout, DevT4 out,
                                   float* __restrict__ a_half, float* __restrict__ a_ds,
-                                  float* __restrict__ b_ds) {
+                                  float* __restrict__ b_ds, const float* __restrict__ aux_row,
+                                  float* __restrict__ a1_ds, float* __restrict__ inv_d) {
   const int bb = blockIdx.y;
   const int n8 = T * H * 8;  // threads needed for this batch row
   const int stride = gridDim.x * blockDim.x;
@@ -151,6 +157,12 @@ __global__ void alpha_beta_kernel(int B, int T, int H, int W, int tpad, int norm
         a = 1.f;
       }
       const long long o = (long long)bh * tpad + t;
+      if (aux_row) {
+        const long long nr = (long long)B * H * T, ar = (long long)bh * T + t;
+        b += aux_row[nr + ar];
+        a1_ds[o] = aux_row[ar] * ds_scale;
+        inv_d[o] = aux_row[2 * nr + ar];
+      }
       a_half[o] = 0.5f * a;
       a_ds[o] = a * ds_scale;
       b_ds[o] = b * ds_scale;
@@ -163,6 +175,10 @@ __global__ void alpha_beta_kernel(int B, int T, int H, int W, int tpad, int norm
     a_half[o] = 0.f;
     a_ds[o] = 0.f;
     b_ds[o] = 0.f;
+    if (aux_row) {
+      a1_ds[o] = 0.f;
+      inv_d[o] = 0.f;
+    }
   }
 }
 
@@ -251,7 +267,7 @@ struct SubGen {
   }
 };
 
-template <bool kBias, bool kDTau>
+template <bool kBias, bool kDTau, bool kAux>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_bwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
@@ -259,7 +275,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const __grid_constant__ CUtensorMap tmdv, const BwdTC p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Layout L = bwd_layout();
+  constexpr int NP = kAux ? 5 : 3;  // coefficient planes per query slot
+  const Layout L = bwd_layout(NP);
   uint8_t* sK = smem + L.k;
   uint8_t* sV = smem + L.v;
   uint8_t* sQ = smem + L.q;
@@ -327,14 +344,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = nq & 1;
         if (nq >= 2) ok = ok && mbar_wait(&bar->q_empty[s], ((nq >> 1) - 1) & 1, err, kErrBwd | 2);
         if (!ok) return;
-        mbar_arrive_expect_tx(&bar->q_full[s], 2 * kTileBytes + 3 * kTile * 4);
+        mbar_arrive_expect_tx(&bar->q_full[s], 2 * kTileBytes + NP * kTile * 4);
         tma_load_4d(sQ + s * kTileBytes, &tmq, &bar->q_full[s], 0, bh % H, jj * kTile, bh / H);
         tma_load_4d(sDO + s * kTileBytes, &tmdo, &bar->q_full[s], 0, bh % H, jj * kTile, bh / H);
         const long long ab_off = (long long)bh * p.tpad + jj * kTile;
         const long long plane = (long long)p.B * H * p.tpad;
 #pragma unroll
-        for (int z = 0; z < 3; ++z)
-          bulk_load_1d(sAB + (s * 3 + z) * kTile, p.coef + z * plane + ab_off, kTile * 4, &bar->q_full[s]);
+        for (int z = 0; z < NP; ++z)
+          bulk_load_1d(sAB + (s * NP + z) * kTile, p.coef + z * plane + ab_off, kTile * 4, &bar->q_full[s]);
         ++nq;
       };
       for (int u = u0; u < u1 && ok; ++u) {
@@ -563,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int bb = bh / H, h = bh % H;
       const int tq0 = (i_key + c) * kTile;
-      const float* cf = sAB + qs * 3 * kTile;  // α/2 | α·c | β·c
+      const float* cf = sAB + qs * NP * kTile;  // α/2 | α·c | β·c (| a1·c | 1/D)
       bool band[2];
       int lo[2], cnt[2];
 #pragma unroll
@@ -622,6 +639,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float ah[4] = {a4.x, a4.y, a4.z, a4.w};
             const float ad[4] = {d4.x, d4.y, d4.z, d4.w};
             const float bd[4] = {b4.x, b4.y, b4.z, b4.w};
+            float a1[4] = {0.f, 0.f, 0.f, 0.f}, ivd[4] = {0.f, 0.f, 0.f, 0.f};
+            if constexpr (kAux) {
+              const float4 u4 = *reinterpret_cast<const float4*>(cf + 3 * kTile + cq0 + e4);
+              const float4 v4 = *reinterpret_cast<const float4*>(cf + 4 * kTile + cq0 + e4);
+              a1[0] = u4.x; a1[1] = u4.y; a1[2] = u4.z; a1[3] = u4.w;
+              ivd[0] = v4.x; ivd[1] = v4.y; ivd[2] = v4.z; ivd[3] = v4.w;
+            }
             float pv[4], dv[4];
 #pragma unroll
             for (int z = 0; z < 4; ++z) {
@@ -632,6 +656,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               if constexpr (kBias) x += gb[e];
               if constexpr (kDTau) dt += gd[e];
               const float th = tanh_approx(x);
+              if constexpr (kAux) {
+                // per-row τ cotangent a1·(log2 q − 1e-8/(q·ln 2)) (its a0 is in β),
+                // q = τ/D + 1e-8 at the recomputed τ = (1 + th)/2
+                const float q = fmaf(fmaf(0.5f, th, 0.5f), ivd[z], 1e-8f);
+                dt = fmaf(a1[z], fmaf(-kEpsOverLn2, __fdividef(1.f, q), __log2f(q)), dt);
+              }
               pv[z] = valid ? fmaf(ah[z], th, ah[z]) : 0.f;
               dv[z] = valid ? dt * fmaf(-th, th, 1.f) : 0.f;
             }
@@ -692,10 +722,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <bool kBias, bool kDTau>
+template <bool kBias, bool kDTau, bool kAux>
 cudaError_t launch_bwd_variant(const CUtensorMap* m, const BwdTC& a, size_t smem, int grid,
                                cudaStream_t st) {
-  auto kern = tc_bwd_kernel<kBias, kDTau>;
+  auto kern = tc_bwd_kernel<kBias, kDTau, kAux>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, smem, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], m[6], a);
@@ -712,7 +742,8 @@ cudaError_t launch_alpha_beta(const BwdP& p, int tpad, float ds_scale, float* co
   const int gx = (int)std::max<long long>(1, std::min<long long>(per_b, (num_sms() * 16LL + p.B - 1) / p.B));
   alpha_beta_kernel<<<dim3(gx, p.B), 256, 0, st>>>(p.B, p.T, p.H, p.W, tpad, p.norm, ds_scale,
                                                    p.row_mass, p.dout, p.out, coef, coef + n,
-                                                   coef + 2 * n);
+                                                   coef + 2 * n, p.aux_row, coef + 3 * n,
+                                                   coef + 4 * n);
   return cudaGetLastError();
 }
 
@@ -769,15 +800,23 @@ cudaError_t launch_tc_bwd(const BwdP& p, cudaStream_t st, int* launches) {
   void* outs[3] = {p.dq, p.dk, p.dv};
   for (int i = 0; i < 3; ++i)
     if (!make_tmap_bthd(&m[4 + i], outs[i], ob, ot, oh, p.B, p.T, p.H, kTile)) return cudaErrorInvalidValue;
-  const Layout L = bwd_layout();
+  const bool has_aux = p.aux_row != nullptr;
+  const Layout L = bwd_layout(has_aux ? 5 : 3);
   const size_t smem = L.total + 1024;
   const int grid = std::min(num_sms(), a.total);
   *launches = 2;
   const bool has_bias = p.bias != nullptr, has_dtau = p.dtau != nullptr;
-  if (has_bias && has_dtau) return launch_bwd_variant<true, true>(m, a, smem, grid, st);
-  if (has_bias) return launch_bwd_variant<true, false>(m, a, smem, grid, st);
-  if (has_dtau) return launch_bwd_variant<false, true>(m, a, smem, grid, st);
-  return launch_bwd_variant<false, false>(m, a, smem, grid, st);
+  const int v = (has_bias ? 4 : 0) | (has_dtau ? 2 : 0) | (has_aux ? 1 : 0);
+  switch (v) {
+    case 0: return launch_bwd_variant<false, false, false>(m, a, smem, grid, st);
+    case 1: return launch_bwd_variant<false, false, true>(m, a, smem, grid, st);
+    case 2: return launch_bwd_variant<false, true, false>(m, a, smem, grid, st);
+    case 3: return launch_bwd_variant<false, true, true>(m, a, smem, grid, st);
+    case 4: return launch_bwd_variant<true, false, false>(m, a, smem, grid, st);
+    case 5: return launch_bwd_variant<true, false, true>(m, a, smem, grid, st);
+    case 6: return launch_bwd_variant<true, true, false>(m, a, smem, grid, st);
+    default: return launch_bwd_variant<true, true, true>(m, a, smem, grid, st);
+  }
 }
 
 }  // namespace bozo

@@ -332,14 +332,16 @@ def tension_entropy_loss(all_tensions):
     return total / len(all_tensions)
 
 
-def aux_losses(all_tensions, window_groups=None):
+def aux_losses(all_tensions, window_groups=None, grad_consistency=True):
     """(diversity, consistency, entropy) as train.py:1083-1087 computes them.
     CUDA τ fields go through the fused τ consumer (``bozo_b200.aux``: one
-    kernel pass over every field, one for the cotangent); the framework-op
-    formulas above serve the harness when it runs on CPU tensors."""
+    kernel pass over every field, one for the cotangent — per query row,
+    inside the tension backward, when the consistency term takes no
+    gradient); the framework-op formulas above serve the harness when it
+    runs on CPU tensors."""
     if all_tensions and all_tensions[0].is_cuda:
         from .aux import tension_aux_losses
-        return tension_aux_losses(all_tensions, window_groups)
+        return tension_aux_losses(all_tensions, window_groups, grad_consistency)
     return (tension_diversity_loss(all_tensions, window_groups),
             constraint_consistency_loss(all_tensions), tension_entropy_loss(all_tensions))
 
@@ -398,7 +400,9 @@ def train_step(model, base_model: TensionLM, optimizer, inputs, targets,
             logits, hidden, tensions = model(inputs), None, []
         loss = F.cross_entropy(logits.reshape(-1, V), targets.reshape(-1))
         if weights.aux_enabled and tensions:
-            div, cons, ent = aux_losses(tensions, base_model.window_groups)
+            # a zero consistency weight gives that term no gradient
+            div, cons, ent = aux_losses(tensions, base_model.window_groups,
+                                        grad_consistency=weights.w_consistency != 0.0)
             loss = (loss
                     + weights.w_closure * manifold_closure_loss(hidden)
                     + weights.w_diversity * div

@@ -137,14 +137,50 @@ def _launch_fwd(q, k, v, *, mode, window, norm, scale, rope, bias, tau_width,
 
 
 def _launch_bwd(q, k, v, d_out, *, mode, window, norm, scale, rope, bias, out,
-                mass, d_tau, qk_rotated=False):
+                mass, d_tau, qk_rotated=False, aux_row=None):
     """One backward through the C ABI (via the C++ extension); returns
-    (dq, dk, dv) in the dtypes of q, k, v."""
+    (dq, dk, dv) in the dtypes of q, k, v.  ``aux_row`` ([3, B·H·T] fp32):
+    a per-query-row cotangent of τ the tensor-core kernel forms itself
+    (``bozo_tension_bwd_args.aux_row``)."""
     cos, sin, theta = _rope_args(rope)
     dq, dk, dv = _capi.ext().tension_bwd(
         q, k, v, d_out, mode, window, norm, float(scale), _PATH[_path_override], cos, sin,
-        theta, bias, out, mass, d_tau, bool(qk_rotated))
+        theta, bias, out, mass, d_tau, bool(qk_rotated), aux_row)
     return dq, dk, dv
+
+
+class _TauSlot:
+    """Per-query-row cotangent of an exported τ field ([a1 | a0 | 1/D] planes
+    over B·H·T rows), left by the fused τ consumer's backward
+    (``bozo_b200.aux``) for the backward of the tension call that exported
+    the field, which forms the per-element cotangent itself instead of
+    reading a materialised one.  Attached to the τ tensor as
+    ``_bozo_tau_slot``."""
+
+    __slots__ = ("row",)
+
+    def __init__(self):
+        self.row = None
+
+    def add(self, coef: Tensor) -> None:
+        # a second consumer of the same field: the a1 and a0 planes add, 1/D is shared
+        if self.row is None:
+            self.row = coef
+        else:
+            self.row = torch.cat([self.row[:2] + coef[:2], self.row[2:]])
+
+    def take(self) -> Optional[Tensor]:
+        row, self.row = self.row, None
+        return row
+
+
+def _row_cotangent_ok(q: Tensor, k: Tensor, v: Tensor, mode: int, window: int) -> bool:
+    """The exported τ of this call can take its consumer's cotangent per row:
+    local window on the tensor-core band kernels (bf16, HD 64) with a width
+    the row-mode consumer serves (W = 32, 64, 128)."""
+    return (mode == _capi.MODE_LOCAL and window in (32, 64, 128) and q.shape[3] == 64
+            and q.dtype == k.dtype == v.dtype == torch.bfloat16
+            and _path_override != "simt")
 
 
 def _prep_bias(bias: Optional[Tensor], shape: tuple) -> Optional[Tensor]:
@@ -242,6 +278,11 @@ class _TensionFn(torch.autograd.Function):
         ctx.qk_rotated = q_rot is not None
         ctx.cfg = (mode, w_arg, norm, scale, rope_base, rope_len, return_tau)
         ctx.mark_non_differentiable(mass)
+        # an unused τ (or out) arrives as None in the backward, not as zeros
+        ctx.set_materialize_grads(False)
+        ctx.tau_slot = None
+        if return_tau and _row_cotangent_ok(q, k, v, mode, w_arg):
+            ctx.tau_slot = tau._bozo_tau_slot = _TauSlot()
         if return_tau:
             return out, tau
         return out
@@ -256,11 +297,14 @@ class _TensionFn(torch.autograd.Function):
         d_tau = grads[1] if return_tau else None
         if d_tau is not None:
             d_tau = d_tau.contiguous()
+        aux_row = ctx.tau_slot.take() if ctx.tau_slot is not None else None
+        if aux_row is not None:
+            d_out = d_out.contiguous()  # the tensor-core kernel's TMA view
         rope = (rope_tables(q.shape[3], rope_len, rope_base, q.device)
                 if rope_base is not None else None)
         dq, dk, dv = _launch_bwd(q, k, v, d_out, mode=mode, window=w_arg, norm=norm,
                                  scale=scale, rope=rope, bias=bias, out=out, mass=mass,
-                                 d_tau=d_tau, qk_rotated=ctx.qk_rotated)
+                                 d_tau=d_tau, qk_rotated=ctx.qk_rotated, aux_row=aux_row)
         return dq, dk, dv, None, None, None, None, None, None, None, None, None
 
 

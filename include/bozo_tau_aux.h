@@ -57,6 +57,15 @@ typedef struct {
   const void* tau[BOZO_TAU_AUX_MAX_LAYERS];
   const float* d_stats;   /* [n_layers][3] fp32 cotangent of stats, device */
   void* d_tau[BOZO_TAU_AUX_MAX_LAYERS]; /* out: same shape and dtype as tau */
+  /* Row mode (every d_tau NULL, every row_coef set): instead of d_tau write
+   * per query row r = (b·H + h)·T + t the coefficients [a1, a0, inv_d]
+   * ([3][B·H·T] fp32) with which the tension backward forms the cotangent
+   * a1·(log2 q − 1e-8/(q·ln 2)) + a0, q = τ·inv_d + 1e-8, itself
+   * (bozo_tension_bwd_args.aux_row).  That is the diversity and entropy
+   * terms' cotangent exactly, evaluated at the τ the backward recomputes; it
+   * needs the consistency cotangent d_stats[l][1] to be zero (not a per-row
+   * quantity).  2-byte fields with W = 32·G, G ∈ {1, 2, 4, 8}, only. */
+  float* row_coef[BOZO_TAU_AUX_MAX_LAYERS];
 } bozo_tau_aux_bwd_args;
 
 /* Bytes of device scratch the forward needs (per-block partial sums). */
@@ -66,7 +75,8 @@ size_t bozo_tau_aux_workspace(const bozo_tau_aux_fwd_args* args);
  * Returns a bozo_status (bozo_tension.h). */
 int bozo_tau_aux_fwd(const bozo_tau_aux_fwd_args* args, void* stream);
 
-/* Cotangent of every field from d_stats. */
+/* Cotangent of every field from d_stats (or, in row mode, its per-row
+ * coefficients). */
 int bozo_tau_aux_bwd(const bozo_tau_aux_bwd_args* args, void* stream);
 
 #ifdef __cplusplus

@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define BOZO_TENSION_ABI_VERSION 3
+#define BOZO_TENSION_ABI_VERSION 4
 
 typedef enum {
   BOZO_OK = 0,
@@ -135,6 +135,15 @@ typedef struct {
   void* dv;
   void* workspace;        /* device scratch of bozo_tension_bwd_workspace() bytes */
   size_t workspace_bytes;
+  /* Optional cotangent of τ given per query row instead of per element (the
+   * fused τ consumer's diversity and entropy terms, bozo_tau_aux.h): for
+   * every valid slot of query row r = (b·H + h)·T + t it adds
+   *     a1·(log2 q − 1e-8/(q·ln 2)) + a0,   q = τ·inv_d + 1e-8,
+   * a1 = aux_row[r], a0 = aux_row[n + r], inv_d = aux_row[2n + r]
+   * (n = B·H·T) to the cotangent of τ, with τ as the backward recomputes
+   * it.  fp32 [3][B·H·T] or NULL.  LOCAL windows on the tensor-core path
+   * only (BOZO_ERR_UNSUPPORTED otherwise); combines with d_tau. */
+  const float* aux_row;
 } bozo_tension_bwd_args;
 
 /* Forward. Returns bozo_status; launches are asynchronous on `stream`

@@ -37,7 +37,7 @@ def test_library_exports_every_declared_symbol():
     assert set(declared) == set(_capi.EXPORTED)
     for name in declared:
         assert hasattr(lib, name), name
-    assert lib.bozo_tension_abi_version() == 3
+    assert lib.bozo_tension_abi_version() == 4
     assert _capi.status_string(0) == "ok"
 
 
@@ -63,12 +63,12 @@ int main(void) {
   O(bozo_tension_bwd_args, row_mass); O(bozo_tension_bwd_args, bias_stride);
   O(bozo_tension_bwd_args, d_tau); O(bozo_tension_bwd_args, grad_dtype);
   O(bozo_tension_bwd_args, dq); O(bozo_tension_bwd_args, workspace);
-  O(bozo_tension_bwd_args, workspace_bytes);
+  O(bozo_tension_bwd_args, workspace_bytes); O(bozo_tension_bwd_args, aux_row);
   S(bozo_tau_aux_fwd_args); O(bozo_tau_aux_fwd_args, W); O(bozo_tau_aux_fwd_args, tau);
   O(bozo_tau_aux_fwd_args, stats); O(bozo_tau_aux_fwd_args, workspace);
   O(bozo_tau_aux_fwd_args, workspace_bytes);
   S(bozo_tau_aux_bwd_args); O(bozo_tau_aux_bwd_args, tau); O(bozo_tau_aux_bwd_args, d_stats);
-  O(bozo_tau_aux_bwd_args, d_tau);
+  O(bozo_tau_aux_bwd_args, d_tau); O(bozo_tau_aux_bwd_args, row_coef);
   return 0;
 }
 """

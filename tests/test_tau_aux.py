@@ -121,3 +121,72 @@ def test_cpu_fields_raise():
     from bozo_b200 import aux
     with pytest.raises(RuntimeError, match="CUDA"):
         aux.tension_aux_losses([torch.rand(1, 8, 2, 4)], None)
+
+
+# ───────────── row mode: the cotangent formed inside the tension backward ─────────────
+
+def _op_with_aux(q, k, v, d_out, W, weights, grad_consistency):
+    import bozo_b200
+    from bozo_b200 import aux
+    leaves = [x.detach().clone().requires_grad_(True) for x in (q, k, v)]
+    out, tau = bozo_b200.tension(*leaves, window=W, scale=8.0, return_tau=True, normalize="mass")
+    slot = getattr(tau, "_bozo_tau_slot", None)
+    d, c, e = aux.tension_aux_losses([tau], None, grad_consistency=grad_consistency)
+    loss = (out.float() * d_out.float()).sum() + weights[0] * d + weights[1] * c + weights[2] * e
+    grads = torch.autograd.grad(loss, leaves)
+    return grads, slot
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("W", [32, 64, 128])
+def test_row_mode_matches_materialised_cotangent_and_oracle(W):
+    """With the consistency weight 0, the diversity/entropy cotangent of τ goes
+    to the tension backward per query row (a1·(log2 q − 1e-8/(q·ln 2)) + a0 at
+    the recomputed τ) instead of as a [B,T,H,W] tensor: dQ/dK/dV agree with
+    the materialised path and with float64 autograd through the oracle
+    tension and the oracle losses."""
+    from oracle import tension_oracle as orc
+    from tests._tol import assert_close
+    g = torch.Generator().manual_seed(W)
+    B, T, H, HD = 2, 320, 3, 64
+    q, k, v, d_out = (torch.randn(B, T, H, HD, generator=g) for _ in range(4))
+    # heavy aux weights so the τ cotangent matters next to the output's
+    w = (400.0, 0.0, 200.0)
+    dev = torch.device("cuda:0")
+    qb, kb, vb, db = (x.to(dev, torch.bfloat16) for x in (q, k, v, d_out))
+    row, slot = _op_with_aux(qb, kb, vb, db, W, w, grad_consistency=False)
+    assert slot is not None and slot.row is None  # created, filled and consumed
+    mat, _ = _op_with_aux(qb, kb, vb, db, W, w, grad_consistency=True)
+    for name, a, b in zip(("dq", "dk", "dv"), row, mat):
+        assert_close(a, b, torch.bfloat16, f"W{W} row vs materialised {name}")
+
+    # float64 oracle on the same bf16-rounded inputs
+    def fn(q_, k_, v_):
+        out, tau = orc.fused_reference(q_, k_, v_, window=W, scale=8.0, normalize="mass")
+        d = aux_oracle.diversity([tau])
+        e = aux_oracle.entropy([tau])
+        return (out, w[0] * d + w[2] * e)
+
+    xs = [x.to(torch.bfloat16).double() for x in (q, k, v)]
+    _, ref = orc.tension_with_grads(fn, xs, [d_out.to(torch.bfloat16).double(),
+                                             torch.tensor(1.0, dtype=torch.float64)])
+    for name, a, b in zip(("dq", "dk", "dv"), row, ref):
+        assert_close(a, b, torch.bfloat16, f"W{W} row mode vs oracle {name}")
+
+
+@pytest.mark.gpu
+def test_row_cotangent_needs_the_tensor_core_band_path():
+    """The C ABI refuses a per-row τ cotangent on the CUDA-core path."""
+    from bozo_b200 import _capi, ops
+    dev = torch.device("cuda:0")
+    B, T, H, HD, W = 1, 64, 2, 64, 32
+    q, k, v, d_out = (torch.randn(B, T, H, HD, device=dev) for _ in range(4))  # fp32: CUDA-core
+    out, _, mass, _, _ = ops._launch_fwd(q, k, v, mode=_capi.MODE_LOCAL, window=W,
+                                         norm=_capi.NORM_MASS, scale=8.0, rope=None, bias=None,
+                                         tau_width=None, out_dtype=q.dtype, tau_dtype=q.dtype,
+                                         want_mass=True)
+    aux_row = torch.zeros(3, B * H * T, device=dev)
+    with pytest.raises(RuntimeError, match="unsupported"):
+        ops._launch_bwd(q, k, v, d_out, mode=_capi.MODE_LOCAL, window=W, norm=_capi.NORM_MASS,
+                        scale=8.0, rope=None, bias=None, out=out, mass=mass, d_tau=None,
+                        aux_row=aux_row)
