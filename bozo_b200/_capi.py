@@ -75,6 +75,7 @@ class TauAuxFwdArgs(C.Structure):
         ("B", C.c_int32), ("T", C.c_int32), ("H", C.c_int32), ("W", C.c_int32),
         ("tau", C.c_void_p * TAU_AUX_MAX_LAYERS), ("stats", C.c_void_p),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+        ("row_ent", C.c_void_p),
     ]
 
 

@@ -9,7 +9,8 @@ w.r.t. every field.  The per-row work — row sums, entropies of the
 normalised rows, the transitivity hinges, the mean-τ band penalties — runs in
 ``bozo_tau_aux_fwd`` (one read of every field, per-layer statistics) and
 its cotangent in ``bozo_tau_aux_bwd`` (one read and one write per field,
-``include/bozo_tau_aux.h``).  What remains here are the reference's scalar
+``include/bozo_tau_aux.h``); ``uncertainty_gate`` (train.py:411-447) reads
+the per-row entropies of the same pass.  What remains here are the reference's scalar
 tails over those statistics (group means, ``relu(log W − ·)``, the averages),
 so their gradient flows back through ordinary autograd into the statistics'
 cotangent, which the backward kernel reads on the device.
@@ -30,7 +31,7 @@ from torch import Tensor
 
 from . import _capi
 
-__all__ = ["tau_field_stats", "tension_aux_losses"]
+__all__ = ["tau_field_stats", "tension_aux_losses", "uncertainty_gate"]
 
 
 class _TauStatsFn(torch.autograd.Function):
@@ -138,3 +139,30 @@ def tension_aux_losses(all_tensions: Sequence[Tensor], window_groups: Optional[d
     # entropy regulariser (model.py:597-611): average over all layers
     ent_loss = stats[:, 2].sum() / len(all_tensions)
     return div, cons, ent_loss
+
+
+def uncertainty_gate(tensions: Sequence[Tensor], threshold: float = 0.15) -> Tensor:
+    """train.py:411-447: [B, T] float mask, 1 where the mean over layers and
+    heads of the row entropy of ``τ/(Στ+1e-8)`` (over the first min W slots)
+    exceeds ``threshold``.  The entropies come from the statistics pass
+    (``bozo_tau_aux_fwd`` with ``row_ent``), one read of every field; fields
+    wider than the narrowest are cut to its width first, as the reference
+    does.  No gradient (the reference computes it under ``no_grad``)."""
+    if not tensions:
+        raise ValueError("uncertainty_gate: no τ fields")
+    with torch.no_grad():
+        min_w = min(t.shape[-1] for t in tensions)
+        fields = [t if t.shape[-1] == min_w else t[..., :min_w] for t in tensions]
+        for t in fields:
+            if not t.is_cuda:
+                raise RuntimeError("uncertainty_gate: τ fields must be CUDA tensors")
+        B, T, H, _ = fields[0].shape
+        by_kind: Dict[tuple, List[int]] = defaultdict(list)
+        for i, t in enumerate(fields):
+            by_kind[(tuple(t.shape), t.dtype)].append(i)
+        sum_ent = torch.zeros(B, T, device=fields[0].device, dtype=torch.float32)
+        for idx in by_kind.values():
+            ent = _capi.ext().tau_row_entropy([fields[i].contiguous() for i in idx])
+            sum_ent += ent.view(len(idx), B, T, H).mean(-1).sum(0)
+        mean_ent = sum_ent / len(fields)
+        return (mean_ent > threshold).float()

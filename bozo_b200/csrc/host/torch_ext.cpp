@@ -232,6 +232,31 @@ at::Tensor tau_aux_fwd(const std::vector<at::Tensor>& taus) {
   return stats;
 }
 
+// Per-row entropies [L, B·T·H] of the τ fields (bozo_tau_aux_fwd's row_ent).
+at::Tensor tau_row_entropy(const std::vector<at::Tensor>& taus) {
+  check_fields(taus);
+  const c10::cuda::CUDAGuard guard(taus[0].device());
+  const auto stream = at::cuda::getCurrentCUDAStream(taus[0].device().index()).stream();
+  const int64_t L = (int64_t)taus.size();
+  const int64_t rows = taus[0].size(0) * taus[0].size(1) * taus[0].size(2);
+  at::Tensor stats = at::empty({L, 3}, taus[0].options().dtype(at::kFloat));
+  at::Tensor ent = at::empty({L, rows}, taus[0].options().dtype(at::kFloat));
+  for (size_t i0 = 0; i0 < taus.size(); i0 += BOZO_TAU_AUX_MAX_LAYERS) {
+    const size_t n = std::min<size_t>(BOZO_TAU_AUX_MAX_LAYERS, taus.size() - i0);
+    bozo_tau_aux_fwd_args a{};
+    fill_aux(a, taus, i0, n);
+    a.stats = stats.data_ptr<float>() + 3 * i0;
+    a.row_ent = ent.data_ptr<float>() + rows * (int64_t)i0;
+    const size_t ws_bytes = bozo_tau_aux_workspace(&a);
+    at::Tensor ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 1)},
+                              taus[0].options().dtype(at::kByte));
+    a.workspace = ws.data_ptr();
+    a.workspace_bytes = ws_bytes;
+    check(bozo_tau_aux_fwd(&a, stream), "bozo_tau_aux_fwd (row entropies)");
+  }
+  return ent;
+}
+
 // Cotangents of the τ fields from the cotangent [L, 3] of their statistics.
 std::vector<at::Tensor> tau_aux_bwd(const std::vector<at::Tensor>& taus, const at::Tensor& d_stats) {
   check_fields(taus);
@@ -286,6 +311,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tension_bwd", &tension_bwd, "backward through bozo_tension_bwd");
   m.def("tau_aux_fwd", &tau_aux_fwd, "τ-field statistics through bozo_tau_aux_fwd");
   m.def("tau_aux_bwd", &tau_aux_bwd, "τ-field cotangents through bozo_tau_aux_bwd");
+  m.def("tau_row_entropy", &tau_row_entropy, "per-row τ entropies through bozo_tau_aux_fwd");
   m.def("tau_aux_rowcoef", &tau_aux_rowcoef,
         "per-query-row τ cotangent coefficients through bozo_tau_aux_bwd (row mode)");
 }

@@ -173,7 +173,7 @@ __device__ __forceinline__ void fetch_row(const E* tau, long long r, const AuxSh
 
 template <typename E, int G>
 __global__ void __launch_bounds__(kAuxThreads)
-    tau_aux_fwd_vec(AuxPtrs P, AuxShape s, float* __restrict__ partial) {
+    tau_aux_fwd_vec(AuxPtrs P, AuxShape s, float* __restrict__ partial, float* __restrict__ row_ent) {
   constexpr int NV = VecOf<E>::n, RPW = 32 / G;
   const int layer = blockIdx.y;
   const E* tau = static_cast<const E*>(P.tau[layer]);
@@ -199,6 +199,7 @@ __global__ void __launch_bounds__(kAuxThreads)
     const float x4 = NV > 4 ? cur.x[NV > 4 ? 4 : 0] : __shfl_down_sync(0xffffffffu, cur.x[0], 1);
     if (cur.live && g == 0) {
       acc_ent += e;
+      if (row_ent) row_ent[(long long)layer * s.N + base + sub] = e;
       const float mu = sum * s.inv_w;
       acc_pen += fmaxf(0.05f - mu, 0.f) + fmaxf(mu - 0.8f, 0.f);
       if (s.m > 0 && cur.t >= 1) {
@@ -334,7 +335,7 @@ __device__ __forceinline__ void fetch_wide(const E* tau, long long r, const AuxS
 
 template <typename E, int G>
 __global__ void __launch_bounds__(kAuxThreads)
-    tau_aux_fwd_wide(AuxPtrs P, AuxShape s, float* __restrict__ partial) {
+    tau_aux_fwd_wide(AuxPtrs P, AuxShape s, float* __restrict__ partial, float* __restrict__ row_ent) {
   constexpr int RPW = 32 / G;
   const int layer = blockIdx.y;
   const E* tau = static_cast<const E*>(P.tau[layer]);
@@ -369,6 +370,7 @@ __global__ void __launch_bounds__(kAuxThreads)
     e = -kLn2 * invD * group_sum<G>(e);
     if (cur.live && g == 0) {
       acc_ent += e;
+      if (row_ent) row_ent[(long long)layer * s.N + base + sub] = e;
       const float mu = sum * s.inv_w;
       acc_pen += fmaxf(0.05f - mu, 0.f) + fmaxf(mu - 0.8f, 0.f);
       if (s.m > 0 && cur.t >= 1) {
@@ -540,7 +542,7 @@ __global__ void __launch_bounds__(kAuxThreads)
 // One warp per row, any W; the row is re-read for every pass.
 template <typename E>
 __global__ void __launch_bounds__(kAuxThreads)
-    tau_aux_fwd_scalar(AuxPtrs P, AuxShape s, float* __restrict__ partial) {
+    tau_aux_fwd_scalar(AuxPtrs P, AuxShape s, float* __restrict__ partial, float* __restrict__ row_ent) {
   const int layer = blockIdx.y;
   const E* tau = static_cast<const E*>(P.tau[layer]);
   const int lane = threadIdx.x & 31;
@@ -558,6 +560,7 @@ __global__ void __launch_bounds__(kAuxThreads)
     e = -kLn2 * invD * warp_sum(e);
     if (lane == 0) {
       acc_ent += e;
+      if (row_ent) row_ent[(long long)layer * s.N + r] = e;
       const float mu = sum * s.inv_w;
       acc_pen += fmaxf(0.05f - mu, 0.f) + fmaxf(mu - 0.8f, 0.f);
       const int t = query_of(r, s);
@@ -676,21 +679,21 @@ int wide_lanes(int W, const void* const* ptrs, int n) {
 
 template <typename E>
 cudaError_t launch_fwd_narrow(const AuxPtrs& P, const AuxShape& s, int n_layers, int nblk,
-                              float* partial, float* stats, cudaStream_t st);
+                              float* partial, float* stats, float* row_ent, cudaStream_t st);
 
 template <typename E>
 cudaError_t launch_fwd_t(const AuxPtrs& P, const AuxShape& s, int n_layers, int nblk, float* partial,
-                         float* stats, cudaStream_t st) {
+                         float* stats, float* row_ent, cudaStream_t st) {
   const dim3 grid(nblk, n_layers);
   if constexpr (sizeof(E) != 2) {
-    return launch_fwd_narrow<E>(P, s, n_layers, nblk, partial, stats, st);
+    return launch_fwd_narrow<E>(P, s, n_layers, nblk, partial, stats, row_ent, st);
   } else {
     switch (wide_lanes<E>(s.W, P.tau, n_layers)) {
-      case 1: tau_aux_fwd_wide<E, 1><<<grid, kAuxThreads, 0, st>>>(P, s, partial); break;
-      case 2: tau_aux_fwd_wide<E, 2><<<grid, kAuxThreads, 0, st>>>(P, s, partial); break;
-      case 4: tau_aux_fwd_wide<E, 4><<<grid, kAuxThreads, 0, st>>>(P, s, partial); break;
-      case 8: tau_aux_fwd_wide<E, 8><<<grid, kAuxThreads, 0, st>>>(P, s, partial); break;
-      default: return launch_fwd_narrow<E>(P, s, n_layers, nblk, partial, stats, st);
+      case 1: tau_aux_fwd_wide<E, 1><<<grid, kAuxThreads, 0, st>>>(P, s, partial, row_ent); break;
+      case 2: tau_aux_fwd_wide<E, 2><<<grid, kAuxThreads, 0, st>>>(P, s, partial, row_ent); break;
+      case 4: tau_aux_fwd_wide<E, 4><<<grid, kAuxThreads, 0, st>>>(P, s, partial, row_ent); break;
+      case 8: tau_aux_fwd_wide<E, 8><<<grid, kAuxThreads, 0, st>>>(P, s, partial, row_ent); break;
+      default: return launch_fwd_narrow<E>(P, s, n_layers, nblk, partial, stats, row_ent, st);
     }
   }
   cudaError_t e = cudaGetLastError();
@@ -701,16 +704,16 @@ cudaError_t launch_fwd_t(const AuxPtrs& P, const AuxShape& s, int n_layers, int 
 
 template <typename E>
 cudaError_t launch_fwd_narrow(const AuxPtrs& P, const AuxShape& s, int n_layers, int nblk,
-                              float* partial, float* stats, cudaStream_t st) {
+                              float* partial, float* stats, float* row_ent, cudaStream_t st) {
   const dim3 grid(nblk, n_layers);
   switch (vec_lanes<E>(s.W, P.tau, n_layers)) {
-    case 1: tau_aux_fwd_vec<E, 1><<<grid, kAuxThreads, 0, st>>>(P, s, partial); break;
-    case 2: tau_aux_fwd_vec<E, 2><<<grid, kAuxThreads, 0, st>>>(P, s, partial); break;
-    case 4: tau_aux_fwd_vec<E, 4><<<grid, kAuxThreads, 0, st>>>(P, s, partial); break;
-    case 8: tau_aux_fwd_vec<E, 8><<<grid, kAuxThreads, 0, st>>>(P, s, partial); break;
-    case 16: tau_aux_fwd_vec<E, 16><<<grid, kAuxThreads, 0, st>>>(P, s, partial); break;
-    case 32: tau_aux_fwd_vec<E, 32><<<grid, kAuxThreads, 0, st>>>(P, s, partial); break;
-    default: tau_aux_fwd_scalar<E><<<grid, kAuxThreads, 0, st>>>(P, s, partial); break;
+    case 1: tau_aux_fwd_vec<E, 1><<<grid, kAuxThreads, 0, st>>>(P, s, partial, row_ent); break;
+    case 2: tau_aux_fwd_vec<E, 2><<<grid, kAuxThreads, 0, st>>>(P, s, partial, row_ent); break;
+    case 4: tau_aux_fwd_vec<E, 4><<<grid, kAuxThreads, 0, st>>>(P, s, partial, row_ent); break;
+    case 8: tau_aux_fwd_vec<E, 8><<<grid, kAuxThreads, 0, st>>>(P, s, partial, row_ent); break;
+    case 16: tau_aux_fwd_vec<E, 16><<<grid, kAuxThreads, 0, st>>>(P, s, partial, row_ent); break;
+    case 32: tau_aux_fwd_vec<E, 32><<<grid, kAuxThreads, 0, st>>>(P, s, partial, row_ent); break;
+    default: tau_aux_fwd_scalar<E><<<grid, kAuxThreads, 0, st>>>(P, s, partial, row_ent); break;
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -788,9 +791,9 @@ cudaError_t launch_tau_aux_fwd(const bozo_tau_aux_fwd_args& a, int nblk, float* 
   for (int i = 0; i < a.n_layers; ++i) P.tau[i] = a.tau[i];
   const AuxShape s = aux_shape(a.B, a.T, a.H, a.W);
   switch (a.dtype) {
-    case BOZO_DT_F32: return launch_fwd_t<float>(P, s, a.n_layers, nblk, partial, a.stats, st);
-    case BOZO_DT_BF16: return launch_fwd_t<__nv_bfloat16>(P, s, a.n_layers, nblk, partial, a.stats, st);
-    default: return launch_fwd_t<__half>(P, s, a.n_layers, nblk, partial, a.stats, st);
+    case BOZO_DT_F32: return launch_fwd_t<float>(P, s, a.n_layers, nblk, partial, a.stats, a.row_ent, st);
+    case BOZO_DT_BF16: return launch_fwd_t<__nv_bfloat16>(P, s, a.n_layers, nblk, partial, a.stats, a.row_ent, st);
+    default: return launch_fwd_t<__half>(P, s, a.n_layers, nblk, partial, a.stats, a.row_ent, st);
   }
 }
 

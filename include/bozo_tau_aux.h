@@ -3,11 +3,12 @@
  * regularisers of the reference training loop, computed on the device from
  * the τ fields the tension operator exports, plus their cotangent.
  *
- * Reference interfaces replaced (BoggersTheFish/bozo, model.py):
+ * Reference interfaces replaced (BoggersTheFish/bozo):
  *   tension_diversity_loss       model.py:498-532
  *   constraint_consistency_loss  model.py:535-577
  *   tension_entropy_loss         model.py:580-611
- * as train.py:1083-1087 calls them, one τ field [B,T,H,W] per tension layer.
+ * as train.py:1083-1087 calls them, one τ field [B,T,H,W] per tension layer,
+ * and the per-row entropies behind train.py:411-447 uncertainty_gate.
  * The reference evaluates each as a chain of framework ops over stacked
  * copies of the fields; here one launch reads every field once and produces
  * per-layer statistics, and one launch writes each field's cotangent.
@@ -48,6 +49,10 @@ typedef struct {
   float* stats;           /* out: [n_layers][3] fp32, device */
   void* workspace;        /* device scratch of bozo_tau_aux_workspace() bytes */
   size_t workspace_bytes;
+  /* Optional out: [n_layers][B·T·H] fp32, each row's entropy ent_r (the
+   * per-row term of stats[l][0]; train.py:411-447 uncertainty_gate averages
+   * it over heads and layers), or NULL. */
+  float* row_ent;
 } bozo_tau_aux_fwd_args;
 
 typedef struct {

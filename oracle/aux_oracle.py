@@ -17,6 +17,8 @@ regularisers of BoggersTheFish/bozo as train.py:1083-1087 calls them:
   averaged over the layers with ``W ≥ 3``, ``T ≥ 3`` and ``m+1 < T``.
 * ``entropy``     — ``model.py:580-611``: ``relu(0.05 − μ) + relu(μ − 0.8)``
   of the row means ``μ``, averaged over rows, then over layers.
+* ``uncertainty_gate`` — ``train.py:411-447``: 1 where the mean over layers
+  and heads of the row entropy (first min W slots) exceeds the threshold.
 
 ``losses_and_grads`` returns the three values and the gradients of a
 weighted sum w.r.t. every field (autograd of these formulas).  Parity is
@@ -99,3 +101,21 @@ def losses_and_grads(taus: Sequence[torch.Tensor], window_groups: Optional[dict]
     grads = torch.autograd.grad(total, xs, allow_unused=True)
     grads = [g if g is not None else torch.zeros_like(x) for g, x in zip(grads, xs)]
     return (float(d.detach()), float(c.detach()), float(e.detach())), grads
+
+
+def row_entropy_mean(taus: Sequence[torch.Tensor]) -> torch.Tensor:
+    """train.py:431-445: mean over layers and heads of the row entropies of
+    the first min W slots, [B, T] float64."""
+    min_w = min(t.shape[-1] for t in taus)
+    acc = None
+    for t in taus:
+        x = t[..., :min_w].detach().to("cpu", torch.float64)
+        p = x / (x.sum(-1, keepdim=True) + EPS)
+        ent = -(p * torch.log(p + EPS)).sum(-1).mean(-1)
+        acc = ent if acc is None else acc + ent
+    return acc / len(taus)
+
+
+def uncertainty_gate(taus: Sequence[torch.Tensor], threshold: float = 0.15) -> torch.Tensor:
+    """train.py:411-447."""
+    return (row_entropy_mean(taus) > threshold).double()

@@ -7,7 +7,9 @@ Run once in a container that has the reference checkout (default
     python tests/golden/make_golden_aux.py
 
 It writes ``tests/golden/golden_aux.npz``: for a few sets of seeded fp32 τ
-fields, the values of the reference ``tension_diversity_loss``
+fields, the masks of the reference ``uncertainty_gate`` (train.py:411-447)
+at the thresholds ``GATE_THRESHOLDS``, and the values of the reference
+``tension_diversity_loss``
 (model.py:498-532), ``constraint_consistency_loss`` (model.py:535-577) and
 ``tension_entropy_loss`` (model.py:580-611), and the gradients w.r.t. every
 field of ``W_DIV·div + W_CONS·cons + W_ENT·ent`` (all weights non-zero, so
@@ -41,6 +43,7 @@ CASES = {
     "w8": ((2, 24, 2, 8), 3, {8: [0, 1, 2]}, 35),
 }
 W_DIV, W_CONS, W_ENT = 1.0, 0.7, 0.3
+GATE_THRESHOLDS = (0.15, 1.0, 2.0)
 
 
 def make_fields(shape, n, seed):
@@ -66,6 +69,7 @@ def main():
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     import model as M  # the reference's model.py
+    import train as TR  # the reference's train.py (uncertainty_gate)
 
     out = {}
     for name, (shape, n, groups, seed) in CASES.items():
@@ -75,6 +79,8 @@ def main():
         ent = M.tension_entropy_loss(fields)
         total = W_DIV * div + W_CONS * cons + W_ENT * ent
         total.backward()
+        for k, th in enumerate(GATE_THRESHOLDS):
+            out[f"{name}/gate{k}"] = TR.uncertainty_gate([t.detach() for t in fields], th).numpy()
         for i, t in enumerate(fields):
             out[f"{name}/tau{i}"] = t.detach().numpy()
             out[f"{name}/grad{i}"] = t.grad.numpy()

@@ -66,7 +66,7 @@ int main(void) {
   O(bozo_tension_bwd_args, workspace_bytes); O(bozo_tension_bwd_args, aux_row);
   S(bozo_tau_aux_fwd_args); O(bozo_tau_aux_fwd_args, W); O(bozo_tau_aux_fwd_args, tau);
   O(bozo_tau_aux_fwd_args, stats); O(bozo_tau_aux_fwd_args, workspace);
-  O(bozo_tau_aux_fwd_args, workspace_bytes);
+  O(bozo_tau_aux_fwd_args, workspace_bytes); O(bozo_tau_aux_fwd_args, row_ent);
   S(bozo_tau_aux_bwd_args); O(bozo_tau_aux_bwd_args, tau); O(bozo_tau_aux_bwd_args, d_stats);
   O(bozo_tau_aux_bwd_args, d_tau); O(bozo_tau_aux_bwd_args, row_coef);
   return 0;

@@ -112,3 +112,16 @@ def test_aux_oracle_matches_reference(name):
     for g, r in zip(got_grads, grads):
         scale = float(np.abs(r).max()) or 1.0
         np.testing.assert_allclose(g.numpy(), r, rtol=1e-5, atol=1e-6 * scale)
+
+
+GATE_THRESHOLDS = (0.15, 1.0, 2.0)  # tests/golden/make_golden_aux.py
+
+
+@pytest.mark.parametrize("name", _aux_names())
+def test_uncertainty_gate_oracle_matches_reference(name):
+    from oracle import aux_oracle
+    from tests.conftest import _load
+    c = _load("golden_aux.npz")[name]
+    taus, _, _, _ = _aux_case(name)
+    for k, th in enumerate(GATE_THRESHOLDS):
+        np.testing.assert_array_equal(aux_oracle.uncertainty_gate(taus, th).numpy(), c[f"gate{k}"])

@@ -190,3 +190,37 @@ def test_row_cotangent_needs_the_tensor_core_band_path():
         ops._launch_bwd(q, k, v, d_out, mode=_capi.MODE_LOCAL, window=W, norm=_capi.NORM_MASS,
                         scale=8.0, rope=None, bias=None, out=out, mass=mass, d_tau=None,
                         aux_row=aux_row)
+
+
+# ───────────── uncertainty_gate (train.py:411-447) ─────────────
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", _aux_names())
+def test_uncertainty_gate_matches_reference_golden(name):
+    from bozo_b200 import aux
+    from tests.conftest import _load
+    from tests.test_oracle_golden import GATE_THRESHOLDS
+    c = _load("golden_aux.npz")[name]
+    taus, _, _, _ = _aux_case(name)
+    dev = torch.device("cuda:0")
+    for k, th in enumerate(GATE_THRESHOLDS):
+        got = aux.uncertainty_gate([t.to(dev) for t in taus], th)
+        assert got.shape == c[f"gate{k}"].shape and got.dtype == torch.float32
+        np.testing.assert_array_equal(got.cpu().numpy(), c[f"gate{k}"], err_msg=f"{name} th={th}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_uncertainty_gate_vs_oracle_mixed_widths(dtype):
+    """Fields of two widths (the reference cuts all to the narrowest) at a
+    threshold near the median entropy: the masks agree except for rows whose
+    mean entropy lies within fp32 round-off of the threshold."""
+    from bozo_b200 import aux
+    taus = _fields((2, 300, 4, 64), 3, dtype, 3) + _fields((2, 300, 4, 128), 1, dtype, 4)
+    mean_ent = aux_oracle.row_entropy_mean(taus)
+    th = float(mean_ent.median())
+    ref = (mean_ent > th).double()
+    got = aux.uncertainty_gate([t.cuda() for t in taus], th).double().cpu()
+    near = (mean_ent - th).abs() < 1e-4
+    assert torch.equal(got[~near], ref[~near])
+    assert 0.3 < float(got.mean()) < 0.7
