@@ -29,6 +29,7 @@ EXPORTED = (
     "bozo_tension_abi_version", "bozo_tension_last_cuda_error",
     "bozo_tension_bwd_noalloc",
     "bozo_tau_aux_workspace", "bozo_tau_aux_fwd", "bozo_tau_aux_bwd",
+    "bozo_tension_decode",
 )
 TAU_AUX_MAX_LAYERS = 64  # BOZO_TAU_AUX_MAX_LAYERS
 
@@ -66,6 +67,20 @@ class BwdArgs(C.Structure):
         ("dq", C.c_void_p), ("dk", C.c_void_p), ("dv", C.c_void_p),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
         ("aux_row", C.c_void_p),
+    ]
+
+
+class DecodeArgs(C.Structure):
+    _fields_ = [
+        ("B", C.c_int32), ("H", C.c_int32), ("HD", C.c_int32), ("mode", C.c_int32),
+        ("window", C.c_int32), ("normalize", C.c_int32), ("capacity", C.c_int32),
+        ("tau_width", C.c_int32), ("scale", C.c_float), ("pos", C.c_void_p),
+        ("rope_len", C.c_int32), ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
+        ("q", Tensor4), ("k", Tensor4), ("v", Tensor4),
+        ("k_cache", C.c_void_p), ("k_cache_dtype", C.c_int32),
+        ("v_cache", C.c_void_p), ("v_cache_dtype", C.c_int32),
+        ("out", C.c_void_p), ("out_dtype", C.c_int32),
+        ("tau", C.c_void_p), ("tau_dtype", C.c_int32),
     ]
 
 
@@ -121,6 +136,8 @@ def lib():
                 L.bozo_status_string.restype = C.c_char_p
                 L.bozo_tension_abi_version.restype = C.c_int
                 L.bozo_tension_last_cuda_error.restype = C.c_char_p
+                L.bozo_tension_decode.argtypes = [C.POINTER(DecodeArgs), C.c_void_p]
+                L.bozo_tension_decode.restype = C.c_int
                 L.bozo_tau_aux_workspace.argtypes = [C.POINTER(TauAuxFwdArgs)]
                 L.bozo_tau_aux_workspace.restype = C.c_size_t
                 L.bozo_tau_aux_fwd.argtypes = [C.POINTER(TauAuxFwdArgs), C.c_void_p]

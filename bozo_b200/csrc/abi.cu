@@ -348,6 +348,51 @@ int bozo_tau_aux_bwd(const bozo_tau_aux_bwd_args* a, void* stream) {
   return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
 }
 
+int bozo_tension_decode(const bozo_tension_decode_args* a, void* stream) {
+  if (!a) return BOZO_ERR_NULL;
+  if (a->B <= 0 || a->H <= 0 || a->HD <= 0 || a->capacity <= 0) return BOZO_ERR_BAD_SHAPE;
+  if (a->HD > 128) return BOZO_ERR_UNSUPPORTED;
+  if (a->mode != BOZO_MODE_LOCAL && a->mode != BOZO_MODE_GLOBAL) return BOZO_ERR_BAD_SHAPE;
+  if (a->mode == BOZO_MODE_LOCAL && (a->window < 1 || a->capacity < a->window + 1))
+    return BOZO_ERR_BAD_SHAPE;
+  if (a->normalize != BOZO_NORM_NONE && a->normalize != BOZO_NORM_MASS &&
+      a->normalize != BOZO_NORM_COUNT)
+    return BOZO_ERR_BAD_SHAPE;
+  if (!(a->scale != 0.f)) return BOZO_ERR_BAD_SHAPE;
+  if (!a->pos || !a->k_cache || !a->v_cache || !a->out) return BOZO_ERR_NULL;
+  int st;
+  if ((st = check_t4(a->q)) || (st = check_t4(a->k)) || (st = check_t4(a->v))) return st;
+  for (int dt : {a->k_cache_dtype, a->v_cache_dtype, a->out_dtype})
+    if (!dtype_ok(dt)) return BOZO_ERR_BAD_DTYPE;
+  if (a->tau && (!dtype_ok(a->tau_dtype) || a->tau_width < 1)) return BOZO_ERR_BAD_SHAPE;
+  if (a->mode == BOZO_MODE_LOCAL && a->tau && a->tau_width != a->window) return BOZO_ERR_BAD_SHAPE;
+  if (a->rope_len != 0) {
+    if (!a->rope_cos || !a->rope_sin) return BOZO_ERR_NULL;
+    if (a->HD % 2 != 0) return BOZO_ERR_UNSUPPORTED;
+  }
+  cudaError_t e = bind_device(a->q.ptr);
+  if (e != cudaSuccess) return cuda_fail(e);
+  DecodeP p{};
+  p.B = a->B; p.H = a->H; p.HD = a->HD; p.mode = a->mode; p.W = a->window;
+  p.norm = a->normalize; p.C = a->capacity; p.tw = a->tau ? a->tau_width : 0;
+  p.rope_len = a->rope_len; p.inv_scale = 1.0f / a->scale; p.pos = a->pos;
+  p.cos = a->rope_len ? a->rope_cos : nullptr;
+  p.sin = a->rope_len ? a->rope_sin : nullptr;
+  p.q = dev_t4(a->q); p.k = dev_t4(a->k); p.v = dev_t4(a->v);
+  p.kc = a->k_cache; p.kc_dt = a->k_cache_dtype;
+  p.vc = a->v_cache; p.vc_dt = a->v_cache_dtype;
+  p.out = a->out; p.out_dt = a->out_dtype;
+  p.tau = a->tau; p.tau_dt = a->tau_dtype;
+  p.err = error_word(&e);
+  if (!p.err) return cuda_fail(e);
+  if (decode_smem_bytes(p) > 200 * 1024) return BOZO_ERR_UNSUPPORTED;
+  e = launch_decode(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e);
+  t_last_path = BOZO_PATH_SIMT;
+  t_last_launches = 1;
+  return BOZO_OK;
+}
+
 int bozo_tension_poll_error(void* stream) {
   cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return BOZO_ERR_CUDA;

@@ -99,6 +99,28 @@ cudaError_t launch_simt_bwd(const BwdP& p, cudaStream_t st, int* launches);
 // Write RoPE(q), RoPE(k) into p.q_rot / p.k_rot (dtype of q / k).
 cudaError_t launch_rope_copy(const FwdP& p, cudaStream_t st, int* launches);
 
+// One decode step (decode.cu): the new token's projections against ring
+// caches [B, C, H, HD] of rotated keys and values.
+struct DecodeP {
+  int B, H, HD, mode, W, norm, C, tw, rope_len;
+  float inv_scale;
+  const int* pos;  // device: absolute position t of the new token
+  const float* cos;
+  const float* sin;
+  DevT4 q, k, v;   // [B, ·, H, HD] views (T stride unused)
+  void* kc;
+  int kc_dt;
+  void* vc;
+  int vc_dt;
+  void* out;
+  int out_dt;
+  void* tau;
+  int tau_dt;
+  int* err;
+};
+size_t decode_smem_bytes(const DecodeP& p);
+cudaError_t launch_decode(const DecodeP& p, cudaStream_t st);
+
 // Fused τ-field consumer (tau_aux.cu).  Shape of one call's fields and the
 // consistency extents: m = min(W−2, 4) slots (0: the layer is skipped),
 // t_out queries per slot.

@@ -1,0 +1,143 @@
+// decode.cu — one decode step of the tension operator (bozo_tension_decode):
+// the new token's query against ring caches of rotated keys and values.
+// Per step and (b, h) this reads the W cached keys of a local layer (all
+// cached keys of a global one) once, instead of model.py:718-768's
+// generate_cached, which re-runs every layer over the whole context for
+// each new token.
+//
+// Step at position t (read from device memory, so a captured CUDA graph of
+// the whole step can be replayed for every token):
+//   1. RoPE(k_t) and v_t go into ring row t mod C; RoPE(q_t) into shared
+//      memory (half-split rotation, model.py:75-81, tables [rope_len, HD/2]);
+//   2. keys: LOCAL s ∈ [max(0, t−W), t−1] (self excluded, ops.py:29-63),
+//      GLOBAL s ∈ [max(0, t−C+1), t] (self included, model.py:217-237; a
+//      wrapped ring keeps the last C keys); one warp per key, lanes over the
+//      head dimension, τ = σ(q·k/scale) with the exact fp32 sigmoid;
+//   3. normaliser: τ-mass max(Σ τ, 1e-6) (model.py:257-258), valid count
+//      max(min(t, W), 1) (model.py:261-264) or 1 (raw);
+//   4. out[d] = Σ τ·v[d] / normaliser, one thread per head dimension reading
+//      whole value rows;
+//   5. optional τ row: LOCAL slot w = W − (t − s), GLOBAL column c = t − s
+//      (model.py:233-236's flipped window), zero where no key exists.
+// One 128-thread block per (b, h); the cache rows of a (b, h) are only
+// touched by its block.
+#include "common.cuh"
+
+namespace bozo {
+namespace {
+
+constexpr int kDecThreads = 128;
+constexpr int kErrDecode = 0x400;
+
+__global__ void __launch_bounds__(kDecThreads) decode_kernel(DecodeP p) {
+  extern __shared__ float sm[];
+  float* sq = sm;           // rotated q [HD]
+  float* stau = sm + p.HD;  // τ per key [n]
+  __shared__ float red[kDecThreads / 32];
+  const int b = blockIdx.x / p.H, h = blockIdx.x - b * p.H;
+  const int HD = p.HD, half = HD / 2;
+  const int t = __ldg(p.pos);
+  if (t < 0 || (p.cos && t >= p.rope_len)) {  // no table row for this position
+    if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, kErrDecode | 1);
+    return;
+  }
+  const long long qo = (long long)b * p.q.sb + (long long)h * p.q.sh;
+  const long long ko = (long long)b * p.k.sb + (long long)h * p.k.sh;
+  const long long vo = (long long)b * p.v.sb + (long long)h * p.v.sh;
+  const long long crow = (((long long)b * p.C + (t % p.C)) * p.H + h) * HD;
+  // 1. rotate q and k; k, v into ring row t mod C
+  if (p.cos) {
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+      const float c = p.cos[(long long)t * half + i], s = p.sin[(long long)t * half + i];
+      const float q1 = ldf(p.q.p, qo + (long long)i * p.q.sd, p.q.dt);
+      const float q2 = ldf(p.q.p, qo + (long long)(i + half) * p.q.sd, p.q.dt);
+      const float k1 = ldf(p.k.p, ko + (long long)i * p.k.sd, p.k.dt);
+      const float k2 = ldf(p.k.p, ko + (long long)(i + half) * p.k.sd, p.k.dt);
+      sq[i] = q1 * c - q2 * s;
+      sq[i + half] = q1 * s + q2 * c;
+      stf(p.kc, crow + i, p.kc_dt, k1 * c - k2 * s);
+      stf(p.kc, crow + i + half, p.kc_dt, k1 * s + k2 * c);
+    }
+  } else {
+    for (int i = threadIdx.x; i < HD; i += blockDim.x) {
+      sq[i] = ldf(p.q.p, qo + (long long)i * p.q.sd, p.q.dt);
+      stf(p.kc, crow + i, p.kc_dt, ldf(p.k.p, ko + (long long)i * p.k.sd, p.k.dt));
+    }
+  }
+  for (int i = threadIdx.x; i < HD; i += blockDim.x)
+    stf(p.vc, crow + i, p.vc_dt, ldf(p.v.p, vo + (long long)i * p.v.sd, p.v.dt));
+  __syncthreads();  // the block's own cache writes and sq are visible below
+
+  // 2. τ of every key: key j is s = t − 1 − j (local) or s = t − j (global)
+  const bool local = p.mode == BOZO_MODE_LOCAL;
+  const int n = local ? min(t, p.W) : min(t + 1, p.C);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int j = warp; j < n; j += kDecThreads / 32) {
+    const int s = local ? t - 1 - j : t - j;
+    const long long row = (((long long)b * p.C + (s % p.C)) * p.H + h) * HD;
+    float dot = 0.f;
+    for (int d = lane; d < HD; d += 32) dot = fmaf(sq[d], ldf(p.kc, row + d, p.kc_dt), dot);
+    dot = warp_sum(dot);
+    if (lane == 0) stau[j] = sigmoid_exact(dot * p.inv_scale);
+  }
+  __syncthreads();
+
+  // 3. normaliser
+  float den = 1.f;
+  if (p.norm == BOZO_NORM_MASS) {
+    float m = 0.f;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) m += stau[j];
+    m = warp_sum(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = 0.f;
+    for (int w = 0; w < kDecThreads / 32; ++w) m += red[w];
+    den = fmaxf(m, kMassEps);
+  } else if (p.norm == BOZO_NORM_COUNT) {
+    den = (float)max(n, 1);
+  }
+  const float inv_den = 1.f / den;
+
+  // 4. out = Σ τ·v / normaliser
+  const long long oo = ((long long)b * p.H + h) * HD;
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < n; ++j) {
+      const int s = local ? t - 1 - j : t - j;
+      const long long row = (((long long)b * p.C + (s % p.C)) * p.H + h) * HD;
+      acc = fmaf(stau[j], ldf(p.vc, row + d, p.vc_dt), acc);
+    }
+    stf(p.out, oo + d, p.out_dt, acc * inv_den);
+  }
+
+  // 5. this row of the exported τ field
+  if (p.tau) {
+    const long long to = ((long long)b * p.H + h) * p.tw;
+    for (int c = threadIdx.x; c < p.tw; c += blockDim.x) {
+      // LOCAL slot c holds key t − (W − c), i.e. key index j = W − 1 − c;
+      // GLOBAL column c holds key t − c, i.e. j = c
+      const int j = local ? p.W - 1 - c : c;
+      stf(p.tau, to + c, p.tau_dt, (j >= 0 && j < n) ? stau[j] : 0.f);
+    }
+  }
+}
+
+}  // namespace
+
+size_t decode_smem_bytes(const DecodeP& p) {
+  const int n = p.mode == BOZO_MODE_LOCAL ? p.W : p.C;
+  return (size_t)(p.HD + n) * sizeof(float);
+}
+
+cudaError_t launch_decode(const DecodeP& p, cudaStream_t st) {
+  const size_t smem = decode_smem_bytes(p);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  decode_kernel<<<p.B * p.H, kDecThreads, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace bozo

@@ -184,6 +184,64 @@ std::vector<at::Tensor> tension_bwd(const at::Tensor& q, const at::Tensor& k, co
   return {dq, dk, dv};
 }
 
+// One decode step (bozo_tension_decode): q, k, v are the new token's
+// projections [B, H, HD] (any strides, unit HD stride not required); the ring
+// caches [B, C, H, HD] are updated in place.  Returns [out, tau] (tau
+// undefined unless tau_width > 0).
+std::vector<at::Tensor> tension_decode(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                       const at::Tensor& k_cache, const at::Tensor& v_cache,
+                                       const at::Tensor& pos, int64_t mode, int64_t window,
+                                       int64_t norm, double scale,
+                                       const c10::optional<at::Tensor>& cos,
+                                       const c10::optional<at::Tensor>& sin, int64_t tau_width,
+                                       int64_t out_dtype, int64_t tau_dtype) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  if (q.dim() != 3 || k.dim() != 3 || v.dim() != 3)
+    throw std::invalid_argument("tension_decode: q, k, v must be [B, H, HD]");
+  if (k_cache.dim() != 4 || !k_cache.is_contiguous() || !v_cache.is_contiguous() ||
+      v_cache.sizes() != k_cache.sizes())
+    throw std::invalid_argument("tension_decode: caches must be contiguous [B, C, H, HD]");
+  if (pos.scalar_type() != at::kInt || pos.numel() != 1 || !pos.is_cuda())
+    throw std::invalid_argument("tension_decode: pos must be a one-element int32 CUDA tensor");
+  const int64_t B = q.size(0), H = q.size(1), HD = q.size(2);
+  at::Tensor out = at::empty({B, H, HD}, q.options().dtype(scalar_type(out_dtype)));
+  at::Tensor tau;
+  if (tau_width > 0) tau = at::empty({B, H, tau_width}, q.options().dtype(scalar_type(tau_dtype)));
+  auto t4_3 = [](const at::Tensor& t) {
+    bozo_tensor4 s{};
+    s.ptr = t.data_ptr();
+    s.dtype = dtype_code(t.scalar_type());
+    s.stride[0] = t.stride(0);
+    s.stride[1] = 0;
+    s.stride[2] = t.stride(1);
+    s.stride[3] = t.stride(2);
+    return s;
+  };
+  bozo_tension_decode_args a{};
+  a.B = (int32_t)B; a.H = (int32_t)H; a.HD = (int32_t)HD;
+  a.mode = (int32_t)mode; a.window = (int32_t)window; a.normalize = (int32_t)norm;
+  a.capacity = (int32_t)k_cache.size(1);
+  a.tau_width = (int32_t)tau_width;
+  a.scale = (float)scale;
+  a.pos = pos.data_ptr<int32_t>();
+  if (cos && cos->defined()) {
+    a.rope_len = (int32_t)cos->size(0);
+    a.rope_cos = cos->data_ptr<float>();
+    a.rope_sin = sin->data_ptr<float>();
+  }
+  a.q = t4_3(q); a.k = t4_3(k); a.v = t4_3(v);
+  a.k_cache = k_cache.data_ptr(); a.k_cache_dtype = dtype_code(k_cache.scalar_type());
+  a.v_cache = v_cache.data_ptr(); a.v_cache_dtype = dtype_code(v_cache.scalar_type());
+  a.out = out.data_ptr(); a.out_dtype = (int32_t)out_dtype;
+  if (tau.defined()) {
+    a.tau = tau.data_ptr();
+    a.tau_dtype = (int32_t)tau_dtype;
+  }
+  check(bozo_tension_decode(&a, at::cuda::getCurrentCUDAStream(q.device().index()).stream()),
+        "bozo_tension_decode");
+  return {out, tau};
+}
+
 // τ fields of one τ-consumer call: same shape, dtype and device, contiguous.
 void check_fields(const std::vector<at::Tensor>& taus) {
   if (taus.empty()) throw std::invalid_argument("tau_aux: no τ fields");
@@ -309,6 +367,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "PyTorch binding of the bozo tension C ABI";
   m.def("tension_fwd", &tension_fwd, "forward through bozo_tension_fwd");
   m.def("tension_bwd", &tension_bwd, "backward through bozo_tension_bwd");
+  m.def("tension_decode", &tension_decode, "one decode step through bozo_tension_decode");
   m.def("tau_aux_fwd", &tau_aux_fwd, "τ-field statistics through bozo_tau_aux_fwd");
   m.def("tau_aux_bwd", &tau_aux_bwd, "τ-field cotangents through bozo_tau_aux_bwd");
   m.def("tau_row_entropy", &tau_row_entropy, "per-row τ entropies through bozo_tau_aux_fwd");

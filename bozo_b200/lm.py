@@ -112,7 +112,8 @@ class MultiHeadCausalTensionLayer(nn.Module):
         # the operator; tests may substitute a CPU restatement with the same keywords
         self.tension_fn: Callable = ops.tension
 
-    def forward(self, x, return_tensions: bool = False, tau_bias=None):
+    def project(self, x):
+        """q, k, v ``[B, T, H, HD]`` of ``x [B, T, D]`` (model.py:196-199)."""
         B, T, D = x.shape
         H, HD = self.num_heads, self.head_dim
         q = self.wq(x).view(B, T, H, HD)
@@ -122,6 +123,11 @@ class MultiHeadCausalTensionLayer(nn.Module):
         else:
             kv = self.wkv(x).view(B, T, H, 2 * HD)
             k, v = kv.split(HD, dim=-1)
+        return q, k, v
+
+    def forward(self, x, return_tensions: bool = False, tau_bias=None):
+        B, T, D = x.shape
+        q, k, v = self.project(x)
         rope = 10_000.0 if self.rope_enabled else None
         if self.global_layer:
             res = self.tension_fn(q, k, v, window=None, scale=self.scale, rope_base=rope,

@@ -146,6 +146,49 @@ typedef struct {
   const float* aux_row;
 } bozo_tension_bwd_args;
 
+/* One decode step: the query of a new token at position t against ring
+ * caches of the earlier tokens' RoPE-rotated keys and values, O(W) work per
+ * (b, h) for a local layer (O(C) for a global one) instead of model.py:
+ * 718-768's re-run of the whole context per generated token.  The step
+ * first writes RoPE(k_t) and v_t into ring row t mod capacity, then
+ *   LOCAL : keys s ∈ [max(0, t−W), t−1]             (self excluded)
+ *   GLOBAL: keys s ∈ [max(0, t−capacity+1), t]      (self included; a wrapped
+ *           ring keeps the last `capacity` keys, as a sliding context does)
+ *   out    = Σ τ·v / (τ-mass | valid count | 1)   (normalize)
+ *   τ row  = LOCAL slot w ↔ key t − (W − w); GLOBAL column c ↔ key t − c
+ *           (row t of the exported field, model.py:233-236), 0 where no key.
+ * t is read from device memory (`pos`), so the step can be captured in a
+ * CUDA graph and replayed per token.  No bias.  A t outside [0, rope_len)
+ * with RoPE sets the device error word (bozo_tension_poll_error). */
+typedef struct {
+  int32_t B, H, HD;
+  int32_t mode;           /* bozo_mode */
+  int32_t window;         /* LOCAL: W.  GLOBAL: unused (0) */
+  int32_t normalize;      /* bozo_norm */
+  int32_t capacity;       /* ring rows C: LOCAL ≥ W + 1 */
+  int32_t tau_width;      /* columns of the τ row (LOCAL: W) when tau is set */
+  float scale;            /* divisor of the dot product */
+  const int32_t* pos;     /* device int32: position t of the new token */
+  int32_t rope_len;       /* rows of the RoPE tables (> t) or 0 for no RoPE */
+  const float* rope_cos;  /* [rope_len, HD/2] fp32 contiguous, or NULL */
+  const float* rope_sin;
+  bozo_tensor4 q, k, v;   /* the new token's projections as [B,1,H,HD] views */
+  void* k_cache;          /* [B, capacity, H, HD] contiguous, RoPE(k) rows */
+  int32_t k_cache_dtype;
+  void* v_cache;          /* [B, capacity, H, HD] contiguous */
+  int32_t v_cache_dtype;
+  void* out;              /* [B, H, HD] contiguous */
+  int32_t out_dtype;
+  void* tau;              /* [B, H, tau_width] contiguous, or NULL */
+  int32_t tau_dtype;
+} bozo_tension_decode_args;
+
+/* Reference interface replaced: model.py:718-768 (generate_cached: one full
+ * forward over the last max_seq_len tokens per generated token) and the τ
+ * row ts_bridge/streaming.py:100-194 (ingest_step) takes from such a
+ * forward. */
+int bozo_tension_decode(const bozo_tension_decode_args* args, void* stream);
+
 /* Forward. Returns bozo_status; launches are asynchronous on `stream`
  * (a cudaStream_t, NULL = legacy default stream). */
 int bozo_tension_fwd(const bozo_tension_fwd_args* args, void* stream);

@@ -64,6 +64,12 @@ int main(void) {
   O(bozo_tension_bwd_args, d_tau); O(bozo_tension_bwd_args, grad_dtype);
   O(bozo_tension_bwd_args, dq); O(bozo_tension_bwd_args, workspace);
   O(bozo_tension_bwd_args, workspace_bytes); O(bozo_tension_bwd_args, aux_row);
+  S(bozo_tension_decode_args); O(bozo_tension_decode_args, scale); O(bozo_tension_decode_args, pos);
+  O(bozo_tension_decode_args, rope_len); O(bozo_tension_decode_args, rope_sin);
+  O(bozo_tension_decode_args, q); O(bozo_tension_decode_args, v);
+  O(bozo_tension_decode_args, k_cache); O(bozo_tension_decode_args, v_cache_dtype);
+  O(bozo_tension_decode_args, out); O(bozo_tension_decode_args, tau);
+  O(bozo_tension_decode_args, tau_dtype);
   S(bozo_tau_aux_fwd_args); O(bozo_tau_aux_fwd_args, W); O(bozo_tau_aux_fwd_args, tau);
   O(bozo_tau_aux_fwd_args, stats); O(bozo_tau_aux_fwd_args, workspace);
   O(bozo_tau_aux_fwd_args, workspace_bytes); O(bozo_tau_aux_fwd_args, row_ent);
@@ -83,6 +89,7 @@ def test_struct_layout_matches_header():
         lines = subprocess.run([exe], check=True, capture_output=True, text=True).stdout.split("\n")
     names = {"bozo_tensor4": _capi.Tensor4, "bozo_tension_fwd_args": _capi.FwdArgs,
              "bozo_tension_bwd_args": _capi.BwdArgs,
+             "bozo_tension_decode_args": _capi.DecodeArgs,
              "bozo_tau_aux_fwd_args": _capi.TauAuxFwdArgs,
              "bozo_tau_aux_bwd_args": _capi.TauAuxBwdArgs}
     for line in filter(None, lines):
