@@ -445,6 +445,66 @@ def run_tau_consumer(local_rank, iters=20):
     }
 
 
+DECODE_B, DECODE_PROMPT, DECODE_NEW = 16, 960, 64
+
+
+def run_decode(local_rank):
+    """117M TensionLM decoding (the configs[3] model, bf16 weights): 16
+    prompts of 960 tokens prefilled, then 64 tokens per sequence fed one at a
+    time through the ring caches (bozo_b200.decode.StepGraph replays; CUDA
+    events over the last 61 steps).  Beside it the reference's scheme
+    (model.py:718-768 generate_cached: one full forward over the context per
+    generated token), timed on the same model and batch at a 992-token
+    context.  Returns a dict for the JSON line."""
+    from bozo_b200 import decode, lm
+    dev = torch.device("cuda", local_rank)
+    torch.manual_seed(0)
+    model = lm.TensionLM(lm.preset_117m()).to(dev).to(torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(99)
+    ids = torch.randint(0, 32768, (DECODE_B, DECODE_PROMPT + DECODE_NEW), generator=g).to(dev)
+    state = decode.DecodeState(model, DECODE_B, DECODE_PROMPT + DECODE_NEW)
+    decode.prefill(state, ids[:, :DECODE_PROMPT])
+    graph = decode.StepGraph(state)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    warm = 3
+    for t in range(DECODE_PROMPT, DECODE_PROMPT + warm):
+        graph(ids[:, t])
+    torch.cuda.synchronize(dev)
+    e0.record()
+    for t in range(DECODE_PROMPT + warm, DECODE_PROMPT + DECODE_NEW):
+        graph(ids[:, t])
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms_tok = e0.elapsed_time(e1) / (DECODE_NEW - warm)
+    ctx = ids[:, :DECODE_PROMPT + 32]
+    with torch.no_grad():
+        for _ in range(2):
+            model(ctx)
+        torch.cuda.synchronize(dev)
+        e0.record()
+        for _ in range(5):
+            model(ctx)
+        e1.record()
+        torch.cuda.synchronize(dev)
+    ms_full = e0.elapsed_time(e1) / 5
+    del graph, state, model
+    return {
+        "metric": "117M TensionLM decode tokens/s (batch of sequences, one token each per step)",
+        "value": round(DECODE_B / (ms_tok * 1e-3), 1), "unit": "tokens/s",
+        "ms_per_token_step": round(ms_tok, 4),
+        "full_forward_per_token": {"value": round(DECODE_B / (ms_full * 1e-3), 1),
+                                   "unit": "tokens/s", "ms_per_token_step": round(ms_full, 3),
+                                   "scheme": "generate_cached: one forward over the context "
+                                             "per generated token (992-token context)"},
+        "speedup": round(ms_full / ms_tok, 1),
+        "config": {"workload": "TensionLM 117M decode, ring caches + CUDA-graph step",
+                   "batch": DECODE_B, "prompt": DECODE_PROMPT, "new_tokens": DECODE_NEW,
+                   "dtype": "bf16 weights and caches",
+                   "data": "uniform random token ids, random init"},
+    }
+
+
 PREFILL_B, PREFILL_T = 4, 2048  # BASELINE configs[4]: batch 32 over 8 GPUs, seq 2048
 
 
@@ -541,9 +601,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end leg (profiling runs)")
-    ap.add_argument("--workload", default="all", choices=["all", "op", "train", "prefill"],
+    ap.add_argument("--workload", default="all",
+                    choices=["all", "op", "train", "prefill", "decode"],
                     help="op: isolated operator (headline); train: 117M training step; "
-                         "prefill: 350M inference prefill with tau export")
+                         "prefill: 350M inference prefill with tau export; "
+                         "decode: 117M token-by-token decoding")
     ap.add_argument("--train-steps", type=int, default=10)
     ap.add_argument("--train-warmup", type=int, default=3)
     ap.add_argument("--windows", type=int, nargs="+", default=list(WINDOWS),
@@ -608,6 +670,11 @@ def main():
     if args.workload in ("all", "prefill"):
         torch.cuda.empty_cache()
         prefill = run_prefill(args, rank, world, local_rank)
+    decode_obj = None
+    if args.workload in ("all", "decode"):
+        torch.cuda.empty_cache()
+        decode_obj = run_decode(local_rank)
+        decode_obj["n_gpus_running"] = 1  # each rank decodes its own batch; rank 0 reports
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -670,12 +737,19 @@ def main():
                        "data": "uniform random token ids, random init"},
         }
     if results is None:
+        if train_obj is None and prefill_obj is None:
+            print(json.dumps(dict(decode_obj, higher_is_better=True, scaling="weak",
+                                  vs_baseline=None, dtype="bf16", data="synthetic",
+                                  n_gpus=args.gpus)))
+            return
         line = dict(train_obj or prefill_obj)
         line.update({"higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                      "dtype": "bf16", "data": "synthetic"})
         line["config"] = (train_obj or prefill_obj)["config"]
         if train_obj is not None and prefill_obj is not None:
             line["prefill_350m"] = prefill_obj
+        if decode_obj is not None:
+            line["decode_117m"] = decode_obj
         print(json.dumps(line))
         return
 
@@ -725,6 +799,8 @@ def main():
         line["train_117m"] = train_obj
     if prefill_obj is not None:
         line["prefill_350m"] = prefill_obj
+    if decode_obj is not None:
+        line["decode_117m"] = decode_obj
     if n == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     print(json.dumps(line))

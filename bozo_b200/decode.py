@@ -19,6 +19,9 @@ written into the ring by the same kernel.
   100-194 (``ingest_step``) reads from a full forward; otherwise local
   layers use the valid-count normalisation of the plain forward
   (model.py:261-264), as ``generate_cached`` sees it.
+* ``StepGraph``: ``step`` captured once as a CUDA graph and replayed per
+  token (a step is a few hundred small launches; replaying them as one
+  graph removes their host cost).
 * ``generate``: the sampling loop of ``generate_cached`` (repetition
   penalty over the last 32 ids, temperature, nucleus sampling) on top.
 
@@ -40,7 +43,7 @@ from torch import Tensor
 
 from . import _capi, ops
 
-__all__ = ["DecodeState", "prefill", "step", "generate"]
+__all__ = ["DecodeState", "StepGraph", "prefill", "step", "generate"]
 
 
 def _rotate(x: Tensor, cos: Tensor, sin: Tensor, t0: int) -> Tensor:
@@ -165,6 +168,40 @@ def step(state: DecodeState, tokens: Tensor, export: bool = False):
     return (logits, rows) if export else logits
 
 
+class StepGraph:
+    """``step(state, tokens, export)`` captured as one CUDA graph.
+
+    ``__call__(tokens)`` copies the tokens into the graph's input buffer and
+    replays it; the returned logits (and τ rows) are the graph's output
+    buffers, overwritten by the next call.  The position advances on the
+    device inside the graph.  Capturing runs warm-up steps on a side stream
+    first; the state's position is restored afterwards, and the cache rows
+    those steps wrote are rewritten by the next real step before anything
+    reads them (a step writes its own row first)."""
+
+    def __init__(self, state: DecodeState, export: bool = False, warmup: int = 2):
+        self.state = state
+        dev = state.pos.device
+        self.tokens = torch.zeros(state.batch, dtype=torch.long, device=dev)
+        pos0 = state.pos.clone()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                step(state, self.tokens, export)
+                state.pos.copy_(pos0)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = step(state, self.tokens, export)
+        state.pos.copy_(pos0)  # capture recorded the increment without running it
+
+    def __call__(self, tokens: Tensor):
+        self.tokens.copy_(tokens)
+        self.graph.replay()
+        return self.out
+
+
 def _sample(logits: Tensor, recent: List[int], temp: float, top_p: float, rep_penalty: float) -> int:
     """Repetition penalty on the ids of ``recent``, temperature, nucleus
     sampling — the token choice of generate_cached (model.py:748-766)."""
@@ -182,19 +219,23 @@ def _sample(logits: Tensor, recent: List[int], temp: float, top_p: float, rep_pe
 @torch.no_grad()
 def generate(model, input_ids: List[int], max_new: int = 200, temp: float = 0.8,
              top_p: float = 0.92, rep_penalty: float = 1.3,
-             dtype: Optional[torch.dtype] = None) -> List[int]:
+             dtype: Optional[torch.dtype] = None, graph: bool = True) -> List[int]:
     """generate_cached (model.py:718-768) with O(W) tension work per token:
     the prompt (its last max_seq_len ids) is prefilled once, then every new
-    id is one ``step``.  Returns the prompt followed by the new ids."""
+    id is one decode step (a replayed ``StepGraph`` unless ``graph=False``).
+    Returns the prompt followed by the new ids."""
     model.eval()
     ids = list(input_ids)
     ctx = ids[-model.cfg.max_seq_len:]
     dev = next(model.parameters()).device
     state = DecodeState(model, 1, len(ctx) + max_new, dtype=dtype)
     logits = prefill(state, torch.tensor([ctx], dtype=torch.long, device=dev))[0]
+    run = StepGraph(state) if graph and max_new > 1 else (lambda tok: step(state, tok))
+    tok = torch.zeros(1, dtype=torch.long, device=dev)
     for i in range(max_new):
         nxt = _sample(logits, ids[-32:], temp, top_p, rep_penalty)
         ids.append(nxt)
         if i + 1 < max_new:
-            logits = step(state, torch.tensor([nxt], dtype=torch.long, device=dev))[0]
+            tok.fill_(nxt)
+            logits = run(tok)[0]
     return ids

@@ -139,6 +139,35 @@ def test_decode_steps_match_full_forward(name, export):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("export", [False, True])
+def test_step_graph_replays_match_eager_steps(export):
+    """A captured step replayed per token gives the eager steps' logits (and
+    τ rows) and leaves the caches in the same state."""
+    from bozo_b200 import decode
+    torch.manual_seed(9)
+    cfg = lm.TensionConfig(**CFGS["rope_global"])
+    model = lm.TensionLM(cfg).to("cuda:0").eval()
+    g = torch.Generator().manual_seed(10)
+    ids = torch.randint(0, cfg.vocab_size, (2, 70), generator=g).to("cuda:0")
+    states = [decode.DecodeState(model, 2, 70) for _ in range(2)]
+    for st in states:
+        decode.prefill(st, ids[:, :30])
+    graph = decode.StepGraph(states[1], export=export)
+    for t in range(30, 70):
+        eager = decode.step(states[0], ids[:, t], export=export)
+        replay = graph(ids[:, t])
+        if export:
+            torch.testing.assert_close(replay[0], eager[0], rtol=0, atol=0)
+            for a, b in zip(replay[1], eager[1]):
+                torch.testing.assert_close(a, b, rtol=0, atol=0)
+        else:
+            torch.testing.assert_close(replay, eager, rtol=0, atol=0)
+    assert int(states[0].pos) == int(states[1].pos) == 70
+    for a, b in zip(states[0].k_cache + states[0].v_cache, states[1].k_cache + states[1].v_cache):
+        assert torch.equal(a, b)
+
+
+@pytest.mark.gpu
 def test_generate_is_seeded_and_sized():
     from bozo_b200 import decode
     torch.manual_seed(7)
@@ -147,7 +176,7 @@ def test_generate_is_seeded_and_sized():
     torch.manual_seed(8)
     a = decode.generate(model, prompt, max_new=25)
     torch.manual_seed(8)
-    b = decode.generate(model, prompt, max_new=25)
+    b = decode.generate(model, prompt, max_new=25, graph=False)
     assert a == b and len(a) == len(prompt) + 25 and a[:len(prompt)] == prompt
     assert all(0 <= i < 97 for i in a)
 
