@@ -21,6 +21,9 @@
 //      (model.py:233-236's flipped window), zero where no key exists.
 // One 128-thread block per (b, h); the cache rows of a (b, h) are only
 // touched by its block.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 
 namespace bozo {
@@ -122,15 +125,230 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(DecodeP p) {
   }
 }
 
+// ─────────────── vector path: caches of one dtype E, HD ∈ {32, 64, 128} ───────────────
+// Steps 2 and 4 with whole-row vector loads: G = HD·sizeof(E)/16 lanes share
+// one cached key row (one 16-byte load each), so a warp scores 32/G keys per
+// load and two key groups are in flight per iteration; for the values each
+// warp accumulates Σ τ·v over its share of the keys with each lane holding
+// HD/32 consecutive dimensions (coalesced row loads, 4 keys in flight), and
+// the 8 warps' partial sums are added in shared memory.
+constexpr int kFastThreads = 256;
+constexpr int kFastWarps = kFastThreads / 32;
+
+template <typename E> struct DecVec;
+template <> struct DecVec<float> { static constexpr int n = 4; };
+template <> struct DecVec<__nv_bfloat16> { static constexpr int n = 8; };
+template <> struct DecVec<__half> { static constexpr int n = 8; };
+
+__device__ __forceinline__ float dec_f(float v) { return v; }
+__device__ __forceinline__ float dec_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float dec_f(__half v) { return __half2float(v); }
+
+// N consecutive elements (N·sizeof(E) ∈ {2, 4, 8, 16} bytes, aligned) as floats
+template <typename E, int N>
+__device__ __forceinline__ void dec_load(const E* p, float* x) {
+  constexpr int bytes = N * (int)sizeof(E);
+  E e[N];
+  if constexpr (bytes == 16) {
+    *reinterpret_cast<uint4*>(e) = __ldg(reinterpret_cast<const uint4*>(p));
+  } else if constexpr (bytes == 8) {
+    *reinterpret_cast<uint2*>(e) = __ldg(reinterpret_cast<const uint2*>(p));
+  } else if constexpr (bytes == 4) {
+    *reinterpret_cast<uint32_t*>(e) = __ldg(reinterpret_cast<const uint32_t*>(p));
+  } else {
+#pragma unroll
+    for (int k = 0; k < N; ++k) e[k] = p[k];
+  }
+#pragma unroll
+  for (int k = 0; k < N; ++k) x[k] = dec_f(e[k]);
+}
+
+template <typename E, int HD>
+__global__ void __launch_bounds__(kFastThreads) decode_kernel_vec(DecodeP p) {
+  constexpr int NV = DecVec<E>::n, G = HD / NV, KPW = 32 / G, DPL = HD / 32;
+  static_assert(HD % NV == 0 && G <= 32 && (G & (G - 1)) == 0, "lanes per key");
+  extern __shared__ float sm[];
+  float* sq = sm;                      // rotated q [HD]
+  float* part = sm + HD;               // per-warp Σ τ·v [warps][HD]
+  float* stau = part + kFastWarps * HD;  // τ per key [n]
+  __shared__ float red[kFastWarps];
+  const int b = blockIdx.x / p.H, h = blockIdx.x - b * p.H;
+  const int half = HD / 2;
+  const int t = __ldg(p.pos);
+  if (t < 0 || (p.cos && t >= p.rope_len)) {
+    if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, kErrDecode | 1);
+    return;
+  }
+  E* kc = static_cast<E*>(p.kc);
+  E* vc = static_cast<E*>(p.vc);
+  const long long qo = (long long)b * p.q.sb + (long long)h * p.q.sh;
+  const long long ko = (long long)b * p.k.sb + (long long)h * p.k.sh;
+  const long long vo = (long long)b * p.v.sb + (long long)h * p.v.sh;
+  const long long crow = (((long long)b * p.C + (t % p.C)) * p.H + h) * HD;
+  if (p.cos) {
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+      const float c = p.cos[(long long)t * half + i], s = p.sin[(long long)t * half + i];
+      const float q1 = ldf(p.q.p, qo + (long long)i * p.q.sd, p.q.dt);
+      const float q2 = ldf(p.q.p, qo + (long long)(i + half) * p.q.sd, p.q.dt);
+      const float k1 = ldf(p.k.p, ko + (long long)i * p.k.sd, p.k.dt);
+      const float k2 = ldf(p.k.p, ko + (long long)(i + half) * p.k.sd, p.k.dt);
+      sq[i] = q1 * c - q2 * s;
+      sq[i + half] = q1 * s + q2 * c;
+      stf(kc, crow + i, p.kc_dt, k1 * c - k2 * s);
+      stf(kc, crow + i + half, p.kc_dt, k1 * s + k2 * c);
+    }
+  } else {
+    for (int i = threadIdx.x; i < HD; i += blockDim.x) {
+      sq[i] = ldf(p.q.p, qo + (long long)i * p.q.sd, p.q.dt);
+      stf(kc, crow + i, p.kc_dt, ldf(p.k.p, ko + (long long)i * p.k.sd, p.k.dt));
+    }
+  }
+  for (int i = threadIdx.x; i < HD; i += blockDim.x)
+    stf(vc, crow + i, p.vc_dt, ldf(p.v.p, vo + (long long)i * p.v.sd, p.v.dt));
+  __syncthreads();
+
+  const bool local = p.mode == BOZO_MODE_LOCAL;
+  const int n = local ? min(t, p.W) : min(t + 1, p.C);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane % G, sub = lane / G;
+  auto key_row = [&](int j) {
+    const int s = local ? t - 1 - j : t - j;
+    return (((long long)b * p.C + (s % p.C)) * p.H + h) * HD;
+  };
+  // 2. scores: keys j = j0 + sub, two groups per iteration
+  float qv[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) qv[k] = sq[g * NV + k];
+  constexpr int kStep = kFastWarps * KPW;
+  for (int j0 = warp * KPW; j0 < n; j0 += 2 * kStep) {
+    const int ja = j0 + sub, jb = j0 + kStep + sub;
+    float xa[NV], xb[NV];
+    if (ja < n) dec_load<E, NV>(kc + key_row(ja) + g * NV, xa);
+    else
+#pragma unroll
+      for (int k = 0; k < NV; ++k) xa[k] = 0.f;
+    if (jb < n) dec_load<E, NV>(kc + key_row(jb) + g * NV, xb);
+    else
+#pragma unroll
+      for (int k = 0; k < NV; ++k) xb[k] = 0.f;
+    float da = 0.f, db = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      da = fmaf(qv[k], xa[k], da);
+      db = fmaf(qv[k], xb[k], db);
+    }
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) {
+      da += __shfl_xor_sync(0xffffffffu, da, o);
+      db += __shfl_xor_sync(0xffffffffu, db, o);
+    }
+    if (g == 0) {
+      if (ja < n) stau[ja] = sigmoid_exact(da * p.inv_scale);
+      if (jb < n) stau[jb] = sigmoid_exact(db * p.inv_scale);
+    }
+  }
+  __syncthreads();
+
+  // 3. normaliser
+  float den = 1.f;
+  if (p.norm == BOZO_NORM_MASS) {
+    float m = 0.f;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) m += stau[j];
+    m = warp_sum(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = 0.f;
+#pragma unroll
+    for (int w = 0; w < kFastWarps; ++w) m += red[w];
+    den = fmaxf(m, kMassEps);
+  } else if (p.norm == BOZO_NORM_COUNT) {
+    den = (float)max(n, 1);
+  }
+
+  // 4. per-warp Σ τ·v over keys j ≡ warp (mod warps), lane = HD/32 dims
+  float acc[DPL];
+#pragma unroll
+  for (int k = 0; k < DPL; ++k) acc[k] = 0.f;
+  int j = warp;
+  for (; j + 3 * kFastWarps < n; j += 4 * kFastWarps) {
+    float v0[DPL], v1[DPL], v2[DPL], v3[DPL];
+    dec_load<E, DPL>(vc + key_row(j) + lane * DPL, v0);
+    dec_load<E, DPL>(vc + key_row(j + kFastWarps) + lane * DPL, v1);
+    dec_load<E, DPL>(vc + key_row(j + 2 * kFastWarps) + lane * DPL, v2);
+    dec_load<E, DPL>(vc + key_row(j + 3 * kFastWarps) + lane * DPL, v3);
+    const float t0 = stau[j], t1 = stau[j + kFastWarps], t2 = stau[j + 2 * kFastWarps],
+                t3 = stau[j + 3 * kFastWarps];
+#pragma unroll
+    for (int k = 0; k < DPL; ++k)
+      acc[k] = fmaf(t3, v3[k], fmaf(t2, v2[k], fmaf(t1, v1[k], fmaf(t0, v0[k], acc[k]))));
+  }
+  for (; j < n; j += kFastWarps) {
+    float v0[DPL];
+    dec_load<E, DPL>(vc + key_row(j) + lane * DPL, v0);
+    const float t0 = stau[j];
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) acc[k] = fmaf(t0, v0[k], acc[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < DPL; ++k) part[warp * HD + lane * DPL + k] = acc[k];
+  __syncthreads();
+  const float inv_den = 1.f / den;
+  const long long oo = ((long long)b * p.H + h) * HD;
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+    float o = 0.f;
+#pragma unroll
+    for (int w = 0; w < kFastWarps; ++w) o += part[w * HD + d];
+    stf(p.out, oo + d, p.out_dt, o * inv_den);
+  }
+  if (p.tau) {
+    const long long to = ((long long)b * p.H + h) * p.tw;
+    for (int c = threadIdx.x; c < p.tw; c += blockDim.x) {
+      const int jj = local ? p.W - 1 - c : c;
+      stf(p.tau, to + c, p.tau_dt, (jj >= 0 && jj < n) ? stau[jj] : 0.f);
+    }
+  }
+}
+
+template <typename E>
+cudaError_t launch_vec(const DecodeP& p, size_t smem, cudaStream_t st) {
+  auto go = [&](auto kern) {
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+    }
+    kern<<<p.B * p.H, kFastThreads, smem, st>>>(p);
+    return cudaGetLastError();
+  };
+  switch (p.HD) {
+    case 32: return go(decode_kernel_vec<E, 32>);
+    case 64: return go(decode_kernel_vec<E, 64>);
+    default: return go(decode_kernel_vec<E, 128>);
+  }
+}
+
+bool vec_path_ok(const DecodeP& p) {
+  if (p.HD != 32 && p.HD != 64 && p.HD != 128) return false;
+  if (p.kc_dt != p.vc_dt) return false;
+  if ((reinterpret_cast<uintptr_t>(p.kc) | reinterpret_cast<uintptr_t>(p.vc)) & 15) return false;
+  return true;
+}
+
 }  // namespace
 
 size_t decode_smem_bytes(const DecodeP& p) {
   const int n = p.mode == BOZO_MODE_LOCAL ? p.W : p.C;
+  if (vec_path_ok(p)) return (size_t)(p.HD * (1 + kFastWarps) + n) * sizeof(float);
   return (size_t)(p.HD + n) * sizeof(float);
 }
 
 cudaError_t launch_decode(const DecodeP& p, cudaStream_t st) {
   const size_t smem = decode_smem_bytes(p);
+  if (vec_path_ok(p)) {
+    switch (p.kc_dt) {
+      case BOZO_DT_F32: return launch_vec<float>(p, smem, st);
+      case BOZO_DT_BF16: return launch_vec<__nv_bfloat16>(p, smem, st);
+      default: return launch_vec<__half>(p, smem, st);
+    }
+  }
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);

@@ -62,6 +62,24 @@ def test_local_decode_matches_oracle_rows(dtype, W, normalize):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("HD", [32, 48, 128])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_decode_head_dims(HD, dtype):
+    """HD 32 and 128 take the vector kernel, 48 the generic one."""
+    q, k, v = _seq(1, 90, 2, HD, dtype, seed=HD)
+    out, tau = _decode_all(q, k, v, mode=_capi.MODE_LOCAL, W=24, norm=_capi.NORM_MASS, cap=25, tw=24)
+    ref_out, ref_tau = orc.fused_reference(*(x.double() for x in (q, k, v)), window=24,
+                                           scale=SCALE, normalize="mass")
+    assert_close(out, ref_out, dtype, f"HD{HD} out")
+    assert_close(tau, ref_tau, dtype, f"HD{HD} τ rows")
+    out, _ = _decode_all(q, k, v, mode=_capi.MODE_GLOBAL, W=0, norm=_capi.NORM_MASS, cap=90, tw=0)
+    cos, sin = orc.rope_tables(HD, 90, 10_000.0, torch.float64)
+    ref, _, _ = orc.global_tension(orc.rope(q.double(), cos, sin), orc.rope(k.double(), cos, sin),
+                                   v.double(), SCALE)
+    assert_close(out, ref, dtype, f"HD{HD} global out")
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_global_decode_matches_oracle_rows(dtype):
     W, T = 32, 130
