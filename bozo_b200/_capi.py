@@ -1,5 +1,5 @@
-"""ctypes binding of the C ABI declared in ``include/bozo_tension.h`` and
-``include/bozo_tau_aux.h``.
+"""ctypes binding of the C ABI declared in ``include/bozo_tension.h``,
+``include/bozo_tau_aux.h`` and ``include/bozo_graph_bias.h``.
 
 The structures below mirror the header field by field; ``tests/test_abi.py``
 compiles a C probe with gcc and checks every size and offset, and checks
@@ -29,7 +29,7 @@ EXPORTED = (
     "bozo_tension_abi_version", "bozo_tension_last_cuda_error",
     "bozo_tension_bwd_noalloc",
     "bozo_tau_aux_workspace", "bozo_tau_aux_fwd", "bozo_tau_aux_bwd",
-    "bozo_tension_decode",
+    "bozo_tension_decode", "bozo_graph_bias_build",
 )
 TAU_AUX_MAX_LAYERS = 64  # BOZO_TAU_AUX_MAX_LAYERS
 
@@ -81,6 +81,14 @@ class DecodeArgs(C.Structure):
         ("v_cache", C.c_void_p), ("v_cache_dtype", C.c_int32),
         ("out", C.c_void_p), ("out_dtype", C.c_int32),
         ("tau", C.c_void_p), ("tau_dtype", C.c_int32),
+    ]
+
+
+class GraphBiasArgs(C.Structure):
+    _fields_ = [
+        ("T", C.c_int32), ("window", C.c_int32), ("alpha", C.c_double),
+        ("ctx_content", C.c_void_p), ("edge_keys", C.c_void_p), ("edge_weights", C.c_void_p),
+        ("n_edges", C.c_int64), ("out", C.c_void_p), ("stats", C.c_void_p),
     ]
 
 
@@ -136,6 +144,8 @@ def lib():
                 L.bozo_status_string.restype = C.c_char_p
                 L.bozo_tension_abi_version.restype = C.c_int
                 L.bozo_tension_last_cuda_error.restype = C.c_char_p
+                L.bozo_graph_bias_build.argtypes = [C.POINTER(GraphBiasArgs), C.c_void_p]
+                L.bozo_graph_bias_build.restype = C.c_int
                 L.bozo_tension_decode.argtypes = [C.POINTER(DecodeArgs), C.c_void_p]
                 L.bozo_tension_decode.restype = C.c_int
                 L.bozo_tau_aux_workspace.argtypes = [C.POINTER(TauAuxFwdArgs)]

@@ -393,6 +393,17 @@ int bozo_tension_decode(const bozo_tension_decode_args* a, void* stream) {
   return BOZO_OK;
 }
 
+int bozo_graph_bias_build(const bozo_graph_bias_args* a, void* stream) {
+  if (!a) return BOZO_ERR_NULL;
+  if (a->T <= 0 || a->window < 0 || a->n_edges < 0) return BOZO_ERR_BAD_SHAPE;
+  if (!a->ctx_content || !a->out || (a->n_edges > 0 && (!a->edge_keys || !a->edge_weights)))
+    return BOZO_ERR_NULL;
+  cudaError_t e = bind_device(a->out);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = launch_graph_bias(*a, num_sms(), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
+}
+
 int bozo_tension_poll_error(void* stream) {
   cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return BOZO_ERR_CUDA;

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "bozo_graph_bias.h"
 #include "bozo_tau_aux.h"
 #include "bozo_tension.h"
 
@@ -120,6 +121,9 @@ struct DecodeP {
 };
 size_t decode_smem_bytes(const DecodeP& p);
 cudaError_t launch_decode(const DecodeP& p, cudaStream_t st);
+
+// Graph bias on the device (graph_bias.cu).
+cudaError_t launch_graph_bias(const bozo_graph_bias_args& a, int sms, cudaStream_t st);
 
 // Fused τ-field consumer (tau_aux.cu).  Shape of one call's fields and the
 // consistency extents: m = min(W−2, 4) slots (0: the layer is skipped),

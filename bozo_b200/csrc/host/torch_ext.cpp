@@ -16,6 +16,7 @@
 #include <stdexcept>
 #include <string>
 
+#include "bozo_graph_bias.h"
 #include "bozo_tau_aux.h"
 #include "bozo_tension.h"
 
@@ -242,6 +243,36 @@ std::vector<at::Tensor> tension_decode(const at::Tensor& q, const at::Tensor& k,
   return {out, tau};
 }
 
+// Graph bias [T, W] (window > 0) or [T, T] (window 0) from the context's
+// content ids and the sorted edge table; stats [3] (pairs, Σ weight, max)
+// as float64.  Returns [bias, stats].
+std::vector<at::Tensor> graph_bias(const at::Tensor& ctx_content, const at::Tensor& keys,
+                                   const at::Tensor& weights, int64_t window, double alpha) {
+  const c10::cuda::CUDAGuard guard(ctx_content.device());
+  if (ctx_content.scalar_type() != at::kInt || ctx_content.dim() != 1 || !ctx_content.is_contiguous() ||
+      keys.scalar_type() != at::kLong || weights.scalar_type() != at::kDouble ||
+      keys.numel() != weights.numel() || !keys.is_contiguous() || !weights.is_contiguous())
+    throw std::invalid_argument("graph_bias: int32 [T] content ids, int64 keys, float64 weights");
+  const int64_t T = ctx_content.size(0);
+  at::Tensor out = at::empty({T, window > 0 ? window : T}, ctx_content.options().dtype(at::kFloat));
+  at::Tensor stats = at::zeros({3}, ctx_content.options().dtype(at::kDouble));
+  bozo_graph_bias_args a{};
+  a.T = (int32_t)T;
+  a.window = (int32_t)window;
+  a.alpha = alpha;
+  a.ctx_content = ctx_content.data_ptr<int32_t>();
+  a.n_edges = keys.numel();
+  if (a.n_edges > 0) {
+    a.edge_keys = reinterpret_cast<const uint64_t*>(keys.data_ptr<int64_t>());
+    a.edge_weights = weights.data_ptr<double>();
+  }
+  a.out = out.data_ptr<float>();
+  a.stats = stats.data_ptr<double>();
+  check(bozo_graph_bias_build(&a, at::cuda::getCurrentCUDAStream(out.device().index()).stream()),
+        "bozo_graph_bias_build");
+  return {out, stats};
+}
+
 // τ fields of one τ-consumer call: same shape, dtype and device, contiguous.
 void check_fields(const std::vector<at::Tensor>& taus) {
   if (taus.empty()) throw std::invalid_argument("tau_aux: no τ fields");
@@ -368,6 +399,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tension_fwd", &tension_fwd, "forward through bozo_tension_fwd");
   m.def("tension_bwd", &tension_bwd, "backward through bozo_tension_bwd");
   m.def("tension_decode", &tension_decode, "one decode step through bozo_tension_decode");
+  m.def("graph_bias", &graph_bias, "graph bias through bozo_graph_bias_build");
   m.def("tau_aux_fwd", &tau_aux_fwd, "τ-field statistics through bozo_tau_aux_fwd");
   m.def("tau_aux_bwd", &tau_aux_bwd, "τ-field cotangents through bozo_tau_aux_bwd");
   m.def("tau_row_entropy", &tau_row_entropy, "per-row τ entropies through bozo_tau_aux_fwd");

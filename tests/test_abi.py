@@ -13,7 +13,8 @@ from bozo_b200 import _capi
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HEADER = os.path.join(ROOT, "include", "bozo_tension.h")
-HEADERS = [os.path.join(ROOT, "include", h) for h in ("bozo_tension.h", "bozo_tau_aux.h")]
+HEADERS = [os.path.join(ROOT, "include", h)
+           for h in ("bozo_tension.h", "bozo_tau_aux.h", "bozo_graph_bias.h")]
 
 
 def _declared_functions():
@@ -46,6 +47,7 @@ PROBE = r"""
 #include <stddef.h>
 #include "bozo_tension.h"
 #include "bozo_tau_aux.h"
+#include "bozo_graph_bias.h"
 #define O(T, f) printf(#T "." #f " %zu\n", offsetof(T, f))
 #define S(T) printf(#T " %zu\n", sizeof(T))
 int main(void) {
@@ -70,6 +72,8 @@ int main(void) {
   O(bozo_tension_decode_args, k_cache); O(bozo_tension_decode_args, v_cache_dtype);
   O(bozo_tension_decode_args, out); O(bozo_tension_decode_args, tau);
   O(bozo_tension_decode_args, tau_dtype);
+  S(bozo_graph_bias_args); O(bozo_graph_bias_args, alpha); O(bozo_graph_bias_args, ctx_content);
+  O(bozo_graph_bias_args, n_edges); O(bozo_graph_bias_args, out); O(bozo_graph_bias_args, stats);
   S(bozo_tau_aux_fwd_args); O(bozo_tau_aux_fwd_args, W); O(bozo_tau_aux_fwd_args, tau);
   O(bozo_tau_aux_fwd_args, stats); O(bozo_tau_aux_fwd_args, workspace);
   O(bozo_tau_aux_fwd_args, workspace_bytes); O(bozo_tau_aux_fwd_args, row_ent);
@@ -90,6 +94,7 @@ def test_struct_layout_matches_header():
     names = {"bozo_tensor4": _capi.Tensor4, "bozo_tension_fwd_args": _capi.FwdArgs,
              "bozo_tension_bwd_args": _capi.BwdArgs,
              "bozo_tension_decode_args": _capi.DecodeArgs,
+             "bozo_graph_bias_args": _capi.GraphBiasArgs,
              "bozo_tau_aux_fwd_args": _capi.TauAuxFwdArgs,
              "bozo_tau_aux_bwd_args": _capi.TauAuxBwdArgs}
     for line in filter(None, lines):

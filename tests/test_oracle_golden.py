@@ -125,3 +125,35 @@ def test_uncertainty_gate_oracle_matches_reference(name):
     taus, _, _, _ = _aux_case(name)
     for k, th in enumerate(GATE_THRESHOLDS):
         np.testing.assert_array_equal(aux_oracle.uncertainty_gate(taus, th).numpy(), c[f"gate{k}"])
+
+
+# ───────────── graph bias (ts_bridge/bias.py:125-233) ─────────────
+
+def _bias_golden():
+    import json
+    import os
+    from tests.conftest import GOLDEN
+    z = np.load(os.path.join(GOLDEN, "golden_bias.npz"))
+    edges = {(s, d): w for s, d, w in json.loads(str(z["edges"]))}
+    return z, edges
+
+
+class _FixedTokenizer:
+    """tests/golden/make_golden_bias.py's tokenizer: tok{i} for i < 18, else None."""
+
+    def id_to_token(self, i):
+        return f"tok{i}" if i < 18 else None
+
+
+@pytest.mark.parametrize("ctx", ["ctx_a", "ctx_b"])
+def test_bias_oracle_matches_reference(ctx):
+    from oracle import bias_oracle
+    z, edges = _bias_golden()
+    ids, alpha, W = z[f"{ctx}_ids"].tolist(), float(z["alpha"]), int(z["W"])
+    lb, ls = bias_oracle.local_bias(edges, alpha, ids, _FixedTokenizer(), W)
+    gb, gs = bias_oracle.global_bias(edges, alpha, ids, _FixedTokenizer())
+    for b in range(2):
+        np.testing.assert_array_equal(lb, z[f"{ctx}_local"][b])
+        np.testing.assert_array_equal(gb, z[f"{ctx}_global"][b])
+    np.testing.assert_allclose(ls, z[f"{ctx}_local_stats"], rtol=1e-12)
+    np.testing.assert_allclose(gs, z[f"{ctx}_global_stats"], rtol=1e-12)
