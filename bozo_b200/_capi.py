@@ -1,5 +1,6 @@
 """ctypes binding of the C ABI declared in ``include/bozo_tension.h``,
-``include/bozo_tau_aux.h`` and ``include/bozo_graph_bias.h``.
+``include/bozo_tau_aux.h``, ``include/bozo_graph_bias.h`` and
+``include/bozo_block_ops.h``.
 
 The structures below mirror the header field by field; ``tests/test_abi.py``
 compiles a C probe with gcc and checks every size and offset, and checks
@@ -30,6 +31,8 @@ EXPORTED = (
     "bozo_tension_bwd_noalloc",
     "bozo_tau_aux_workspace", "bozo_tau_aux_fwd", "bozo_tau_aux_bwd",
     "bozo_tension_decode", "bozo_graph_bias_build",
+    "bozo_add_rmsnorm_workspace", "bozo_add_rmsnorm_fwd", "bozo_add_rmsnorm_bwd",
+    "bozo_swiglu_fwd", "bozo_swiglu_bwd",
 )
 TAU_AUX_MAX_LAYERS = 64  # BOZO_TAU_AUX_MAX_LAYERS
 
@@ -81,6 +84,23 @@ class DecodeArgs(C.Structure):
         ("v_cache", C.c_void_p), ("v_cache_dtype", C.c_int32),
         ("out", C.c_void_p), ("out_dtype", C.c_int32),
         ("tau", C.c_void_p), ("tau_dtype", C.c_int32),
+    ]
+
+
+class AddRMSNormArgs(C.Structure):
+    _fields_ = [
+        ("rows", C.c_int64), ("width", C.c_int32), ("eps", C.c_float),
+        ("x", C.c_void_p), ("x_dtype", C.c_int32), ("y", C.c_void_p), ("y_dtype", C.c_int32),
+        ("scale", C.c_void_p), ("out", C.c_void_p), ("rstd", C.c_void_p),
+        ("d_out", C.c_void_p), ("dx", C.c_void_p), ("dy", C.c_void_p), ("d_scale", C.c_void_p),
+        ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+    ]
+
+
+class SwiGLUArgs(C.Structure):
+    _fields_ = [
+        ("n", C.c_int64), ("dtype", C.c_int32), ("gate", C.c_void_p), ("value", C.c_void_p),
+        ("out", C.c_void_p), ("d_out", C.c_void_p), ("d_gate", C.c_void_p), ("d_value", C.c_void_p),
     ]
 
 

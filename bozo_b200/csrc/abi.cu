@@ -404,6 +404,82 @@ int bozo_graph_bias_build(const bozo_graph_bias_args* a, void* stream) {
   return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
 }
 
+static int check_norm(const bozo_add_rmsnorm_args* a) {
+  if (!a) return BOZO_ERR_NULL;
+  if (a->rows <= 0 || a->width <= 0) return BOZO_ERR_BAD_SHAPE;
+  if (!norm_width_ok(a->width)) return BOZO_ERR_UNSUPPORTED;
+  if (a->x_dtype != BOZO_DT_F32 && a->x_dtype != BOZO_DT_BF16) return BOZO_ERR_BAD_DTYPE;
+  if (a->y && a->y_dtype != BOZO_DT_F32 && a->y_dtype != BOZO_DT_BF16) return BOZO_ERR_BAD_DTYPE;
+  if (a->y && a->x_dtype == BOZO_DT_BF16 && a->y_dtype != BOZO_DT_BF16) return BOZO_ERR_UNSUPPORTED;
+  if (!a->x || !a->scale || !a->rstd) return BOZO_ERR_NULL;
+  return BOZO_OK;
+}
+
+static NormP norm_params(const bozo_add_rmsnorm_args* a) {
+  NormP p{};
+  p.N = a->rows; p.D = a->width; p.eps = a->eps; p.sms = num_sms();
+  p.x = a->x; p.x_dt = a->x_dtype; p.y = a->y; p.y_dt = a->y_dtype; p.scale = a->scale;
+  p.out = a->out; p.rstd = a->rstd; p.dout = a->d_out; p.dx = a->dx; p.dy = a->dy;
+  p.dscale = a->d_scale; p.part = static_cast<float*>(a->workspace);
+  return p;
+}
+
+size_t bozo_add_rmsnorm_workspace(const bozo_add_rmsnorm_args* a) {
+  if (!a || a->rows <= 0 || a->width <= 0) return 0;
+  return round256((size_t)norm_partial_blocks(a->rows, num_sms()) * a->width * sizeof(float));
+}
+
+int bozo_add_rmsnorm_fwd(const bozo_add_rmsnorm_args* a, void* stream) {
+  int st = check_norm(a);
+  if (st) return st;
+  if (!a->out) return BOZO_ERR_NULL;
+  cudaError_t e = bind_device(a->x);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = launch_add_rmsnorm(norm_params(a), false, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
+}
+
+int bozo_add_rmsnorm_bwd(const bozo_add_rmsnorm_args* a, void* stream) {
+  int st = check_norm(a);
+  if (st) return st;
+  if (!a->d_out || !a->dx || !a->d_scale || (a->y && !a->dy)) return BOZO_ERR_NULL;
+  cudaError_t e = bind_device(a->x);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (!a->workspace || a->workspace_bytes < bozo_add_rmsnorm_workspace(a)) return BOZO_ERR_WORKSPACE;
+  e = launch_add_rmsnorm(norm_params(a), true, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
+}
+
+static int check_swiglu(const bozo_swiglu_args* a) {
+  if (!a) return BOZO_ERR_NULL;
+  if (a->n <= 0 || a->n % 4 != 0) return BOZO_ERR_BAD_SHAPE;
+  if (a->dtype != BOZO_DT_F32 && a->dtype != BOZO_DT_BF16) return BOZO_ERR_BAD_DTYPE;
+  if (!a->gate || !a->value) return BOZO_ERR_NULL;
+  return BOZO_OK;
+}
+
+int bozo_swiglu_fwd(const bozo_swiglu_args* a, void* stream) {
+  int st = check_swiglu(a);
+  if (st) return st;
+  if (!a->out) return BOZO_ERR_NULL;
+  cudaError_t e = bind_device(a->gate);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = launch_swiglu(a->gate, a->value, a->out, nullptr, nullptr, nullptr, a->n, a->dtype, num_sms(),
+                    static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
+}
+
+int bozo_swiglu_bwd(const bozo_swiglu_args* a, void* stream) {
+  int st = check_swiglu(a);
+  if (st) return st;
+  if (!a->d_out || !a->d_gate || !a->d_value) return BOZO_ERR_NULL;
+  cudaError_t e = bind_device(a->gate);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = launch_swiglu(a->gate, a->value, nullptr, a->d_out, a->d_gate, a->d_value, a->n, a->dtype,
+                    num_sms(), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
+}
+
 int bozo_tension_poll_error(void* stream) {
   cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return BOZO_ERR_CUDA;

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "bozo_block_ops.h"
 #include "bozo_graph_bias.h"
 #include "bozo_tau_aux.h"
 #include "bozo_tension.h"
@@ -121,6 +122,31 @@ struct DecodeP {
 };
 size_t decode_smem_bytes(const DecodeP& p);
 cudaError_t launch_decode(const DecodeP& p, cudaStream_t st);
+
+// Fused add + RMSNorm and SwiGLU (norm.cu).
+struct NormP {
+  long long N;
+  int D;
+  float eps;
+  int sms;
+  const void* x;
+  int x_dt;
+  const void* y;
+  int y_dt;
+  const void* scale;
+  void* out;
+  float* rstd;
+  const void* dout;
+  void* dx;
+  void* dy;
+  void* dscale;
+  float* part;  // backward: [blocks][D] partial sums of dscale
+};
+int norm_partial_blocks(long long N, int sms);
+bool norm_width_ok(int D);
+cudaError_t launch_add_rmsnorm(const NormP& p, bool backward, cudaStream_t st);
+cudaError_t launch_swiglu(const void* g, const void* v, void* h, const void* dh, void* dg, void* dv,
+                          long long n, int dt, int sms, cudaStream_t st);
 
 // Graph bias on the device (graph_bias.cu).
 cudaError_t launch_graph_bias(const bozo_graph_bias_args& a, int sms, cudaStream_t st);

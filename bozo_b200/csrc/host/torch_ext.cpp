@@ -16,6 +16,7 @@
 #include <stdexcept>
 #include <string>
 
+#include "bozo_block_ops.h"
 #include "bozo_graph_bias.h"
 #include "bozo_tau_aux.h"
 #include "bozo_tension.h"
@@ -273,6 +274,67 @@ std::vector<at::Tensor> graph_bias(const at::Tensor& ctx_content, const at::Tens
   return {out, stats};
 }
 
+// add + RMSNorm forward: x [N, D] (+ y [N, D]) → (out [N, D] in x's dtype, rstd [N] fp32).
+std::vector<at::Tensor> add_rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& y,
+                                        const at::Tensor& scale, double eps) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor out = at::empty_like(x);
+  at::Tensor rstd = at::empty({x.size(0)}, x.options().dtype(at::kFloat));
+  bozo_add_rmsnorm_args a{};
+  a.rows = x.size(0); a.width = (int32_t)x.size(1); a.eps = (float)eps;
+  a.x = x.data_ptr(); a.x_dtype = dtype_code(x.scalar_type());
+  if (y && y->defined()) { a.y = y->data_ptr(); a.y_dtype = dtype_code(y->scalar_type()); }
+  a.scale = scale.data_ptr(); a.out = out.data_ptr(); a.rstd = rstd.data_ptr<float>();
+  check(bozo_add_rmsnorm_fwd(&a, at::cuda::getCurrentCUDAStream(x.device().index()).stream()),
+        "bozo_add_rmsnorm_fwd");
+  return {out, rstd};
+}
+
+// add + RMSNorm backward → (dx, dy (undefined without y), dscale).
+std::vector<at::Tensor> add_rmsnorm_bwd(const at::Tensor& d_out, const at::Tensor& x,
+                                        const c10::optional<at::Tensor>& y, const at::Tensor& scale,
+                                        const at::Tensor& rstd) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor dx = at::empty_like(x), dy, dscale = at::empty_like(scale);
+  bozo_add_rmsnorm_args a{};
+  a.rows = x.size(0); a.width = (int32_t)x.size(1);
+  a.x = x.data_ptr(); a.x_dtype = dtype_code(x.scalar_type());
+  if (y && y->defined()) {
+    a.y = y->data_ptr(); a.y_dtype = dtype_code(y->scalar_type());
+    dy = at::empty_like(*y);
+    a.dy = dy.data_ptr();
+  }
+  a.scale = scale.data_ptr(); a.rstd = rstd.data_ptr<float>();
+  a.d_out = d_out.data_ptr(); a.dx = dx.data_ptr(); a.d_scale = dscale.data_ptr();
+  const size_t ws_bytes = bozo_add_rmsnorm_workspace(&a);
+  at::Tensor ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 1)}, x.options().dtype(at::kByte));
+  a.workspace = ws.data_ptr(); a.workspace_bytes = ws_bytes;
+  check(bozo_add_rmsnorm_bwd(&a, at::cuda::getCurrentCUDAStream(x.device().index()).stream()),
+        "bozo_add_rmsnorm_bwd");
+  return {dx, dy, dscale};
+}
+
+at::Tensor swiglu_fwd(const at::Tensor& g, const at::Tensor& v) {
+  const c10::cuda::CUDAGuard guard(g.device());
+  at::Tensor h = at::empty_like(g);
+  bozo_swiglu_args a{};
+  a.n = g.numel(); a.dtype = dtype_code(g.scalar_type());
+  a.gate = g.data_ptr(); a.value = v.data_ptr(); a.out = h.data_ptr();
+  check(bozo_swiglu_fwd(&a, at::cuda::getCurrentCUDAStream(g.device().index()).stream()), "bozo_swiglu_fwd");
+  return h;
+}
+
+std::vector<at::Tensor> swiglu_bwd(const at::Tensor& dh, const at::Tensor& g, const at::Tensor& v) {
+  const c10::cuda::CUDAGuard guard(g.device());
+  at::Tensor dg = at::empty_like(g), dv = at::empty_like(v);
+  bozo_swiglu_args a{};
+  a.n = g.numel(); a.dtype = dtype_code(g.scalar_type());
+  a.gate = g.data_ptr(); a.value = v.data_ptr(); a.d_out = dh.data_ptr();
+  a.d_gate = dg.data_ptr(); a.d_value = dv.data_ptr();
+  check(bozo_swiglu_bwd(&a, at::cuda::getCurrentCUDAStream(g.device().index()).stream()), "bozo_swiglu_bwd");
+  return {dg, dv};
+}
+
 // τ fields of one τ-consumer call: same shape, dtype and device, contiguous.
 void check_fields(const std::vector<at::Tensor>& taus) {
   if (taus.empty()) throw std::invalid_argument("tau_aux: no τ fields");
@@ -400,6 +462,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tension_bwd", &tension_bwd, "backward through bozo_tension_bwd");
   m.def("tension_decode", &tension_decode, "one decode step through bozo_tension_decode");
   m.def("graph_bias", &graph_bias, "graph bias through bozo_graph_bias_build");
+  m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd, "residual add + RMSNorm through bozo_add_rmsnorm_fwd");
+  m.def("add_rmsnorm_bwd", &add_rmsnorm_bwd, "its backward through bozo_add_rmsnorm_bwd");
+  m.def("swiglu_fwd", &swiglu_fwd, "SwiGLU through bozo_swiglu_fwd");
+  m.def("swiglu_bwd", &swiglu_bwd, "its backward through bozo_swiglu_bwd");
   m.def("tau_aux_fwd", &tau_aux_fwd, "τ-field statistics through bozo_tau_aux_fwd");
   m.def("tau_aux_bwd", &tau_aux_bwd, "τ-field cotangents through bozo_tau_aux_bwd");
   m.def("tau_row_entropy", &tau_row_entropy, "per-row τ entropies through bozo_tau_aux_fwd");

@@ -1,0 +1,283 @@
+// norm.cu — the elementwise work around the tension operator in a TensionLM
+// block, fused: residual add + RMSNorm (model.py:86-98, the
+// `norm(x + wo(msg))` of model.py:259 and `norm(x + proj(h))` of
+// model.py:330) and SwiGLU (model.py:328-329), forward and backward.
+//
+// add + RMSNorm, rows of width D (a multiple of 128): one warp per row, lane
+// ℓ holding elements 4(ℓ + 32k) … +3 (one 16-byte load of x and one 8- or
+// 16-byte load of y per k), so every warp load is a whole contiguous span of
+// the row.  s = x + y (rounded to X when X is bf16, as a bf16 add is),
+// rstd = rsqrt(mean(s²) + eps), out = s·rstd·scale.  The backward recomputes
+// s from x and y: with g = dout·scale and ŝ = s·rstd,
+//   ds = rstd·(g − ŝ·mean(g·ŝ)),  dx = ds,  dy = ds (in y's dtype),
+//   dscale = Σ_rows dout·ŝ
+// — the last as fixed-order per-block partial sums (each lane keeps its own
+// columns' sums across the block's rows) reduced by a second kernel, instead
+// of a column reduction over the whole [N, D] gradient.
+//
+// SwiGLU: h = silu(g)·v, dg = dh·v·σ(g)·(1 + g·(1 − σ(g))), dv = dh·silu(g),
+// in fp32 per element, one read and one write of each tensor.
+#include <cuda_bf16.h>
+
+#include "bozo_block_ops.h"
+#include "common.cuh"
+
+namespace bozo {
+namespace {
+
+constexpr int kNormWarps = 8;
+
+__device__ __forceinline__ void load4(const float* p, float* v) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+}
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, float* v) {
+  const uint2 a = *reinterpret_cast<const uint2*>(p);
+  v[0] = __uint_as_float(a.x << 16); v[1] = __uint_as_float(a.x & 0xffff0000u);
+  v[2] = __uint_as_float(a.y << 16); v[3] = __uint_as_float(a.y & 0xffff0000u);
+}
+__device__ __forceinline__ void store4(float* p, const float* v) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ void store4(__nv_bfloat16* p, const float* v) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+  *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<const uint32_t*>(&a),
+                                            *reinterpret_cast<const uint32_t*>(&b));
+}
+__device__ __forceinline__ float round_to(float v, float*) { return v; }
+__device__ __forceinline__ float round_to(float v, __nv_bfloat16*) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+// K = D/128 chunks of 4 per lane
+template <typename X, typename Y, int K>
+__global__ void __launch_bounds__(kNormWarps * 32)
+    add_rmsnorm_fwd_kernel(const X* __restrict__ x, const Y* __restrict__ y, const X* __restrict__ scale,
+                           X* __restrict__ out, float* __restrict__ rstd_out, long long N, float eps) {
+  constexpr int D = K * 128;
+  const int lane = threadIdx.x & 31;
+  float sc[K][4];
+#pragma unroll
+  for (int k = 0; k < K; ++k) load4(scale + 4 * (lane + 32 * k), sc[k]);
+  for (long long r = (long long)blockIdx.x * kNormWarps + (threadIdx.x >> 5); r < N;
+       r += (long long)gridDim.x * kNormWarps) {
+    float s[K][4], ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const long long e = r * D + 4 * (lane + 32 * k);
+      load4(x + e, s[k]);
+      if (y) {
+        float yv[4];
+        load4(y + e, yv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s[k][i] = round_to(s[k][i] + yv[i], (X*)nullptr);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ss = fmaf(s[k][i], s[k][i], ss);
+    }
+    ss = warp_sum(ss);
+    const float rstd = rsqrtf(ss * (1.f / D) + eps);
+    if (lane == 0) rstd_out[r] = rstd;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = s[k][i] * rstd * sc[k][i];
+      store4(out + r * D + 4 * (lane + 32 * k), o);
+    }
+  }
+}
+
+template <typename X, typename Y, int K>
+__global__ void __launch_bounds__(kNormWarps * 32)
+    add_rmsnorm_bwd_kernel(const X* __restrict__ dout, const X* __restrict__ x, const Y* __restrict__ y,
+                           const X* __restrict__ scale, const float* __restrict__ rstd_in,
+                           X* __restrict__ dx, Y* __restrict__ dy, float* __restrict__ dscale_part,
+                           long long N) {
+  constexpr int D = K * 128;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float sc[K][4], acc[K][4];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    load4(scale + 4 * (lane + 32 * k), sc[k]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[k][i] = 0.f;
+  }
+  for (long long r = (long long)blockIdx.x * kNormWarps + warp; r < N; r += (long long)gridDim.x * kNormWarps) {
+    const float rstd = rstd_in[r];
+    float sh[K][4], g[K][4], dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const long long e = r * D + 4 * (lane + 32 * k);
+      float dv[4];
+      load4(x + e, sh[k]);
+      if (y) {
+        float yv[4];
+        load4(y + e, yv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sh[k][i] = round_to(sh[k][i] + yv[i], (X*)nullptr);
+      }
+      load4(dout + e, dv);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        sh[k][i] *= rstd;
+        g[k][i] = dv[i] * sc[k][i];
+        dot = fmaf(g[k][i], sh[k][i], dot);
+        acc[k][i] = fmaf(dv[i], sh[k][i], acc[k][i]);
+      }
+    }
+    dot = warp_sum(dot) * (1.f / D);
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float d[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) d[i] = rstd * (g[k][i] - sh[k][i] * dot);
+      const long long e = r * D + 4 * (lane + 32 * k);
+      store4(dx + e, d);
+      if (dy) store4(dy + e, d);
+    }
+  }
+  // block partial of dscale: the warps' column sums, added in warp order
+  __shared__ float red[kNormWarps][D];
+#pragma unroll
+  for (int k = 0; k < K; ++k)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) red[warp][4 * (lane + 32 * k) + i] = acc[k][i];
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNormWarps; ++w) v += red[w][c];
+    dscale_part[(long long)blockIdx.x * D + c] = v;
+  }
+}
+
+// dscale[c] = Σ_blocks part[b][c], in block order (deterministic)
+template <typename X>
+__global__ void dscale_reduce_kernel(const float* __restrict__ part, int nblk, int D, X* __restrict__ dscale) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= D) return;
+  float v = 0.f;
+  for (int b = 0; b < nblk; ++b) v += part[(long long)b * D + c];
+  dscale[c] = (X)v;
+}
+
+template <typename T>
+__global__ void swiglu_fwd_kernel(const T* __restrict__ g, const T* __restrict__ v, T* __restrict__ h,
+                                  long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n / 4;
+       i += (long long)gridDim.x * blockDim.x) {
+    float gv[4], vv[4], o[4];
+    load4(g + 4 * i, gv);
+    load4(v + 4 * i, vv);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = gv[k] / (1.f + expf(-gv[k])) * vv[k];
+    store4(h + 4 * i, o);
+  }
+}
+
+template <typename T>
+__global__ void swiglu_bwd_kernel(const T* __restrict__ dh, const T* __restrict__ g, const T* __restrict__ v,
+                                  T* __restrict__ dg, T* __restrict__ dv, long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n / 4;
+       i += (long long)gridDim.x * blockDim.x) {
+    float d[4], gv[4], vv[4], og[4], ov[4];
+    load4(dh + 4 * i, d);
+    load4(g + 4 * i, gv);
+    load4(v + 4 * i, vv);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float sig = 1.f / (1.f + expf(-gv[k]));
+      ov[k] = d[k] * gv[k] * sig;
+      og[k] = d[k] * vv[k] * sig * (1.f + gv[k] * (1.f - sig));
+    }
+    store4(dg + 4 * i, og);
+    store4(dv + 4 * i, ov);
+  }
+}
+
+int norm_grid(long long N, int sms) {
+  const long long want = (N + kNormWarps - 1) / kNormWarps;
+  const long long cap = (long long)sms * 4;
+  return (int)(want < cap ? (want < 1 ? 1 : want) : cap);
+}
+
+template <typename X, typename Y>
+cudaError_t fwd_t(const NormP& p, cudaStream_t st) {
+  const int grid = norm_grid(p.N, p.sms);
+  const X* x = static_cast<const X*>(p.x);
+  const Y* y = static_cast<const Y*>(p.y);
+  const X* sc = static_cast<const X*>(p.scale);
+  X* out = static_cast<X*>(p.out);
+  switch (p.D / 128) {
+    case 1: add_rmsnorm_fwd_kernel<X, Y, 1><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, p.rstd, p.N, p.eps); break;
+    case 2: add_rmsnorm_fwd_kernel<X, Y, 2><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, p.rstd, p.N, p.eps); break;
+    case 4: add_rmsnorm_fwd_kernel<X, Y, 4><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, p.rstd, p.N, p.eps); break;
+    case 6: add_rmsnorm_fwd_kernel<X, Y, 6><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, p.rstd, p.N, p.eps); break;
+    case 8: add_rmsnorm_fwd_kernel<X, Y, 8><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, p.rstd, p.N, p.eps); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+template <typename X, typename Y>
+cudaError_t bwd_t(const NormP& p, cudaStream_t st) {
+  const int grid = norm_grid(p.N, p.sms);
+  const X* dout = static_cast<const X*>(p.dout);
+  const X* x = static_cast<const X*>(p.x);
+  const Y* y = static_cast<const Y*>(p.y);
+  const X* sc = static_cast<const X*>(p.scale);
+  X* dx = static_cast<X*>(p.dx);
+  Y* dy = static_cast<Y*>(p.dy);
+  switch (p.D / 128) {
+    case 1: add_rmsnorm_bwd_kernel<X, Y, 1><<<grid, kNormWarps * 32, 0, st>>>(dout, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
+    case 2: add_rmsnorm_bwd_kernel<X, Y, 2><<<grid, kNormWarps * 32, 0, st>>>(dout, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
+    case 4: add_rmsnorm_bwd_kernel<X, Y, 4><<<grid, kNormWarps * 32, 0, st>>>(dout, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
+    case 6: add_rmsnorm_bwd_kernel<X, Y, 6><<<grid, kNormWarps * 32, 0, st>>>(dout, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
+    case 8: add_rmsnorm_bwd_kernel<X, Y, 8><<<grid, kNormWarps * 32, 0, st>>>(dout, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
+    default: return cudaErrorInvalidValue;
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  dscale_reduce_kernel<X><<<(p.D + 255) / 256, 256, 0, st>>>(p.part, grid, p.D, static_cast<X*>(p.dscale));
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int norm_partial_blocks(long long N, int sms) { return norm_grid(N, sms); }
+
+bool norm_width_ok(int D) {
+  const int k = D / 128;
+  return D % 128 == 0 && (k == 1 || k == 2 || k == 4 || k == 6 || k == 8);
+}
+
+cudaError_t launch_add_rmsnorm(const NormP& p, bool backward, cudaStream_t st) {
+  const bool xb = p.x_dt == BOZO_DT_BF16;
+  const int yk = p.y ? p.y_dt : -1;
+  if (!backward) {
+    if (!xb && yk == BOZO_DT_BF16) return fwd_t<float, __nv_bfloat16>(p, st);
+    if (!xb) return fwd_t<float, float>(p, st);
+    return fwd_t<__nv_bfloat16, __nv_bfloat16>(p, st);
+  }
+  if (!xb && yk == BOZO_DT_BF16) return bwd_t<float, __nv_bfloat16>(p, st);
+  if (!xb) return bwd_t<float, float>(p, st);
+  return bwd_t<__nv_bfloat16, __nv_bfloat16>(p, st);
+}
+
+cudaError_t launch_swiglu(const void* g, const void* v, void* h, const void* dh, void* dg, void* dv,
+                          long long n, int dt, int sms, cudaStream_t st) {
+  const long long want = (n / 4 + 255) / 256;
+  const int grid = (int)(want < (long long)sms * 8 ? (want < 1 ? 1 : want) : (long long)sms * 8);
+  if (dt == BOZO_DT_BF16) {
+    using T = __nv_bfloat16;
+    if (dh) swiglu_bwd_kernel<T><<<grid, 256, 0, st>>>((const T*)dh, (const T*)g, (const T*)v, (T*)dg, (T*)dv, n);
+    else swiglu_fwd_kernel<T><<<grid, 256, 0, st>>>((const T*)g, (const T*)v, (T*)h, n);
+  } else {
+    if (dh) swiglu_bwd_kernel<float><<<grid, 256, 0, st>>>((const float*)dh, (const float*)g, (const float*)v, (float*)dg, (float*)dv, n);
+    else swiglu_fwd_kernel<float><<<grid, 256, 0, st>>>((const float*)g, (const float*)v, (float*)h, n);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace bozo

@@ -81,7 +81,17 @@ class RMSNorm(nn.Module):
         self.scale = nn.Parameter(torch.ones(dim))
 
     def forward(self, x):
+        from . import block_ops
+        if block_ops.norm_applies(x, None):
+            return block_ops.add_rms_norm(x, None, self.scale, self.eps)
         return F.rms_norm(x, x.shape[-1:], self.scale, self.eps)
+
+    def add_forward(self, x, y):
+        """``self(x + y)`` — one fused kernel each way where it applies."""
+        from . import block_ops
+        if block_ops.norm_applies(x, y):
+            return block_ops.add_rms_norm(x, y, self.scale, self.eps)
+        return self(x + y)
 
 
 class MultiHeadCausalTensionLayer(nn.Module):
@@ -135,18 +145,18 @@ class MultiHeadCausalTensionLayer(nn.Module):
                                   return_tau=return_tensions, normalize="mass",
                                   tau_window=self.local_window)
             msg, tau = res if return_tensions else (res, None)
-            out = self.norm(x + self.dropout(self.wo(msg.reshape(B, T, D))))
+            out = self.norm.add_forward(x, self.dropout(self.wo(msg.reshape(B, T, D))))
             return (out, tau) if return_tensions else out
         if return_tensions:
             msg, tau = self.tension_fn(q, k, v, window=self.window, scale=self.scale,
                                        rope_base=rope, rope_len=self.max_seq_len,
                                        bias=tau_bias, return_tau=True, normalize="mass")
-            out = self.norm(x + self.dropout(self.wo(msg.reshape(B, T, D))))
+            out = self.norm.add_forward(x, self.dropout(self.wo(msg.reshape(B, T, D))))
             return out, tau
         msg = self.tension_fn(q, k, v, window=self.window, scale=self.scale, rope_base=rope,
                               rope_len=self.max_seq_len, bias=tau_bias, normalize="count")
         msg = self.dropout(msg)
-        return self.norm(x + self.wo(msg.reshape(B, T, D)))
+        return self.norm.add_forward(x, self.wo(msg.reshape(B, T, D)))
 
 
 class OscillatoryModulation(nn.Module):
@@ -179,8 +189,10 @@ class TensionFFN(nn.Module):
         self.dropout = nn.Dropout(cfg.dropout)
 
     def forward(self, x):
-        h = F.silu(self.gate(x)) * self.val(x)
-        return self.norm(x + self.dropout(self.proj(h)))
+        from . import block_ops
+        g, v = self.gate(x), self.val(x)
+        h = block_ops.swiglu(g, v) if block_ops.swiglu_applies(g, v) else F.silu(g) * v
+        return self.norm.add_forward(x, self.dropout(self.proj(h)))
 
 
 class TensionBlock(nn.Module):

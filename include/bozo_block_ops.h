@@ -1,0 +1,77 @@
+/*
+ * bozo_block_ops.h — C ABI of the fused elementwise work around the tension
+ * operator in a TensionLM block.
+ *
+ * Reference interfaces replaced (BoggersTheFish/bozo, model.py):
+ *   RMSNorm after a residual add   model.py:86-98 applied to x + wo(msg)
+ *                                  (model.py:259, 283) and x + proj(h)
+ *                                  (model.py:330); plain RMSNorm (y NULL) for
+ *                                  the pre-norm and final norm (model.py:376, 458)
+ *   SwiGLU                         model.py:328-329, silu(gate(x)) · val(x)
+ * each with its backward, in place of the framework's separate add, norm,
+ * silu and multiply kernels and its column reduction for the norm scale's
+ * gradient.
+ *
+ * add + RMSNorm (rows × width, width a multiple of 128 with width/128 ∈
+ * {1, 2, 4, 6, 8}; all tensors contiguous):
+ *   s = x + y (rounded to x's dtype when that is bf16), rstd = rsqrt(mean(s²)
+ *   + eps), out = s·rstd·scale in x's dtype.  x fp32 with y fp32 or bf16, or
+ *   x bf16 with y bf16.  Backward: dx (x's dtype), dy (y's dtype, when y is
+ *   given) = rstd·(g − ŝ·mean(g·ŝ)), g = d_out·scale, ŝ = s·rstd;
+ *   d_scale = Σ_rows d_out·ŝ, summed in a fixed order (deterministic).
+ * SwiGLU (n elements, n a multiple of 4, fp32 or bf16, fp32 arithmetic):
+ *   out = silu(gate)·value; d_gate = d_out·value·σ(gate)·(1 + gate·(1 − σ(gate))),
+ *   d_value = d_out·silu(gate).
+ */
+#ifndef BOZO_BLOCK_OPS_H
+#define BOZO_BLOCK_OPS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+  int64_t rows;
+  int32_t width;
+  float eps;
+  const void* x;          /* [rows, width] residual stream */
+  int32_t x_dtype;        /* bozo_dtype: F32 or BF16 */
+  const void* y;          /* [rows, width] addend, or NULL (plain RMSNorm) */
+  int32_t y_dtype;
+  const void* scale;      /* [width], x's dtype */
+  void* out;              /* forward: [rows, width], x's dtype */
+  float* rstd;            /* [rows]: written by the forward, read by the backward */
+  const void* d_out;      /* backward: cotangent of out, x's dtype */
+  void* dx;               /* backward: x's dtype */
+  void* dy;               /* backward: y's dtype (NULL when y is NULL) */
+  void* d_scale;          /* backward: [width], x's dtype */
+  void* workspace;        /* backward: bozo_add_rmsnorm_workspace() bytes */
+  size_t workspace_bytes;
+} bozo_add_rmsnorm_args;
+
+size_t bozo_add_rmsnorm_workspace(const bozo_add_rmsnorm_args* args);
+int bozo_add_rmsnorm_fwd(const bozo_add_rmsnorm_args* args, void* stream);
+int bozo_add_rmsnorm_bwd(const bozo_add_rmsnorm_args* args, void* stream);
+
+typedef struct {
+  int64_t n;              /* elements, a multiple of 4 */
+  int32_t dtype;          /* bozo_dtype: F32 or BF16 (all tensors) */
+  const void* gate;
+  const void* value;
+  void* out;              /* forward */
+  const void* d_out;      /* backward */
+  void* d_gate;
+  void* d_value;
+} bozo_swiglu_args;
+
+int bozo_swiglu_fwd(const bozo_swiglu_args* args, void* stream);
+int bozo_swiglu_bwd(const bozo_swiglu_args* args, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BOZO_BLOCK_OPS_H */

@@ -14,7 +14,7 @@ from bozo_b200 import _capi
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HEADER = os.path.join(ROOT, "include", "bozo_tension.h")
 HEADERS = [os.path.join(ROOT, "include", h)
-           for h in ("bozo_tension.h", "bozo_tau_aux.h", "bozo_graph_bias.h")]
+           for h in ("bozo_tension.h", "bozo_tau_aux.h", "bozo_graph_bias.h", "bozo_block_ops.h")]
 
 
 def _declared_functions():
@@ -48,6 +48,7 @@ PROBE = r"""
 #include "bozo_tension.h"
 #include "bozo_tau_aux.h"
 #include "bozo_graph_bias.h"
+#include "bozo_block_ops.h"
 #define O(T, f) printf(#T "." #f " %zu\n", offsetof(T, f))
 #define S(T) printf(#T " %zu\n", sizeof(T))
 int main(void) {
@@ -72,6 +73,10 @@ int main(void) {
   O(bozo_tension_decode_args, k_cache); O(bozo_tension_decode_args, v_cache_dtype);
   O(bozo_tension_decode_args, out); O(bozo_tension_decode_args, tau);
   O(bozo_tension_decode_args, tau_dtype);
+  S(bozo_add_rmsnorm_args); O(bozo_add_rmsnorm_args, eps); O(bozo_add_rmsnorm_args, y_dtype);
+  O(bozo_add_rmsnorm_args, scale); O(bozo_add_rmsnorm_args, d_scale);
+  O(bozo_add_rmsnorm_args, workspace_bytes);
+  S(bozo_swiglu_args); O(bozo_swiglu_args, gate); O(bozo_swiglu_args, d_value);
   S(bozo_graph_bias_args); O(bozo_graph_bias_args, alpha); O(bozo_graph_bias_args, ctx_content);
   O(bozo_graph_bias_args, n_edges); O(bozo_graph_bias_args, out); O(bozo_graph_bias_args, stats);
   S(bozo_tau_aux_fwd_args); O(bozo_tau_aux_fwd_args, W); O(bozo_tau_aux_fwd_args, tau);
@@ -95,6 +100,8 @@ def test_struct_layout_matches_header():
              "bozo_tension_bwd_args": _capi.BwdArgs,
              "bozo_tension_decode_args": _capi.DecodeArgs,
              "bozo_graph_bias_args": _capi.GraphBiasArgs,
+             "bozo_add_rmsnorm_args": _capi.AddRMSNormArgs,
+             "bozo_swiglu_args": _capi.SwiGLUArgs,
              "bozo_tau_aux_fwd_args": _capi.TauAuxFwdArgs,
              "bozo_tau_aux_bwd_args": _capi.TauAuxBwdArgs}
     for line in filter(None, lines):

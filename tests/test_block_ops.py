@@ -1,0 +1,91 @@
+"""Fused residual add + RMSNorm and SwiGLU (``bozo_b200.block_ops``,
+``include/bozo_block_ops.h``) against the framework ops they replace
+(``F.rms_norm(x + y)``, ``F.silu(g) * v``), forward and backward, for the
+dtype pairings of the model (fp32 stream + bf16 projection under autocast,
+fp32 + fp32, bf16 + bf16) and every supported width; the scale gradient is
+bit-identical run to run.  CPU: the kernels are not taken for CPU tensors.
+"""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from bozo_b200 import block_ops
+
+
+def _ref_norm(x, y, scale, eps):
+    s = x + y if y is not None else x
+    return F.rms_norm(s, s.shape[-1:], scale, eps)
+
+
+TOL = {torch.float32: dict(rtol=2e-5, atol=2e-5), torch.bfloat16: dict(rtol=1.6e-2, atol=1.6e-2)}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("D", [128, 768, 1024])
+@pytest.mark.parametrize("xd,yd", [(torch.float32, torch.bfloat16), (torch.float32, torch.float32),
+                                   (torch.bfloat16, torch.bfloat16), (torch.float32, None)])
+def test_add_rms_norm_matches_framework(D, xd, yd):
+    g = torch.Generator().manual_seed(D)
+    dev = torch.device("cuda:0")
+    x = (torch.randn(3, 333, D, generator=g) * 2).to(dev, xd)
+    y = torch.randn(3, 333, D, generator=g).to(dev, yd) if yd is not None else None
+    scale = (1 + 0.1 * torch.randn(D, generator=g)).to(dev, xd)
+    dout = torch.randn(3, 333, D, generator=g).to(dev, xd)
+    leaves = [t.clone().requires_grad_(True) if t is not None else None for t in (x, y, scale)]
+    ref_leaves = [t.clone().requires_grad_(True) if t is not None else None for t in (x, y, scale)]
+    assert block_ops.norm_applies(x, y)
+    out = block_ops.add_rms_norm(leaves[0], leaves[1], leaves[2], 1e-6)
+    ref = _ref_norm(ref_leaves[0], ref_leaves[1], ref_leaves[2], 1e-6)
+    assert out.dtype == ref.dtype == xd
+    torch.testing.assert_close(out, ref, **TOL[xd])
+    out.backward(dout)
+    ref.backward(dout)
+    for name, a, b in zip(("dx", "dy", "dscale"), leaves, ref_leaves):
+        if a is None:
+            continue
+        assert a.grad.dtype == b.grad.dtype
+        scale_ = float(b.grad.abs().max())
+        tol = dict(TOL[a.dtype])
+        tol["atol"] = tol["atol"] * max(1.0, scale_)
+        torch.testing.assert_close(a.grad, b.grad, **tol, msg=f"{name} D{D} {xd} {yd}")
+
+
+@pytest.mark.gpu
+def test_scale_gradient_is_deterministic():
+    dev = torch.device("cuda:0")
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(16384, 768, generator=g).to(dev)
+    y = torch.randn(16384, 768, generator=g).to(dev, torch.bfloat16)
+    dout = torch.randn(16384, 768, generator=g).to(dev)
+    grads = []
+    for _ in range(2):
+        s = torch.ones(768, device=dev, requires_grad=True)
+        block_ops.add_rms_norm(x, y, s, 1e-6).backward(dout)
+        grads.append(s.grad.clone())
+    assert torch.equal(grads[0], grads[1])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_swiglu_matches_framework(dtype):
+    gen = torch.Generator().manual_seed(2)
+    dev = torch.device("cuda:0")
+    g = (torch.randn(4, 100, 2304, generator=gen) * 3).to(dev, dtype)
+    v = torch.randn(4, 100, 2304, generator=gen).to(dev, dtype)
+    dh = torch.randn(4, 100, 2304, generator=gen).to(dev, dtype)
+    a = [g.clone().requires_grad_(True), v.clone().requires_grad_(True)]
+    b = [g.clone().requires_grad_(True), v.clone().requires_grad_(True)]
+    out = block_ops.swiglu(*a)
+    ref = F.silu(b[0]) * b[1]
+    tol = TOL[dtype] if dtype == torch.float32 else dict(rtol=1.6e-2, atol=2e-2)
+    torch.testing.assert_close(out, ref, **tol)
+    out.backward(dh)
+    ref.backward(dh)
+    for x, y in zip(a, b):
+        torch.testing.assert_close(x.grad, y.grad, rtol=tol["rtol"], atol=tol["atol"] * 4)
+
+
+def test_cpu_tensors_take_the_framework_ops():
+    x = torch.randn(2, 4, 128)
+    assert not block_ops.norm_applies(x, None)
+    assert not block_ops.swiglu_applies(x, x)
