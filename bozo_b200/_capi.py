@@ -33,6 +33,7 @@ EXPORTED = (
     "bozo_tension_decode", "bozo_graph_bias_build",
     "bozo_add_rmsnorm_workspace", "bozo_add_rmsnorm_fwd", "bozo_add_rmsnorm_bwd",
     "bozo_swiglu_fwd", "bozo_swiglu_bwd",
+    "bozo_cross_entropy_fwd", "bozo_cross_entropy_bwd",
 )
 TAU_AUX_MAX_LAYERS = 64  # BOZO_TAU_AUX_MAX_LAYERS
 
@@ -101,6 +102,14 @@ class SwiGLUArgs(C.Structure):
     _fields_ = [
         ("n", C.c_int64), ("dtype", C.c_int32), ("gate", C.c_void_p), ("value", C.c_void_p),
         ("out", C.c_void_p), ("d_out", C.c_void_p), ("d_gate", C.c_void_p), ("d_value", C.c_void_p),
+    ]
+
+
+class CrossEntropyArgs(C.Structure):
+    _fields_ = [
+        ("rows", C.c_int64), ("vocab", C.c_int32), ("logits", C.c_void_p),
+        ("logits_dtype", C.c_int32), ("targets", C.c_void_p), ("row_lse", C.c_void_p),
+        ("row_loss", C.c_void_p), ("d_scale", C.c_void_p), ("d_logits", C.c_void_p),
     ]
 
 

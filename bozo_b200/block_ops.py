@@ -10,6 +10,9 @@ and backward, as autograd functions.
   dtype — fp32 for the model's fp32 residual stream, as ``rms_norm`` gives
   under bf16 autocast.
 * ``swiglu(g, v)`` = ``silu(g) * v`` (model.py:328-329): one pass each way.
+* ``cross_entropy(logits, targets)`` = ``F.cross_entropy`` (train.py:920,
+  mean over targets ≠ −100) from the logits in their own dtype: one pass
+  for the per-row logsumexp, one for the gradient, no fp32 copy.
 
 ``applies(...)`` says whether a call can take the kernels (CUDA tensors,
 contiguous rows of width 128·{1, 2, 4, 6, 8} for the norm, a multiple of 4
@@ -25,7 +28,8 @@ from torch import Tensor
 
 from . import _capi
 
-__all__ = ["add_rms_norm", "swiglu", "norm_applies", "swiglu_applies"]
+__all__ = ["add_rms_norm", "swiglu", "cross_entropy", "norm_applies", "swiglu_applies",
+           "xent_applies"]
 
 _WIDTHS = {128, 256, 512, 768, 1024}
 _DTYPES = (torch.float32, torch.bfloat16)
@@ -96,3 +100,31 @@ def add_rms_norm(x: Tensor, y: Optional[Tensor], scale: Tensor, eps: float) -> T
 def swiglu(g: Tensor, v: Tensor) -> Tensor:
     """``silu(g) * v`` through the fused kernels."""
     return _SwiGLUFn.apply(g, v)
+
+
+def xent_applies(logits: Tensor, targets: Tensor) -> bool:
+    return (logits.is_cuda and logits.dim() == 2 and logits.dtype in _DTYPES
+            and logits.shape[1] % (8 if logits.dtype == torch.bfloat16 else 4) == 0
+            and targets.dtype == torch.long and targets.shape == logits.shape[:1])
+
+
+class _CrossEntropyFn(torch.autograd.Function):
+
+    @staticmethod
+    def forward(ctx, logits, targets):
+        lg, tg = logits.contiguous(), targets.contiguous()
+        row_loss, lse = _capi.ext().cross_entropy_fwd(lg, tg)
+        live = (tg != -100).sum().clamp(min=1).float()
+        ctx.save_for_backward(lg, tg, lse, live)
+        return row_loss.sum() / live
+
+    @staticmethod
+    def backward(ctx, d_mean):
+        lg, tg, lse, live = ctx.saved_tensors
+        g = (d_mean.float() / live).reshape(1).contiguous()
+        return _capi.ext().cross_entropy_bwd(lg, tg, lse, g), None
+
+
+def cross_entropy(logits: Tensor, targets: Tensor) -> Tensor:
+    """Mean cross-entropy of ``logits [R, V]`` against ``targets [R]`` (fp32)."""
+    return _CrossEntropyFn.apply(logits, targets)

@@ -480,6 +480,35 @@ int bozo_swiglu_bwd(const bozo_swiglu_args* a, void* stream) {
   return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
 }
 
+static int check_xent(const bozo_cross_entropy_args* a) {
+  if (!a) return BOZO_ERR_NULL;
+  if (a->rows <= 0 || a->rows > 0x7fffffffLL) return BOZO_ERR_BAD_SHAPE;
+  if (a->logits_dtype != BOZO_DT_F32 && a->logits_dtype != BOZO_DT_BF16) return BOZO_ERR_BAD_DTYPE;
+  if (!xent_shape_ok(a->vocab, a->logits_dtype)) return BOZO_ERR_UNSUPPORTED;
+  if (!a->logits || !a->targets || !a->row_lse) return BOZO_ERR_NULL;
+  return BOZO_OK;
+}
+
+int bozo_cross_entropy_fwd(const bozo_cross_entropy_args* a, void* stream) {
+  int st = check_xent(a);
+  if (st) return st;
+  if (!a->row_loss) return BOZO_ERR_NULL;
+  cudaError_t e = bind_device(a->logits);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = launch_xent(*a, false, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
+}
+
+int bozo_cross_entropy_bwd(const bozo_cross_entropy_args* a, void* stream) {
+  int st = check_xent(a);
+  if (st) return st;
+  if (!a->d_scale || !a->d_logits) return BOZO_ERR_NULL;
+  cudaError_t e = bind_device(a->logits);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = launch_xent(*a, true, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
+}
+
 int bozo_tension_poll_error(void* stream) {
   cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return BOZO_ERR_CUDA;

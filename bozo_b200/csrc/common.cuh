@@ -148,6 +148,10 @@ cudaError_t launch_add_rmsnorm(const NormP& p, bool backward, cudaStream_t st);
 cudaError_t launch_swiglu(const void* g, const void* v, void* h, const void* dh, void* dg, void* dv,
                           long long n, int dt, int sms, cudaStream_t st);
 
+// Cross-entropy from the logits (xent.cu).
+bool xent_shape_ok(int V, int dt);
+cudaError_t launch_xent(const bozo_cross_entropy_args& a, bool backward, cudaStream_t st);
+
 // Graph bias on the device (graph_bias.cu).
 cudaError_t launch_graph_bias(const bozo_graph_bias_args& a, int sms, cudaStream_t st);
 

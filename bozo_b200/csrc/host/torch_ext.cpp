@@ -335,6 +335,36 @@ std::vector<at::Tensor> swiglu_bwd(const at::Tensor& dh, const at::Tensor& g, co
   return {dg, dv};
 }
 
+// Cross-entropy: forward → (row_loss, row_lse); backward → d_logits.
+std::vector<at::Tensor> cross_entropy_fwd(const at::Tensor& logits, const at::Tensor& targets) {
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const int64_t R = logits.size(0);
+  at::Tensor loss = at::empty({R}, logits.options().dtype(at::kFloat));
+  at::Tensor lse = at::empty({R}, logits.options().dtype(at::kFloat));
+  bozo_cross_entropy_args a{};
+  a.rows = R; a.vocab = (int32_t)logits.size(1);
+  a.logits = logits.data_ptr(); a.logits_dtype = dtype_code(logits.scalar_type());
+  a.targets = targets.data_ptr<int64_t>(); a.row_lse = lse.data_ptr<float>();
+  a.row_loss = loss.data_ptr<float>();
+  check(bozo_cross_entropy_fwd(&a, at::cuda::getCurrentCUDAStream(logits.device().index()).stream()),
+        "bozo_cross_entropy_fwd");
+  return {loss, lse};
+}
+
+at::Tensor cross_entropy_bwd(const at::Tensor& logits, const at::Tensor& targets, const at::Tensor& lse,
+                             const at::Tensor& g) {
+  const c10::cuda::CUDAGuard guard(logits.device());
+  at::Tensor d = at::empty_like(logits);
+  bozo_cross_entropy_args a{};
+  a.rows = logits.size(0); a.vocab = (int32_t)logits.size(1);
+  a.logits = logits.data_ptr(); a.logits_dtype = dtype_code(logits.scalar_type());
+  a.targets = targets.data_ptr<int64_t>(); a.row_lse = lse.data_ptr<float>();
+  a.d_scale = g.data_ptr<float>(); a.d_logits = d.data_ptr();
+  check(bozo_cross_entropy_bwd(&a, at::cuda::getCurrentCUDAStream(logits.device().index()).stream()),
+        "bozo_cross_entropy_bwd");
+  return d;
+}
+
 // τ fields of one τ-consumer call: same shape, dtype and device, contiguous.
 void check_fields(const std::vector<at::Tensor>& taus) {
   if (taus.empty()) throw std::invalid_argument("tau_aux: no τ fields");
@@ -465,6 +495,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd, "residual add + RMSNorm through bozo_add_rmsnorm_fwd");
   m.def("add_rmsnorm_bwd", &add_rmsnorm_bwd, "its backward through bozo_add_rmsnorm_bwd");
   m.def("swiglu_fwd", &swiglu_fwd, "SwiGLU through bozo_swiglu_fwd");
+  m.def("cross_entropy_fwd", &cross_entropy_fwd, "cross-entropy through bozo_cross_entropy_fwd");
+  m.def("cross_entropy_bwd", &cross_entropy_bwd, "its backward through bozo_cross_entropy_bwd");
   m.def("swiglu_bwd", &swiglu_bwd, "its backward through bozo_swiglu_bwd");
   m.def("tau_aux_fwd", &tau_aux_fwd, "τ-field statistics through bozo_tau_aux_fwd");
   m.def("tau_aux_bwd", &tau_aux_bwd, "τ-field cotangents through bozo_tau_aux_bwd");

@@ -416,7 +416,12 @@ def train_step(model, base_model: TensionLM, optimizer, inputs, targets,
             logits, hidden, tensions = model(inputs, return_all=True)
         else:
             logits, hidden, tensions = model(inputs), None, []
-        loss = F.cross_entropy(logits.reshape(-1, V), targets.reshape(-1))
+        from . import block_ops
+        flat, tflat = logits.reshape(-1, V), targets.reshape(-1)
+        if block_ops.xent_applies(flat, tflat):
+            loss = block_ops.cross_entropy(flat, tflat)
+        else:
+            loss = F.cross_entropy(flat, tflat)
         if weights.aux_enabled and tensions:
             # a zero consistency weight gives that term no gradient
             div, cons, ent = aux_losses(tensions, base_model.window_groups,

@@ -8,6 +8,8 @@
  *                                  (model.py:330); plain RMSNorm (y NULL) for
  *                                  the pre-norm and final norm (model.py:376, 458)
  *   SwiGLU                         model.py:328-329, silu(gate(x)) · val(x)
+ *   cross-entropy loss             train.py:920 nn.CrossEntropyLoss() (mean over
+ *                                  rows whose target is not −100) of the logits
  * each with its backward, in place of the framework's separate add, norm,
  * silu and multiply kernels and its column reduction for the norm scale's
  * gradient.
@@ -69,6 +71,28 @@ typedef struct {
 
 int bozo_swiglu_fwd(const bozo_swiglu_args* args, void* stream);
 int bozo_swiglu_bwd(const bozo_swiglu_args* args, void* stream);
+
+/* Cross-entropy from the logits in their own dtype (bf16 or fp32, fp32
+ * arithmetic).  Forward: row_lse[r] = logsumexp(logits[r]) and row_loss[r] =
+ * row_lse[r] − logits[r][targets[r]] (0 where the target is outside
+ * [0, vocab), e.g. −100); the mean is the caller's sum of row_loss over the
+ * live rows.  Backward: d_logits[r] = (softmax(logits[r]) − onehot)·g with
+ * g = *d_scale (device scalar: the mean's cotangent ÷ live rows), zero rows
+ * for ignored targets. */
+typedef struct {
+  int64_t rows;
+  int32_t vocab;          /* a multiple of 8 (bf16) or 4 (fp32) */
+  const void* logits;     /* [rows, vocab] contiguous */
+  int32_t logits_dtype;
+  const int64_t* targets; /* [rows] */
+  float* row_lse;         /* [rows]: forward writes, backward reads */
+  float* row_loss;        /* [rows]: forward */
+  const float* d_scale;   /* backward: device scalar g */
+  void* d_logits;         /* backward: [rows, vocab], logits' dtype */
+} bozo_cross_entropy_args;
+
+int bozo_cross_entropy_fwd(const bozo_cross_entropy_args* args, void* stream);
+int bozo_cross_entropy_bwd(const bozo_cross_entropy_args* args, void* stream);
 
 #ifdef __cplusplus
 }

@@ -77,6 +77,8 @@ int main(void) {
   O(bozo_add_rmsnorm_args, scale); O(bozo_add_rmsnorm_args, d_scale);
   O(bozo_add_rmsnorm_args, workspace_bytes);
   S(bozo_swiglu_args); O(bozo_swiglu_args, gate); O(bozo_swiglu_args, d_value);
+  S(bozo_cross_entropy_args); O(bozo_cross_entropy_args, logits_dtype);
+  O(bozo_cross_entropy_args, targets); O(bozo_cross_entropy_args, d_logits);
   S(bozo_graph_bias_args); O(bozo_graph_bias_args, alpha); O(bozo_graph_bias_args, ctx_content);
   O(bozo_graph_bias_args, n_edges); O(bozo_graph_bias_args, out); O(bozo_graph_bias_args, stats);
   S(bozo_tau_aux_fwd_args); O(bozo_tau_aux_fwd_args, W); O(bozo_tau_aux_fwd_args, tau);
@@ -102,6 +104,7 @@ def test_struct_layout_matches_header():
              "bozo_graph_bias_args": _capi.GraphBiasArgs,
              "bozo_add_rmsnorm_args": _capi.AddRMSNormArgs,
              "bozo_swiglu_args": _capi.SwiGLUArgs,
+             "bozo_cross_entropy_args": _capi.CrossEntropyArgs,
              "bozo_tau_aux_fwd_args": _capi.TauAuxFwdArgs,
              "bozo_tau_aux_bwd_args": _capi.TauAuxBwdArgs}
     for line in filter(None, lines):

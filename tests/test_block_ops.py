@@ -89,3 +89,33 @@ def test_cpu_tensors_take_the_framework_ops():
     x = torch.randn(2, 4, 128)
     assert not block_ops.norm_applies(x, None)
     assert not block_ops.swiglu_applies(x, x)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,R,V", [(torch.bfloat16, 4096, 32768), (torch.float32, 1000, 1000),
+                                       (torch.bfloat16, 77, 97 * 8)])
+def test_cross_entropy_matches_framework(dtype, R, V):
+    """Mean cross-entropy and its logits gradient against F.cross_entropy in
+    fp32 on the same logits, the gradient rounded to the logits' dtype (the
+    kernel's rounding point); some targets are the ignore index −100.  (The
+    framework's own autocast path rounds each row's log-probabilities to
+    bf16, so its loss differs from the fp32 value by ~1e-4 relative.)"""
+    gen = torch.Generator().manual_seed(R)
+    dev = torch.device("cuda:0")
+    logits = (torch.randn(R, V, generator=gen) * 4).to(dev, dtype)
+    targets = torch.randint(0, V, (R,), generator=gen)
+    targets[::13] = -100
+    targets = targets.to(dev)
+    a = logits.clone().requires_grad_(True)
+    b = logits.clone().requires_grad_(True)
+    assert block_ops.xent_applies(a, targets)
+    loss = block_ops.cross_entropy(a, targets)
+    ref = F.cross_entropy(b.float(), targets)
+    assert loss.dtype == torch.float32
+    torch.testing.assert_close(loss, ref, rtol=1e-5, atol=1e-6)
+    (loss * 3.0).backward()
+    (ref * 3.0).backward()
+    assert a.grad.dtype == b.grad.dtype == dtype
+    tol = dict(rtol=1e-5, atol=1e-8) if dtype == torch.float32 else dict(rtol=1e-2, atol=1e-7)
+    torch.testing.assert_close(a.grad, b.grad, **tol)
+    assert float(a.grad[::13].abs().max()) == 0.0
