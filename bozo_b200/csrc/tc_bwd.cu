@@ -202,6 +202,7 @@ __device__ __forceinline__ Step step_of(int u, int u0, int u1, int nT) {
 // A 64-query sub-chunk as the MMA issuer tracks it.
 struct Sub {
   int n, it, ks, qs, hh, bq, kk0;
+  int bh, ikey, c;  // key tile (bh, ikey) against query tile ikey + c
   int kidx, qidx;  // load index of a key / query tile first used here, else −1
   bool zero, warm, dq, dq_acc, kv_first, last_of_iter, rel_q, rel_k;
 };
@@ -232,6 +233,9 @@ struct SubGen {
       s.n = n++;
       s.it = it;
       s.hh = hh;
+      s.bh = st.bh;
+      s.ikey = kind < 2 ? st.i - 1 : st.i;
+      s.c = (kind < 2 || kind >= 4) ? 1 : 0;
       s.kidx = s.qidx = -1;
       const int bq_i = st.i & 1;
       if (kind < 2) {  // warm-up over key tile i−1 for dQ_i
@@ -557,21 +561,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = qd * 32 + lane;
     const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
     const uint32_t pds = smem_u32(sPDS);
-    int n = 0, nq = 0;
+    int n = 0;
     bool ok = true;
-
-    // α/β of a query tile arrive with its TMA load (q_full)
-    auto take_query = [&]() {
-      const int s = nq & 1;
-      ok = ok && mbar_wait(&bar->q_full[s], (nq >> 1) & 1, err, kErrBwd | 35);
-      ++nq;
-      return s;
-    };
 
     // One 64-query sub-chunk: key tile i_key, query tile i_key+c, half hh.
     // Thread = key row r; this warp covers query columns 32·hf … 32·hf+31 in
     // two 16-column pieces.  Per element (c = 1/(4·scale), th = tanh(x/2)):
     //   τ·α = α/2 + α/2·th,  ds = (α·c·dP + β·c + c·dTau)·(1 − th²)
+    // Without per-element inputs both pieces' Sᵀ/dPᵀ leave TMEM under one
+    // completion wait and the TMEM buffer is handed back before the element
+    // math; with bias / τ cotangent gathers each piece loads after its gathers
+    // were issued, so their global latency overlaps the TMEM load (the per-row
+    // τ cotangent also loads per piece: its two extra coefficient planes leave
+    // no room for both pieces' registers).
     auto subchunk = [&](int bh, int i_key, int c, int hh, int qs, bool zero) {
       const int b = n & 1;
       ok = ok && mbar_wait(&bar->sdp_full[b], (n >> 1) & 1, err, kErrBwd | 30);
@@ -595,22 +597,81 @@ __global__ void __launch_bounds__(kThreads, 1)
         lo[ss] = max(lo[ss], 0);
       }
       uint32_t pk[2][8], dk[2][8];
-#pragma unroll
-      for (int ss = 0; ss < 2; ++ss) {
+      // element math of piece ss from its Sᵀ (R[0,16)) and dPᵀ (R[16,32))
+      auto piece = [&](int ss, const uint32_t* R, const float* gb, const float* gd) {
         const int cq0 = 64 * hh + 32 * hf + 16 * ss;
-        if (band[ss]) {
-          uint32_t R[32];  // Sᵀ | dPᵀ of this 16-column piece
-          const uint32_t col = tbase + lane_off + 128 * b + 32 * hf + 16 * ss;
-          // optional per-element inputs (bias, τ cotangent) are gathered
-          // before the TMEM load so their global latency overlaps it (the
-          // TMEM load is a memory-clobbering asm the loads cannot move past);
-          // across the warp each load reads 32 consecutive window slots of
-          // one query row
-          // Element e of the piece is query t = tq0+cq0+e at window slot
-          // w = W − (128c + cq0 + e − r): one base address per piece, then a
-          // constant step per element; out-of-band elements load nothing.
-          float gb[16], gd[16];
-          if constexpr (kBias || kDTau) {
+#pragma unroll
+        for (int e4 = 0; e4 < 16; e4 += 4) {
+          const float4 a4 = *reinterpret_cast<const float4*>(cf + cq0 + e4);
+          const float4 d4 = *reinterpret_cast<const float4*>(cf + kTile + cq0 + e4);
+          const float4 b4 = *reinterpret_cast<const float4*>(cf + 2 * kTile + cq0 + e4);
+          const float ah[4] = {a4.x, a4.y, a4.z, a4.w};
+          const float ad[4] = {d4.x, d4.y, d4.z, d4.w};
+          const float bd[4] = {b4.x, b4.y, b4.z, b4.w};
+          float a1[4] = {0.f, 0.f, 0.f, 0.f}, ivd[4] = {0.f, 0.f, 0.f, 0.f};
+          if constexpr (kAux) {
+            const float4 u4 = *reinterpret_cast<const float4*>(cf + 3 * kTile + cq0 + e4);
+            const float4 v4 = *reinterpret_cast<const float4*>(cf + 4 * kTile + cq0 + e4);
+            a1[0] = u4.x; a1[1] = u4.y; a1[2] = u4.z; a1[3] = u4.w;
+            ivd[0] = v4.x; ivd[1] = v4.y; ivd[2] = v4.z; ivd[3] = v4.w;
+          }
+          float pv[4], dv[4];
+#pragma unroll
+          for (int z = 0; z < 4; ++z) {
+            const int e = e4 + z;
+            const bool valid = (unsigned)(e - lo[ss]) < (unsigned)cnt[ss];
+            float x = __uint_as_float(R[e]) * p.half_inv_scale;
+            float dt = fmaf(ad[z], __uint_as_float(R[16 + e]), bd[z]);
+            if constexpr (kBias) x += gb[e];
+            if constexpr (kDTau) dt += gd[e];
+            const float th = tanh_approx(x);
+            if constexpr (kAux) {
+              // per-row τ cotangent a1·(log2 q − 1e-8/(q·ln 2)) (its a0 is in β),
+              // q = τ/D + 1e-8 at the recomputed τ = (1 + th)/2
+              const float q = fmaf(fmaf(0.5f, th, 0.5f), ivd[z], 1e-8f);
+              dt = fmaf(a1[z], fmaf(-kEpsOverLn2, __fdividef(1.f, q), __log2f(q)), dt);
+            }
+            pv[z] = valid ? fmaf(ah[z], th, ah[z]) : 0.f;
+            dv[z] = valid ? dt * fmaf(-th, th, 1.f) : 0.f;
+          }
+          pk[ss][e4 >> 1] = pack_bf16(pv[0], pv[1]);
+          pk[ss][(e4 >> 1) + 1] = pack_bf16(pv[2], pv[3]);
+          dk[ss][e4 >> 1] = pack_bf16(dv[0], dv[1]);
+          dk[ss][(e4 >> 1) + 1] = pack_bf16(dv[2], dv[3]);
+        }
+      };
+      if constexpr (!(kBias || kDTau || kAux)) {
+        uint32_t R[64];  // piece ss: Sᵀ at R[32ss], dPᵀ at R[32ss+16]
+        const uint32_t col = tbase + lane_off + 128 * b + 32 * hf;
+        if (band[0] && band[1]) tmem_ld16x4_wait(col, col + 64, col + 16, col + 80, R);
+        else if (band[0]) tmem_ld16x2_wait(col, col + 64, R);
+        else if (band[1]) tmem_ld16x2_wait(col + 16, col + 80, R + 32);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->sdp_free[b]);
+#pragma unroll
+        for (int ss = 0; ss < 2; ++ss) {
+          if (band[ss]) {
+            piece(ss, R + 32 * ss, nullptr, nullptr);
+          } else {
+#pragma unroll
+            for (int z = 0; z < 8; ++z) pk[ss][z] = dk[ss][z] = 0u;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int ss = 0; ss < 2; ++ss) {
+          const int cq0 = 64 * hh + 32 * hf + 16 * ss;
+          if (band[ss]) {
+            uint32_t R[32];  // Sᵀ | dPᵀ of this 16-column piece
+            const uint32_t col = tbase + lane_off + 128 * b + 32 * hf + 16 * ss;
+            // the optional per-element inputs are gathered before the TMEM
+            // load (a memory-clobbering asm the loads cannot move past); across
+            // the warp each load reads 32 consecutive window slots of one query
+            // row.  Element e of the piece is query t = tq0+cq0+e at window
+            // slot w = W − (128c + cq0 + e − r): one base address per piece,
+            // then a constant step per element; out-of-band elements load nothing.
+            float gb[16], gd[16];
             const int t0 = tq0 + cq0, w0 = W - (kTile * c + cq0 - r);
             const float* b0 = nullptr;
             const __nv_bfloat16* d0 = nullptr;
@@ -629,55 +690,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               if constexpr (kBias) gb[e] = valid ? 0.5f * __ldg(b0 + e * bstep) : 0.f;
               if constexpr (kDTau) gd[e] = valid ? p.ds_scale * __bfloat162float(d0[e * dstep]) : 0.f;
             }
+            tmem_ld16x2_wait(col, col + 64, R);
+            piece(ss, R, gb, gd);
+          } else {
+#pragma unroll
+            for (int z = 0; z < 8; ++z) pk[ss][z] = dk[ss][z] = 0u;
           }
-          tmem_ld16x2_wait(col, col + 64, R);
-#pragma unroll
-          for (int e4 = 0; e4 < 16; e4 += 4) {
-            const float4 a4 = *reinterpret_cast<const float4*>(cf + cq0 + e4);
-            const float4 d4 = *reinterpret_cast<const float4*>(cf + kTile + cq0 + e4);
-            const float4 b4 = *reinterpret_cast<const float4*>(cf + 2 * kTile + cq0 + e4);
-            const float ah[4] = {a4.x, a4.y, a4.z, a4.w};
-            const float ad[4] = {d4.x, d4.y, d4.z, d4.w};
-            const float bd[4] = {b4.x, b4.y, b4.z, b4.w};
-            float a1[4] = {0.f, 0.f, 0.f, 0.f}, ivd[4] = {0.f, 0.f, 0.f, 0.f};
-            if constexpr (kAux) {
-              const float4 u4 = *reinterpret_cast<const float4*>(cf + 3 * kTile + cq0 + e4);
-              const float4 v4 = *reinterpret_cast<const float4*>(cf + 4 * kTile + cq0 + e4);
-              a1[0] = u4.x; a1[1] = u4.y; a1[2] = u4.z; a1[3] = u4.w;
-              ivd[0] = v4.x; ivd[1] = v4.y; ivd[2] = v4.z; ivd[3] = v4.w;
-            }
-            float pv[4], dv[4];
-#pragma unroll
-            for (int z = 0; z < 4; ++z) {
-              const int e = e4 + z;
-              const bool valid = (unsigned)(e - lo[ss]) < (unsigned)cnt[ss];
-              float x = __uint_as_float(R[e]) * p.half_inv_scale;
-              float dt = fmaf(ad[z], __uint_as_float(R[16 + e]), bd[z]);
-              if constexpr (kBias) x += gb[e];
-              if constexpr (kDTau) dt += gd[e];
-              const float th = tanh_approx(x);
-              if constexpr (kAux) {
-                // per-row τ cotangent a1·(log2 q − 1e-8/(q·ln 2)) (its a0 is in β),
-                // q = τ/D + 1e-8 at the recomputed τ = (1 + th)/2
-                const float q = fmaf(fmaf(0.5f, th, 0.5f), ivd[z], 1e-8f);
-                dt = fmaf(a1[z], fmaf(-kEpsOverLn2, __fdividef(1.f, q), __log2f(q)), dt);
-              }
-              pv[z] = valid ? fmaf(ah[z], th, ah[z]) : 0.f;
-              dv[z] = valid ? dt * fmaf(-th, th, 1.f) : 0.f;
-            }
-            pk[ss][e4 >> 1] = pack_bf16(pv[0], pv[1]);
-            pk[ss][(e4 >> 1) + 1] = pack_bf16(pv[2], pv[3]);
-            dk[ss][e4 >> 1] = pack_bf16(dv[0], dv[1]);
-            dk[ss][(e4 >> 1) + 1] = pack_bf16(dv[2], dv[3]);
-          }
-        } else {
-#pragma unroll
-          for (int z = 0; z < 8; ++z) pk[ss][z] = dk[ss][z] = 0u;
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->sdp_free[b]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->sdp_free[b]);
       // shared buffer b is free once the consumers of sub-chunks n−2, n−1 ran
       if (n >= 2) ok = mbar_wait(&bar->p_free[b], ((n >> 1) - 1) & 1, err, kErrBwd | 31);
       if (!ok) return;
@@ -696,21 +719,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++n;
     };
 
-    int qslot_cur = 0;
-    for (int u = u0; u < u1 && ok; ++u) {
-      const Step st = step_of(u, u0, u1, nT);
-      if (st.warm) {
-        qslot_cur = take_query();
-        for (int hh = 0; hh < 2; ++hh) subchunk(st.bh, st.i - 1, 1, hh, qslot_cur, hh == 1 && c1h1_zero);
-      } else if (st.first_of_seg) {
-        qslot_cur = take_query();
-      }
-      for (int hh = 0; hh < 2; ++hh) subchunk(st.bh, st.i, 0, hh, qslot_cur, false);
-      if (st.has_c1) {
-        const int qs1 = take_query();
-        for (int hh = 0; hh < 2; ++hh) subchunk(st.bh, st.i, 1, hh, qs1, hh == 1 && c1h1_zero);
-        qslot_cur = qs1;
-      }
+    // the sub-chunks in the MMA issuers' order; one call site keeps the
+    // element code inlined once (instruction-cache footprint).  α/β of a
+    // query tile arrive with its TMA load (q_full).
+    SubGen gen{u0, u0, u1, nT, Wr, 0, 0, 0, 0, 0, 0, 0, c1h1_zero};
+    Sub sc{};
+    while (ok && gen.next(sc)) {
+      if (sc.qidx >= 0)
+        ok = mbar_wait(&bar->q_full[sc.qidx & 1], (sc.qidx >> 1) & 1, err, kErrBwd | 35);
+      subchunk(sc.bh, sc.ikey, sc.c, sc.hh, sc.qs, sc.zero);
     }
   }
 
