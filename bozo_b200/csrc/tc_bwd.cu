@@ -125,6 +125,8 @@ __global__ void alpha_beta_kernel(int B, int T, int H, int W, int tpad, int norm
     const bool live = idx < n8;
     const int rr = live ? idx >> 3 : 0;  // (t, h) row within the batch
     const int t = rr / H, h = rr - t * H;
+    // the row's τ-mass is loaded with the row (one latency per iteration, not two)
+    const float m = (norm == BOZO_NORM_MASS && live) ? __ldg(row_mass + (long long)(bb * H + h) * T + t) : 0.f;
     float dd = 0.f;
     if (norm == BOZO_NORM_MASS && live) {
       const uint4 x = __ldg(reinterpret_cast<const uint4*>(dob + (long long)t * dout.st + h * dout.sh) + c);
@@ -148,7 +150,6 @@ __global__ void alpha_beta_kernel(int B, int T, int H, int W, int tpad, int norm
       const int bh = bb * H + h;
       float a, b = 0.f;
       if (norm == BOZO_NORM_MASS) {
-        const float m = row_mass[(long long)bh * T + t];
         a = 1.f / fmaxf(m, kMassEps);
         b = m >= kMassEps ? -dd * a : 0.f;
       } else if (norm == BOZO_NORM_COUNT) {
