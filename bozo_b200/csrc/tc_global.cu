@@ -37,6 +37,7 @@
 
 #include "tc.cuh"
 #include "tc_host.cuh"
+#define BOZO_INLINE_WAIT_LOOP 1  // see tc_ptx.cuh mbar_wait
 #include "tc_ptx.cuh"
 
 namespace bozo {
@@ -339,13 +340,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* o = sOuter + os * Tr::kOuterTiles * kTileBytes;  // dead outer slot
       const uint32_t st0 = smem_u32(o);
       if (R == kFwd) {
+        // the τ-mass halves are read before acc_free is handed back: the
+        // epilogue rewrites this mass slot (outer tile m+2) once acc_free fires
+        const float mass = sMass[(ub * 2 + 0) * kTile + r] + sMass[(ub * 2 + 1) * kTile + r];
         uint32_t g[64];
         tmem_ld32_wait(acc, g);
         tmem_ld32_wait(acc + 32, g + 32);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar->acc_free[ub]);
-        const float mass = sMass[(ub * 2 + 0) * kTile + r] + sMass[(ub * 2 + 1) * kTile + r];
         float inv = 1.f;
         if (p.norm == BOZO_NORM_MASS) inv = 1.f / fmaxf(mass, kMassEps);
         else if (p.norm == BOZO_NORM_COUNT) inv = 1.f / (float)max(min(pos, p.W), 1);  // model.py:261-264

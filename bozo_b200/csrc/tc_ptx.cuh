@@ -80,6 +80,26 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s
 constexpr uint32_t kPollCap = 1u << 24;
 
+// The polling loop is out of line: every wait site inlines only the first
+// probe and a call.  The tensor-core kernels run several roles per SM whose
+// code competes for the instruction cache; misses are served through the
+// shared memory system and slowed every SM (inlining this loop at each of the
+// ~40 wait sites made the backward kernel 18 % slower).
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* err,
+                                                   int code) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1; i < kPollCap; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 15u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
+  if (err) atomicCAS(err, 0, code);
+  return false;
+}
+
+#ifdef BOZO_INLINE_WAIT_LOOP
+// Translation units that keep the polling loop inline (tc_global.cu: its
+// forward with a τ-mass produced wrong outputs for W = 129 with the loop out
+// of line; the cause is not found yet, so that kernel keeps the inline form).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
@@ -90,6 +110,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   if (err) atomicCAS(err, 0, code);
   return false;
 }
+#else
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, err, code);
+}
+#endif
 
 // ───────────────────────────── TMA ─────────────────────────────
 // 4-D tiled load global → shared, completion counted on `bar` (bytes).
