@@ -115,7 +115,8 @@ __device__ __forceinline__ void rope_chunk(uint32_t base, int r, int c, const fl
 // Rotate rows [0,128) of tiles a (and b, if non-null) — same positions t0+r.
 // Thread tid always handles 16-byte chunk c = tid & 3, so it keeps the eight
 // frequencies θ[8c..8c+7] in registers and evaluates cos/sin on the fly.
-__device__ void rope_tiles(uint8_t* ta, uint8_t* tb, int t0, int T, const float (&th)[8], int tid) {
+__device__ __noinline__ void rope_tiles(uint8_t* ta, uint8_t* tb, int t0, int T, const float (&th)[8],
+                                       int tid) {
   const uint32_t ba = smem_u32(ta), bb = tb ? smem_u32(tb) : 0u;
   const int c = tid & 3;
   for (int item = tid; item < kTile * 4; item += kRotThreads) {
@@ -504,17 +505,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         st_shared_v4(rowb + sw128_off(i, c16 + 1), pk[4], pk[5], pk[6], pk[7]);
       };
 
+      // one 16-column chunk per TMEM read: a single inlined copy of the
+      // element code (instruction-cache footprint)
       const uint32_t s_addr = tbase + lane_off + bi * 256;
-      for (int ch = my_lo; ch < my_hi; ch += 2) {
-        uint32_t r[32];
-        if (ch + 1 < my_hi) {
-          tmem_ld32_wait(s_addr + ch * 16, r);
-          process16(ch, r);
-          process16(ch + 1, r + 16);
-        } else {
-          tmem_ld16_wait(s_addr + ch * 16, r);
-          process16(ch, r);
-        }
+      for (int ch = my_lo; ch < my_hi; ++ch) {
+        uint32_t r[16];
+        tmem_ld16_wait(s_addr + ch * 16, r);
+        process16(ch, r);
       }
       fence_proxy_async_smem();
       __syncwarp();
