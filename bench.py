@@ -10,7 +10,7 @@ rank runs its own batch, no data-path collective — the op shards by batch).
 
 Printed JSON (one line, rank 0):
   value     algorithmic HBM GB/s of the whole job (bytes: N_rows·(24·HD+8)
-            per step), inputs resident in HBM, CUDA events on
+            per step, N_rows = B·H·T), inputs resident in HBM, CUDA events on
             the launching stream, max over ranks;
   e2e       the same metric through the public API with pinned HOST inputs
             copied in and (out, dq, dk, dv) copied back every step;

@@ -14,11 +14,12 @@ from __future__ import annotations
 import sys
 import types
 
-from .ops import (causal_tension, last_launches, last_path, poll_device_error,
-                  rope_tables, set_kernel_path, tension)
+from .ops import (causal_tension, check_device_error, last_launches, last_path,
+                  poll_device_error, rope_tables, set_kernel_path, tension)
 
 __all__ = ["causal_tension", "tension", "install_as_triton_tension", "set_kernel_path",
-           "last_path", "last_launches", "poll_device_error", "rope_tables"]
+           "last_path", "last_launches", "poll_device_error", "check_device_error",
+           "rope_tables"]
 
 
 def install_as_triton_tension() -> types.ModuleType:

@@ -34,6 +34,7 @@ EXPORTED = (
     "bozo_add_rmsnorm_workspace", "bozo_add_rmsnorm_fwd", "bozo_add_rmsnorm_bwd",
     "bozo_swiglu_fwd", "bozo_swiglu_bwd",
     "bozo_cross_entropy_fwd", "bozo_cross_entropy_bwd",
+    "bozo_tension_error_async", "bozo_tension_wait_selftest",
 )
 TAU_AUX_MAX_LAYERS = 64  # BOZO_TAU_AUX_MAX_LAYERS
 
@@ -167,6 +168,10 @@ def lib():
                 L.bozo_tension_bwd_workspace.restype = C.c_size_t
                 L.bozo_tension_poll_error.argtypes = [C.c_void_p]
                 L.bozo_tension_poll_error.restype = C.c_int
+                L.bozo_tension_error_async.argtypes = [C.c_void_p, C.c_void_p]
+                L.bozo_tension_error_async.restype = C.c_int
+                L.bozo_tension_wait_selftest.argtypes = [C.c_uint64, C.c_void_p, C.c_void_p]
+                L.bozo_tension_wait_selftest.restype = C.c_int
                 L.bozo_tension_last_path.restype = C.c_int
                 L.bozo_tension_last_launches.restype = C.c_int
                 L.bozo_status_string.argtypes = [C.c_int]

@@ -83,12 +83,28 @@ void* noalloc_scratch(cudaError_t* e) {
 // through this library (e.g. an autograd worker thread); without this the
 // driver-level tensor-map encoder sees no context and kernels would go to the
 // runtime's default device.
-cudaError_t bind_device(const void* ptr) {
+//
+// The caller's current device is put back when the entry point returns
+// (DeviceRestore), so a call with data on another GPU does not switch the
+// calling thread — and the framework that owns it — to that GPU.
+struct DeviceRestore {
+  int prev = -1;
+  DeviceRestore() = default;
+  DeviceRestore(const DeviceRestore&) = delete;
+  DeviceRestore& operator=(const DeviceRestore&) = delete;
+  ~DeviceRestore() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+cudaError_t bind_device(const void* ptr, DeviceRestore& restore) {
   cudaPointerAttributes attr;
   cudaError_t e = cudaPointerGetAttributes(&attr, ptr);
   if (e != cudaSuccess) return e;
   if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)
     return cudaErrorInvalidDevicePointer;
+  int cur = -1;
+  if (cudaGetDevice(&cur) == cudaSuccess && cur != attr.device) restore.prev = cur;
   return cudaSetDevice(attr.device);
 }
 
@@ -177,7 +193,8 @@ int bozo_tension_fwd(const bozo_tension_fwd_args* a, void* stream) {
   if (a->tau && !dtype_ok(a->tau_dtype)) return BOZO_ERR_BAD_DTYPE;
   if (a->mode == BOZO_MODE_GLOBAL && a->tau && a->window > a->T) return BOZO_ERR_BAD_SHAPE;
 
-  cudaError_t e = bind_device(a->q.ptr);
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->q.ptr, restore);
   if (e != cudaSuccess) return cuda_fail(e);
   FwdP p{};
   p.B = a->B; p.T = a->T; p.H = a->H; p.HD = a->HD; p.mode = a->mode; p.W = a->window;
@@ -247,7 +264,8 @@ int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
   const size_t need = bozo_tension_bwd_workspace(a);
   if (need && (!a->workspace || a->workspace_bytes < need)) return BOZO_ERR_WORKSPACE;
 
-  cudaError_t e = bind_device(a->q.ptr);
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->q.ptr, restore);
   if (e != cudaSuccess) return cuda_fail(e);
   BwdP p{};
   p.B = a->B; p.T = a->T; p.H = a->H; p.HD = a->HD; p.mode = a->mode; p.W = a->window;
@@ -300,7 +318,8 @@ int bozo_tension_bwd_noalloc(const bozo_tension_bwd_args* a, void* stream) {
   if (bozo_tension_bwd_workspace(a) > (size_t)BOZO_NOALLOC_SCRATCH_BYTES)
     return BOZO_ERR_SCRATCH_LIMIT;
   // the scratch address is per device: take it with the data's device current
-  cudaError_t e = bind_device(a->q.ptr);
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->q.ptr, restore);
   if (e != cudaSuccess) return cuda_fail(e);
   void* scratch = noalloc_scratch(&e);
   if (!scratch) return cuda_fail(e);
@@ -320,7 +339,8 @@ int bozo_tau_aux_fwd(const bozo_tau_aux_fwd_args* a, void* stream) {
   int st = check_aux(a);
   if (st) return st;
   if (!a->stats) return BOZO_ERR_NULL;
-  cudaError_t e = bind_device(a->tau[0]);
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->tau[0], restore);
   if (e != cudaSuccess) return cuda_fail(e);
   const size_t need = bozo_tau_aux_workspace(a);
   if (!a->workspace || a->workspace_bytes < need) return BOZO_ERR_WORKSPACE;
@@ -341,7 +361,8 @@ int bozo_tau_aux_bwd(const bozo_tau_aux_bwd_args* a, void* stream) {
     if (rows && a->d_tau[i]) return BOZO_ERR_BAD_SHAPE;
   }
   if (rows && !tau_aux_row_mode_ok(*a)) return BOZO_ERR_UNSUPPORTED;
-  cudaError_t e = bind_device(a->tau[0]);
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->tau[0], restore);
   if (e != cudaSuccess) return cuda_fail(e);
   const AuxShape s = aux_shape(a->B, a->T, a->H, a->W);
   e = launch_tau_aux_bwd(*a, aux_blocks(s, a->n_layers, num_sms()), static_cast<cudaStream_t>(stream));
@@ -370,7 +391,8 @@ int bozo_tension_decode(const bozo_tension_decode_args* a, void* stream) {
     if (!a->rope_cos || !a->rope_sin) return BOZO_ERR_NULL;
     if (a->HD % 2 != 0) return BOZO_ERR_UNSUPPORTED;
   }
-  cudaError_t e = bind_device(a->q.ptr);
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->q.ptr, restore);
   if (e != cudaSuccess) return cuda_fail(e);
   DecodeP p{};
   p.B = a->B; p.H = a->H; p.HD = a->HD; p.mode = a->mode; p.W = a->window;
@@ -398,7 +420,8 @@ int bozo_graph_bias_build(const bozo_graph_bias_args* a, void* stream) {
   if (a->T <= 0 || a->window < 0 || a->n_edges < 0) return BOZO_ERR_BAD_SHAPE;
   if (!a->ctx_content || !a->out || (a->n_edges > 0 && (!a->edge_keys || !a->edge_weights)))
     return BOZO_ERR_NULL;
-  cudaError_t e = bind_device(a->out);
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->out, restore);
   if (e != cudaSuccess) return cuda_fail(e);
   e = launch_graph_bias(*a, num_sms(), static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
@@ -433,7 +456,8 @@ int bozo_add_rmsnorm_fwd(const bozo_add_rmsnorm_args* a, void* stream) {
   int st = check_norm(a);
   if (st) return st;
   if (!a->out) return BOZO_ERR_NULL;
-  cudaError_t e = bind_device(a->x);
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->x, restore);
   if (e != cudaSuccess) return cuda_fail(e);
   e = launch_add_rmsnorm(norm_params(a), false, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
@@ -443,7 +467,8 @@ int bozo_add_rmsnorm_bwd(const bozo_add_rmsnorm_args* a, void* stream) {
   int st = check_norm(a);
   if (st) return st;
   if (!a->d_out || !a->dx || !a->d_scale || (a->y && !a->dy)) return BOZO_ERR_NULL;
-  cudaError_t e = bind_device(a->x);
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->x, restore);
   if (e != cudaSuccess) return cuda_fail(e);
   if (!a->workspace || a->workspace_bytes < bozo_add_rmsnorm_workspace(a)) return BOZO_ERR_WORKSPACE;
   e = launch_add_rmsnorm(norm_params(a), true, static_cast<cudaStream_t>(stream));
@@ -462,7 +487,8 @@ int bozo_swiglu_fwd(const bozo_swiglu_args* a, void* stream) {
   int st = check_swiglu(a);
   if (st) return st;
   if (!a->out) return BOZO_ERR_NULL;
-  cudaError_t e = bind_device(a->gate);
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->gate, restore);
   if (e != cudaSuccess) return cuda_fail(e);
   e = launch_swiglu(a->gate, a->value, a->out, nullptr, nullptr, nullptr, a->n, a->dtype, num_sms(),
                     static_cast<cudaStream_t>(stream));
@@ -473,7 +499,8 @@ int bozo_swiglu_bwd(const bozo_swiglu_args* a, void* stream) {
   int st = check_swiglu(a);
   if (st) return st;
   if (!a->d_out || !a->d_gate || !a->d_value) return BOZO_ERR_NULL;
-  cudaError_t e = bind_device(a->gate);
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->gate, restore);
   if (e != cudaSuccess) return cuda_fail(e);
   e = launch_swiglu(a->gate, a->value, nullptr, a->d_out, a->d_gate, a->d_value, a->n, a->dtype,
                     num_sms(), static_cast<cudaStream_t>(stream));
@@ -493,7 +520,8 @@ int bozo_cross_entropy_fwd(const bozo_cross_entropy_args* a, void* stream) {
   int st = check_xent(a);
   if (st) return st;
   if (!a->row_loss) return BOZO_ERR_NULL;
-  cudaError_t e = bind_device(a->logits);
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->logits, restore);
   if (e != cudaSuccess) return cuda_fail(e);
   e = launch_xent(*a, false, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
@@ -503,9 +531,31 @@ int bozo_cross_entropy_bwd(const bozo_cross_entropy_args* a, void* stream) {
   int st = check_xent(a);
   if (st) return st;
   if (!a->d_scale || !a->d_logits) return BOZO_ERR_NULL;
-  cudaError_t e = bind_device(a->logits);
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->logits, restore);
   if (e != cudaSuccess) return cuda_fail(e);
   e = launch_xent(*a, true, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
+}
+
+int bozo_tension_wait_selftest(uint64_t limit_ns, int32_t* result, void* stream) {
+  if (limit_ns < 1000ull || limit_ns > 1000000000ull) return BOZO_ERR_BAD_SHAPE;
+  DeviceRestore restore;
+  cudaError_t e = cudaSuccess;
+  if (result && (e = bind_device(result, restore)) != cudaSuccess) return cuda_fail(e);
+  int* err = error_word(&e);
+  if (!err) return cuda_fail(e);
+  e = launch_wait_selftest(limit_ns, err, result, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
+}
+
+int bozo_tension_error_async(int32_t* host_dst, void* stream) {
+  if (!host_dst) return BOZO_ERR_NULL;
+  cudaError_t e = cudaSuccess;
+  int* err = error_word(&e);
+  if (!err) return cuda_fail(e);
+  e = cudaMemcpyAsync(host_dst, err, sizeof(int), cudaMemcpyDeviceToHost,
+                      static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
 }
 

@@ -22,4 +22,8 @@ cudaError_t launch_tc_global_fwd(const FwdP& p, cudaStream_t st, int* launches);
 bool tc_global_bwd_eligible(const BwdP& p);
 cudaError_t launch_tc_global_bwd(const BwdP& p, cudaStream_t st, int* launches);
 
+// Bounded-wait self-test kernel (wait_selftest.cu): one wait on an mbarrier
+// nothing arrives on, limited to limit_ns; result (device int[4] or null).
+cudaError_t launch_wait_selftest(uint64_t limit_ns, int* err, int* result, cudaStream_t st);
+
 }  // namespace bozo

@@ -70,6 +70,7 @@ struct __align__(8) Bars {
   uint64_t mass_ready[2];  // the 8 epilogue warps have published their τ-mass halves
   uint64_t ostage_full, ostage_empty;
   uint64_t tau_free;  // every epilogue warp has copied its τ rows out
+  uint64_t drain;     // the MMA thread's exit commit
   uint32_t tmem_base;
 };
 
@@ -178,6 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bar->ostage_full, 8);
     mbar_init(&bar->ostage_empty, 1);
     mbar_init(&bar->tau_free, 8);
+    mbar_init(&bar->drain, 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -205,6 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&tmkr);
       }
       int n = 0, n_cur = 0;
+      int nq_issued = 0, nk_issued = 0, nv_issued = 0;  // loads in flight at exit
       bool ok = true, pending_stores = false;
       // rotated tiles are stored from the ring slots: a slot is refilled only
       // after every store issued so far has finished reading shared memory
@@ -223,11 +226,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         before_refill();
         mbar_arrive_expect_tx(&bar->k_full[s], kTileBytes);
         tma_load_4d(sK + s * kTileBytes, &tmk, &bar->k_full[s], 0, h, jj * kTile, b);
+        ++nk_issued;
         if (n >= NKV)
           ok = ok && mbar_wait(&bar->v_empty[s], ((n / NKV) - 1) & 1, err, kErrFwd | 17);
         if (!ok) return;
         mbar_arrive_expect_tx(&bar->v_full[s], kTileBytes);
         tma_load_4d(sV + s * kTileBytes, &tmv, &bar->v_full[s], 0, h, jj * kTile, b);
+        ++nv_issued;
         ++n;
       };
       // store RoPE(Q), RoPE(K) of tile (bh, j) once the rotators are done
@@ -251,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         before_refill();
         mbar_arrive_expect_tx(&bar->q_full[qs], kTileBytes);
         tma_load_4d(sQ + qs * kTileBytes, &tmq, &bar->q_full[qs], 0, bh % p.H, j * kTile, bh / p.H);
+        ++nq_issued;
         if (j >= 1 && u == u0) load_key(bh, j - 1);
         n_cur = n;
         load_key(bh, j);
@@ -259,6 +265,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (ok && p.store_rot && u1 > u0) store_rot(u1 - u0 - 1, prev_bh, prev_j, prev_n);
       if (pending_stores) bulk_wait_group0();
+      drain_loads(bar->q_full, kQSlots, nq_issued, err, kErrFwd | 22);
+      drain_loads(bar->k_full, NKV, nk_issued, err, kErrFwd | 23);
+      drain_loads(bar->v_full, NKV, nv_issued, err, kErrFwd | 24);
     }
   } else if (warp == 1) {
     // ─────────────── MMA issuer ───────────────
@@ -395,6 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) store_o(u1 - 1, u1 - u0 - 1);
         bulk_wait_group0();
       }
+      drain_mma(&bar->drain, err, kErrFwd | 25);
     }
   } else if (warp < 4 || warp >= 12) {
     // ─────────────── RoPE rotators (4 warps) ───────────────

@@ -37,7 +37,6 @@
 
 #include "tc.cuh"
 #include "tc_host.cuh"
-#define BOZO_INLINE_WAIT_LOOP 1  // see tc_ptx.cuh mbar_wait
 #include "tc_ptx.cuh"
 
 namespace bozo {
@@ -85,6 +84,7 @@ struct __align__(8) GBars {
   uint64_t s_full[2], s_free[2], p_full[2], p_free[2];
   uint64_t acc_full[2], acc_free[2];
   uint64_t mass_ready[2], staged;
+  uint64_t drain;  // the MMA thread's exit commit
   uint32_t tmem_base;
 };
 
@@ -168,6 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar->inner_empty[s], 1);
     }
     mbar_init(&bar->staged, 4);
+    mbar_init(&bar->drain, 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -188,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (R == kDKV) prefetch_tmap(&tmout1);
       const long long plane = (long long)BH * p.tpad;
       bool ok = true;
-      int ni = 0;
+      int ni = 0, no = 0;  // inner / outer loads issued
       for (int k = blockIdx.x, m = 0; k < p.units && ok; k += G, ++m) {
         int bh, ot, fi, nin;
         unit_of(R, k, BH, nT, p.local, p.W, bh, ot, fi, nin);
@@ -196,6 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int os = m & 1;
         if (m >= 2) ok = mbar_wait(&bar->outer_empty[os], ((m >> 1) - 1) & 1, err, kErrG | 1);
         if (!ok) break;
+        ++no;
         uint8_t* o = sOuter + os * Tr::kOuterTiles * kTileBytes;
         mbar_arrive_expect_tx(&bar->outer_full[os],
                               Tr::kOuterTiles * kTileBytes + (Tr::kOuterCoef ? kCoefBytes : 0));
@@ -227,6 +229,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++ni;
         }
       }
+      drain_loads(bar->outer_full, 2, no, err, kErrG | 17);
+      drain_loads(bar->inner_full, kStages, ni, err, kErrG | 18);
     }
   } else if (warp == 1) {
     // ─────────────────────────── MMA issuer ───────────────────────────
@@ -238,26 +242,91 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dInner = sdesc_sw128(smem_u32(sInner), 16, 1024);
       const uint64_t dEpi = sdesc_sw128(smem_u32(sEpi), 16, 1024);
       bool ok = true;
-      int n = 0, ni = 0;
-      // the previous sub-step, whose consumers are still to be issued
-      bool have_prev = false;
-      int pn = 0, pm = 0, pst = 0, phh = 0;
-      bool pfirst = false, plast = false;
 
-      auto consumers = [&](int cn, int cm, int cst, int chh, bool cfirst, bool clast) {
-        const int b = cn & 1, ub = cm & 1;
-        ok = ok && mbar_wait(&bar->p_full[b], (cn >> 1) & 1, err, kErrG | 3);
-        if (ok && cfirst && cm >= 2) ok = mbar_wait(&bar->acc_free[ub], ((cm >> 1) - 1) & 1, err, kErrG | 4);
+      // The CTA's sub-steps in order (the order the epilogue walks): unit m,
+      // inner tile x of it (ring load ni, stage st), 64-row half hh.
+      struct GSub {
+        int n, m, ni, st, hh;
+        bool unit_first, last;
+      };
+      int gk = blockIdx.x, gm = 0, gx = 0, ghh = 0, gn = 0, gni = 0, gnin = 0;
+      bool in_unit = false;
+      auto next_sub = [&](GSub& s) -> bool {
+        for (;;) {
+          if (!in_unit) {
+            if (gk >= p.units) return false;
+            int bh, ot, fi;
+            unit_of(R, gk, BH, nT, p.local, p.W, bh, ot, fi, gnin);
+            gx = 0;
+            ghh = 0;
+            in_unit = true;
+          }
+          if (gx < gnin) {
+            s.n = gn++;
+            s.m = gm;
+            s.ni = gni;
+            s.st = gni % kStages;
+            s.hh = ghh;
+            s.unit_first = gx == 0 && ghh == 0;
+            s.last = gx == gnin - 1 && ghh == 1;
+            if (++ghh == 2) {
+              ghh = 0;
+              ++gx;
+              ++gni;
+            }
+            return true;
+          }
+          in_unit = false;
+          gk += G;
+          ++gm;
+        }
+      };
+
+      // Sᵀ/S (and dPᵀ/dP) of sub-step c into TMEM buffer c.n & 1
+      auto producers = [&](const GSub& c) {
+        const int b = c.n & 1;
+        if (c.unit_first) ok = mbar_wait(&bar->outer_full[c.m & 1], (c.m >> 1) & 1, err, kErrG | 5);
+        if (ok && c.hh == 0) ok = mbar_wait(&bar->inner_full[c.st], (c.ni / kStages) & 1, err, kErrG | 6);
+        if (ok && c.n >= 2) ok = mbar_wait(&bar->s_free[b], ((c.n >> 1) - 1) & 1, err, kErrG | 7);
         if (!ok) return;
         tc_fence_after();
-        const uint64_t in0 = dInner + (uint64_t)(cst * 2) * kTD;   // K / Q / K
-        const uint64_t in1 = in0 + kTD;                             // V / dO / V
+        const uint64_t o0 = dOuter + (uint64_t)((c.m & 1) * Tr::kOuterTiles) * kTD;
+        const uint64_t o1 = o0 + kTD;
+        const uint64_t in0 = dInner + (uint64_t)(c.st * 2) * kTD;
+        const uint64_t in1 = in0 + kTD;
+        const uint64_t half = (uint64_t)(64 * c.hh) * 8;
+        const uint32_t sc = tbase + 128 * b;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          if (R == kFwd) {
+            mma_bf16(sc, o0 + 2 * kk, in0 + half + 2 * kk, id_p, kk > 0);        // S = Q·Kᵀ
+          } else if (R == kDKV) {
+            mma_bf16(sc, o0 + 2 * kk, in0 + half + 2 * kk, id_p, kk > 0);        // Sᵀ = K·Qᵀ
+            mma_bf16(sc + 64, o1 + 2 * kk, in1 + half + 2 * kk, id_p, kk > 0);   // dPᵀ = V·dOᵀ
+          } else {
+            mma_bf16(sc, o0 + 2 * kk, in0 + half + 2 * kk, id_p, kk > 0);        // S = Q·Kᵀ
+            mma_bf16(sc + 64, o1 + 2 * kk, in1 + half + 2 * kk, id_p, kk > 0);   // dP = dO·Vᵀ
+          }
+        }
+        mma_commit(&bar->s_full[b]);
+      };
+
+      // accumulator MMAs of sub-step c (its bf16 tiles in shared buffer c.n & 1)
+      auto consumers = [&](const GSub& c) {
+        const int b = c.n & 1, ub = c.m & 1;
+        ok = mbar_wait(&bar->p_full[b], (c.n >> 1) & 1, err, kErrG | 3);
+        if (ok && c.unit_first && c.m >= 2)
+          ok = mbar_wait(&bar->acc_free[ub], ((c.m >> 1) - 1) & 1, err, kErrG | 4);
+        if (!ok) return;
+        tc_fence_after();
+        const uint64_t in0 = dInner + (uint64_t)(c.st * 2) * kTD;   // K / Q / K
+        const uint64_t in1 = in0 + kTD;                              // V / dO / V
         const uint64_t e0 = dEpi + (uint64_t)(b * Tr::kEpiTiles) * kTD;
         const uint32_t acc_col = tbase + 256 + ub * Tr::kAccCols;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t rows = (uint64_t)(64 * chh + 16 * kk) * 8;  // 16 B units
-          const uint32_t acc = (cfirst && kk == 0) ? 0u : 1u;
+          const uint64_t rows = (uint64_t)(64 * c.hh + 16 * kk) * 8;  // 16 B units
+          const uint32_t acc = (c.unit_first && kk == 0) ? 0u : 1u;
           if (R == kFwd) {
             mma_bf16(acc_col, e0 + 2 * kk, in1 + rows, id_c, acc);            // O += P·V
           } else if (R == kDKV) {
@@ -268,53 +337,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         mma_commit(&bar->p_free[b]);
-        if (chh == 1) mma_commit(&bar->inner_empty[cst]);
-        if (clast) mma_commit(&bar->acc_full[ub]);
+        if (c.hh == 1) mma_commit(&bar->inner_empty[c.st]);
+        if (c.last) mma_commit(&bar->acc_full[ub]);
       };
 
-      for (int k = blockIdx.x, m = 0; k < p.units && ok; k += G, ++m) {
-        int bh, ot, fi, nin;
-        unit_of(R, k, BH, nT, p.local, p.W, bh, ot, fi, nin);
-        const int os = m & 1;
-        ok = mbar_wait(&bar->outer_full[os], (m >> 1) & 1, err, kErrG | 5);
-        const uint64_t o0 = dOuter + (uint64_t)(os * Tr::kOuterTiles) * kTD;
-        const uint64_t o1 = o0 + kTD;
-        for (int x = 0; x < nin && ok; ++x) {
-          const int st = ni % kStages;
-          ok = mbar_wait(&bar->inner_full[st], (ni / kStages) & 1, err, kErrG | 6);
-          const uint64_t in0 = dInner + (uint64_t)(st * 2) * kTD;
-          const uint64_t in1 = in0 + kTD;
-          for (int hh = 0; hh < 2 && ok; ++hh) {
-            const int b = n & 1;
-            if (n >= 2) ok = mbar_wait(&bar->s_free[b], ((n >> 1) - 1) & 1, err, kErrG | 7);
-            if (!ok) break;
-            tc_fence_after();
-            const uint64_t half = (uint64_t)(64 * hh) * 8;
-            const uint32_t sc = tbase + 128 * b;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              if (R == kFwd) {
-                mma_bf16(sc, o0 + 2 * kk, in0 + half + 2 * kk, id_p, kk > 0);        // S = Q·Kᵀ
-              } else if (R == kDKV) {
-                mma_bf16(sc, o0 + 2 * kk, in0 + half + 2 * kk, id_p, kk > 0);        // Sᵀ = K·Qᵀ
-                mma_bf16(sc + 64, o1 + 2 * kk, in1 + half + 2 * kk, id_p, kk > 0);   // dPᵀ = V·dOᵀ
-              } else {
-                mma_bf16(sc, o0 + 2 * kk, in0 + half + 2 * kk, id_p, kk > 0);        // S = Q·Kᵀ
-                mma_bf16(sc + 64, o1 + 2 * kk, in1 + half + 2 * kk, id_p, kk > 0);   // dP = dO·Vᵀ
-              }
-            }
-            mma_commit(&bar->s_full[b]);
-            if (have_prev) consumers(pn, pm, pst, phh, pfirst, plast);
-            have_prev = true;
-            pn = n; pm = m; pst = st; phh = hh;
-            pfirst = (x == 0 && hh == 0);
-            plast = (x == nin - 1 && hh == 1);
-            ++n;
-          }
-          ++ni;
-        }
+      // Producers of sub-step n are issued before the consumers of n − 1, so
+      // the epilogue of n overlaps the accumulator MMAs of n − 1.  Each kind
+      // of MMA has exactly one issue site: the consumer MMAs of a unit's last
+      // sub-step, when issued from a second inlined copy of this code after
+      // the loop, read their B tile with a corrupted layout (every 16-byte
+      // column chunk of the product equal to the first) whenever the wait
+      // before them ran out of line.
+      GSub cur{}, prev{};
+      bool have_prev = false;
+      while (ok) {
+        const bool more = next_sub(cur);
+        if (more) producers(cur);
+        if (ok && have_prev) consumers(prev);
+        if (!more) break;
+        prev = cur;
+        have_prev = true;
       }
-      if (ok && have_prev) consumers(pn, pm, pst, phh, pfirst, plast);
+      drain_mma(&bar->drain, err, kErrG | 16);
     }
   } else if (warp < 4 || warp >= 12) {
     // ─────────── output warps: accumulators → bf16 → TMA store ───────────

@@ -85,37 +85,45 @@ constexpr uint32_t kPollCap = 1u << 24;
 // code competes for the instruction cache; misses are served through the
 // shared memory system and slowed every SM (inlining this loop at each of the
 // ~40 wait sites made the backward kernel 18 % slower).
-static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* err,
-                                                   int code) {
+//
+// The limit is an argument of the loop itself (mbar_wait_until): the kernels'
+// wait sites use kWaitLimitNs through mbar_wait_slow, the wait self-test
+// kernel a short limit given at launch, so a test can make a wait run out on
+// purpose (a barrier nothing arrives on) and read the status.
+static __device__ __noinline__ bool mbar_wait_until(uint64_t* bar, uint32_t parity, int* err,
+                                                    int code, uint64_t limit_ns) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1; i < kPollCap; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 15u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) break;
+    if ((i & 15u) == 0 && globaltimer_ns() - t0 > limit_ns) break;
   }
   if (err) atomicCAS(err, 0, code);
   return false;
 }
 
-#ifdef BOZO_INLINE_WAIT_LOOP
-// Translation units that keep the polling loop inline (tc_global.cu: its
-// forward with a τ-mass produced wrong outputs for W = 129 with the loop out
-// of line; the cause is not found yet, so that kernel keeps the inline form).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 1; i < kPollCap; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 15u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) break;
-  }
-  if (err) atomicCAS(err, 0, code);
-  return false;
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* err,
+                                                   int code) {
+  return mbar_wait_until(bar, parity, err, code, kWaitLimitNs);
 }
-#else
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   return mbar_wait_slow(bar, parity, err, code);
 }
-#endif
+
+// Exit path of a producer thread: wait (bounded) until the last load issued
+// on each slot of a ring has landed, so no TMA copy is still writing shared
+// memory when the CTA leaves — on the timeout path the consumers stopped
+// waiting for them.  Slot s of `slots` got loads s, s + slots, …; the last of
+// the n_issued loads on it completes phase last / slots.  On the normal path
+// every phase was consumed already and each wait returns at the first probe.
+static __device__ __noinline__ void drain_loads(uint64_t* full, int slots, int n_issued, int* err,
+                                         int code) {
+  for (int s = 0; s < slots && s < n_issued; ++s) {
+    const int last = s + ((n_issued - 1 - s) / slots) * slots;
+    mbar_wait_slow(&full[s], (uint32_t)(last / slots) & 1u, err, code);
+  }
+}
 
 // ───────────────────────────── TMA ─────────────────────────────
 // 4-D tiled load global → shared, completion counted on `bar` (bytes).
@@ -209,6 +217,14 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
           smem_u32(bar))
       : "memory");
+}
+
+// Exit path of an MMA-issuing thread: one more commit on a barrier of its own
+// (count 1, used once) and a bounded wait for it, so every tensor-core op the
+// thread issued has finished writing TMEM before the TMEM is released.
+__device__ __forceinline__ void drain_mma(uint64_t* drain_bar, int* err, int code) {
+  mma_commit(drain_bar);
+  mbar_wait_slow(drain_bar, 0u, err, code);
 }
 
 // 32 lanes × 16 consecutive 32-bit columns.

@@ -165,6 +165,9 @@ def step(state: DecodeState, tokens: Tensor, export: bool = False):
         rows.append(tau)
     logits = model.lm_head(model.final_norm(x))[:, 0]
     state.pos += 1
+    # a position outside the RoPE table sets the device error word: report it
+    # (at most one step late, without a synchronisation; skipped in capture)
+    ops.check_device_error(tokens.device)
     return (logits, rows) if export else logits
 
 
@@ -199,6 +202,7 @@ class StepGraph:
     def __call__(self, tokens: Tensor):
         self.tokens.copy_(tokens)
         self.graph.replay()
+        ops.check_device_error(self.tokens.device)
         return self.out
 
 

@@ -435,4 +435,9 @@ def train_step(model, base_model: TensionLM, optimizer, inputs, targets,
     nn.utils.clip_grad_norm_(base_model.parameters(), clip_grad)
     optimizer.step()
     optimizer.zero_grad(set_to_none=True)
+    if inputs.is_cuda:
+        # a bounded wait that gave up in this step's kernels raises here, at
+        # most one step late (an asynchronous read of the device error word)
+        from .ops import check_device_error
+        check_device_error(inputs.device)
     return loss.detach()

@@ -362,7 +362,50 @@ def last_launches() -> int:
 
 
 def poll_device_error(device=None) -> None:
-    """Synchronise and raise if a bounded device-side wait timed out."""
+    """Synchronise and raise if a bounded device-side wait timed out (the
+    error word is cleared by the read)."""
     dev = torch.device(device) if device is not None else torch.device("cuda")
-    code = _capi.lib().bozo_tension_poll_error(_stream(dev))
+    with torch.cuda.device(dev):
+        code = _capi.lib().bozo_tension_poll_error(_stream(dev))
     _capi.check(code, "device error poll")
+
+
+class _ErrorWatch:
+    """Per-device state of ``check_device_error``: a pinned host word the
+    error word is copied into, and the event that marks the copy."""
+
+    def __init__(self):
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.event = None
+
+
+_watch: dict = {}
+
+
+def check_device_error(device=None) -> None:
+    """Non-blocking check of the device error word, for once-per-step use.
+
+    Reads the word copied by the previous call if that copy has completed
+    (no synchronisation), raises through ``poll_device_error`` when a bounded
+    wait gave up in some earlier launch, then enqueues the next asynchronous
+    copy on the current stream.  A timeout is thus reported at most one step
+    late instead of never; nothing is enqueued while the stream is capturing
+    a CUDA graph."""
+    if torch.cuda.is_current_stream_capturing():
+        return  # no event query or copy may join a graph capture
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    w = _watch.get(dev.index)
+    if w is None:
+        w = _watch[dev.index] = _ErrorWatch()
+    if w.event is not None and w.event.query() and int(w.host[0]) != 0:
+        w.host.zero_()
+        w.event = None
+        poll_device_error(dev)  # raises BOZO_ERR_DEVICE_TIMEOUT and clears the word
+    with torch.cuda.device(dev):
+        code = _capi.lib().bozo_tension_error_async(w.host.data_ptr(), _stream(dev))
+    _capi.check(code, "device error copy")
+    if w.event is None:
+        w.event = torch.cuda.Event()
+    w.event.record(torch.cuda.current_stream(dev))

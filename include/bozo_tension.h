@@ -201,8 +201,7 @@ size_t bozo_tension_bwd_workspace(const bozo_tension_bwd_args* args);
 int bozo_tension_bwd(const bozo_tension_bwd_args* args, void* stream);
 
 /* Backward that allocates nothing. This entry point has no counterpart in the
- * reference (triton_tension/ops.py:126-187 lets torch allocate its scratch).
- * It is for callers that cannot allocate device memory per call: a plain C,
+ * reference. It is for callers that cannot allocate device memory per call: a plain C,
  * cgo or ctypes host with no caching allocator (a cudaMalloc/cudaFree pair per
  * backward would synchronise the device each step), or a service that reserves
  * all device memory at start-up and may not allocate afterwards.
@@ -222,6 +221,27 @@ int bozo_tension_bwd_noalloc(const bozo_tension_bwd_args* args, void* stream);
  * bounded waits inside the tensor-core kernels set when they give up.
  * Returns BOZO_OK or BOZO_ERR_DEVICE_TIMEOUT (or BOZO_ERR_CUDA). */
 int bozo_tension_poll_error(void* stream);
+
+/* Enqueue on `stream` an asynchronous copy of the device error word of the
+ * current device into host memory (pinned for a truly asynchronous copy), so
+ * a caller can check it once the stream has passed that point without
+ * synchronising every step.  A non-zero value means a bounded wait gave up in
+ * some earlier launch: call bozo_tension_poll_error to read and clear it.
+ * No counterpart in the reference (it has no device-side waits). */
+int bozo_tension_error_async(int32_t* host_dst, void* stream);
+
+/* Self-test of the bounded device waits; no counterpart in the reference (its
+ * only timeout is the NCCL one train.py:561-564 comments on).  One CTA starts
+ * a bulk copy and a tensor-core MMA, then waits on an mbarrier that nothing
+ * arrives on, limited to limit_ns nanoseconds (1 µs … 1 s, else
+ * BOZO_ERR_BAD_SHAPE) instead of the kernels' 4 s.  The wait gives up and
+ * sets the device error word (bozo_tension_poll_error then returns
+ * BOZO_ERR_DEVICE_TIMEOUT); the CTA drains the copy and the MMA with bounded
+ * waits and releases its TMEM before it exits — the exit path of every
+ * tensor-core kernel — so the context stays usable.  `result`: device
+ * int32[4] or NULL — [0] 1 if the wait gave up, [1] 1 if the copy drained,
+ * [2] 1 if the MMA drained, [3] microseconds the wait took. */
+int bozo_tension_wait_selftest(uint64_t limit_ns, int32_t* result, void* stream);
 
 /* Which kernel path the last successful call in this process ran:
  * BOZO_PATH_SIMT or BOZO_PATH_TCGEN05 (0 before any call). */

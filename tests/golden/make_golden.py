@@ -1,7 +1,7 @@
 """Generate golden vectors by running the REFERENCE implementation on the CPU.
 
-Run once in a container that has the reference checkout (default path
-``/root/reference``, or ``--ref PATH``)::
+Run once in a container that has the reference checkout, passing its path
+with ``--ref PATH`` or the ``BOZO_REFERENCE`` environment variable::
 
     python tests/golden/make_golden.py
 
@@ -151,7 +151,9 @@ def layer_cases(model_mod):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("BOZO_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("BOZO_REFERENCE"),
+                    required="BOZO_REFERENCE" not in os.environ,
+                    help="path of the reference checkout (or set BOZO_REFERENCE)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     import model as model_mod  # noqa: E402  (reference model.py)

@@ -1,8 +1,8 @@
 """Golden vectors for the fused τ consumer (``bozo_b200/aux.py``), made by the
 REFERENCE loss functions on the CPU.
 
-Run once in a container that has the reference checkout (default
-``/root/reference``, or ``--ref PATH``)::
+Run once in a container that has the reference checkout, passing its path
+with ``--ref PATH`` or the ``BOZO_REFERENCE`` environment variable::
 
     python tests/golden/make_golden_aux.py
 
@@ -65,7 +65,9 @@ def make_fields(shape, n, seed):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("BOZO_REFERENCE"),
+                    required="BOZO_REFERENCE" not in os.environ,
+                    help="path of the reference checkout (or set BOZO_REFERENCE)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     import model as M  # the reference's model.py

@@ -1,8 +1,8 @@
 """Golden vectors for the device graph bias (``bozo_b200/graph_bias.py``),
 made by the REFERENCE ``GraphBias`` (ts_bridge/bias.py:81-233) on the CPU.
 
-Run once in a container that has the reference checkout (default
-``/root/reference``, or ``--ref PATH``)::
+Run once in a container that has the reference checkout, passing its path
+with ``--ref PATH`` or the ``BOZO_REFERENCE`` environment variable::
 
     python tests/golden/make_golden_bias.py
 
@@ -49,7 +49,9 @@ def make_edge_map(seed):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("BOZO_REFERENCE"),
+                    required="BOZO_REFERENCE" not in os.environ,
+                    help="path of the reference checkout (or set BOZO_REFERENCE)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     from ts_bridge.bias import GraphBias  # the reference class

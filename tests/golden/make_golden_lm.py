@@ -1,8 +1,8 @@
 """Golden vectors for the TensionLM harness (``bozo_b200/lm.py``), made by the
 REFERENCE model on the CPU.
 
-Run once in a container that has the reference checkout (default
-``/root/reference``, or ``--ref PATH``)::
+Run once in a container that has the reference checkout, passing its path
+with ``--ref PATH`` or the ``BOZO_REFERENCE`` environment variable::
 
     python tests/golden/make_golden_lm.py
 
@@ -53,7 +53,9 @@ W_CLOSURE, W_DIVERSITY, W_CONSISTENCY, W_ENTROPY = 0.01, 0.02, 0.0, 0.0
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("BOZO_REFERENCE"),
+                    required="BOZO_REFERENCE" not in os.environ,
+                    help="path of the reference checkout (or set BOZO_REFERENCE)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     import model as M  # the reference's model.py

@@ -354,3 +354,53 @@ def test_backward_on_autograd_thread_small_shapes(bz, shape):
                                          [d.double().cpu()])
     for g, r, what in zip((out, gq, gk, gv), (o, *grads), ("out", "dq", "dk", "dv")):
         assert_close(g, r, torch.bfloat16, f"{shape}/{what}")
+
+
+@cuda
+@pytest.mark.parametrize("W", [64, 256])
+def test_bench_shape_parity(bz, W):
+    """The benchmark's own step (B8 H12 T2048 HD64, RoPE,
+    τ-mass) at full size: out and every gradient of batch row 0, heads 0-1,
+    against the float64 oracle — W 64 on the band kernels, W 256 on the
+    key-tile kernels."""
+    B, H, T, HD = 8, 12, 2048, 64
+    g = torch.Generator().manual_seed(1234)
+    q, k, v, d = [torch.randn(B, T, H, HD, generator=g).to(torch.bfloat16) for _ in range(4)]
+    qg, kg, vg = [x.cuda().requires_grad_(True) for x in (q, k, v)]
+    out = bz.tension(qg, kg, vg, window=W, normalize="mass")
+    gq, gk, gv = torch.autograd.grad(out, (qg, kg, vg), d.cuda())
+    assert bz.last_path() == "tcgen05"
+    sl = lambda x: x[0:1, :, 0:2]
+
+    def fn(a, b, c):
+        return orc.fused_reference(a, b, c, window=W, scale=8.0)[0]
+    (o,), grads = orc.tension_with_grads(fn, [sl(x).double() for x in (q, k, v)], [sl(d).double()])
+    for got, ref, what in zip((out, gq, gk, gv), (o, *grads), ("out", "dq", "dk", "dv")):
+        assert_close(sl(got), ref, torch.bfloat16, f"bench shape W{W}/{what}")
+
+
+@cuda
+@pytest.mark.parametrize("window,T", [(64, 700), (200, 700), (None, 700)])
+def test_tensor_core_paths_repeat_bit_identical(bz, window, T):
+    """Every tensor-core kernel family gives bit-identical out, τ and grads
+    over repeated calls on the same inputs (no atomics anywhere, so any
+    difference would be a pipeline hand-off that depends on timing): the
+    band kernels (W 64), the key-tile kernels for wide windows (W 200) and
+    the global block, with bias and τ cotangent."""
+    torch.manual_seed(300 + T)
+    B, H, HD = 2, 4, 64
+    q, k, v, d = [torch.randn(B, T, H, HD, dtype=torch.bfloat16, device="cuda") for _ in range(4)]
+    W = window if window is not None else 64
+    bias = torch.randn(B, T, W if window is not None else T, device="cuda") * 0.5
+    d_tau = (torch.randn(B, T, H, W, device="cuda") * 0.1).to(torch.bfloat16)
+    runs = []
+    for _ in range(6):
+        qg, kg, vg = [x.clone().requires_grad_(True) for x in (q, k, v)]
+        out, tau = bz.tension(qg, kg, vg, window=window, bias=bias, return_tau=True,
+                              tau_window=None if window is not None else W)
+        ((out.float() * d.float()).sum() + (tau.float() * d_tau.float()).sum()).backward()
+        assert bz.last_path() == "tcgen05"
+        runs.append([x.detach().clone() for x in (out, tau, qg.grad, kg.grad, vg.grad)])
+    for r in runs[1:]:
+        for a, b, what in zip(runs[0], r, ("out", "tau", "dq", "dk", "dv")):
+            assert torch.equal(a, b), f"{what} differs between identical calls"
