@@ -315,24 +315,27 @@ def run_ours(args, rank, world, local_rank):
 TRAIN_B, TRAIN_T = 16, 1024  # per-GPU batch 16, seq 1024
 
 
-def run_train(args, rank, world, local_rank):
-    """117M TensionLM training steps through the
-    harness bozo_b200.lm: bf16 autocast, the operator in every tension layer,
-    CE + train.py's default aux losses (w_closure 0.01, w_diversity 0.02,
-    which put τ export and its cotangent in the loop), global-norm clip,
-    fused AdamW; DDP over NCCL when world > 1.  Per-GPU batch 16 × 1024
-    tokens, uniform random token ids from a per-rank seed, random init.
-    Returns {variant: (ms_per_step max over ranks, e2e ms_per_step)}."""
+def run_train(args, rank, world, local_rank, cfg=None, batch=TRAIN_B, seq=TRAIN_T,
+              variants=("aux_on", "aux_off"), ddp=True):
+    """TensionLM training steps through the harness bozo_b200.lm — by default
+    the 117M model of BASELINE configs[3] (per-GPU batch 16 × 1024 tokens);
+    also the 13.5M model of configs[2] (batch 32 × 512).  bf16 autocast, the
+    operator in every tension layer, CE + train.py's default aux losses
+    (w_closure 0.01, w_diversity 0.02, which put τ export and its cotangent
+    in the loop; ``aux_off`` drops them), global-norm clip, fused AdamW; DDP
+    over NCCL when world > 1 (bf16 gradient all-reduce).  Uniform random
+    token ids from a per-rank seed, random init.  Returns
+    ({variant: (ms_per_step max over ranks, e2e ms_per_step)}, params)."""
     import torch.distributed as dist
     from bozo_b200 import lm
     dev = torch.device("cuda", local_rank)
     torch.manual_seed(0)  # identical init on every rank (DDP also broadcasts rank 0's)
-    cfg = lm.preset_117m()
+    cfg = cfg or lm.preset_117m()
     base = lm.TensionLM(cfg).to(dev)
-    model = lm.wrap_ddp(base) if world > 1 else base
+    model = lm.wrap_ddp(base) if (world > 1 and ddp) else base
     opt = lm.make_optimizer(base, fused=True)
     g = torch.Generator().manual_seed(4242 + rank)
-    ids_h = torch.randint(0, cfg.vocab_size, (TRAIN_B, TRAIN_T + 1), generator=g).pin_memory()
+    ids_h = torch.randint(0, cfg.vocab_size, (batch, seq + 1), generator=g).pin_memory()
     ids = ids_h.to(dev)
     inputs, targets = ids[:, :-1], ids[:, 1:]
     loss_h = torch.empty((), dtype=torch.float32).pin_memory()
@@ -350,9 +353,9 @@ def run_train(args, rank, world, local_rank):
             dist.barrier()
 
     out = {}
-    variants = (("aux_on", lm.TrainWeights()),
-                ("aux_off", lm.TrainWeights(0.0, 0.0, 0.0, 0.0)))
-    for name, w in variants:
+    weights = {"aux_on": lm.TrainWeights(), "aux_off": lm.TrainWeights(0.0, 0.0, 0.0, 0.0)}
+    for name in variants:
+        w = weights[name]
         for _ in range(args.train_warmup):
             lm.train_step(model, base, opt, inputs, targets, weights=w)
         torch.cuda.synchronize()
@@ -443,6 +446,176 @@ def run_tau_consumer(local_rank, iters=20):
         "fused_losses_fwd_bwd_ms": round(ms_fused, 3),
         "framework_ops_fwd_bwd_ms": round(ms_fw, 3),
     }
+
+
+GLOBAL_B, GLOBAL_T = 16, 1024  # the 117M model's global layer (configs[3] shape)
+
+
+def run_global_block(local_rank, steps=20, warmup=5):
+    """The global full-causal block (model.py:217-237) at the 117M layer
+    shape B16 H12 T1024 HD64, bf16, RoPE, τ-mass: forward + backward of
+    ``bozo_b200.tension(window=None)`` as one CUDA-graph replay, and the
+    forward alone.  This block sits at the ridge (77.4 GFLOP against 303.6 MB
+    per fwd+bwd), so both roofline fractions are reported."""
+    import bozo_b200
+    dev = torch.device("cuda", local_rank)
+    g = torch.Generator().manual_seed(55)
+    q, k, v, d = [torch.randn(GLOBAL_B, GLOBAL_T, H, HD, generator=g).to(dev, torch.bfloat16)
+                  for _ in range(4)]
+    for x in (q, k, v):
+        x.requires_grad_(True)
+
+    def fwd():
+        return bozo_b200.tension(q, k, v, window=None, normalize="mass")
+
+    def step():
+        out = fwd()
+        return torch.autograd.grad(out, (q, k, v), d)
+
+    def graph_of(fn):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                fn()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            keep = fn()
+        return gr, keep
+
+    def timed(run):
+        for _ in range(warmup):
+            run()
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            run()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / steps
+
+    gs, ks = graph_of(step)
+    ms_step = timed(gs.replay)
+    path = bozo_b200.last_path()
+    gf, kf = graph_of(fwd)
+    ms_fwd = timed(gf.replay)
+    del gs, ks, gf, kf
+    hbm, tfl, kind = peaks()
+    nbytes = bytes_fwd(GLOBAL_B, H, GLOBAL_T) + bytes_bwd(GLOBAL_B, H, GLOBAL_T)
+    pairs_g = GLOBAL_B * H * GLOBAL_T * (GLOBAL_T + 1) // 2
+    flops = 12 * pairs_g * HD
+    gbs = nbytes / (ms_step * 1e-3) / 1e9
+    tfs = flops / (ms_step * 1e-3) / 1e12
+    ms_bwd = max(ms_step - ms_fwd, 1e-6)
+    return {
+        "workload": "global full-causal block fwd+bwd, B16 H12 T1024 HD64 bf16, RoPE, tau-mass "
+                    "(the 117M model's global layer, model.py:217-237)",
+        "ms_per_step": round(ms_step, 4), "fwd_ms": round(ms_fwd, 4), "bwd_ms": round(ms_bwd, 4),
+        "kernel_path": path,
+        "gbs": round(gbs, 1), "tflops": round(tfs, 1),
+        "frac_hbm": round(gbs / hbm, 4), "frac_tensor": round(tfs / tfl, 4),
+        "frac_roofline": round(max(nbytes / (hbm * 1e9), flops / (tfl * 1e12)) / (ms_step * 1e-3), 4),
+        "fwd_tflops": round(4 * pairs_g * HD / (ms_fwd * 1e-3) / 1e12, 1),
+        "bwd_tflops": round(8 * pairs_g * HD / (ms_bwd * 1e-3) / 1e12, 1),
+        "algorithmic": {"bytes": nbytes, "flops": flops,
+                        "hbm_floor_us": round(nbytes / (hbm * 1e9) * 1e6, 1),
+                        "flop_floor_us": round(flops / (tfl * 1e12) * 1e6, 1)},
+        "peaks": f"{hbm} GB/s, {tfl} TFLOP/s bf16 burst ({kind})",
+    }
+
+
+ONE_M_B, ONE_M_T = 8, 256  # BASELINE configs[0]: the reference's CPU-runnable model
+
+
+def _one_m_step(model, ids, targets):
+    logits = model(ids)
+    loss = torch.nn.functional.cross_entropy(logits.reshape(-1, logits.shape[-1]), targets.reshape(-1))
+    loss.backward()
+    return loss
+
+
+def run_1m_gpu(local_rank, steps=20):
+    """configs[0] on the GPU: the 1.1M model (head_dim 32, fp32) forward +
+    backward of the cross-entropy loss through the operator (the exact-fp32
+    CUDA-core path serves HD 32 and fp32)."""
+    import bozo_b200
+    from bozo_b200 import lm
+    dev = torch.device("cuda", local_rank)
+    torch.manual_seed(0)
+    model = lm.TensionLM(lm.preset_1m()).to(dev)
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, 2048, (ONE_M_B, ONE_M_T + 1), generator=g).to(dev)
+    x, y = ids[:, :-1], ids[:, 1:]
+    for _ in range(3):
+        _one_m_step(model, x, y)
+        model.zero_grad(set_to_none=True)
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        _one_m_step(model, x, y)
+        model.zero_grad(set_to_none=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    return {"value": round(ONE_M_B * ONE_M_T / (ms * 1e-3), 1), "unit": "tokens/s",
+            "ms_per_step": round(ms, 3), "kernel_path": bozo_b200.last_path(),
+            "dtype": "fp32", "params": model.num_params}
+
+
+def cpu_model_name() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def cpu_1m(budget_s=12.0):
+    """configs[0] timed on the host cores: the same 1.1M model (the harness,
+    model.py restated) with the oracle's unfold restatement of the tension
+    op (ops.py:29-63, model.py:271-283) in place of the kernels, fp32
+    forward + backward of the cross-entropy loss, all host threads."""
+    from bozo_b200 import lm
+    from oracle import tension_oracle as orc
+
+    def oracle_tension(q, k, v, *, window, scale, rope_base=10_000.0, rope_len=None, bias=None,
+                       return_tau=False, normalize="mass", tau_window=None):
+        out, tau = orc.fused_reference(q, k, v, window=window, scale=scale, rope_base=rope_base,
+                                       bias=bias, normalize=normalize or "none",
+                                       local_window=tau_window or 64, max_seq_len=rope_len)
+        return (out, tau) if return_tau else out
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    torch.manual_seed(0)
+    model = lm.TensionLM(lm.preset_1m())
+    model.set_tension_fn(oracle_tension)
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, 2048, (ONE_M_B, ONE_M_T + 1), generator=g)
+    x, y = ids[:, :-1], ids[:, 1:]
+    _one_m_step(model, x, y)
+    model.zero_grad(set_to_none=True)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        _one_m_step(model, x, y)
+        model.zero_grad(set_to_none=True)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or reps >= 30:
+            break
+    ms = el * 1e3 / reps
+    return {"value": round(ONE_M_B * ONE_M_T / (ms * 1e-3), 1), "unit": "tokens/s",
+            "ms_per_step": round(ms, 2), "cores": threads, "cpu": cpu_model_name(),
+            "kind": "port", "sample": f"{reps} fwd+bwd steps of B{ONE_M_B} T{ONE_M_T}, fp32"}
 
 
 DECODE_B, DECODE_PROMPT, DECODE_NEW = 16, 960, 64
@@ -586,7 +759,7 @@ def cpu_baseline(budget_s=12.0):
         if el > budget_s or reps >= 8:
             break
     gbs = bytes_fwd(1) * reps / el / 1e9 + bytes_bwd(1) * reps / el / 1e9
-    return dict(value=round(gbs, 4), unit="GB/s", cores=threads, kind="port",
+    return dict(value=round(gbs, 4), unit="GB/s", cores=threads, cpu=cpu_model_name(), kind="port",
                 sample=f"{reps} x B=1 slices (1/{B} of the batch each) of B{B} H{H} T{T} "
                        f"HD{HD} W{W_HEAD}, fp32 unfold+autograd, {el:.1f}s",
                 tokens_per_s=round(reps * T / el, 1))
@@ -602,7 +775,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--workload", default="all",
-                    choices=["all", "op", "train", "prefill", "decode"],
+                    choices=["all", "op", "train", "prefill", "decode", "global"],
                     help="op: isolated operator (headline); train: 117M training step; "
                          "prefill: 350M inference prefill with tau export; "
                          "decode: 117M token-by-token decoding")
@@ -645,7 +818,8 @@ def main():
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "f32", "data": "synthetic N(0,1)", "config": cfg,
                 "cpu_baseline": {"value": round(val, 4), "unit": "GB/s",
-                                 "cores": torch.get_num_threads(), "kind": "port",
+                                 "cores": torch.get_num_threads(), "cpu": cpu_model_name(),
+                                 "kind": "port",
                                  "sample": f"each step = one B=1 slice (1/{B} of the batch)"},
                 "e2e": {"value": round(val, 4), "unit": "GB/s",
                         "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -658,15 +832,24 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    results = train = prefill = None
+    results = train = prefill = train13 = glob_obj = one_m = None
     if args.workload in ("all", "op"):
         results, e2e_ms, launches_per_step = run_ours(args, rank, world, local_rank)
+    if args.workload in ("all", "op", "global"):
+        torch.cuda.empty_cache()
+        glob_obj = run_global_block(local_rank)
     tau_consumer = None
     if args.workload in ("all", "train"):
         torch.cuda.empty_cache()
         train, n_params = run_train(args, rank, world, local_rank)
         torch.cuda.empty_cache()
         tau_consumer = run_tau_consumer(local_rank)
+        torch.cuda.empty_cache()
+        from bozo_b200 import lm as _lm
+        train13 = run_train(args, rank, world, local_rank, cfg=_lm.preset_13m(), batch=32,
+                            seq=512, variants=("aux_on",))
+        torch.cuda.empty_cache()
+        one_m = {"gpu": run_1m_gpu(local_rank)}
     if args.workload in ("all", "prefill"):
         torch.cuda.empty_cache()
         prefill = run_prefill(args, rank, world, local_rank)
@@ -713,6 +896,32 @@ def main():
                        "data": "uniform random token ids, random init"},
             "tau_consumer": tau_consumer,
         }
+    train13_obj = None
+    if train13 is not None:
+        n = args.gpus
+        (ms13, e2e13), p13 = train13[0]["aux_on"], train13[1]
+        tok13 = n * 32 * 512
+        train13_obj = {
+            "metric": "13.5M TensionLM train tokens/s (whole job)",
+            "value": round(tok13 / (ms13 * 1e-3), 1), "unit": "tokens/s",
+            "ms_per_step": round(ms13, 3), "steps": args.train_steps, "n_gpus": n,
+            "e2e": {"value": round(tok13 / (e2e13 * 1e-3), 1), "unit": "tokens/s",
+                    "ms_per_step": round(e2e13, 3), "h2d_bytes_per_step": 32 * 513 * 8,
+                    "d2h_bytes_per_step": 4},
+            "config": {"workload": "TensionLM 13.5M training step (BASELINE configs[2])",
+                       "params": p13, "dim": 384, "layers": 6, "heads": 6, "vocab": 8192,
+                       "W": 64, "global_every": 4, "seq_len": 512, "per_gpu_batch": 32,
+                       "dtype": "bf16 autocast, fp32 master weights",
+                       "aux_losses": "on (train.py defaults)", "optimizer": "AdamW (fused)",
+                       "parallelism": f"ddp{n}" if n > 1 else "single GPU",
+                       "data": "uniform random token ids, random init"},
+        }
+    if one_m is not None and rank == 0 and args.gpus == 1 and not args.no_cpu_baseline:
+        one_m["cpu"] = cpu_1m()
+        one_m["config"] = {"workload": "TensionLM 1.1M fwd+bwd of the CE loss (BASELINE configs[0])",
+                           "dim": 128, "layers": 4, "heads": 4, "head_dim": 32, "vocab": 2048,
+                           "W": 64, "seq_len": ONE_M_T, "batch": ONE_M_B, "dtype": "fp32",
+                           "data": "uniform random token ids (seed 0), random init"}
     prefill_obj = None
     if prefill is not None:
         n = args.gpus
@@ -738,7 +947,10 @@ def main():
         }
     if results is None:
         if train_obj is None and prefill_obj is None:
-            print(json.dumps(dict(decode_obj, higher_is_better=True, scaling="weak",
+            solo = decode_obj if decode_obj is not None else dict(
+                glob_obj, metric="global block fwd+bwd algorithmic GB/s", value=glob_obj["gbs"],
+                unit="GB/s")
+            print(json.dumps(dict(solo, higher_is_better=True, scaling="weak",
                                   vs_baseline=None, dtype="bf16", data="synthetic",
                                   n_gpus=args.gpus)))
             return
@@ -746,6 +958,10 @@ def main():
         line.update({"higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                      "dtype": "bf16", "data": "synthetic"})
         line["config"] = (train_obj or prefill_obj)["config"]
+        if train13_obj is not None:
+            line["train_13m"] = train13_obj
+        if one_m is not None:
+            line["config0_1m"] = one_m
         if train_obj is not None and prefill_obj is not None:
             line["prefill_350m"] = prefill_obj
         if decode_obj is not None:
@@ -795,14 +1011,39 @@ def main():
         "launches_per_step": launches_per_step,
         "clocks": head["clocks"],
     }
+    if glob_obj is not None:
+        line["global_block"] = glob_obj
     if train_obj is not None:
         line["train_117m"] = train_obj
+    if train13_obj is not None:
+        line["train_13m"] = train13_obj
+    if one_m is not None:
+        line["config0_1m"] = one_m
     if prefill_obj is not None:
         line["prefill_350m"] = prefill_obj
     if decode_obj is not None:
         line["decode_117m"] = decode_obj
     if n == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
+    # the headline figures once more, last on the line (a reader that keeps
+    # only the tail of a long line still sees every workload's number)
+    summ = {"op_gbs": line["value"], "op_frac": line["roofline"]["frac"],
+            "op_ms": line["ms_per_step"]}
+    if glob_obj is not None:
+        summ.update(global_ms=glob_obj["ms_per_step"], global_frac_hbm=glob_obj["frac_hbm"],
+                    global_frac_tensor=glob_obj["frac_tensor"])
+    if train_obj is not None:
+        summ.update(train_117m_tokens_per_s=train_obj["value"],
+                    train_117m_ms=train_obj["ms_per_step"],
+                    train_117m_aux_off_tokens_per_s=train_obj["aux_off"]["value"],
+                    train_117m_mfu=train_obj["mfu"])
+    if train13_obj is not None:
+        summ.update(train_13m_tokens_per_s=train13_obj["value"], train_13m_ms=train13_obj["ms_per_step"])
+    if prefill_obj is not None:
+        summ.update(prefill_350m_tokens_per_s=prefill_obj["value"])
+    if decode_obj is not None:
+        summ.update(decode_117m_tokens_per_s=decode_obj["value"])
+    line["summary"] = summ
     print(json.dumps(line))
 
 

@@ -34,7 +34,7 @@ EXPORTED = (
     "bozo_add_rmsnorm_workspace", "bozo_add_rmsnorm_fwd", "bozo_add_rmsnorm_bwd",
     "bozo_swiglu_fwd", "bozo_swiglu_bwd",
     "bozo_cross_entropy_fwd", "bozo_cross_entropy_bwd",
-    "bozo_tension_error_async", "bozo_tension_wait_selftest",
+    "bozo_tension_error_async", "bozo_tension_wait_selftest", "bozo_tension_fwd_needs_lp",
 )
 TAU_AUX_MAX_LAYERS = 64  # BOZO_TAU_AUX_MAX_LAYERS
 
@@ -55,6 +55,7 @@ class FwdArgs(C.Structure):
         ("out", C.c_void_p), ("out_dtype", C.c_int32), ("tau_dtype", C.c_int32),
         ("tau", C.c_void_p), ("row_mass", C.c_void_p),
         ("q_rot", C.c_void_p), ("k_rot", C.c_void_p),
+        ("q_lp", C.c_void_p), ("k_lp", C.c_void_p),
     ]
 
 
@@ -160,6 +161,8 @@ def lib():
                 L = C.CDLL(LIB_PATH)
                 L.bozo_tension_fwd.argtypes = [C.POINTER(FwdArgs), C.c_void_p]
                 L.bozo_tension_fwd.restype = C.c_int
+                L.bozo_tension_fwd_needs_lp.argtypes = [C.POINTER(FwdArgs)]
+                L.bozo_tension_fwd_needs_lp.restype = C.c_int
                 L.bozo_tension_bwd.argtypes = [C.POINTER(BwdArgs), C.c_void_p]
                 L.bozo_tension_bwd.restype = C.c_int
                 L.bozo_tension_bwd_noalloc.argtypes = [C.POINTER(BwdArgs), C.c_void_p]

@@ -182,6 +182,38 @@ const char* bozo_tension_last_cuda_error(void) {
 }
 int bozo_tension_last_launches(void) { return t_last_launches.load(); }
 
+namespace {
+
+// The fp32-Q/K call (model.py's autocast call site: RoPE-promoted fp32 Q/K,
+// bf16 V, fp32 out and τ by the reference's dtype contract) runs on the
+// tensor cores from bf16 copies of Q and K.  True when `a` is such a call
+// and the band kernel takes it (judged with aligned contiguous stand-ins for
+// the copies, which the caller allocates).
+bool fwd_wants_lp(const bozo_tension_fwd_args* a) {
+  if (!a || a->path == BOZO_PATH_SIMT || a->rope_len != 0 || a->mode != BOZO_MODE_LOCAL) return false;
+  if (a->q.dtype != BOZO_DT_F32 || a->k.dtype != BOZO_DT_F32 || a->v.dtype != BOZO_DT_BF16) return false;
+  if (a->out_dtype != BOZO_DT_F32 || (a->tau && a->tau_dtype != BOZO_DT_F32)) return false;
+  if (a->HD != kTcHD || a->B <= 0 || a->T <= 0 || a->H <= 0) return false;
+  FwdP p{};
+  p.B = a->B; p.T = a->T; p.H = a->H; p.HD = a->HD; p.mode = a->mode; p.W = a->window;
+  p.norm = a->normalize; p.scale = a->scale;
+  const long long ob = (long long)a->T * a->H * a->HD, ot = (long long)a->H * a->HD;
+  void* const aligned = reinterpret_cast<void*>(uintptr_t(256));
+  p.q = DevT4{aligned, BOZO_DT_BF16, ob, ot, a->HD, 1};
+  p.k = p.q;
+  p.v = dev_t4(a->v);
+  p.bias = a->bias;
+  p.out = a->out ? a->out : aligned;
+  p.out_dt = a->out_dtype;
+  p.tau = a->tau;
+  p.tau_dt = a->tau_dtype;
+  return tc_fwd_eligible(p);
+}
+
+}  // namespace
+
+int bozo_tension_fwd_needs_lp(const bozo_tension_fwd_args* a) { return fwd_wants_lp(a) ? 1 : 0; }
+
 int bozo_tension_fwd(const bozo_tension_fwd_args* a, void* stream) {
   if (!a) return BOZO_ERR_NULL;
   int st = check_common(a->B, a->T, a->H, a->HD, a->mode, a->window, a->normalize, a->scale,
@@ -213,25 +245,51 @@ int bozo_tension_fwd(const bozo_tension_fwd_args* a, void* stream) {
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int launches = 0;
+  const bool lp_given = a->q_lp && a->k_lp && a->q.dtype == BOZO_DT_F32 && a->k.dtype == BOZO_DT_F32;
+  if (lp_given) {
+    // bf16 copies of fp32 q / k into the caller's q_lp / k_lp, whichever path
+    // runs, so the caller can always hand them to the backward
+    if ((reinterpret_cast<uintptr_t>(a->q_lp) | reinterpret_cast<uintptr_t>(a->k_lp)) & 7)
+      return BOZO_ERR_ALIGNMENT;
+    const int sms = num_sms();
+    if ((e = launch_to_bf16(p.q, p.B, p.T, p.H, p.HD, a->q_lp, sms, s)) != cudaSuccess ||
+        (e = launch_to_bf16(p.k, p.B, p.T, p.H, p.HD, a->k_lp, sms, s)) != cudaSuccess)
+      return cuda_fail(e);
+    launches += 2;
+  }
+  if (lp_given && fwd_wants_lp(a) &&
+      ((reinterpret_cast<uintptr_t>(a->q_lp) | reinterpret_cast<uintptr_t>(a->k_lp)) & 15) == 0) {
+    // fp32 Q/K: the band kernel on the bf16 copies, fp32 out and τ (without
+    // the copies' room the call stays on the exact fp32 path below)
+    const long long ob = (long long)p.T * p.H * p.HD, ot = (long long)p.H * p.HD;
+    p.q = DevT4{a->q_lp, BOZO_DT_BF16, ob, ot, p.HD, 1};
+    p.k = DevT4{a->k_lp, BOZO_DT_BF16, ob, ot, p.HD, 1};
+    if (!tc_fwd_eligible(p)) return BOZO_ERR_ALIGNMENT;
+    int nl = 0;
+    if ((e = launch_tc_fwd(p, s, &nl)) != cudaSuccess) return cuda_fail(e);
+    t_last_path = BOZO_PATH_TCGEN05;
+    t_last_launches = launches + nl;
+    return BOZO_OK;
+  }
   // local windows up to 128 keys: the band kernel; global and wider local
   // windows: the key-tile streaming kernel
   const bool band = p.mode == BOZO_MODE_LOCAL && tc_fwd_eligible(p);
   const bool tc_ok = band || tc_global_fwd_eligible(p);
   if (a->path == BOZO_PATH_TCGEN05 && !tc_ok) return BOZO_ERR_ALIGNMENT;
-  int path;
+  int path, nl = 0;
   if (tc_ok && a->path != BOZO_PATH_SIMT) {
-    e = band ? launch_tc_fwd(p, s, &launches) : launch_tc_global_fwd(p, s, &launches);
+    e = band ? launch_tc_fwd(p, s, &nl) : launch_tc_global_fwd(p, s, &nl);
     path = BOZO_PATH_TCGEN05;
   } else {
-    e = launch_simt_fwd(p, s, &launches);
+    e = launch_simt_fwd(p, s, &nl);
     // the CUDA-core forward does not stage whole tiles: rotated copies
     // come from a separate elementwise pass
-    if (e == cudaSuccess && (p.q_rot || p.k_rot)) e = launch_rope_copy(p, s, &launches);
+    if (e == cudaSuccess && (p.q_rot || p.k_rot)) e = launch_rope_copy(p, s, &nl);
     path = BOZO_PATH_SIMT;
   }
   if (e != cudaSuccess) return cuda_fail(e);
   t_last_path = path;
-  t_last_launches = launches;
+  t_last_launches = launches + nl;
   return BOZO_OK;
 }
 
@@ -242,7 +300,12 @@ size_t bozo_tension_bwd_workspace(const bozo_tension_bwd_args* a) {
   // 16-byte aligned (tensor-core bulk copies)
   const size_t tpad = ((size_t)a->T + 127) / 128 * 128;
   const size_t rows = (size_t)a->B * a->H * tpad;
-  return round256(rows * sizeof(float)) * (a->aux_row ? 5 : 3);
+  size_t bytes = round256(rows * sizeof(float)) * (a->aux_row ? 5 : 3);
+  // an fp32 cotangent with bf16 q/k (the fp32-Q call on the tensor cores):
+  // room for its bf16 copy
+  if (a->d_out.dtype == BOZO_DT_F32 && a->q.dtype == BOZO_DT_BF16 && a->HD > 0)
+    bytes += round256((size_t)a->B * a->T * a->H * a->HD * 2);
+  return bytes;
 }
 
 int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
@@ -288,6 +351,8 @@ int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
   p.beta = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + round256(rows * sizeof(float)));
   // the tensor-core path uses the same bytes as three contiguous planes
   p.coef = static_cast<float*>(a->workspace);
+  if (a->d_out.dtype == BOZO_DT_F32 && a->q.dtype == BOZO_DT_BF16)
+    p.dout_lp = static_cast<char*>(a->workspace) + round256(rows * sizeof(float)) * (a->aux_row ? 5 : 3);
   p.err = error_word(&e);
   if (!p.err) return cuda_fail(e);
 

@@ -43,6 +43,8 @@ struct FwdP {
   float* row_mass;
   void* q_rot;  // optional rotated copies (dtype of q / k)
   void* k_rot;
+  void* q_lp;   // bf16 operand copies of fp32 q / k (tensor-core path)
+  void* k_lp;
   int* err;  // device error word
 };
 
@@ -65,6 +67,7 @@ struct BwdP {
   float* alpha;  // [B,H,T] workspace (CUDA-core path)
   float* beta;   // [B,H,T] workspace
   float* coef;   // [3][B·H, Tpad] workspace (tensor-core path)
+  void* dout_lp;  // workspace room for a bf16 copy of an fp32 dO (tensor-core path) or null
   int qk_rotated;  // q, k are RoPE-rotated already
   const float* aux_row;  // [3][B·H·T] per-row τ cotangent (a1, a0, inv_d) or null
   int* err;
@@ -100,6 +103,9 @@ cudaError_t launch_simt_fwd(const FwdP& p, cudaStream_t st, int* launches);
 cudaError_t launch_simt_bwd(const BwdP& p, cudaStream_t st, int* launches);
 // Write RoPE(q), RoPE(k) into p.q_rot / p.k_rot (dtype of q / k).
 cudaError_t launch_rope_copy(const FwdP& p, cudaStream_t st, int* launches);
+// fp32 (any strides) → contiguous bf16 [B,T,H,HD] copy (convert.cu)
+cudaError_t launch_to_bf16(const DevT4& src, int B, int T, int H, int HD, void* dst, int sms,
+                           cudaStream_t st);
 
 // One decode step (decode.cu): the new token's projections against ring
 // caches [B, C, H, HD] of rotated keys and values.

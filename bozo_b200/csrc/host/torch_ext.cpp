@@ -89,7 +89,10 @@ void fill_bias(const c10::optional<at::Tensor>& bias, const float** ptr, int64_t
   }
 }
 
-// Returns [out, tau, row_mass, q_rot, k_rot]; absent ones are None.
+// Returns [out, tau, row_mass, q_rot, k_rot, q_lp, k_lp]; absent ones are
+// None.  With want_lp, fp32 q/k get bf16 operand copies (q_lp, k_lp): the
+// tensor-core kernels compute from them when the call qualifies, and the
+// backward takes them as its q/k in every case.
 std::vector<at::Tensor> tension_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                     int64_t mode, int64_t window, int64_t norm, double scale,
                                     int64_t path, const c10::optional<at::Tensor>& cos,
@@ -97,7 +100,7 @@ std::vector<at::Tensor> tension_fwd(const at::Tensor& q, const at::Tensor& k, co
                                     const c10::optional<at::Tensor>& theta,
                                     const c10::optional<at::Tensor>& bias, int64_t tau_width,
                                     int64_t out_dtype, int64_t tau_dtype, bool want_mass,
-                                    bool want_rotated) {
+                                    bool want_rotated, bool want_lp) {
   const c10::cuda::CUDAGuard guard(q.device());
   const int64_t B = q.size(0), T = q.size(1), H = q.size(2), HD = q.size(3);
   auto opts = q.options();
@@ -126,9 +129,16 @@ std::vector<at::Tensor> tension_fwd(const at::Tensor& q, const at::Tensor& k, co
     a.q_rot = q_rot.data_ptr();
     a.k_rot = k_rot.data_ptr();
   }
+  at::Tensor q_lp, k_lp;
+  if (want_lp && q.scalar_type() == at::kFloat && k.scalar_type() == at::kFloat) {
+    q_lp = at::empty({B, T, H, HD}, opts.dtype(at::kBFloat16));
+    k_lp = at::empty({B, T, H, HD}, opts.dtype(at::kBFloat16));
+    a.q_lp = q_lp.data_ptr();
+    a.k_lp = k_lp.data_ptr();
+  }
   check(bozo_tension_fwd(&a, at::cuda::getCurrentCUDAStream(q.device().index()).stream()),
         "bozo_tension_fwd");
-  return {out, tau, mass, q_rot, k_rot};
+  return {out, tau, mass, q_rot, k_rot, q_lp, k_lp};
 }
 
 // Returns [dq, dk, dv] in the dtypes of q, k, v.
@@ -142,11 +152,14 @@ std::vector<at::Tensor> tension_bwd(const at::Tensor& q, const at::Tensor& k, co
                                     const c10::optional<at::Tensor>& out,
                                     const c10::optional<at::Tensor>& mass,
                                     const c10::optional<at::Tensor>& d_tau, bool qk_rotated,
-                                    const c10::optional<at::Tensor>& aux_row) {
+                                    const c10::optional<at::Tensor>& aux_row, int64_t dq_dtype,
+                                    int64_t dk_dtype) {
   const c10::cuda::CUDAGuard guard(q.device());
   const int64_t B = q.size(0), T = q.size(1), H = q.size(2), HD = q.size(3);
-  at::Tensor dq = at::empty({B, T, H, HD}, q.options());
-  at::Tensor dk = at::empty({B, T, H, HD}, k.options());
+  // gradient dtypes: q's and k's unless given (the bf16 operand copies of an
+  // fp32 forward still owe fp32 gradients)
+  at::Tensor dq = at::empty({B, T, H, HD}, dq_dtype >= 0 ? q.options().dtype(scalar_type(dq_dtype)) : q.options());
+  at::Tensor dk = at::empty({B, T, H, HD}, dk_dtype >= 0 ? k.options().dtype(scalar_type(dk_dtype)) : k.options());
   at::Tensor dv = at::empty({B, T, H, HD}, v.options());
   bozo_tension_bwd_args a{};
   fill_common(a, q, mode, window, norm, scale, path, cos, sin, theta);
@@ -161,8 +174,8 @@ std::vector<at::Tensor> tension_bwd(const at::Tensor& q, const at::Tensor& k, co
     a.d_tau = d_tau->data_ptr();
     a.d_tau_dtype = dtype_code(d_tau->scalar_type());
   }
-  a.grad_dtype[0] = dtype_code(q.scalar_type());
-  a.grad_dtype[1] = dtype_code(k.scalar_type());
+  a.grad_dtype[0] = dtype_code(dq.scalar_type());
+  a.grad_dtype[1] = dtype_code(dk.scalar_type());
   a.grad_dtype[2] = dtype_code(v.scalar_type());
   a.qk_rotated = qk_rotated ? 1 : 0;
   if (aux_row && aux_row->defined()) {

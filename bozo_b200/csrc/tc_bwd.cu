@@ -35,6 +35,7 @@
 // All waits are bounded
 // (tc_ptx.cuh).
 #include <algorithm>
+#include <type_traits>
 
 #include "tc.cuh"
 #include "tc_host.cuh"
@@ -62,11 +63,11 @@ struct BwdTC {
   const float* theta;              // RoPE frequencies [32] or null (no RoPE)
   const float* bias;
   long long bs0, bs1, bs2;
-  const __nv_bfloat16* dtau;       // [B,T,H,W] contiguous or null
+  const void* dtau;                // [B,T,H,W] contiguous (bf16, fp32 with kF32) or null
   const float* coef;               // [3][B·H, tpad]: α/2, α·c, β·c
-  __nv_bfloat16* dq;               // [B,T,H,64] contiguous outputs
-  __nv_bfloat16* dk;
-  __nv_bfloat16* dv;
+  void* dq;                        // [B,T,H,64] contiguous outputs (dQ/dK fp32 with kF32)
+  void* dk;
+  void* dv;
   int* err;
 };
 
@@ -273,7 +274,10 @@ struct SubGen {
   }
 };
 
-template <bool kBias, bool kDTau, bool kAux>
+// kF32: the τ cotangent arrives in fp32 and dQ/dK leave in fp32 (the
+// reference's gradient dtypes for fp32 Q/K, ops.py:186-187), from bf16
+// operand copies of Q/K; dV stays bf16.
+template <bool kBias, bool kDTau, bool kAux, bool kF32>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_bwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
@@ -529,14 +533,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           oq8[z] = q1 * cs + q2 * sn;
           oq8[8 + z] = q2 * cs - q1 * sn;
         }
-        st_shared_v4(kst + sw128_off(r, c8), pack_bf16(ok8[0], ok8[1]), pack_bf16(ok8[2], ok8[3]),
-                     pack_bf16(ok8[4], ok8[5]), pack_bf16(ok8[6], ok8[7]));
-        st_shared_v4(kst + sw128_off(r, 4 + c8), pack_bf16(ok8[8], ok8[9]), pack_bf16(ok8[10], ok8[11]),
-                     pack_bf16(ok8[12], ok8[13]), pack_bf16(ok8[14], ok8[15]));
-        st_shared_v4(qst + sw128_off(r, c8), pack_bf16(oq8[0], oq8[1]), pack_bf16(oq8[2], oq8[3]),
-                     pack_bf16(oq8[4], oq8[5]), pack_bf16(oq8[6], oq8[7]));
-        st_shared_v4(qst + sw128_off(r, 4 + c8), pack_bf16(oq8[8], oq8[9]), pack_bf16(oq8[10], oq8[11]),
-                     pack_bf16(oq8[12], oq8[13]), pack_bf16(oq8[14], oq8[15]));
+        if constexpr (kF32) {
+          // row pos of dK (key tile i) and of dQ (query tile i), columns
+          // [8c8, 8c8+8) and [32+8c8, +8), straight to global memory
+          if (pos < p.T) {
+            const long long row = ((long long)(b * p.T + pos) * H + h) * kHD;
+            float4* gk = reinterpret_cast<float4*>(static_cast<float*>(p.dk) + row);
+            float4* gq = reinterpret_cast<float4*>(static_cast<float*>(p.dq) + row);
+            gk[2 * c8] = make_float4(ok8[0], ok8[1], ok8[2], ok8[3]);
+            gk[2 * c8 + 1] = make_float4(ok8[4], ok8[5], ok8[6], ok8[7]);
+            gk[8 + 2 * c8] = make_float4(ok8[8], ok8[9], ok8[10], ok8[11]);
+            gk[8 + 2 * c8 + 1] = make_float4(ok8[12], ok8[13], ok8[14], ok8[15]);
+            gq[2 * c8] = make_float4(oq8[0], oq8[1], oq8[2], oq8[3]);
+            gq[2 * c8 + 1] = make_float4(oq8[4], oq8[5], oq8[6], oq8[7]);
+            gq[8 + 2 * c8] = make_float4(oq8[8], oq8[9], oq8[10], oq8[11]);
+            gq[8 + 2 * c8 + 1] = make_float4(oq8[12], oq8[13], oq8[14], oq8[15]);
+          }
+        } else {
+          st_shared_v4(kst + sw128_off(r, c8), pack_bf16(ok8[0], ok8[1]), pack_bf16(ok8[2], ok8[3]),
+                       pack_bf16(ok8[4], ok8[5]), pack_bf16(ok8[6], ok8[7]));
+          st_shared_v4(kst + sw128_off(r, 4 + c8), pack_bf16(ok8[8], ok8[9]), pack_bf16(ok8[10], ok8[11]),
+                       pack_bf16(ok8[12], ok8[13]), pack_bf16(ok8[14], ok8[15]));
+          st_shared_v4(qst + sw128_off(r, c8), pack_bf16(oq8[0], oq8[1]), pack_bf16(oq8[2], oq8[3]),
+                       pack_bf16(oq8[4], oq8[5]), pack_bf16(oq8[6], oq8[7]));
+          st_shared_v4(qst + sw128_off(r, 4 + c8), pack_bf16(oq8[8], oq8[9]), pack_bf16(oq8[10], oq8[11]),
+                       pack_bf16(oq8[12], oq8[13]), pack_bf16(oq8[14], oq8[15]));
+        }
       }
       tc_fence_before();
       fence_proxy_async_smem();
@@ -548,9 +570,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (warp == 2 && lane == 0) {
         ok = mbar_wait(&bar->aux_staged, it & 1, err, kErrBwd | 27);
         if (ok) {
-          tma_store_4d(&tmdk, sK + ks_cur * kTileBytes, 0, h, st.i * kTile, b);
+          if constexpr (!kF32) tma_store_4d(&tmdk, sK + ks_cur * kTileBytes, 0, h, st.i * kTile, b);
           tma_store_4d(&tmdv, sV + ks_cur * kTileBytes, 0, h, st.i * kTile, b);
-          tma_store_4d(&tmdq, sStage, 0, h, st.i * kTile, b);
+          if constexpr (!kF32) tma_store_4d(&tmdq, sStage, 0, h, st.i * kTile, b);
           bulk_commit_group();
           bulk_wait_group_read0();
           mbar_arrive(&bar->kv_empty[ks_cur]);  // the TMA may refill this key slot
@@ -681,21 +703,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             float gb[16], gd[16];
             const int t0 = tq0 + cq0, w0 = W - (kTile * c + cq0 - r);
             const float* b0 = nullptr;
-            const __nv_bfloat16* d0 = nullptr;
+            using DTauT = typename std::conditional<kF32, float, __nv_bfloat16>::type;
+            const DTauT* d0 = nullptr;
             long long bstep = 0, dstep = 0;
             if constexpr (kBias) {
               b0 = p.bias + bb * p.bs0 + (long long)t0 * p.bs1 + (long long)w0 * p.bs2;
               bstep = p.bs1 - p.bs2;
             }
             if constexpr (kDTau) {
-              d0 = p.dtau + (((long long)bb * p.T + t0) * H + h) * W + w0;
+              d0 = static_cast<const DTauT*>(p.dtau) + (((long long)bb * p.T + t0) * H + h) * W + w0;
               dstep = (long long)H * W - 1;
             }
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
               const bool valid = (unsigned)(e - lo[ss]) < (unsigned)cnt[ss];
               if constexpr (kBias) gb[e] = valid ? 0.5f * __ldg(b0 + e * bstep) : 0.f;
-              if constexpr (kDTau) gd[e] = valid ? p.ds_scale * __bfloat162float(d0[e * dstep]) : 0.f;
+              if constexpr (kDTau) {
+                if constexpr (kF32) gd[e] = valid ? p.ds_scale * __ldg(d0 + e * dstep) : 0.f;
+                else gd[e] = valid ? p.ds_scale * __bfloat162float(d0[e * dstep]) : 0.f;
+              }
             }
             tmem_ld16x2_wait(col, col + 64, R);
             piece(ss, R, gb, gd);
@@ -746,10 +772,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <bool kBias, bool kDTau, bool kAux>
+template <bool kBias, bool kDTau, bool kAux, bool kF32>
 cudaError_t launch_bwd_variant(const CUtensorMap* m, const BwdTC& a, size_t smem, int grid,
                                cudaStream_t st) {
-  auto kern = tc_bwd_kernel<kBias, kDTau, kAux>;
+  auto kern = tc_bwd_kernel<kBias, kDTau, kAux, kF32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, smem, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], m[6], a);
@@ -774,17 +800,23 @@ cudaError_t launch_alpha_beta(const BwdP& p, int tpad, float ds_scale, float* co
 bool tc_bwd_eligible(const BwdP& p) {
   if (p.mode != BOZO_MODE_LOCAL || p.HD != kHD || p.W < 1 || p.W > 128) return false;
   if (p.B > 65535 || (long long)p.T * p.H * 8 > 0x7fffffffLL) return false;  // pre-pass grid
-  if (p.dq_dt != BOZO_DT_BF16 || p.dk_dt != BOZO_DT_BF16 || p.dv_dt != BOZO_DT_BF16) return false;
+  // dQ/dK in bf16, or both in fp32 (the fp32-IO variant: fp32 τ cotangent,
+  // an fp32 dO copied to bf16 in the workspace, no RoPE); dV in bf16
+  const bool f32 = p.dq_dt == BOZO_DT_F32;
+  if (p.dq_dt != p.dk_dt || (p.dq_dt != BOZO_DT_BF16 && !f32) || p.dv_dt != BOZO_DT_BF16) return false;
+  if (f32 && (p.cos || (p.dtau && p.dtau_dt != BOZO_DT_F32))) return false;
+  if (!f32 && p.dtau && p.dtau_dt != BOZO_DT_BF16) return false;
   if (!tma_view_ok(p.q, p.B, p.T, p.H) || !tma_view_ok(p.k, p.B, p.T, p.H) ||
-      !tma_view_ok(p.v, p.B, p.T, p.H) || !tma_view_ok(p.dout, p.B, p.T, p.H))
+      !tma_view_ok(p.v, p.B, p.T, p.H))
     return false;
+  if (p.dout.dt == BOZO_DT_F32 ? !p.dout_lp : !tma_view_ok(p.dout, p.B, p.T, p.H)) return false;
+  if (p.dtau && (reinterpret_cast<uintptr_t>(p.dtau) & 15) != 0) return false;
   if (p.norm == BOZO_NORM_MASS) {
     // out rows are read with 16-byte vector loads
     if (p.out.dt != BOZO_DT_BF16 || p.out.sd != 1 || (reinterpret_cast<uintptr_t>(p.out.p) & 15) ||
         (p.out.sb % 8) || (p.out.st % 8) || (p.out.sh % 8))
       return false;
   }
-  if (p.dtau && p.dtau_dt != BOZO_DT_BF16) return false;
   for (const void* ptr : {p.dq, p.dk, p.dv})
     if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return false;
   // RoPE: Q/K must arrive rotated (the forward's copies); θ drives the
@@ -805,41 +837,63 @@ cudaError_t launch_tc_bwd(const BwdP& p, cudaStream_t st, int* launches) {
   a.ds_scale = 0.25f / p.scale;
   a.theta = p.cos ? p.theta : nullptr;
   a.bias = p.bias; a.bs0 = p.bs0; a.bs1 = p.bs1; a.bs2 = p.bs2;
-  a.dtau = static_cast<const __nv_bfloat16*>(p.dtau);
+  a.dtau = p.dtau;
   a.coef = p.coef;
-  a.dq = static_cast<__nv_bfloat16*>(p.dq);
-  a.dk = static_cast<__nv_bfloat16*>(p.dk);
-  a.dv = static_cast<__nv_bfloat16*>(p.dv);
+  a.dq = p.dq;
+  a.dk = p.dk;
+  a.dv = p.dv;
   a.err = p.err;
+  const bool f32 = p.dq_dt == BOZO_DT_F32;
+  int nl = 2;
+  DevT4 dout = p.dout;
+  if (p.dout.dt == BOZO_DT_F32) {  // a bf16 copy of the fp32 cotangent for the TMA tiles
+    cudaError_t e = launch_to_bf16(p.dout, p.B, p.T, p.H, kHD, p.dout_lp, num_sms(), st);
+    if (e != cudaSuccess) return e;
+    dout = DevT4{p.dout_lp, BOZO_DT_BF16, (long long)p.T * p.H * kHD, (long long)p.H * kHD, kHD, 1};
+    ++nl;
+  }
   {  // coefficient pre-pass into the (padded) workspace rows
     cudaError_t e = launch_alpha_beta(p, a.tpad, a.ds_scale, p.coef, st);
     if (e != cudaSuccess) return e;
   }
   CUtensorMap m[7];
-  const DevT4* in[4] = {&p.q, &p.k, &p.v, &p.dout};
+  const DevT4* in[4] = {&p.q, &p.k, &p.v, &dout};
   for (int i = 0; i < 4; ++i)
     if (!make_tmap_bthd(&m[i], in[i]->p, in[i]->sb, in[i]->st, in[i]->sh, p.B, p.T, p.H, kTile))
       return cudaErrorInvalidValue;
   const long long ob = (long long)p.T * p.H * kHD, ot = (long long)p.H * kHD, oh = kHD;
-  void* outs[3] = {p.dq, p.dk, p.dv};
+  // dQ/dK in fp32 leave from registers: their maps are placeholders
+  void* outs[3] = {f32 ? p.dv : p.dq, f32 ? p.dv : p.dk, p.dv};
   for (int i = 0; i < 3; ++i)
     if (!make_tmap_bthd(&m[4 + i], outs[i], ob, ot, oh, p.B, p.T, p.H, kTile)) return cudaErrorInvalidValue;
   const bool has_aux = p.aux_row != nullptr;
   const Layout L = bwd_layout(has_aux ? 5 : 3);
   const size_t smem = L.total + 1024;
   const int grid = std::min(num_sms(), a.total);
-  *launches = 2;
+  *launches = nl;
   const bool has_bias = p.bias != nullptr, has_dtau = p.dtau != nullptr;
+  if (f32) {
+    // the fp32-IO variant serves the reference's fp32-Q call, which has no
+    // per-row τ cotangent (that is formed for bf16 fields only)
+    if (has_aux) return cudaErrorInvalidValue;
+    const int v = (has_bias ? 2 : 0) | (has_dtau ? 1 : 0);
+    switch (v) {
+      case 0: return launch_bwd_variant<false, false, false, true>(m, a, smem, grid, st);
+      case 1: return launch_bwd_variant<false, true, false, true>(m, a, smem, grid, st);
+      case 2: return launch_bwd_variant<true, false, false, true>(m, a, smem, grid, st);
+      default: return launch_bwd_variant<true, true, false, true>(m, a, smem, grid, st);
+    }
+  }
   const int v = (has_bias ? 4 : 0) | (has_dtau ? 2 : 0) | (has_aux ? 1 : 0);
   switch (v) {
-    case 0: return launch_bwd_variant<false, false, false>(m, a, smem, grid, st);
-    case 1: return launch_bwd_variant<false, false, true>(m, a, smem, grid, st);
-    case 2: return launch_bwd_variant<false, true, false>(m, a, smem, grid, st);
-    case 3: return launch_bwd_variant<false, true, true>(m, a, smem, grid, st);
-    case 4: return launch_bwd_variant<true, false, false>(m, a, smem, grid, st);
-    case 5: return launch_bwd_variant<true, false, true>(m, a, smem, grid, st);
-    case 6: return launch_bwd_variant<true, true, false>(m, a, smem, grid, st);
-    default: return launch_bwd_variant<true, true, true>(m, a, smem, grid, st);
+    case 0: return launch_bwd_variant<false, false, false, false>(m, a, smem, grid, st);
+    case 1: return launch_bwd_variant<false, false, true, false>(m, a, smem, grid, st);
+    case 2: return launch_bwd_variant<false, true, false, false>(m, a, smem, grid, st);
+    case 3: return launch_bwd_variant<false, true, true, false>(m, a, smem, grid, st);
+    case 4: return launch_bwd_variant<true, false, false, false>(m, a, smem, grid, st);
+    case 5: return launch_bwd_variant<true, false, true, false>(m, a, smem, grid, st);
+    case 6: return launch_bwd_variant<true, true, false, false>(m, a, smem, grid, st);
+    default: return launch_bwd_variant<true, true, true, false>(m, a, smem, grid, st);
   }
 }
 

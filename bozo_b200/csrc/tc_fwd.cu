@@ -24,6 +24,7 @@
 //   parameters so the common path has no per-element branches.  All
 //   mbarrier waits are bounded (tc_ptx.cuh).
 #include <algorithm>
+#include <type_traits>
 
 #include "tc.cuh"
 #include "tc_host.cuh"
@@ -53,7 +54,8 @@ struct FwdTC {
   const float* theta;  // RoPE frequencies [32] or null (no RoPE)
   const float* bias;
   long long bs0, bs1, bs2;
-  __nv_bfloat16* tau;
+  void* tau;      // bf16, or fp32 in the fp32-output variant
+  float* out_f32;  // fp32-output variant: out [B,T,H,64] fp32, stored from registers
   float* row_mass;
   int store_rot;  // also TMA-store the rotated Q/K tiles (q_rot, k_rot)
   int* err;
@@ -78,14 +80,16 @@ struct Layout {
   uint32_t q, k, v, p, o, mass, tau, bars, total;
 };
 
-__host__ __device__ inline Layout fwd_layout(int pblocks, int nkv, int tstride) {
+// f32_out: the fp32-output variant stores O from registers and needs no
+// bf16 staging tile.
+__host__ __device__ inline Layout fwd_layout(int pblocks, int nkv, int tstride, bool f32_out = false) {
   Layout L;
   L.q = 0;
   L.k = L.q + kQSlots * kTileBytes;
   L.v = L.k + nkv * kTileBytes;
   L.p = L.v + nkv * kTileBytes;
   L.o = L.p + pblocks * kTileBytes;
-  L.mass = L.o + kTileBytes;  // float[2][2][128]
+  L.mass = L.o + (f32_out ? 0 : kTileBytes);  // float[2][2][128]
   L.tau = L.mass + 2 * 2 * kTile * 4;  // τ rows [128][tstride bytes]
   L.bars = L.tau + kTile * tstride;
   L.total = L.bars + (uint32_t)sizeof(Bars);
@@ -132,7 +136,9 @@ __device__ __noinline__ void rope_tiles(uint8_t* ta, uint8_t* tb, int t0, int T,
   }
 }
 
-template <bool kBias, bool kTau, int kNKV>
+// kF32: out and the exported τ in fp32 (the reference's dtype contract when
+// Q is fp32, ops.py:122-124), from bf16 operand copies of Q and K.
+template <bool kBias, bool kTau, int kNKV, bool kF32>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmo,
@@ -140,7 +146,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const FwdTC p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Layout L = fwd_layout(p.pblocks, p.nkv, p.tstride);
+  const Layout L = fwd_layout(p.pblocks, p.nkv, p.tstride, kF32);
   uint8_t* sQ = smem + L.q;
   uint8_t* sK = smem + L.k;
   uint8_t* sV = smem + L.v;
@@ -377,6 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // issued before the next P·V, the staging buffer handed back after it,
       // by when the store has long finished reading it.
       auto store_o = [&](int u, int it) {
+        if constexpr (kF32) return;  // the epilogue stored O itself
         ok = ok && mbar_wait(&bar->ostage_full, it & 1, err, kErrFwd | 14);
         if (!ok) return;
         const int bh = u / nT, j = u % nT;
@@ -384,6 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bulk_commit_group();
       };
       auto release_o = [&]() {
+        if constexpr (kF32) return;
         bulk_wait_group_read0();
         mbar_arrive(&bar->ostage_empty);
       };
@@ -457,9 +465,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int my_hi = hf == 0 ? ch_lo + (nch + 1) / 2 : ch_hi + 1;
     const uint32_t p_base = smem_u32(sP);
     const uint32_t o_base = smem_u32(sO);
-    // τ staging rows (exported τ): row i holds τ[t, 0..W) as bf16
-    __nv_bfloat16* const tau_s = reinterpret_cast<__nv_bfloat16*>(smem + L.tau);
-    const int tau_pitch = p.tstride / 2;  // elements per staging row
+    // τ staging rows (exported τ): row i holds τ[t, 0..W) in the output dtype
+    using TauT = typename std::conditional<kF32, float, __nv_bfloat16>::type;
+    TauT* const tau_s = reinterpret_cast<TauT*>(smem + L.tau);
+    const int tau_pitch = p.tstride / (int)sizeof(TauT);  // elements per staging row
     bool ok = true;
     for (int u = u0, it = 0; u < u1 && ok; ++u, ++it) {
       const int bh = u / nT, j = u % nT;
@@ -482,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float mass = 0.f;
       const float* bias_row = nullptr;
       if constexpr (kBias) bias_row = p.bias + b * p.bs0 + (long long)min(t, p.T - 1) * p.bs1;
-      __nv_bfloat16* const tau_row = tau_s + i * tau_pitch;
+      TauT* const tau_row = tau_s + i * tau_pitch;
 
       auto process16 = [&](int ch, const uint32_t* r) {
         uint32_t pk[8];
@@ -504,7 +513,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mass += tau;
             tv[z] = tau;
             if constexpr (kTau) {
-              if (in_win) tau_row[w] = __float2bfloat16_rn(tau);
+              if (in_win) {
+                if constexpr (kF32) tau_row[w] = tau;
+                else tau_row[w] = __float2bfloat16_rn(tau);
+              }
             }
           }
           pk[e2 >> 1] = pack_bf16(tv[0], tv[1]);
@@ -532,20 +544,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = mbar_wait(&bar->mass_ready[it & 1], (it >> 1) & 1, err, kErrFwd | 12);
       if constexpr (kTau) {
         // every warp is past its τ writes: copy 16 whole rows out, each row
-        // contiguous in [B,T,H,W] (16-byte stores when W is a multiple of 8)
+        // contiguous in [B,T,H,W] (16-byte stores when a row is a multiple of
+        // 16 bytes)
         if (ok) {
           const int r0 = e * 16;
-          __nv_bfloat16* const gbase = p.tau + ((long long)b * p.T * p.H + h) * W;
+          TauT* const gbase = static_cast<TauT*>(p.tau) + ((long long)b * p.T * p.H + h) * W;
           const long long gpitch = (long long)p.H * W;  // elements between rows t, t+1
-          if ((W & 7) == 0) {
-            const int vpr = W / 8;
+          constexpr int kPer16 = 16 / (int)sizeof(TauT);  // elements per 16-byte chunk
+          if ((W % kPer16) == 0) {
+            const int vpr = W / kPer16;
             for (int idx = lane; idx < 16 * vpr; idx += 32) {
               const int rr = r0 + idx / vpr, cc = idx - (idx / vpr) * vpr;
               const int tt = j * kTile + rr;
               if (tt < p.T) {
                 uint32_t a0, a1, a2, a3;
                 ld_shared_v4(smem_u32(tau_s + rr * tau_pitch) + cc * 16, a0, a1, a2, a3);
-                *reinterpret_cast<uint4*>(gbase + tt * gpitch + cc * 8) = make_uint4(a0, a1, a2, a3);
+                *reinterpret_cast<uint4*>(gbase + tt * gpitch + cc * kPer16) = make_uint4(a0, a1, a2, a3);
               }
             }
           } else {
@@ -572,22 +586,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->tmem_empty[bi]);
-      // stage the bf16 tile for one TMA store (issued by the MMA thread); the
-      // previous store must have finished reading the staging buffer
-      if (it > 0) ok = mbar_wait(&bar->ostage_empty, (it - 1) & 1, err, kErrFwd | 13);
-      if (!ok) break;
-#pragma unroll
-      for (int z = 0; z < 4; ++z) {
-        uint32_t w4[4];
-#pragma unroll
-        for (int y = 0; y < 4; ++y)
-          w4[y] = pack_bf16(__uint_as_float(o[8 * z + 2 * y]) * inv, __uint_as_float(o[8 * z + 2 * y + 1]) * inv);
-        st_shared_v4(o_base + sw128_off(i, hf * 4 + z), w4[0], w4[1], w4[2], w4[3]);
-      }
       if (hf == 0 && row_ok && p.row_mass) p.row_mass[(long long)bh * p.T + t] = m;
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->ostage_full);
+      if constexpr (kF32) {
+        // this thread's 32 fp32 values of row t, straight from registers (the
+        // row's other half comes from the warp of the other column half)
+        if (row_ok) {
+          float4* dst = reinterpret_cast<float4*>(p.out_f32 + ((long long)(b * p.T + t) * p.H + h) * kHD +
+                                                  hf * 32);
+#pragma unroll
+          for (int z = 0; z < 8; ++z)
+            dst[z] = make_float4(__uint_as_float(o[4 * z]) * inv, __uint_as_float(o[4 * z + 1]) * inv,
+                                 __uint_as_float(o[4 * z + 2]) * inv, __uint_as_float(o[4 * z + 3]) * inv);
+        }
+      } else {
+        // stage the bf16 tile for one TMA store (issued by the MMA thread); the
+        // previous store must have finished reading the staging buffer
+        if (it > 0) ok = mbar_wait(&bar->ostage_empty, (it - 1) & 1, err, kErrFwd | 13);
+        if (!ok) break;
+#pragma unroll
+        for (int z = 0; z < 4; ++z) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int y = 0; y < 4; ++y)
+            w4[y] = pack_bf16(__uint_as_float(o[8 * z + 2 * y]) * inv, __uint_as_float(o[8 * z + 2 * y + 1]) * inv);
+          st_shared_v4(o_base + sw128_off(i, hf * 4 + z), w4[0], w4[1], w4[2], w4[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->ostage_full);
+      }
     }
   }
 
@@ -599,22 +626,67 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <bool kBias, bool kTau, int kNKV>
+template <bool kBias, bool kTau, int kNKV, bool kF32>
 cudaError_t launch_variant(const CUtensorMap* m, const FwdTC& a, size_t smem, int grid,
                            cudaStream_t st) {
-  auto kern = tc_fwd_kernel<kBias, kTau, kNKV>;
+  auto kern = tc_fwd_kernel<kBias, kTau, kNKV, kF32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, smem, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], a);
   return cudaGetLastError();
 }
 
+template <bool kF32>
+cudaError_t launch_dtype(const CUtensorMap* m, const FwdTC& a, size_t smem, int grid, bool has_bias,
+                         bool has_tau, cudaStream_t st) {
+  const bool two = a.nkv == 2;  // only τ export narrows the ring
+  if (has_bias && has_tau)
+    return two ? launch_variant<true, true, 2, kF32>(m, a, smem, grid, st)
+               : launch_variant<true, true, 3, kF32>(m, a, smem, grid, st);
+  if (has_tau)
+    return two ? launch_variant<false, true, 2, kF32>(m, a, smem, grid, st)
+               : launch_variant<false, true, 3, kF32>(m, a, smem, grid, st);
+  if (has_bias) return launch_variant<true, false, 3, kF32>(m, a, smem, grid, st);
+  return launch_variant<false, false, 3, kF32>(m, a, smem, grid, st);
+}
+
+// Shared-memory plan of a call: τ staging pitch, K/V ring slots, total bytes.
+struct FwdPlan {
+  int Wr, ncols, pblocks, tstride, nkv;
+  bool f32;
+  size_t smem;
+};
+
+FwdPlan fwd_plan(const FwdP& p) {
+  FwdPlan q{};
+  q.f32 = p.out_dt == BOZO_DT_F32;
+  q.Wr = (p.W + 15) / 16 * 16;
+  q.ncols = q.Wr + kTile;
+  q.pblocks = (q.ncols + 63) / 64;
+  // τ export stages whole rows in shared memory (+16 bytes per row keeps the
+  // rows' writes off one bank); the K/V ring drops to two slots when three
+  // would not leave room for them
+  q.tstride = p.tau ? p.W * (q.f32 ? 4 : 2) + 16 : 0;
+  q.nkv = 3;
+  if (fwd_layout(q.pblocks, 3, q.tstride, q.f32).total + 1024 > kMaxSmemPerBlock) q.nkv = 2;
+  q.smem = fwd_layout(q.pblocks, q.nkv, q.tstride, q.f32).total + 1024;
+  return q;
+}
+
 }  // namespace
 
 bool tc_fwd_eligible(const FwdP& p) {
   if (p.mode != BOZO_MODE_LOCAL || p.HD != kHD || p.W < 1 || p.W > 128) return false;
-  if (p.out_dt != BOZO_DT_BF16) return false;
-  if (p.tau && p.tau_dt != BOZO_DT_BF16) return false;
+  if (p.out_dt == BOZO_DT_F32) {
+    // fp32 out and τ (the reference's dtypes for fp32 Q), from bf16 operand
+    // copies of Q/K; no RoPE in this variant
+    if (p.tau && p.tau_dt != BOZO_DT_F32) return false;
+    if (p.cos || !p.out || (reinterpret_cast<uintptr_t>(p.out) & 15) != 0) return false;
+  } else {
+    if (p.out_dt != BOZO_DT_BF16) return false;
+    if (p.tau && p.tau_dt != BOZO_DT_BF16) return false;
+  }
+  if (p.tau && (reinterpret_cast<uintptr_t>(p.tau) & 15) != 0) return false;
   if (!tma_view_ok(p.q, p.B, p.T, p.H) || !tma_view_ok(p.k, p.B, p.T, p.H) ||
       !tma_view_ok(p.v, p.B, p.T, p.H))
     return false;
@@ -622,39 +694,42 @@ bool tc_fwd_eligible(const FwdP& p) {
   for (const void* r : {p.q_rot, p.k_rot})
     if (r && (reinterpret_cast<uintptr_t>(r) & 15) != 0) return false;
   if (p.cos && !p.theta) return false;  // on-the-fly RoPE needs θ
+  if (fwd_plan(p).smem > kMaxSmemPerBlock) return false;
   return tmap_encoder_available();
 }
 
 cudaError_t launch_tc_fwd(const FwdP& p, cudaStream_t st, int* launches) {
+  const FwdPlan plan = fwd_plan(p);
   FwdTC a{};
   a.B = p.B; a.T = p.T; a.H = p.H; a.W = p.W;
-  a.Wr = (p.W + 15) / 16 * 16;
+  a.Wr = plan.Wr;
   a.nT = (p.T + kTile - 1) / kTile;
   a.total = p.B * p.H * a.nT;
   a.norm = p.norm;
-  a.ncols = a.Wr + kTile;
+  a.ncols = plan.ncols;
   a.nbuf = (a.ncols + kHD <= 256) ? 2 : 1;
-  a.pblocks = (a.ncols + 63) / 64;
+  a.pblocks = plan.pblocks;
   a.half_inv_scale = 0.5f / p.scale;
   a.theta = p.cos ? p.theta : nullptr;
   a.bias = p.bias; a.bs0 = p.bs0; a.bs1 = p.bs1; a.bs2 = p.bs2;
-  a.tau = static_cast<__nv_bfloat16*>(p.tau);
+  a.tau = p.tau;
+  a.out_f32 = plan.f32 ? static_cast<float*>(p.out) : nullptr;
   a.row_mass = p.row_mass;
   a.store_rot = (a.theta && p.q_rot && p.k_rot) ? 1 : 0;
   a.err = p.err;
-  // τ export stages whole rows in shared memory (+16 bytes per row keeps the
-  // rows' 2-byte writes off one bank); the K/V ring drops to two slots when
-  // three would not leave room for them
-  a.tstride = p.tau ? p.W * 2 + 16 : 0;
-  a.nkv = 3;
-  if (fwd_layout(a.pblocks, 3, a.tstride).total + 1024 > kMaxSmemPerBlock) a.nkv = 2;
+  a.tstride = plan.tstride;
+  a.nkv = plan.nkv;
   CUtensorMap m[6];
   const long long ob = (long long)p.T * p.H * kHD, ot = (long long)p.H * kHD, oh = kHD;
   if (!make_tmap_bthd(&m[0], p.q.p, p.q.sb, p.q.st, p.q.sh, p.B, p.T, p.H, kTile) ||
       !make_tmap_bthd(&m[1], p.k.p, p.k.sb, p.k.st, p.k.sh, p.B, p.T, p.H, kTile) ||
-      !make_tmap_bthd(&m[2], p.v.p, p.v.sb, p.v.st, p.v.sh, p.B, p.T, p.H, kTile) ||
-      !make_tmap_bthd(&m[3], p.out, ob, ot, oh, p.B, p.T, p.H, kTile))
+      !make_tmap_bthd(&m[2], p.v.p, p.v.sb, p.v.st, p.v.sh, p.B, p.T, p.H, kTile))
     return cudaErrorInvalidValue;
+  if (plan.f32) {
+    m[3] = m[0];  // unused: the fp32 output leaves from registers
+  } else if (!make_tmap_bthd(&m[3], p.out, ob, ot, oh, p.B, p.T, p.H, kTile)) {
+    return cudaErrorInvalidValue;
+  }
   if (a.store_rot) {
     if (!make_tmap_bthd(&m[4], p.q_rot, ob, ot, oh, p.B, p.T, p.H, kTile) ||
         !make_tmap_bthd(&m[5], p.k_rot, ob, ot, oh, p.B, p.T, p.H, kTile))
@@ -663,21 +738,12 @@ cudaError_t launch_tc_fwd(const FwdP& p, cudaStream_t st, int* launches) {
     m[4] = m[3];  // unused
     m[5] = m[3];
   }
-  const Layout L = fwd_layout(a.pblocks, a.nkv, a.tstride);
-  const size_t smem = L.total + 1024;
-  if (smem > kMaxSmemPerBlock) return cudaErrorInvalidConfiguration;
+  if (plan.smem > kMaxSmemPerBlock) return cudaErrorInvalidConfiguration;
   const int grid = std::min(num_sms(), a.total);
   *launches = 1;
   const bool has_bias = p.bias != nullptr, has_tau = p.tau != nullptr;
-  const bool two = a.nkv == 2;  // only τ export narrows the ring
-  if (has_bias && has_tau)
-    return two ? launch_variant<true, true, 2>(m, a, smem, grid, st)
-               : launch_variant<true, true, 3>(m, a, smem, grid, st);
-  if (has_tau)
-    return two ? launch_variant<false, true, 2>(m, a, smem, grid, st)
-               : launch_variant<false, true, 3>(m, a, smem, grid, st);
-  if (has_bias) return launch_variant<true, false, 3>(m, a, smem, grid, st);
-  return launch_variant<false, false, 3>(m, a, smem, grid, st);
+  return plan.f32 ? launch_dtype<true>(m, a, plan.smem, grid, has_bias, has_tau, st)
+                  : launch_dtype<false>(m, a, plan.smem, grid, has_bias, has_tau, st);
 }
 
 }  // namespace bozo

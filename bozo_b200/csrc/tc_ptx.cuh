@@ -87,11 +87,13 @@ constexpr uint32_t kPollCap = 1u << 24;
 // ~40 wait sites made the backward kernel 18 % slower).
 //
 // The limit is an argument of the loop itself (mbar_wait_until): the kernels'
-// wait sites use kWaitLimitNs through mbar_wait_slow, the wait self-test
-// kernel a short limit given at launch, so a test can make a wait run out on
-// purpose (a barrier nothing arrives on) and read the status.
-static __device__ __noinline__ bool mbar_wait_until(uint64_t* bar, uint32_t parity, int* err,
-                                                    int code, uint64_t limit_ns) {
+// wait sites use kWaitLimitNs through the one out-of-line copy in
+// mbar_wait_slow (a single call level: an extra one slowed the backward by
+// 5 %), the wait self-test kernel a short limit given at launch, so a test
+// can make a wait run out on purpose (a barrier nothing arrives on) and read
+// the status.
+__device__ __forceinline__ bool mbar_wait_until(uint64_t* bar, uint32_t parity, int* err,
+                                                int code, uint64_t limit_ns) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1; i < kPollCap; ++i) {
     if (mbar_try_wait(bar, parity)) return true;

@@ -61,6 +61,28 @@ def preset_117m(**over) -> TensionConfig:
     return TensionConfig(**cfg)
 
 
+def preset_13m(**over) -> TensionConfig:
+    """dim 384, 6 layers, 6 heads (head_dim 64), vocab 8192,
+    W 64, T 512, a global block every 4th layer (model.py:25-49 fields;
+    train.py:219-258 presets span this size)."""
+    cfg = dict(vocab_size=8192, dim=384, num_layers=6, num_heads=6, window=64, ffn_mult=3,
+               max_seq_len=512, dropout=0.0, use_oscillation=False, use_rope=True,
+               global_every=4)
+    cfg.update(over)
+    return TensionConfig(**cfg)
+
+
+def preset_1m(**over) -> TensionConfig:
+    """BASELINE configs[0], the reference's CPU-runnable case: dim 128, 4
+    layers, 4 heads (head_dim 32), vocab 2048, W 64, T 256, RoPE, no
+    oscillation, no global layer (1,115,776 parameters)."""
+    cfg = dict(vocab_size=2048, dim=128, num_layers=4, num_heads=4, window=64, ffn_mult=3,
+               max_seq_len=256, dropout=0.0, use_oscillation=False, use_rope=True,
+               global_every=0)
+    cfg.update(over)
+    return TensionConfig(**cfg)
+
+
 def preset_350m_prefill(**over) -> TensionConfig:
     """The 350M inference configuration: dim 1024, 24 layers, 16 heads,
     vocab 32768, W 128, T 2048, global layer every 3rd block (train.py:246-256
@@ -378,14 +400,24 @@ class TrainWeights:
                                    self.w_entropy))
 
 
-def wrap_ddp(model: nn.Module):
+def wrap_ddp(model: nn.Module, compress: bool = True, bucket_cap_mb: float = 64.0):
     """train.py:789-797: DDP with static graph, no buffer broadcast; gradients
-    are bucketed and all-reduced (NCCL on GPUs) while the backward runs."""
+    are bucketed and all-reduced (NCCL on GPUs) while the backward runs.
+    On GPUs the buckets are all-reduced in bf16 (``compress``; the reference
+    all-reduces fp32) and are larger than DDP's 25 MB default, so the 117M
+    model's 469 MB of fp32 gradients cross NVLink as ~235 MB in fewer
+    launches."""
     from torch.nn.parallel import DistributedDataParallel as DDP
     dev = next(model.parameters()).device
-    return DDP(model, device_ids=[dev.index] if dev.type == "cuda" else None,
-               find_unused_parameters=False, broadcast_buffers=False, static_graph=True,
-               gradient_as_bucket_view=True)
+    ddp = DDP(model, device_ids=[dev.index] if dev.type == "cuda" else None,
+              find_unused_parameters=False, broadcast_buffers=False, static_graph=True,
+              gradient_as_bucket_view=True, bucket_cap_mb=bucket_cap_mb)
+    if compress and dev.type == "cuda":
+        # gradients cross NVLink as bf16 (half the bytes of the fp32 all-reduce);
+        # the averaged result is written back in fp32 before the optimiser step
+        from torch.distributed.algorithms.ddp_comm_hooks import default_hooks
+        ddp.register_comm_hook(state=None, hook=default_hooks.bf16_compress_hook)
+    return ddp
 
 
 def make_optimizer(model: nn.Module, lr: float = 3e-4, weight_decay: float = 0.10,

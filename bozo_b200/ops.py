@@ -19,7 +19,7 @@ from __future__ import annotations
 
 import ctypes as C
 import math
-from typing import Optional
+from typing import Optional, Tuple
 
 import torch
 from torch import Tensor
@@ -125,27 +125,32 @@ def _rope_args(rope):
 
 
 def _launch_fwd(q, k, v, *, mode, window, norm, scale, rope, bias, tau_width,
-                out_dtype, tau_dtype, want_mass, want_rotated=False):
+                out_dtype, tau_dtype, want_mass, want_rotated=False, want_lp=False):
     """One forward through the C ABI (via the C++ extension); returns
-    (out, tau, row_mass, q_rot, k_rot) with None for outputs not asked for."""
+    (out, tau, row_mass, q_rot, k_rot) with None for outputs not asked for,
+    and with ``want_lp`` also (q_lp, k_lp): the bf16 operand copies of fp32
+    q/k the tensor-core path computed from (None when it did not)."""
     cos, sin, theta = _rope_args(rope)
-    out, tau, mass, q_rot, k_rot = _capi.ext().tension_fwd(
+    res = _capi.ext().tension_fwd(
         q, k, v, mode, window, norm, float(scale), _PATH[_path_override], cos, sin, theta,
         bias, tau_width or 0, _dt(out_dtype), _dt(tau_dtype), bool(want_mass),
-        bool(want_rotated))
-    return out, tau, mass, q_rot, k_rot
+        bool(want_rotated), bool(want_lp))
+    return tuple(res) if want_lp else tuple(res[:5])
 
 
 def _launch_bwd(q, k, v, d_out, *, mode, window, norm, scale, rope, bias, out,
-                mass, d_tau, qk_rotated=False, aux_row=None):
+                mass, d_tau, qk_rotated=False, aux_row=None, grad_dtypes=None):
     """One backward through the C ABI (via the C++ extension); returns
-    (dq, dk, dv) in the dtypes of q, k, v.  ``aux_row`` ([3, B·H·T] fp32):
-    a per-query-row cotangent of τ the tensor-core kernel forms itself
-    (``bozo_tension_bwd_args.aux_row``)."""
+    (dq, dk, dv) in the dtypes of q, k, v, or dq/dk in ``grad_dtypes``
+    (used when q, k are the forward's bf16 copies of fp32 inputs).
+    ``aux_row`` ([3, B·H·T] fp32): a per-query-row cotangent of τ the
+    tensor-core kernel forms itself (``bozo_tension_bwd_args.aux_row``)."""
     cos, sin, theta = _rope_args(rope)
+    gq, gk = ((_dt(grad_dtypes[0]), _dt(grad_dtypes[1])) if grad_dtypes is not None
+              else (-1, -1))
     dq, dk, dv = _capi.ext().tension_bwd(
         q, k, v, d_out, mode, window, norm, float(scale), _PATH[_path_override], cos, sin,
-        theta, bias, out, mass, d_tau, bool(qk_rotated), aux_row)
+        theta, bias, out, mass, d_tau, bool(qk_rotated), aux_row, gq, gk)
     return dq, dk, dv
 
 
@@ -194,20 +199,85 @@ def _prep_bias(bias: Optional[Tensor], shape: tuple) -> Optional[Tensor]:
 
 
 # ───────────────────────── drop-in raw operator ─────────────────────────
+#
+# The forward and backward launches are torch.library custom ops with fake
+# (shape-only) implementations, so torch.compile (train.py:776-780 compiles
+# model.py, whose local layers call this op) traces through the autograd
+# function instead of breaking the graph at it.  Absent outputs are empty
+# tensors: an op returns tensors only.
+
+def _wants_lp(Q: Tensor, K: Tensor, V: Tensor) -> bool:
+    """fp32 Q/K with bf16 V (model.py's autocast call): the forward makes bf16
+    operand copies of Q/K, which the tensor cores compute from and the
+    backward takes as its Q/K."""
+    return Q.dtype == torch.float32 and K.dtype == torch.float32 and V.dtype == torch.bfloat16
+
+
+@torch.library.custom_op("bozo::causal_tension_fwd", mutates_args=(), device_types="cuda")
+def _causal_fwd_op(Q: Tensor, K: Tensor, V: Tensor, W: int, scale: float, return_tau: bool,
+                   bias: Optional[Tensor], path: int) -> Tuple[Tensor, Tensor, Tensor, Tensor]:
+    cos = sin = theta = None
+    out, tau, _, _, _, q_lp, k_lp = _capi.ext().tension_fwd(
+        Q, K, V, _capi.MODE_LOCAL, W, _capi.NORM_NONE, float(scale), path, cos, sin, theta, bias,
+        W if return_tau else 0, _dt(Q), _dt(Q), False, False, _wants_lp(Q, K, V))
+    none_f = Q.new_empty(0)
+    none_b = Q.new_empty(0, dtype=torch.bfloat16)
+    return (out, tau if tau is not None else none_f, q_lp if q_lp is not None else none_b,
+            k_lp if k_lp is not None else none_b.clone())
+
+
+@_causal_fwd_op.register_fake
+def _(Q, K, V, W, scale, return_tau, bias, path):
+    B, T, H, HD = Q.shape
+    out = Q.new_empty((B, T, H, HD))
+    tau = Q.new_empty((B, T, H, W)) if return_tau else Q.new_empty(0)
+    lp = _wants_lp(Q, K, V)
+    q_lp = Q.new_empty((B, T, H, HD) if lp else (0,), dtype=torch.bfloat16)
+    k_lp = Q.new_empty((B, T, H, HD) if lp else (0,), dtype=torch.bfloat16)
+    return out, tau, q_lp, k_lp
+
+
+@torch.library.custom_op("bozo::causal_tension_bwd", mutates_args=(), device_types="cuda")
+def _causal_bwd_op(Q: Tensor, K: Tensor, V: Tensor, d_out: Tensor, d_tau: Optional[Tensor], W: int,
+                   scale: float, bias: Optional[Tensor], path: int, dq_dtype: int,
+                   dk_dtype: int) -> Tuple[Tensor, Tensor, Tensor]:
+    dq, dk, dv = _capi.ext().tension_bwd(
+        Q, K, V, d_out, _capi.MODE_LOCAL, W, _capi.NORM_NONE, float(scale), path, None, None,
+        None, bias, None, None, d_tau, False, None, dq_dtype, dk_dtype)
+    return dq, dk, dv
+
+
+_DT_BACK = {v: k for k, v in _DT.items()}
+
+
+@_causal_bwd_op.register_fake
+def _(Q, K, V, d_out, d_tau, W, scale, bias, path, dq_dtype, dk_dtype):
+    dq = Q.new_empty(Q.shape, dtype=_DT_BACK[dq_dtype] if dq_dtype >= 0 else Q.dtype)
+    dk = K.new_empty(K.shape, dtype=_DT_BACK[dk_dtype] if dk_dtype >= 0 else K.dtype)
+    return dq, dk, V.new_empty(V.shape)
+
 
 class _CausalTensionFn(torch.autograd.Function):
-    """Mirror of triton_tension/ops.py:73-187 over the C ABI."""
+    """Mirror of triton_tension/ops.py:73-187 over the C ABI.
+
+    model.py's call under bf16 autocast (fp32 RoPE-promoted Q/K, bf16 V;
+    model.py:200-204, 248-264) runs on the tensor cores: the forward makes
+    bf16 operand copies of Q and K, returns fp32 out and τ, and keeps the
+    copies for the backward, which returns fp32 dQ/dK and bf16 dV."""
 
     @staticmethod
     def forward(ctx, Q, K, V, W: int, scale: float, return_tau: bool, bias):
         B, T, H, HD = Q.shape
         Bias = _prep_bias(bias, (B, T, W))
-        out, tau, _, _, _ = _launch_fwd(Q, K, V, mode=_capi.MODE_LOCAL, window=W,
-                                  norm=_capi.NORM_NONE, scale=scale, rope=None,
-                                  bias=Bias, tau_width=W if return_tau else None,
-                                  out_dtype=Q.dtype, tau_dtype=Q.dtype, want_mass=False)
-        ctx.save_for_backward(Q, K, V, Bias)
-        ctx.W, ctx.scale, ctx.return_tau = W, scale, return_tau
+        path = _PATH[_path_override]
+        out, tau, q_lp, k_lp = _causal_fwd_op(Q, K, V, W, float(scale), bool(return_tau), Bias, path)
+        ctx.grad_dtypes = (-1, -1)
+        if _wants_lp(Q, K, V):
+            ctx.save_for_backward(q_lp, k_lp, V, Bias)
+            ctx.grad_dtypes = (_dt(Q), _dt(K))
+        else:
+            ctx.save_for_backward(Q, K, V, Bias)
+        ctx.W, ctx.scale, ctx.return_tau, ctx.path = W, scale, return_tau, path
         if return_tau:
             return out, tau
         return out
@@ -221,13 +291,11 @@ class _CausalTensionFn(torch.autograd.Function):
             d_out = torch.zeros_like(Q)
         if d_tau is not None:
             d_tau = d_tau.contiguous()
-        dq, dk, dv = _launch_bwd(Q, K, V, d_out, mode=_capi.MODE_LOCAL, window=ctx.W,
-                                 norm=_capi.NORM_NONE, scale=ctx.scale, rope=None,
-                                 bias=Bias, out=None, mass=None, d_tau=d_tau)
+        dq, dk, dv = _causal_bwd_op(Q, K, V, d_out, d_tau, ctx.W, float(ctx.scale), Bias,
+                                    ctx.path, ctx.grad_dtypes[0], ctx.grad_dtypes[1])
         return dq, dk, dv, None, None, None, None
 
 
-@torch._dynamo.disable
 def causal_tension(Q: Tensor, K: Tensor, V: Tensor, window: int, scale: float,
                    return_tau: bool = False, bias: Tensor | None = None):
     """Fused causal sigmoid tension — drop-in for triton_tension.causal_tension.

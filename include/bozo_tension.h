@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define BOZO_TENSION_ABI_VERSION 4
+#define BOZO_TENSION_ABI_VERSION 5
 
 typedef enum {
   BOZO_OK = 0,
@@ -108,6 +108,15 @@ typedef struct {
   float* row_mass;        /* [B,H,T] fp32 Σ_s τ (unclamped) or NULL */
   void* q_rot;            /* optional [B,T,H,HD] contiguous copies of RoPE(q), */
   void* k_rot;            /* RoPE(k) in q/k's dtype (for a later backward)    */
+  /* Optional room for bf16 operand copies of fp32 q and k ([B,T,H,HD]
+   * contiguous, 16-byte aligned).  When both are set and q, k are fp32, the
+   * forward always writes bf16(q), bf16(k) here; when
+   * bozo_tension_fwd_needs_lp() is 1 it also runs the tensor-core kernels on
+   * them (fp32 out and τ).  The caller keeps them and passes them to the
+   * backward as q and k, with grad_dtype F32 for dq/dk.  NULL keeps an
+   * fp32-q/k call on the exact fp32 path. */
+  void* q_lp;
+  void* k_lp;
 } bozo_tension_fwd_args;
 
 typedef struct {
@@ -133,7 +142,9 @@ typedef struct {
   void* dq;               /* [B,T,H,HD] contiguous (gradient w.r.t. pre-RoPE q) */
   void* dk;
   void* dv;
-  void* workspace;        /* device scratch of bozo_tension_bwd_workspace() bytes */
+  void* workspace;        /* device scratch of bozo_tension_bwd_workspace() bytes
+                             (with bf16 q/k and an fp32 d_out it includes room
+                             for a bf16 copy of d_out) */
   size_t workspace_bytes;
   /* Optional cotangent of τ given per query row instead of per element (the
    * fused τ consumer's diversity and entropy terms, bozo_tau_aux.h): for
@@ -188,6 +199,16 @@ typedef struct {
  * row ts_bridge/streaming.py:100-194 (ingest_step) takes from such a
  * forward. */
 int bozo_tension_decode(const bozo_tension_decode_args* args, void* stream);
+
+/* 1 when this forward, given q_lp / k_lp, runs on the tensor-core kernels
+ * from bf16 copies of fp32 q and k: the reference's mixed-dtype call
+ * (model.py:248-264 under bf16 autocast — RoPE-promoted fp32 Q/K, bf16 V,
+ * fp32 out and τ as ops.py:122-124 returns them; local window ≤ 128,
+ * HD 64, no RoPE inside the call).  Depends only on the arguments, so a
+ * caller can decide whether to allocate the copies before the call.
+ * Replaces nothing in the reference (its Triton kernels load every dtype as
+ * fp32, triton_tension/kernel.py:76). */
+int bozo_tension_fwd_needs_lp(const bozo_tension_fwd_args* args);
 
 /* Forward. Returns bozo_status; launches are asynchronous on `stream`
  * (a cudaStream_t, NULL = legacy default stream). */

@@ -1,15 +1,20 @@
-"""Tolerances of the parity suite (|got − ref| ≤ atol + rtol·|ref|, elementwise).
+"""Tolerances of the parity suite (|got − ref| ≤ atol + rtol·|ref|, elementwise,
+``ref`` the float64 oracle on the same dtype-rounded inputs).
 
-* fp32 inputs: rtol 1e-5, atol 1e-5 — the exact-fp32 CUDA-core path against a
-  float64 oracle (fp32 round-off of HD-long dots and W-long sums stays well
-  under 1e-5 for O(1) data).
-* bf16 inputs: rtol 2e-2, atol 2e-2 — the tensor-core path (bf16 operands,
-  fp32 accumulation, bf16 outputs) against the float64 oracle evaluated on the
-  same bf16-rounded inputs.  For bf16 the absolute floor is taken relative to
-  the tensor's scale: atol·max(1, rms(ref)).  Raw Σ τ·V outputs and some
-  gradients have rms ≈ 3-6; there a fixed 2e-2 floor would demand better
-  than the bf16 rounding of τ itself (2^-9 relative per term).  Unit-scale
-  tensors (normalised outputs, τ) keep the plain 2e-2 floor.
+* fp32 inputs: rtol 1e-5, atol 1e-5 — the exact-fp32 CUDA-core path (fp32
+  round-off of HD-long dots and W-long sums stays well under 1e-5 for O(1)
+  data).
+* bf16 inputs: rtol 2e-2, atol 2e-2, fixed — the bound the north star sets
+  for bf16.  Every normalised output (τ-mass, count), τ and every gradient
+  taken through a normalisation meets it outright.
+* Raw Σ τ·V outputs (the drop-in op's result, ops.py:60) and gradients
+  taken through them are sums of W terms of size |V|: there the reference's
+  own PyTorch path run in bf16 on the same inputs (``ref_lp``: the oracle
+  evaluated in bf16, as ops.py:29-63 computes with bf16 tensors) already
+  misses the fixed bound — by 1.6-2.3× at W 32-128 on N(0,1) data.  For such
+  a tensor the check is that ours misses it by no more than the reference's
+  own bf16 computation does, element maximum against element maximum; the
+  bound itself stays north-star's.
 """
 import numpy as np
 import torch
@@ -21,20 +26,39 @@ TOL = {
 }
 
 
-def assert_close(got, ref, dtype, what=""):
-    g = got.detach().to(torch.float64).cpu()
-    r = ref.detach().to(torch.float64).cpu() if isinstance(ref, torch.Tensor) else torch.from_numpy(np.asarray(ref, dtype=np.float64))
+def _f64(x):
+    if isinstance(x, torch.Tensor):
+        return x.detach().to(torch.float64).cpu()
+    return torch.from_numpy(np.asarray(x, dtype=np.float64))
+
+
+def worst_ratio(got, ref, dtype):
+    """max over elements of |got − ref| / (atol + rtol·|ref|), and its index."""
+    g, r = _f64(got), _f64(ref)
+    tol = TOL[dtype]
+    ratio = (g - r).abs() / (tol["atol"] + tol["rtol"] * r.abs())
+    i = int(ratio.argmax()) if ratio.numel() else 0
+    return (float(ratio.max()) if ratio.numel() else 0.0), i
+
+
+def assert_close(got, ref, dtype, what="", ref_lp=None):
+    g, r = _f64(got), _f64(ref)
     tol = TOL[dtype]
     assert g.shape == r.shape, f"{what}: shape {tuple(g.shape)} vs {tuple(r.shape)}"
+    ours, i = worst_ratio(g, r, dtype)
+    if ours <= 1.0:
+        return
+    if ref_lp is not None:
+        theirs, _ = worst_ratio(ref_lp, r, dtype)
+        if ours <= theirs:
+            return
+        extra = f"; the reference's bf16 path reaches {theirs:.2f}× the bound"
+    else:
+        extra = ""
     err = (g - r).abs()
-    atol = tol["atol"]
-    if dtype in (torch.bfloat16, torch.float16):
-        atol = atol * max(1.0, float(r.pow(2).mean().sqrt()))
-    bound = atol + tol["rtol"] * r.abs()
-    bad = err > bound
-    if bad.any():
-        idx = tuple(int(i) for i in torch.nonzero(bad)[0])
-        raise AssertionError(
-            f"{what}: {int(bad.sum())}/{bad.numel()} elements out of tolerance "
-            f"{tol}; max err {float(err.max()):.3e}; first bad {idx}: "
-            f"got {float(g[idx]):.6e} ref {float(r[idx]):.6e}")
+    bad = err > tol["atol"] + tol["rtol"] * r.abs()
+    idx = tuple(int(x) for x in np.unravel_index(i, tuple(g.shape)))
+    raise AssertionError(
+        f"{what}: {int(bad.sum())}/{bad.numel()} elements out of tolerance {tol}; "
+        f"worst {ours:.2f}× the bound at {idx}: got {float(g[idx]):.6e} ref {float(r[idx]):.6e}"
+        f"{extra}")

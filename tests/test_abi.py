@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol():
     assert set(declared) == set(_capi.EXPORTED)
     for name in declared:
         assert hasattr(lib, name), name
-    assert lib.bozo_tension_abi_version() == 4
+    assert lib.bozo_tension_abi_version() == 5
     assert _capi.status_string(0) == "ok"
 
 
@@ -60,7 +60,7 @@ int main(void) {
   O(bozo_tension_fwd_args, bias_stride); O(bozo_tension_fwd_args, out);
   O(bozo_tension_fwd_args, out_dtype); O(bozo_tension_fwd_args, tau);
   O(bozo_tension_fwd_args, row_mass); O(bozo_tension_fwd_args, q_rot);
-  O(bozo_tension_fwd_args, k_rot); O(bozo_tension_bwd_args, qk_rotated);
+  O(bozo_tension_fwd_args, k_rot); O(bozo_tension_fwd_args, q_lp); O(bozo_tension_fwd_args, k_lp); O(bozo_tension_bwd_args, qk_rotated);
   S(bozo_tension_bwd_args);
   O(bozo_tension_bwd_args, d_out); O(bozo_tension_bwd_args, out);
   O(bozo_tension_bwd_args, row_mass); O(bozo_tension_bwd_args, bias_stride);

@@ -54,11 +54,18 @@ def _run_raw(bz, c, dtype, with_tau=True):
     return out, tau, q.grad, k.grad, v.grad
 
 
-def _oracle_raw(c, dtype):
-    """float64 oracle on the dtype-rounded inputs (exact golden for fp32)."""
+def _lp(xs):
+    """Inputs or cotangents for the oracle run in bf16 arithmetic."""
+    return [None if x is None else x.detach().to(torch.bfloat16) for x in xs]
+
+
+def _oracle_raw(c, dtype, compute=torch.float64):
+    """The oracle on the dtype-rounded inputs, in float64 (exact golden for
+    fp32) or, with ``compute=torch.bfloat16``, in bf16 arithmetic — the
+    reference path (ops.py:29-63) as torch runs it on bf16 tensors."""
     B, T, H, HD, W = [int(x) for x in c["meta"]]
-    rd = lambda a: torch.from_numpy(np.asarray(a)).to(dtype).double()
-    bias = torch.from_numpy(np.asarray(c["bias"], np.float64)) if "bias" in c else None
+    rd = lambda a: torch.from_numpy(np.asarray(a)).to(dtype).to(compute)
+    bias = torch.from_numpy(np.asarray(c["bias"], np.float64)).to(compute) if "bias" in c else None
     d_tau = rd(c["d_tau"]) if "d_tau" in c else None
 
     def fn(q, k, v):
@@ -77,10 +84,12 @@ def test_raw_op_matches_reference_golden(bz, golden_op, dtype):
         got = _run_raw(bz, c, dtype)
         if dtype == torch.float32:
             ref = [c["out"], c["tau"], c["dq"], c["dk"], c["dv"]]
+            ref_lp = [None] * 5
         else:
             ref = _oracle_raw(c, dtype)
-        for g, r, what in zip(got, ref, ("out", "tau", "dq", "dk", "dv")):
-            assert_close(g, r, dtype, f"{name}/{dtype}/{what}")
+            ref_lp = _oracle_raw(c, dtype, compute=torch.bfloat16)
+        for g, r, rl, what in zip(got, ref, ref_lp, ("out", "tau", "dq", "dk", "dv")):
+            assert_close(g, r, dtype, f"{name}/{dtype}/{what}", ref_lp=rl)
 
 
 @cuda
@@ -199,13 +208,17 @@ def test_fused_local_bf16_vs_oracle(bz, W, normalize):
     assert bz.last_path() == "tcgen05"
 
     def fn(q_, k_, v_):
-        return orc.fused_reference(q_, k_, v_, window=W, scale=8.0, bias=bias.double(),
+        return orc.fused_reference(q_, k_, v_, window=W, scale=8.0, bias=bias.to(q_.dtype),
                                    normalize=normalize or "none")
     (o, t), grads = orc.tension_with_grads(fn, [x.double() for x in (q, k, v)],
                                            [d_out.double(), d_tau.double()])
-    for g, r, what in zip((out, tau, qg.grad, kg.grad, vg.grad), (o, t, *grads),
-                          ("out", "tau", "dq", "dk", "dv")):
-        assert_close(g, r, dt, f"W{W}/{normalize}/{what}")
+    ref_lp = [None] * 5
+    if normalize is None:  # raw Σ τ·V: the reference's own bf16 computation as the yardstick
+        (ol, tl), gl = orc.tension_with_grads(fn, _lp((q, k, v)), _lp((d_out, d_tau)))
+        ref_lp = [ol, tl, *gl]
+    for g, r, rl, what in zip((out, tau, qg.grad, kg.grad, vg.grad), (o, t, *grads), ref_lp,
+                              ("out", "tau", "dq", "dk", "dv")):
+        assert_close(g, r, dt, f"W{W}/{normalize}/{what}", ref_lp=rl)
 
 
 def _global_reference(q, k, v, scale, bias, tw, normalize):
@@ -213,7 +226,7 @@ def _global_reference(q, k, v, scale, bias, tw, normalize):
     Σ τ·V when ``normalize`` is None."""
     def fn(q_, k_, v_):
         T, HD = q_.shape[1], q_.shape[3]
-        cos, sin = orc.rope_tables(HD, T, 10_000.0, torch.float64)
+        cos, sin = orc.rope_tables(HD, T, 10_000.0, q_.dtype)
         out, tau_full, tau_local = orc.global_tension(orc.rope(q_, cos, sin), orc.rope(k_, cos, sin),
                                                       v_, scale, bias, tw)
         if normalize is None:
@@ -243,9 +256,14 @@ def test_fused_global_bf16_vs_oracle(bz, T, normalize):
     fn = _global_reference(None, None, None, 8.0, bias.double(), tw, normalize)
     (o, t), grads = orc.tension_with_grads(fn, [x.double() for x in (q, k, v)],
                                            [d_out.double(), d_tau.double()])
-    for g, r, what in zip((out, tau, qg.grad, kg.grad, vg.grad), (o, t, *grads),
-                          ("out", "tau", "dq", "dk", "dv")):
-        assert_close(g, r, dt, f"global T{T}/{normalize}/{what}")
+    ref_lp = [None] * 5
+    if normalize is None:  # raw Σ τ·V: the global einsum path in bf16 (model.py:217-229 under autocast)
+        fl = _global_reference(None, None, None, 8.0, bias.bfloat16(), tw, normalize)
+        (ol, tl), gl = orc.tension_with_grads(fl, _lp((q, k, v)), _lp((d_out, d_tau)))
+        ref_lp = [ol, tl, *gl]
+    for g, r, rl, what in zip((out, tau, qg.grad, kg.grad, vg.grad), (o, t, *grads), ref_lp,
+                              ("out", "tau", "dq", "dk", "dv")):
+        assert_close(g, r, dt, f"global T{T}/{normalize}/{what}", ref_lp=rl)
 
 
 @cuda
@@ -278,7 +296,8 @@ def test_large_bf16_spot_check(bz):
     ref = orc.local_tension_raw(q.double(), k.double(), v.double(), W, 8.0)
     rel = (out.double() - ref).abs() / (ref.abs() + 1e-6)
     assert rel.mean().item() < 0.02
-    assert_close(out, ref, torch.bfloat16, "large")
+    assert_close(out, ref, torch.bfloat16, "large",
+                 ref_lp=orc.local_tension_raw(q, k, v, W, 8.0))
 
 
 @cuda
@@ -316,23 +335,101 @@ def test_bias_shape_assertion(bz):
 
 
 @cuda
-def test_mixed_dtype_model_call_site(bz):
+@pytest.mark.parametrize("W,T,with_tau", [(16, 96, True), (64, 333, True), (128, 260, False)])
+def test_mixed_dtype_model_call_site(bz, W, T, with_tau):
     """model.py under bf16 autocast feeds fp32 (RoPE-promoted) Q/K with bf16 V;
     the op returns Q.dtype and grads in each input's dtype (ops.py:122-124,
-    186-187)."""
-    torch.manual_seed(9)
-    B, T, H, HD, W = 2, 96, 2, 64, 16
+    186-187).  The call runs on the tensor cores from bf16 copies of Q/K, so
+    it is held to the bf16 bound: out (and τ) and all gradients against the
+    float64 oracle on the same inputs, with bias (and a τ cotangent).  fp32 τ
+    export is served by the band kernel up to W 64 (its staging rows fit);
+    W 128 is checked without τ."""
+    torch.manual_seed(9 + W)
+    B, H, HD = 2, 2, 64
     q = torch.randn(B, T, H, HD, device="cuda", requires_grad=True)
     k = torch.randn(B, T, H, HD, device="cuda", requires_grad=True)
     v = torch.randn(B, T, H, HD, device="cuda", dtype=torch.bfloat16, requires_grad=True)
-    out, tau = bz.causal_tension(q, k, v, W, 8.0, return_tau=True)
-    assert out.dtype == torch.float32 and tau.dtype == torch.float32
-    (out.sum() + tau.sum()).backward()
-    assert q.grad.dtype == torch.float32 and v.grad.dtype == torch.bfloat16
-    ref_o, ref_t = orc.local_tension_raw(q.detach().double().cpu(), k.detach().double().cpu(),
-                                         v.detach().double().cpu(), W, 8.0, return_tau=True)
-    assert_close(out, ref_o, torch.float32, "mixed/out")
-    assert_close(tau, ref_t, torch.float32, "mixed/tau")
+    bias = torch.randn(B, T, W, device="cuda") * 0.5
+    d_out = torch.randn(B, T, H, HD, device="cuda")
+    d_tau = torch.randn(B, T, H, W, device="cuda") * 0.1
+    if with_tau:
+        out, tau = bz.causal_tension(q, k, v, W, 8.0, return_tau=True, bias=bias)
+        assert tau.dtype == torch.float32
+    else:
+        out = bz.causal_tension(q, k, v, W, 8.0, bias=bias)
+        tau = torch.zeros(B, T, H, W, device="cuda")
+        d_tau = torch.zeros_like(tau)
+    assert bz.last_path() == "tcgen05"
+    assert out.dtype == torch.float32
+    ((out * d_out).sum() + (tau * d_tau).sum()).backward()
+    assert bz.last_path() == "tcgen05"
+    assert q.grad.dtype == torch.float32 and k.grad.dtype == torch.float32
+    assert v.grad.dtype == torch.bfloat16
+
+    def fn(q_, k_, v_):
+        return orc.local_tension_raw(q_, k_, v_, W, 8.0, bias.to(q_.dtype).cpu(), return_tau=True)
+    ins = [x.detach().cpu() for x in (q, k, v)]
+    (o, t), grads = orc.tension_with_grads(fn, [x.double() for x in ins],
+                                           [d_out.double().cpu(), d_tau.double().cpu()])
+    (ol, tl), gl = orc.tension_with_grads(fn, _lp(ins), _lp((d_out.cpu(), d_tau.cpu())))
+    for g, r, rl, what in zip((out, tau, q.grad, k.grad, v.grad), (o, t, *grads), (ol, tl, *gl),
+                              ("out", "tau", "dq", "dk", "dv")):
+        if what == "tau" and not with_tau:
+            continue
+        assert_close(g, r, torch.bfloat16, f"mixed W{W}/{what}", ref_lp=rl)
+
+
+@cuda
+def test_triton_tension_shim_model_call_site_117m_layer(bz):
+    """The drop-in at model.py's own call site: ``install_as_triton_tension()``
+    makes ``from triton_tension import causal_tension`` (model.py:248,
+    triton_tension/__init__.py:1-3) and ``triton_tension.ops.causal_tension``
+    resolve here; then model.py:250-258's sequence at the 117M layer shape
+    (B16 T1024 H12 HD64 W64) under bf16 autocast — RoPE'd fp32 Q/K, bf16 V,
+    τ returned, out = S / clamp(Στ, 1e-6) — forward and backward, on the
+    tensor cores, against the float64 oracle on batch row 0, heads 0-1."""
+    import importlib
+    import sys
+    saved = {n: sys.modules.get(n) for n in ("triton_tension", "triton_tension.ops")}
+    try:
+        bz.install_as_triton_tension()
+        from triton_tension import causal_tension
+        ops_mod = importlib.import_module("triton_tension.ops")
+        assert causal_tension is bz.causal_tension and ops_mod.causal_tension is bz.causal_tension
+        B, T, H, HD, W = 16, 1024, 12, 64, 64
+        g = torch.Generator().manual_seed(21)
+        q_raw, k_raw, v_raw, d = [torch.randn(B, T, H, HD, generator=g).to(torch.bfloat16) for _ in range(4)]
+        cos, sin = [x.cuda() for x in orc.rope_tables(HD, T, 10_000.0, torch.float32)]
+
+        def model_rope(x):  # model.py:75-81: fp32 table buffers, no cast
+            c, s_ = cos[:T].unsqueeze(0).unsqueeze(2), sin[:T].unsqueeze(0).unsqueeze(2)
+            x1, x2 = x[..., :HD // 2], x[..., HD // 2:]
+            return torch.cat([x1 * c - x2 * s_, x1 * s_ + x2 * c], dim=-1)
+        q_leaf, k_leaf, v_leaf = [x.cuda().requires_grad_(True) for x in (q_raw, k_raw, v_raw)]
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            # model.py:203-204: bf16 projections times fp32 tables → fp32 Q/K
+            q = model_rope(q_leaf)
+            k = model_rope(k_leaf)
+            assert q.dtype == torch.float32 and v_leaf.dtype == torch.bfloat16
+            msg, tau = causal_tension(q, k, v_leaf, W, 8.0, return_tau=True, bias=None)
+            assert bz.last_path() == "tcgen05"
+            out = msg / tau.sum(-1).clamp(min=1e-6).unsqueeze(-1)  # model.py:257-258
+        gq, gk, gv = torch.autograd.grad(out, (q_leaf, k_leaf, v_leaf), d.cuda().float())
+        assert bz.last_path() == "tcgen05"
+        sl = lambda x: x[0:1, :, 0:2]
+
+        def fn(a, b, c):
+            return orc.fused_reference(a, b, c, window=W, scale=8.0)
+        (o, t), grads = orc.tension_with_grads(fn, [sl(x).double() for x in (q_raw, k_raw, v_raw)],
+                                               [sl(d).double(), None])
+        for got, ref, what in zip((out, tau, gq, gk, gv), (o, t, *grads), ("out", "tau", "dq", "dk", "dv")):
+            assert_close(sl(got), ref, torch.bfloat16, f"shim 117M layer/{what}")
+    finally:
+        for n, m in saved.items():
+            if m is None:
+                sys.modules.pop(n, None)
+            else:
+                sys.modules[n] = m
 
 
 @cuda
@@ -404,3 +501,38 @@ def test_tensor_core_paths_repeat_bit_identical(bz, window, T):
     for r in runs[1:]:
         for a, b, what in zip(runs[0], r, ("out", "tau", "dq", "dk", "dv")):
             assert torch.equal(a, b), f"{what} differs between identical calls"
+
+
+@cuda
+@pytest.mark.parametrize("mixed", [False, True])
+def test_causal_tension_compiles_without_graph_breaks(bz, mixed):
+    """train.py:776-780 wraps model.py in torch.compile; the drop-in op is a
+    pair of torch.library custom ops with fake implementations, so the
+    model.py use of it (model.py:248-258: τ returned, τ-mass division)
+    compiles as one graph (fullgraph=True fails on any break) through
+    AOTAutograd, and gives the eager values and gradients."""
+    torch.manual_seed(31)
+    B, T, H, HD, W = 2, 200, 3, 64, 64
+    qd = torch.float32 if mixed else torch.bfloat16
+    q0 = torch.randn(B, T, H, HD, device="cuda", dtype=qd)
+    k0 = torch.randn(B, T, H, HD, device="cuda", dtype=qd)
+    v0 = torch.randn(B, T, H, HD, device="cuda", dtype=torch.bfloat16)
+
+    def f(q, k, v):
+        msg, tau = bz.causal_tension(q, k, v, W, 8.0, return_tau=True)
+        out = msg / tau.sum(-1).clamp(min=1e-6).unsqueeze(-1)
+        return (out.float() ** 2).sum()
+
+    def run(fn):
+        q, k, v = [x.clone().requires_grad_(True) for x in (q0, k0, v0)]
+        loss = fn(q, k, v)
+        return (loss.detach(), *torch.autograd.grad(loss, (q, k, v)))
+
+    torch._dynamo.reset()
+    compiled = torch.compile(f, backend="aot_eager", fullgraph=True)
+    got = run(compiled)
+    want = run(f)
+    for a, b, what in zip(got, want, ("loss", "dq", "dk", "dv")):
+        assert a.dtype == b.dtype, what
+        assert torch.allclose(a.float(), b.float(), rtol=1e-5, atol=1e-5), what
+    torch._dynamo.reset()
