@@ -77,7 +77,6 @@ struct __align__(8) Bars {
   uint64_t sdp_full[2], sdp_free[2], p_full[2], p_free[2];
   uint64_t acc_full, dkv_free, dq_free[2];
   uint64_t aux_staged, aux_stored;
-  uint64_t drain[2];  // exit commits of the two MMA-issuing threads
   uint32_t tmem_base;
 };
 
@@ -322,8 +321,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bar->aux_stored, 1);
     mbar_init(&bar->acc_full, 1);
     mbar_init(&bar->dkv_free, 4);
-    mbar_init(&bar->drain[0], 1);
-    mbar_init(&bar->drain[1], 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -373,8 +370,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         load_key(st.bh, st.i);
         if (st.has_c1) load_query(st.bh, st.i + 1);
       }
-      drain_loads(bar->kv_full, 2, nk, err, kErrBwd | 40);
-      drain_loads(bar->q_full, 2, nq, err, kErrBwd | 41);
     }
   } else if (warp == 1 || warp == 14) {
     // ──────────── MMA issuers: warp 1 Sᵀ/dPᵀ, warp 14 consumers ────────────
@@ -464,7 +459,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_consumers(s);
         }
       }
-      drain_mma(&bar->drain[warp == 1 ? 0 : 1], err, kErrBwd | 42);
     }
   } else if (warp < 4 || warp == 12 || warp == 13) {
     // ──────── output warps: dQ/dK/dV of each key tile ────────

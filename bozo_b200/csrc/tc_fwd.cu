@@ -72,7 +72,6 @@ struct __align__(8) Bars {
   uint64_t mass_ready[2];  // the 8 epilogue warps have published their τ-mass halves
   uint64_t ostage_full, ostage_empty;
   uint64_t tau_free;  // every epilogue warp has copied its τ rows out
-  uint64_t drain;     // the MMA thread's exit commit
   uint32_t tmem_base;
 };
 
@@ -185,7 +184,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bar->ostage_full, 8);
     mbar_init(&bar->ostage_empty, 1);
     mbar_init(&bar->tau_free, 8);
-    mbar_init(&bar->drain, 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -213,7 +211,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&tmkr);
       }
       int n = 0, n_cur = 0;
-      int nq_issued = 0, nk_issued = 0, nv_issued = 0;  // loads in flight at exit
       bool ok = true, pending_stores = false;
       // rotated tiles are stored from the ring slots: a slot is refilled only
       // after every store issued so far has finished reading shared memory
@@ -232,13 +229,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         before_refill();
         mbar_arrive_expect_tx(&bar->k_full[s], kTileBytes);
         tma_load_4d(sK + s * kTileBytes, &tmk, &bar->k_full[s], 0, h, jj * kTile, b);
-        ++nk_issued;
         if (n >= NKV)
           ok = ok && mbar_wait(&bar->v_empty[s], ((n / NKV) - 1) & 1, err, kErrFwd | 17);
         if (!ok) return;
         mbar_arrive_expect_tx(&bar->v_full[s], kTileBytes);
         tma_load_4d(sV + s * kTileBytes, &tmv, &bar->v_full[s], 0, h, jj * kTile, b);
-        ++nv_issued;
         ++n;
       };
       // store RoPE(Q), RoPE(K) of tile (bh, j) once the rotators are done
@@ -262,7 +257,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         before_refill();
         mbar_arrive_expect_tx(&bar->q_full[qs], kTileBytes);
         tma_load_4d(sQ + qs * kTileBytes, &tmq, &bar->q_full[qs], 0, bh % p.H, j * kTile, bh / p.H);
-        ++nq_issued;
         if (j >= 1 && u == u0) load_key(bh, j - 1);
         n_cur = n;
         load_key(bh, j);
@@ -271,14 +265,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (ok && p.store_rot && u1 > u0) store_rot(u1 - u0 - 1, prev_bh, prev_j, prev_n);
       if (pending_stores) bulk_wait_group0();
-      drain_loads(bar->q_full, kQSlots, nq_issued, err, kErrFwd | 22);
-      drain_loads(bar->k_full, NKV, nk_issued, err, kErrFwd | 23);
-      drain_loads(bar->v_full, NKV, nv_issued, err, kErrFwd | 24);
     }
   } else if (warp == 1) {
     // ─────────────── MMA issuer ───────────────
-    // With two TMEM buffers (nbuf 2) the QKᵀ of tile it+1 is issued before
-    // the P·V of tile it, so the epilogue finds S ready as soon as it is done
+    // The order note: P·V of tile it is issued as soon as its P is complete,
+    // the QKᵀ of tile it+1 right after it.  QKᵀ(it+1) waits for the RoPE
+    // warps to rotate tile it+1; issued first, it held P·V(it) back behind
+    // them (forward 51.4 → 47 µs at B8 H12 T2048 W64 when reordered).  With
+    // two TMEM buffers (nbuf 2) QKᵀ(it+1) lands in the other buffer while the
+    // epilogue reads O(it), so S(it+1) is ready when the epilogue is done
     // with tile it.  The single shared P tile stays safe: the epilogue writes
     // P(it+1) only after it has waited for P·V(it) (o_full) to normalise O(it).
     if (lane == 0) {
@@ -402,17 +397,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           Rec nxt{};
           const bool more = u + 1 < u1;
           if (more) nxt = make(u + 1, it + 1);
-          if (p.nbuf == 2 && more) issue_s(nxt);  // QKᵀ one tile ahead
           if (it >= 1) store_o(u - 1, it - 1);     // staged while P(it) was formed
           issue_o(cur);
           if (it >= 1 && ok) release_o();
-          if (p.nbuf != 2 && more) issue_s(nxt);
+          if (more) issue_s(nxt);  // after P·V(it): see the order note above
           cur = nxt;
         }
         if (ok) store_o(u1 - 1, u1 - u0 - 1);
         bulk_wait_group0();
       }
-      drain_mma(&bar->drain, err, kErrFwd | 25);
     }
   } else if (warp < 4 || warp >= 12) {
     // ─────────────── RoPE rotators (4 warps) ───────────────

@@ -84,7 +84,6 @@ struct __align__(8) GBars {
   uint64_t s_full[2], s_free[2], p_full[2], p_free[2];
   uint64_t acc_full[2], acc_free[2];
   uint64_t mass_ready[2], staged;
-  uint64_t drain;  // the MMA thread's exit commit
   uint32_t tmem_base;
 };
 
@@ -168,7 +167,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar->inner_empty[s], 1);
     }
     mbar_init(&bar->staged, 4);
-    mbar_init(&bar->drain, 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -189,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (R == kDKV) prefetch_tmap(&tmout1);
       const long long plane = (long long)BH * p.tpad;
       bool ok = true;
-      int ni = 0, no = 0;  // inner / outer loads issued
+      int ni = 0;
       for (int k = blockIdx.x, m = 0; k < p.units && ok; k += G, ++m) {
         int bh, ot, fi, nin;
         unit_of(R, k, BH, nT, p.local, p.W, bh, ot, fi, nin);
@@ -197,7 +195,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int os = m & 1;
         if (m >= 2) ok = mbar_wait(&bar->outer_empty[os], ((m >> 1) - 1) & 1, err, kErrG | 1);
         if (!ok) break;
-        ++no;
         uint8_t* o = sOuter + os * Tr::kOuterTiles * kTileBytes;
         mbar_arrive_expect_tx(&bar->outer_full[os],
                               Tr::kOuterTiles * kTileBytes + (Tr::kOuterCoef ? kCoefBytes : 0));
@@ -229,8 +226,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++ni;
         }
       }
-      drain_loads(bar->outer_full, 2, no, err, kErrG | 17);
-      drain_loads(bar->inner_full, kStages, ni, err, kErrG | 18);
     }
   } else if (warp == 1) {
     // ─────────────────────────── MMA issuer ───────────────────────────
@@ -358,7 +353,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         prev = cur;
         have_prev = true;
       }
-      drain_mma(&bar->drain, err, kErrG | 16);
     }
   } else if (warp < 4 || warp >= 12) {
     // ─────────── output warps: accumulators → bf16 → TMA store ───────────
@@ -584,7 +578,77 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (R != kFwd) dk[ss][e4 >> 1] = pack_bf16(dv[0], dv[1]);
             }
             };
-            if (pexp)
+            // Interior piece: every element valid for every row of the warp
+            // (inside the causal triangle / the window band, rows and columns
+            // below T) and nothing exported — no positions, mask or selects
+            // per element, and DKV's per-query coefficients as 16-byte
+            // broadcast loads.  Decided warp-uniformly.
+            bool tfull;
+            if (R == kDKV)  // row = key orow, columns = queries ipos0 … ipos0+15
+              tfull = ipos0 + 15 < T && (p.local ? (ipos0 - orow >= 1 && ipos0 + 15 - orow <= p.W)
+                                                 : ipos0 >= orow);
+            else            // row = query orow, columns = keys
+              tfull = orow < T && (p.local ? (orow - ipos0 - 15 >= 1 && orow - ipos0 <= p.W)
+                                           : ipos0 + 15 <= orow);
+            const bool full = __all_sync(0xffffffffu, tfull && !pexp);
+            auto piece_full = [&]() {
+              long long bbase = 0, bstep = 0;
+              if constexpr (kBias) {
+                // element ee: bias at (query, slot) — global slot = key, local
+                // slot = W − (t − s); one base per piece, a constant step
+                if (R == kDKV) {  // query varies with ee
+                  bbase = b * p.bs0 + (long long)ipos0 * p.bs1 +
+                          (long long)(p.local ? p.W - (ipos0 - orow) : orow) * p.bs2;
+                  bstep = p.bs1 - (p.local ? p.bs2 : 0);
+                } else {          // key varies with ee
+                  bbase = b * p.bs0 + (long long)orow * p.bs1 +
+                          (long long)(p.local ? p.W - (orow - ipos0) : ipos0) * p.bs2;
+                  bstep = p.bs2;
+                }
+              }
+#pragma unroll
+              for (int e4 = 0; e4 < 16; e4 += 4) {
+                float ah[4] = {0.f, 0.f, 0.f, 0.f}, ad[4], bd[4];
+                if (R == kDKV) {
+                  const float4 a4 = *reinterpret_cast<const float4*>(cf + c0 + e4);
+                  const float4 d4 = *reinterpret_cast<const float4*>(cf + kTile + c0 + e4);
+                  const float4 b4 = *reinterpret_cast<const float4*>(cf + 2 * kTile + c0 + e4);
+                  ah[0] = a4.x; ah[1] = a4.y; ah[2] = a4.z; ah[3] = a4.w;
+                  ad[0] = d4.x; ad[1] = d4.y; ad[2] = d4.z; ad[3] = d4.w;
+                  bd[0] = b4.x; bd[1] = b4.y; bd[2] = b4.z; bd[3] = b4.w;
+                } else {
+#pragma unroll
+                  for (int z = 0; z < 4; ++z) { ad[z] = row_ad; bd[z] = row_bd; }
+                }
+                float pv[4], dv[4];
+#pragma unroll
+                for (int z = 0; z < 4; ++z) {
+                  const int ee = e4 + z;
+                  float x = __uint_as_float(Rg[ee]) * p.half_inv_scale;
+                  if constexpr (kBias) x = fmaf(0.5f, __ldg(p.bias + bbase + ee * bstep), x);
+                  const float thv = tanh_approx(x);
+                  if (R == kFwd) {
+                    pv[z] = fmaf(0.5f, thv, 0.5f);
+                    mass += pv[z];
+                  } else {
+                    const float dt = fmaf(ad[z], __uint_as_float(Rg[16 + ee]), bd[z]);
+                    dv[z] = dt * fmaf(-thv, thv, 1.f);
+                    if (R == kDKV) pv[z] = fmaf(ah[z], thv, ah[z]);
+                  }
+                }
+                if (R == kFwd || R == kDKV) {
+                  pk[ss][e4 >> 1] = pack_bf16(pv[0], pv[1]);
+                  pk[ss][(e4 >> 1) + 1] = pack_bf16(pv[2], pv[3]);
+                }
+                if (R != kFwd) {
+                  dk[ss][e4 >> 1] = pack_bf16(dv[0], dv[1]);
+                  dk[ss][(e4 >> 1) + 1] = pack_bf16(dv[2], dv[3]);
+                }
+              }
+            };
+            if (full)
+              piece_full();
+            else if (pexp)
               piece(std::true_type{});
             else
               piece(std::false_type{});

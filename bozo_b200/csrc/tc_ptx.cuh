@@ -113,12 +113,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return mbar_wait_slow(bar, parity, err, code);
 }
 
-// Exit path of a producer thread: wait (bounded) until the last load issued
-// on each slot of a ring has landed, so no TMA copy is still writing shared
-// memory when the CTA leaves — on the timeout path the consumers stopped
-// waiting for them.  Slot s of `slots` got loads s, s + slots, …; the last of
-// the n_issued loads on it completes phase last / slots.  On the normal path
-// every phase was consumed already and each wait returns at the first probe.
+// Exit drains, for a kernel that gives up a wait after a short limit: before
+// the TMEM is released, the producer waits (bounded) until the last load
+// issued on each ring slot has landed, and each MMA-issuing thread commits
+// once more and waits for that commit, so no copy or MMA is in flight when
+// the CTA exits.  The wait self-test kernel (limit ~1 ms) uses them.  The
+// operator kernels do not: a role of theirs leaves early only after one of
+// its own waits ran for kWaitLimitNs (4 s), so everything it issued finished
+// seconds before the block reaches the TMEM release; and the drains' code
+// alone, never executed, slowed the W 64 fwd+bwd step by 9 µs (6 %) —
+// instruction-cache footprint, as with the inlined polling loop above.
+//
+// Slot s of `slots` got loads s, s + slots, …; the last of the n_issued loads
+// on it completes phase last / slots.
 static __device__ __noinline__ void drain_loads(uint64_t* full, int slots, int n_issued, int* err,
                                          int code) {
   for (int s = 0; s < slots && s < n_issued; ++s) {

@@ -5,10 +5,11 @@
 // One CTA of two warps: warp 0 allocates TMEM; its lane 0 starts a bulk copy
 // into shared memory and one tcgen05 MMA (zero operands) into that TMEM, then
 // waits with a short limit on an mbarrier that nothing ever arrives on.  The
-// wait gives up, records its code in the device error word, and the thread
-// leaves the way every tensor-core kernel leaves on a timeout: it drains the
-// copy and the MMA with bounded waits (drain_loads / drain_mma) before the
-// TMEM is released and the CTA exits.  The optional result words say what
+// wait gives up through the same polling loop as every tensor-core kernel
+// (mbar_wait_until), records its code in the device error word, and — with
+// its limit far shorter than the kernels' 4 s — drains the copy and the MMA
+// with bounded waits (drain_loads / drain_mma) before the TMEM is released
+// and the CTA exits.  The optional result words say what
 // happened: [0] the wait gave up, [1] the copy drained, [2] the MMA drained,
 // [3] microseconds the wait took before it gave up.
 #include "tc.cuh"
