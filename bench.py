@@ -527,6 +527,72 @@ def run_global_block(local_rank, steps=20, warmup=5):
     }
 
 
+def run_drop_in_layer(local_rank, steps=20, warmup=5):
+    """model.py's own call site at the 117M layer shape, through the drop-in
+    ``causal_tension`` exactly as model.py:248-258 uses it under train.py's
+    bf16 autocast: bf16 projections rotated by fp32 RoPE tables (fp32 Q/K,
+    model.py:203-204), bf16 V, τ returned, out = S / clamp(Στ, 1e-6);
+    forward + backward of ⟨out, dO⟩, B16 T1024 H12 HD64 W64.  Timed on the
+    tensor cores (the default path) and, for context, forced onto the
+    exact-fp32 CUDA-core kernels the same call would take without the
+    bf16 operand copies."""
+    import bozo_b200
+    from bozo_b200 import ops as bops
+    dev = torch.device("cuda", local_rank)
+    Bq, Tq, W = TRAIN_B, TRAIN_T, 64
+    g = torch.Generator().manual_seed(66)
+    qr, kr, vr, d = [torch.randn(Bq, Tq, H, HD, generator=g).to(dev, torch.bfloat16) for _ in range(4)]
+    for x in (qr, kr, vr):
+        x.requires_grad_(True)
+    cos, sin, _ = bops.rope_tables(HD, Tq, 10_000.0, dev)
+    c_, s_ = cos.unsqueeze(0).unsqueeze(2), sin.unsqueeze(0).unsqueeze(2)
+
+    def rope(x):  # model.py:75-81 with the fp32 table buffers
+        x1, x2 = x[..., :HD // 2], x[..., HD // 2:]
+        return torch.cat([x1 * c_ - x2 * s_, x1 * s_ + x2 * c_], dim=-1)
+
+    def step():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            msg, tau = bozo_b200.causal_tension(rope(qr), rope(kr), vr, W, 8.0, return_tau=True)
+            out = msg / tau.sum(-1).clamp(min=1e-6).unsqueeze(-1)
+        return torch.autograd.grad(out, (qr, kr, vr), d.float())
+
+    def timed():
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / steps
+
+    ms_tc = timed()
+    path_tc = bozo_b200.last_path()
+    prev = bops._path_override
+    bozo_b200.set_kernel_path("simt")
+    try:
+        steps_s, steps = steps, max(3, steps // 5)
+        ms_simt = timed()
+        steps = steps_s
+    finally:
+        bozo_b200.set_kernel_path(prev)
+    tok = Bq * Tq
+    return {
+        "workload": "model.py call site via the drop-in causal_tension under bf16 autocast "
+                    "(fp32 RoPE'd Q/K, bf16 V, tau returned, tau-mass division; model.py:248-258), "
+                    "fwd+bwd incl. the RoPE and division ops, B16 T1024 H12 HD64 W64",
+        "ms_per_step": round(ms_tc, 4), "tokens_per_s": round(tok / (ms_tc * 1e-3), 1),
+        "kernel_path": path_tc,
+        "cuda_core_fp32_ms_per_step": round(ms_simt, 4),
+        "speedup_vs_cuda_core": round(ms_simt / ms_tc, 2),
+        "timing": "eager calls, CUDA events",
+    }
+
+
 ONE_M_B, ONE_M_T = 8, 256  # BASELINE configs[0]: the reference's CPU-runnable model
 
 
@@ -775,8 +841,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--workload", default="all",
-                    choices=["all", "op", "train", "prefill", "decode", "global"],
-                    help="op: isolated operator (headline); train: 117M training step; "
+                    choices=["all", "op", "iso", "train", "prefill", "decode", "global"],
+                    help="op: isolated operator (headline) + global block + drop-in call site; "
+                         "iso: the isolated operator alone (profiling); train: 117M training step; "
                          "prefill: 350M inference prefill with tau export; "
                          "decode: 117M token-by-token decoding")
     ap.add_argument("--train-steps", type=int, default=10)
@@ -833,11 +900,15 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     results = train = prefill = train13 = glob_obj = one_m = None
-    if args.workload in ("all", "op"):
+    if args.workload in ("all", "op", "iso"):
         results, e2e_ms, launches_per_step = run_ours(args, rank, world, local_rank)
+    drop_in = None
     if args.workload in ("all", "op", "global"):
         torch.cuda.empty_cache()
         glob_obj = run_global_block(local_rank)
+    if args.workload in ("all", "op"):
+        torch.cuda.empty_cache()
+        drop_in = run_drop_in_layer(local_rank)
     tau_consumer = None
     if args.workload in ("all", "train"):
         torch.cuda.empty_cache()
@@ -1013,6 +1084,8 @@ def main():
     }
     if glob_obj is not None:
         line["global_block"] = glob_obj
+    if drop_in is not None:
+        line["drop_in_117m_layer"] = drop_in
     if train_obj is not None:
         line["train_117m"] = train_obj
     if train13_obj is not None:
@@ -1032,6 +1105,8 @@ def main():
     if glob_obj is not None:
         summ.update(global_ms=glob_obj["ms_per_step"], global_frac_hbm=glob_obj["frac_hbm"],
                     global_frac_tensor=glob_obj["frac_tensor"])
+    if drop_in is not None:
+        summ.update(drop_in_ms=drop_in["ms_per_step"], drop_in_path=drop_in["kernel_path"])
     if train_obj is not None:
         summ.update(train_117m_tokens_per_s=train_obj["value"],
                     train_117m_ms=train_obj["ms_per_step"],

@@ -35,6 +35,7 @@ EXPORTED = (
     "bozo_swiglu_fwd", "bozo_swiglu_bwd",
     "bozo_cross_entropy_fwd", "bozo_cross_entropy_bwd",
     "bozo_tension_error_async", "bozo_tension_wait_selftest", "bozo_tension_fwd_needs_lp",
+    "bozo_wo_add_rmsnorm_fwd", "bozo_wo_add_rmsnorm_supported",
 )
 TAU_AUX_MAX_LAYERS = 64  # BOZO_TAU_AUX_MAX_LAYERS
 
@@ -97,6 +98,14 @@ class AddRMSNormArgs(C.Structure):
         ("scale", C.c_void_p), ("out", C.c_void_p), ("rstd", C.c_void_p),
         ("d_out", C.c_void_p), ("dx", C.c_void_p), ("dy", C.c_void_p), ("d_scale", C.c_void_p),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+    ]
+
+
+class WoAddRMSNormArgs(C.Structure):
+    _fields_ = [
+        ("rows", C.c_int64), ("width", C.c_int32), ("eps", C.c_float),
+        ("msg", C.c_void_p), ("wo", C.c_void_p), ("x", C.c_void_p), ("x_dtype", C.c_int32),
+        ("scale", C.c_void_p), ("out", C.c_void_p), ("rstd", C.c_void_p),
     ]
 
 
@@ -191,6 +200,10 @@ def lib():
                 L.bozo_tau_aux_fwd.restype = C.c_int
                 L.bozo_tau_aux_bwd.argtypes = [C.POINTER(TauAuxBwdArgs), C.c_void_p]
                 L.bozo_tau_aux_bwd.restype = C.c_int
+                L.bozo_wo_add_rmsnorm_fwd.argtypes = [C.POINTER(WoAddRMSNormArgs), C.c_void_p]
+                L.bozo_wo_add_rmsnorm_fwd.restype = C.c_int
+                L.bozo_wo_add_rmsnorm_supported.argtypes = [C.c_int32, C.c_int32]
+                L.bozo_wo_add_rmsnorm_supported.restype = C.c_int
                 _lib = L
     return _lib
 

@@ -9,6 +9,16 @@ and backward, as autograd functions.
   dy and the scale's gradient (fixed-order partial sums).  Output in x's
   dtype — fp32 for the model's fp32 residual stream, as ``rms_norm`` gives
   under bf16 autocast.
+* ``wo_add_rms_norm(x, msg, wo_weight, scale, eps)`` = ``rms_norm(x +
+  wo(msg))`` with a bf16 projection (model.py:259, 283 under bf16 autocast),
+  forward only: one tensor-core kernel per 128 rows computes the projection
+  and applies the add and the norm to its accumulator, so the projection's
+  output never goes through device memory.  For prefill, decoding and
+  evaluation (no gradients); ``wo_norm_applies`` says when it can be used.
+  Off in the model unless ``FUSED_WO_NORM`` is set: on B200 it is still
+  slower than the library GEMM followed by ``add_rms_norm`` at every
+  measured size (one 128-row tile pulls the whole weight through at most
+  eight SMs), so the model keeps the two-kernel path by default.
 * ``swiglu(g, v)`` = ``silu(g) * v`` (model.py:328-329): one pass each way.
 * ``cross_entropy(logits, targets)`` = ``F.cross_entropy`` (train.py:920,
   mean over targets ≠ −100) from the logits in their own dtype: one pass
@@ -29,7 +39,7 @@ from torch import Tensor
 from . import _capi
 
 __all__ = ["add_rms_norm", "swiglu", "cross_entropy", "norm_applies", "swiglu_applies",
-           "xent_applies"]
+           "xent_applies", "wo_add_rms_norm", "wo_norm_applies"]
 
 _WIDTHS = {128, 256, 512, 768, 1024}
 _DTYPES = (torch.float32, torch.bfloat16)
@@ -95,6 +105,65 @@ def add_rms_norm(x: Tensor, y: Optional[Tensor], scale: Tensor, eps: float) -> T
     if scale.dtype != x.dtype:
         scale = scale.to(x.dtype)
     return _AddRMSNormFn.apply(x, y, scale, eps)
+
+
+_WO_OK = {}
+FUSED_WO_NORM = False  # route the model's no-grad wo + add + norm through the fused kernel
+
+
+def _wo_width_ok(D: int, dtype: torch.dtype) -> bool:
+    """Whether the library's kernel takes this width for x of this dtype."""
+    key = (D, dtype)
+    if key not in _WO_OK:
+        code = 1 if dtype == torch.bfloat16 else 0
+        _WO_OK[key] = bool(_capi.lib().bozo_wo_add_rmsnorm_supported(D, code))
+    return _WO_OK[key]
+
+
+def wo_norm_applies(x: Tensor, msg: Tensor, weight: Tensor) -> bool:
+    """Whether the model routes this call to ``wo_add_rms_norm``:
+    ``FUSED_WO_NORM`` set, no gradient wanted, CUDA
+    tensors, a supported width, and a projection that would run in bf16 (bf16
+    autocast, or bf16 operands)."""
+    if not FUSED_WO_NORM:
+        return False
+    if torch.is_grad_enabled() and (x.requires_grad or msg.requires_grad or weight.requires_grad):
+        return False
+    if not (x.is_cuda and msg.is_cuda and weight.is_cuda) or x.dtype not in _DTYPES:
+        return False
+    D = x.shape[-1]
+    if msg.shape != x.shape or tuple(weight.shape) != (D, D) or not _wo_width_ok(D, x.dtype):
+        return False
+    if torch.is_autocast_enabled("cuda"):
+        return torch.get_autocast_dtype("cuda") == torch.bfloat16
+    return msg.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16
+
+
+def _bf16_weight(weight: Tensor) -> Tensor:
+    """A contiguous bf16 copy of ``weight``, kept on the tensor until the
+    weight changes (its version counter moves), as autocast keeps its casts."""
+    if weight.dtype == torch.bfloat16 and weight.is_contiguous():
+        return weight
+    key = (weight.data_ptr(), weight._version)
+    cached = getattr(weight, "_bozo_bf16", None)
+    if cached is None or cached[0] != key:
+        with torch.no_grad():
+            cached = (key, weight.detach().to(torch.bfloat16).contiguous())
+        weight._bozo_bf16 = cached
+    return cached[1]
+
+
+def wo_add_rms_norm(x: Tensor, msg: Tensor, weight: Tensor, scale: Tensor, eps: float) -> Tensor:
+    """``rms_norm(x + bf16(msg)·bf16(weight)ᵀ)`` in one kernel, forward only."""
+    D = x.shape[-1]
+    if x.numel() == 0:
+        return torch.empty_like(x)
+    x2 = x.reshape(-1, D).contiguous()
+    m2 = msg.reshape(-1, D).to(torch.bfloat16).contiguous()
+    w2 = _bf16_weight(weight)
+    sc = scale.to(x.dtype).contiguous()
+    out, _ = _capi.ext().wo_add_rmsnorm_fwd(m2, w2, x2, sc, float(eps))
+    return out.view(x.shape)
 
 
 def swiglu(g: Tensor, v: Tensor) -> Tensor:

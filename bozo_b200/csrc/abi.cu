@@ -540,6 +540,30 @@ int bozo_add_rmsnorm_bwd(const bozo_add_rmsnorm_args* a, void* stream) {
   return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
 }
 
+int bozo_wo_add_rmsnorm_fwd(const bozo_wo_add_rmsnorm_args* a, void* stream) {
+  if (!a) return BOZO_ERR_NULL;
+  if (a->rows <= 0 || a->width <= 0) return BOZO_ERR_BAD_SHAPE;
+  if (a->x_dtype != BOZO_DT_F32 && a->x_dtype != BOZO_DT_BF16) return BOZO_ERR_BAD_DTYPE;
+  if (!wo_norm_cluster(a->width, a->x_dtype == BOZO_DT_BF16)) return BOZO_ERR_UNSUPPORTED;
+  if (!a->msg || !a->wo || !a->x || !a->scale || !a->out) return BOZO_ERR_NULL;
+  const void* ptrs[5] = {a->msg, a->wo, a->x, a->out, a->scale};
+  for (const void* ptr : ptrs)
+    if (reinterpret_cast<uintptr_t>(ptr) & 15) return BOZO_ERR_ALIGNMENT;
+  if (!tmap_encoder_available()) return BOZO_ERR_UNSUPPORTED;
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->x, restore);
+  if (e != cudaSuccess) return cuda_fail(e);
+  int* err = error_word(&e);
+  if (!err) return cuda_fail(e);
+  e = launch_wo_norm(*a, err, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
+}
+
+int bozo_wo_add_rmsnorm_supported(int32_t width, int32_t x_dtype) {
+  if (x_dtype != BOZO_DT_F32 && x_dtype != BOZO_DT_BF16) return 0;
+  return wo_norm_cluster(width, x_dtype == BOZO_DT_BF16) ? 1 : 0;
+}
+
 static int check_swiglu(const bozo_swiglu_args* a) {
   if (!a) return BOZO_ERR_NULL;
   if (a->n <= 0 || a->n % 4 != 0) return BOZO_ERR_BAD_SHAPE;

@@ -151,6 +151,10 @@ struct NormP {
 int norm_partial_blocks(long long N, int sms);
 bool norm_width_ok(int D);
 cudaError_t launch_add_rmsnorm(const NormP& p, bool backward, cudaStream_t st);
+// wo projection + residual add + RMSNorm, forward (wo_norm.cu): cluster size
+// for a width (0 = unsupported) and the launch
+int wo_norm_cluster(int width, bool x_bf16);
+cudaError_t launch_wo_norm(const bozo_wo_add_rmsnorm_args& a, int* err, cudaStream_t st);
 cudaError_t launch_swiglu(const void* g, const void* v, void* h, const void* dh, void* dg, void* dv,
                           long long n, int dt, int sms, cudaStream_t st);
 

@@ -327,6 +327,25 @@ std::vector<at::Tensor> add_rmsnorm_bwd(const at::Tensor& d_out, const at::Tenso
   return {dx, dy, dscale};
 }
 
+// wo projection + residual add + RMSNorm forward: msg [N, D] bf16, wo [D, D] bf16,
+// x [N, D] → (out [N, D] in x's dtype, rstd [N] fp32).
+std::vector<at::Tensor> wo_add_rmsnorm_fwd(const at::Tensor& msg, const at::Tensor& wo,
+                                           const at::Tensor& x, const at::Tensor& scale, double eps) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor out = at::empty_like(x);
+  at::Tensor rstd = at::empty({x.size(0)}, x.options().dtype(at::kFloat));
+  bozo_wo_add_rmsnorm_args a{};
+  a.rows = x.size(0); a.width = (int32_t)x.size(1); a.eps = (float)eps;
+  a.msg = msg.data_ptr(); a.wo = wo.data_ptr();
+  a.x = x.data_ptr(); a.x_dtype = dtype_code(x.scalar_type());
+  a.scale = scale.data_ptr(); a.out = out.data_ptr(); a.rstd = rstd.data_ptr<float>();
+  TORCH_CHECK(msg.scalar_type() == at::kBFloat16 && wo.scalar_type() == at::kBFloat16,
+              "wo_add_rmsnorm_fwd: msg and wo must be bf16");
+  check(bozo_wo_add_rmsnorm_fwd(&a, at::cuda::getCurrentCUDAStream(x.device().index()).stream()),
+        "bozo_wo_add_rmsnorm_fwd");
+  return {out, rstd};
+}
+
 at::Tensor swiglu_fwd(const at::Tensor& g, const at::Tensor& v) {
   const c10::cuda::CUDAGuard guard(g.device());
   at::Tensor h = at::empty_like(g);
@@ -507,6 +526,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("graph_bias", &graph_bias, "graph bias through bozo_graph_bias_build");
   m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd, "residual add + RMSNorm through bozo_add_rmsnorm_fwd");
   m.def("add_rmsnorm_bwd", &add_rmsnorm_bwd, "its backward through bozo_add_rmsnorm_bwd");
+  m.def("wo_add_rmsnorm_fwd", &wo_add_rmsnorm_fwd,
+        "wo projection + residual add + RMSNorm through bozo_wo_add_rmsnorm_fwd");
   m.def("swiglu_fwd", &swiglu_fwd, "SwiGLU through bozo_swiglu_fwd");
   m.def("cross_entropy_fwd", &cross_entropy_fwd, "cross-entropy through bozo_cross_entropy_fwd");
   m.def("cross_entropy_bwd", &cross_entropy_bwd, "its backward through bozo_cross_entropy_bwd");

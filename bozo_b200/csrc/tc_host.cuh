@@ -19,6 +19,12 @@ bool tma_view_ok(const DevT4& x, int B, int T, int H);
 bool make_tmap_bthd(CUtensorMap* m, const void* base, long long sb, long long st, long long sh,
                     int B, int T, int H, int box_t);
 
+// 2-D tiled tensor map over a row-major bf16 (or fp32) matrix [outer, inner]
+// with the given row pitch: box (box_inner, box_outer), 128-byte swizzle
+// (box_inner × element size = 128 bytes), zero fill out of bounds.
+bool make_tmap_2d(CUtensorMap* m, const void* base, bool f32, uint64_t inner, uint64_t outer,
+                  uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
+
 bool tmap_encoder_available();
 int num_sms();
 

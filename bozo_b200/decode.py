@@ -158,7 +158,7 @@ def step(state: DecodeState, tokens: Tensor, export: bool = False):
             q[:, 0], k[:, 0], v[:, 0], state.k_cache[li], state.v_cache[li], state.pos, mode,
             0 if glob else cfg.window, norm, float(layer.scale), cos, sin, tw, ops._dt(q.dtype),
             ops._dt(q.dtype))
-        hh = layer.norm.add_forward(h, layer.wo(out.view(B, 1, D)))
+        hh = layer.norm.wo_add_forward(h, out.view(B, 1, D), layer.wo, layer.dropout)
         if blk.oscillate is not None:
             hh = _oscillate(blk.oscillate, hh, state.pos)
         x = blk.ffn(hh)

@@ -115,6 +115,16 @@ class RMSNorm(nn.Module):
             return block_ops.add_rms_norm(x, y, self.scale, self.eps)
         return self(x + y)
 
+    def wo_add_forward(self, x, msg, wo: nn.Linear, dropout: nn.Dropout):
+        """``self(x + dropout(wo(msg)))``: without gradients and with an
+        inactive dropout, one tensor-core kernel for the projection, the add
+        and the norm together."""
+        from . import block_ops
+        if ((not dropout.training or dropout.p == 0.0)
+                and block_ops.wo_norm_applies(x, msg, wo.weight)):
+            return block_ops.wo_add_rms_norm(x, msg, wo.weight, self.scale, self.eps)
+        return self.add_forward(x, dropout(wo(msg)))
+
 
 class MultiHeadCausalTensionLayer(nn.Module):
     """model.py:103-283 with the tension core on the fused operator."""
@@ -167,18 +177,19 @@ class MultiHeadCausalTensionLayer(nn.Module):
                                   return_tau=return_tensions, normalize="mass",
                                   tau_window=self.local_window)
             msg, tau = res if return_tensions else (res, None)
-            out = self.norm.add_forward(x, self.dropout(self.wo(msg.reshape(B, T, D))))
+            out = self.norm.wo_add_forward(x, msg.reshape(B, T, D), self.wo, self.dropout)
             return (out, tau) if return_tensions else out
         if return_tensions:
             msg, tau = self.tension_fn(q, k, v, window=self.window, scale=self.scale,
                                        rope_base=rope, rope_len=self.max_seq_len,
                                        bias=tau_bias, return_tau=True, normalize="mass")
-            out = self.norm.add_forward(x, self.dropout(self.wo(msg.reshape(B, T, D))))
+            out = self.norm.wo_add_forward(x, msg.reshape(B, T, D), self.wo, self.dropout)
             return out, tau
         msg = self.tension_fn(q, k, v, window=self.window, scale=self.scale, rope_base=rope,
                               rope_len=self.max_seq_len, bias=tau_bias, normalize="count")
-        msg = self.dropout(msg)
-        return self.norm.add_forward(x, self.wo(msg.reshape(B, T, D)))
+        if self.dropout.training and self.dropout.p > 0.0:  # dropout before wo here
+            return self.norm.add_forward(x, self.wo(self.dropout(msg).reshape(B, T, D)))
+        return self.norm.wo_add_forward(x, msg.reshape(B, T, D), self.wo, self.dropout)
 
 
 class OscillatoryModulation(nn.Module):

@@ -72,6 +72,36 @@ typedef struct {
 int bozo_swiglu_fwd(const bozo_swiglu_args* args, void* stream);
 int bozo_swiglu_bwd(const bozo_swiglu_args* args, void* stream);
 
+/* The attention-output projection fused with the residual add and RMSNorm
+ * that follow it, forward only:
+ *   y = bf16(msg · woᵀ), s = x + y (rounded to x's dtype when that is bf16),
+ *   rstd = rsqrt(mean(s²) + eps), out = s·rstd·scale in x's dtype
+ * — the same numbers as a bf16 projection followed by bozo_add_rmsnorm_fwd,
+ * without the projection's [rows, width] output going through device memory.
+ * Replaces model.py:259 / 283 (`self.norm(x + self.wo(msg))`, RMSNorm
+ * model.py:86-98) on paths without gradients (prefill, decode, evaluation).
+ * msg [rows, width] and wo [width, width] (nn.Linear weight, out × in) bf16
+ * contiguous and 16-byte aligned; x, scale, out as in bozo_add_rmsnorm_args;
+ * rstd [rows] fp32 or NULL.  Widths: bozo_wo_add_rmsnorm_supported says
+ * (64, 128, 256, 384, 512, 768, 1024 for both x dtypes, 2048 for bf16 x;
+ * BOZO_ERR_UNSUPPORTED otherwise). */
+typedef struct {
+  int64_t rows;
+  int32_t width;
+  float eps;
+  const void* msg;        /* [rows, width] bf16: the tension layer's normalised output */
+  const void* wo;         /* [width, width] bf16: the projection's weight */
+  const void* x;          /* [rows, width] residual stream */
+  int32_t x_dtype;        /* bozo_dtype: F32 or BF16 */
+  const void* scale;      /* [width], x's dtype */
+  void* out;              /* [rows, width], x's dtype */
+  float* rstd;            /* [rows] or NULL */
+} bozo_wo_add_rmsnorm_args;
+
+int bozo_wo_add_rmsnorm_fwd(const bozo_wo_add_rmsnorm_args* args, void* stream);
+/* 1 if bozo_wo_add_rmsnorm_fwd takes this width with x of this dtype. */
+int bozo_wo_add_rmsnorm_supported(int32_t width, int32_t x_dtype);
+
 /* Cross-entropy from the logits in their own dtype (bf16 or fp32, fp32
  * arithmetic).  Forward: row_lse[r] = logsumexp(logits[r]) and row_loss[r] =
  * row_lse[r] − logits[r][targets[r]] (0 where the target is outside

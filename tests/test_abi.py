@@ -76,6 +76,9 @@ int main(void) {
   S(bozo_add_rmsnorm_args); O(bozo_add_rmsnorm_args, eps); O(bozo_add_rmsnorm_args, y_dtype);
   O(bozo_add_rmsnorm_args, scale); O(bozo_add_rmsnorm_args, d_scale);
   O(bozo_add_rmsnorm_args, workspace_bytes);
+  S(bozo_wo_add_rmsnorm_args); O(bozo_wo_add_rmsnorm_args, eps); O(bozo_wo_add_rmsnorm_args, msg);
+  O(bozo_wo_add_rmsnorm_args, x_dtype); O(bozo_wo_add_rmsnorm_args, scale);
+  O(bozo_wo_add_rmsnorm_args, rstd);
   S(bozo_swiglu_args); O(bozo_swiglu_args, gate); O(bozo_swiglu_args, d_value);
   S(bozo_cross_entropy_args); O(bozo_cross_entropy_args, logits_dtype);
   O(bozo_cross_entropy_args, targets); O(bozo_cross_entropy_args, d_logits);
@@ -104,6 +107,7 @@ def test_struct_layout_matches_header():
              "bozo_graph_bias_args": _capi.GraphBiasArgs,
              "bozo_add_rmsnorm_args": _capi.AddRMSNormArgs,
              "bozo_swiglu_args": _capi.SwiGLUArgs,
+             "bozo_wo_add_rmsnorm_args": _capi.WoAddRMSNormArgs,
              "bozo_cross_entropy_args": _capi.CrossEntropyArgs,
              "bozo_tau_aux_fwd_args": _capi.TauAuxFwdArgs,
              "bozo_tau_aux_bwd_args": _capi.TauAuxBwdArgs}

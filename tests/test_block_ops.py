@@ -119,3 +119,96 @@ def test_cross_entropy_matches_framework(dtype, R, V):
     tol = dict(rtol=1e-5, atol=1e-8) if dtype == torch.float32 else dict(rtol=1e-2, atol=1e-7)
     torch.testing.assert_close(a.grad, b.grad, **tol)
     assert float(a.grad[::13].abs().max()) == 0.0
+
+
+def _ref_wo_norm(x, msg, w, scale, eps):
+    """float64 restatement of rms_norm(x + wo(msg)) with the projection's
+    output rounded to bf16 (model.py:259/283 under bf16 autocast) and the sum
+    rounded to x's dtype."""
+    y = (msg.to(torch.bfloat16).double() @ w.to(torch.bfloat16).double().T).to(torch.bfloat16)
+    s = (x.double() + y.double()).to(x.dtype).double()
+    rstd = torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + eps)
+    return s * rstd * scale.to(x.dtype).double()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("D", [64, 128, 256, 384, 512, 768, 1024, 2048])
+@pytest.mark.parametrize("rows", [1, 77, 999])
+@pytest.mark.parametrize("xd", [torch.float32, torch.bfloat16])
+def test_wo_add_rms_norm_matches_unfused(D, rows, xd):
+    if D == 2048 and xd == torch.float32:
+        pytest.skip("fp32 residual tile of a 2048-wide row share does not fit beside the ring")
+    from tests._tol import assert_close
+    g = torch.Generator().manual_seed(D * 7 + rows)
+    dev = torch.device("cuda:0")
+    x = (torch.randn(rows, D, generator=g) * 2).to(dev, xd)
+    msg = torch.randn(rows, D, generator=g).to(dev, torch.bfloat16)
+    w = (torch.randn(D, D, generator=g) / D ** 0.5).to(dev, torch.bfloat16)
+    scale = (1 + 0.1 * torch.randn(D, generator=g)).to(dev, xd)
+    out = block_ops.wo_add_rms_norm(x, msg, w, scale, 1e-6)
+    assert out.dtype == xd and out.shape == x.shape
+    assert_close(out, _ref_wo_norm(x, msg, w, scale, 1e-6), torch.bfloat16, f"D{D} rows{rows} {xd}")
+    y = F.linear(msg, w)
+    if block_ops.norm_applies(x, y):  # the unfused kernels' widths
+        unfused = block_ops.add_rms_norm(x, y, scale, 1e-6)
+        assert_close(out, unfused, torch.bfloat16, f"vs unfused D{D} rows{rows} {xd}")
+
+
+@pytest.mark.gpu
+def test_wo_add_rms_norm_at_prefill_size():
+    # the 117M model's width over B8 x T2048 rows, fp32 residual stream under
+    # autocast; fp32 weights go through the cached bf16 copy
+    g = torch.Generator().manual_seed(5)
+    dev = torch.device("cuda:0")
+    R, D = 8 * 2048, 768
+    x = torch.randn(R, D, generator=g).to(dev)
+    msg = torch.randn(R, D, generator=g).to(dev)
+    w = (torch.randn(D, D, generator=g) / D ** 0.5).to(dev)
+    scale = (1 + 0.1 * torch.randn(D, generator=g)).to(dev)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        out = block_ops.wo_add_rms_norm(x, msg, w, scale, 1e-6)
+        again = block_ops.wo_add_rms_norm(x, msg, w, scale, 1e-6)
+    assert torch.equal(out, again)
+    ref = _ref_wo_norm(x, msg, w, scale, 1e-6)
+    from tests._tol import assert_close
+    for lo in range(0, R, 4096):  # float64 reference in slices to bound host memory
+        assert_close(out[lo:lo + 4096], ref[lo:lo + 4096], torch.bfloat16, f"rows {lo}+")
+    # unit RMS of every normalised row (before the scale)
+    rms = (out.double() / scale.double()).pow(2).mean(-1).sqrt()
+    assert float((rms - 1).abs().max()) < 1e-3
+
+
+@pytest.mark.gpu
+def test_model_eval_takes_the_fused_projection(monkeypatch):
+    from bozo_b200 import lm
+    torch.manual_seed(0)
+    cfg = lm.TensionConfig(vocab_size=512, dim=256, num_heads=4, num_layers=2, window=32,
+                           max_seq_len=128)
+    model = lm.TensionLM(cfg).cuda().eval()
+    ids = torch.randint(0, 512, (2, 128), device="cuda")
+    calls = []
+    monkeypatch.setattr(block_ops, "FUSED_WO_NORM", True)
+    real = block_ops.wo_add_rms_norm
+    monkeypatch.setattr(block_ops, "wo_add_rms_norm",
+                        lambda *a, **k: calls.append(1) or real(*a, **k))
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        fused = model(ids)
+        assert len(calls) == cfg.num_layers
+        monkeypatch.setattr(block_ops, "wo_norm_applies", lambda *a: False)
+        unfused = model(ids)
+    assert len(calls) == cfg.num_layers
+    from tests._tol import assert_close
+    assert_close(fused.float(), unfused.float(), torch.bfloat16, "logits")
+
+
+def test_wo_norm_gating_on_cpu(monkeypatch):
+    x = torch.randn(4, 128)
+    w = torch.randn(128, 128)
+    assert not block_ops.wo_norm_applies(x, x, w)
+    monkeypatch.setattr(block_ops, "FUSED_WO_NORM", True)
+    assert not block_ops.wo_norm_applies(x, x, w)
+    f32, bf = torch.float32, torch.bfloat16
+    for D in (64, 128, 256, 384, 512, 768, 1024):
+        assert block_ops._wo_width_ok(D, f32) and block_ops._wo_width_ok(D, bf), D
+    assert block_ops._wo_width_ok(2048, bf) and not block_ops._wo_width_ok(2048, f32)
+    assert not block_ops._wo_width_ok(96, f32) and not block_ops._wo_width_ok(4096, bf)
