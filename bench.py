@@ -323,7 +323,7 @@ def run_train(args, rank, world, local_rank, cfg=None, batch=TRAIN_B, seq=TRAIN_
     operator in every tension layer, CE + train.py's default aux losses
     (w_closure 0.01, w_diversity 0.02, which put τ export and its cotangent
     in the loop; ``aux_off`` drops them), global-norm clip, fused AdamW; DDP
-    over NCCL when world > 1 (bf16 gradient all-reduce).  Uniform random
+    over NCCL when world > 1 (fp32 gradient all-reduce in 64 MB buckets).  Uniform random
     token ids from a per-rank seed, random init.  Returns
     ({variant: (ms_per_step max over ranks, e2e ms_per_step)}, params)."""
     import torch.distributed as dist
@@ -964,6 +964,8 @@ def main():
                        "per_gpu_batch": TRAIN_B, "global_batch": TRAIN_B * n,
                        "dtype": "bf16 autocast, fp32 master weights", "optimizer": "AdamW (fused)",
                        "parallelism": f"ddp{n}" if n > 1 else "single GPU",
+                       "gradient_allreduce": ("NCCL, fp32, 64 MB buckets overlapped with the "
+                                              "backward (static graph)") if n > 1 else None,
                        "data": "uniform random token ids, random init"},
             "tau_consumer": tau_consumer,
         }
