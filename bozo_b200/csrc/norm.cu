@@ -152,14 +152,35 @@ __global__ void __launch_bounds__(kNormWarps * 32)
   }
 }
 
-// dscale[c] = Σ_blocks part[b][c], in block order (deterministic)
+// dscale[c] = Σ_blocks part[b][c] in a fixed order (deterministic): one CTA
+// per 32 columns, lane = column (each warp reads whole 128-byte rows), warp w
+// sums blocks w, w + 8, … in four interleaved chains, then the eight warp
+// sums are added in warp order.
+constexpr int kReduceWarps = 8;
 template <typename X>
-__global__ void dscale_reduce_kernel(const float* __restrict__ part, int nblk, int D, X* __restrict__ dscale) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= D) return;
-  float v = 0.f;
-  for (int b = 0; b < nblk; ++b) v += part[(long long)b * D + c];
-  dscale[c] = (X)v;
+__global__ void __launch_bounds__(kReduceWarps * 32)
+    dscale_reduce_kernel(const float* __restrict__ part, int nblk, int D, X* __restrict__ dscale) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
+  float v[4] = {0.f, 0.f, 0.f, 0.f};
+  if (c < D) {
+    int b = warp;
+#pragma unroll 1
+    for (; b + 3 * kReduceWarps < nblk; b += 4 * kReduceWarps) {
+#pragma unroll
+      for (int z = 0; z < 4; ++z) v[z] += __ldg(part + (long long)(b + z * kReduceWarps) * D + c);
+    }
+    for (int z = 0; b < nblk; b += kReduceWarps, ++z) v[z] += __ldg(part + (long long)b * D + c);
+  }
+  __shared__ float red[kReduceWarps][32];
+  red[warp][lane] = (v[0] + v[1]) + (v[2] + v[3]);
+  __syncthreads();
+  if (warp == 0 && c < D) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kReduceWarps; ++w) s += red[w][lane];
+    dscale[c] = (X)s;
+  }
 }
 
 template <typename T>
@@ -239,7 +260,8 @@ cudaError_t bwd_t(const NormP& p, cudaStream_t st) {
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  dscale_reduce_kernel<X><<<(p.D + 255) / 256, 256, 0, st>>>(p.part, grid, p.D, static_cast<X*>(p.dscale));
+  dscale_reduce_kernel<X><<<(p.D + 31) / 32, kReduceWarps * 32, 0, st>>>(p.part, grid, p.D,
+                                                                      static_cast<X*>(p.dscale));
   return cudaGetLastError();
 }
 
