@@ -98,6 +98,7 @@ class AddRMSNormArgs(C.Structure):
         ("scale", C.c_void_p), ("out", C.c_void_p), ("rstd", C.c_void_p),
         ("d_out", C.c_void_p), ("dx", C.c_void_p), ("dy", C.c_void_p), ("d_scale", C.c_void_p),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+        ("out_lp", C.c_void_p), ("d_out_lp", C.c_void_p),
     ]
 
 
@@ -113,6 +114,7 @@ class SwiGLUArgs(C.Structure):
     _fields_ = [
         ("n", C.c_int64), ("dtype", C.c_int32), ("gate", C.c_void_p), ("value", C.c_void_p),
         ("out", C.c_void_p), ("d_out", C.c_void_p), ("d_gate", C.c_void_p), ("d_value", C.c_void_p),
+        ("width", C.c_int64), ("row_stride", C.c_int64),
     ]
 
 

@@ -19,7 +19,14 @@ and backward, as autograd functions.
   slower than the library GEMM followed by ``add_rms_norm`` at every
   measured size (one 128-row tile pulls the whole weight through at most
   eight SMs), so the model keeps the two-kernel path by default.
-* ``swiglu(g, v)`` = ``silu(g) * v`` (model.py:328-329): one pass each way.
+* ``add_rms_norm_lp(x, y, scale, eps)``: the same for an fp32 stream, also
+  returning the output rounded to bf16 — the operand bf16 autocast would
+  cast it to for every projection that reads it, made once by the same
+  kernel; the backward takes that copy's bf16 cotangent into the kernel
+  instead of an fp32 cast and add per projection.
+* ``swiglu(g, v)`` = ``silu(g) * v`` (model.py:328-329): one pass each way;
+  ``swiglu_packed(gv)`` takes one GEMM's packed ``[g | v]`` rows and returns
+  the cotangent in that layout.
 * ``cross_entropy(logits, targets)`` = ``F.cross_entropy`` (train.py:920,
   mean over targets ≠ −100) from the logits in their own dtype: one pass
   for the per-row logsumexp, one for the gradient, no fp32 copy.
@@ -38,8 +45,9 @@ from torch import Tensor
 
 from . import _capi
 
-__all__ = ["add_rms_norm", "swiglu", "cross_entropy", "norm_applies", "swiglu_applies",
-           "xent_applies", "wo_add_rms_norm", "wo_norm_applies"]
+__all__ = ["add_rms_norm", "add_rms_norm_lp", "swiglu", "swiglu_packed", "cross_entropy",
+           "norm_applies", "swiglu_applies", "swiglu_packed_applies", "xent_applies",
+           "wo_add_rms_norm", "wo_norm_applies"]
 
 _WIDTHS = {128, 256, 512, 768, 1024}
 _DTYPES = (torch.float32, torch.bfloat16)
@@ -56,6 +64,11 @@ def norm_applies(x: Tensor, y: Optional[Tensor]) -> bool:
     return True
 
 
+def swiglu_packed_applies(gv: Tensor) -> bool:
+    return (gv.is_cuda and gv.dtype in _DTYPES and gv.shape[-1] % 8 == 0 and gv.is_contiguous()
+            and gv.numel() > 0)
+
+
 def swiglu_applies(g: Tensor, v: Tensor) -> bool:
     return (g.is_cuda and g.shape == v.shape and g.dtype == v.dtype and g.dtype in _DTYPES
             and g.numel() % 4 == 0)
@@ -68,7 +81,7 @@ class _AddRMSNormFn(torch.autograd.Function):
         D = x.shape[-1]
         x2 = x.reshape(-1, D).contiguous()
         y2 = y.reshape(-1, D).contiguous() if y is not None else None
-        out, rstd = _capi.ext().add_rmsnorm_fwd(x2, y2, scale.contiguous(), float(eps))
+        out, rstd, _ = _capi.ext().add_rmsnorm_fwd(x2, y2, scale.contiguous(), float(eps), False)
         ctx.save_for_backward(x2, y2, scale, rstd)
         ctx.has_y = y is not None
         ctx.shape = x.shape
@@ -80,9 +93,52 @@ class _AddRMSNormFn(torch.autograd.Function):
         D = x2.shape[-1]
         dx, dy, dscale = _capi.ext().add_rmsnorm_bwd(d_out.reshape(-1, D).contiguous().to(x2.dtype),
                                                      x2, y2 if ctx.has_y else None,
-                                                     scale.contiguous(), rstd)
+                                                     scale.contiguous(), rstd, None)
         return (dx.view(ctx.shape), dy.view(ctx.shape) if ctx.has_y else None,
                 dscale.to(scale.dtype), None)
+
+
+class _AddRMSNormLPFn(torch.autograd.Function):
+
+    @staticmethod
+    def forward(ctx, x, y, scale, eps):
+        D = x.shape[-1]
+        x2 = x.reshape(-1, D).contiguous()
+        y2 = y.reshape(-1, D).contiguous() if y is not None else None
+        out, rstd, out_lp = _capi.ext().add_rmsnorm_fwd(x2, y2, scale.contiguous(), float(eps), True)
+        ctx.save_for_backward(x2, y2, scale, rstd)
+        ctx.has_y = y is not None
+        ctx.shape = x.shape
+        return out.view(x.shape), out_lp.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, d_out, d_out_lp):
+        x2, y2, scale, rstd = ctx.saved_tensors
+        D = x2.shape[-1]
+        d_out = torch.zeros_like(x2) if d_out is None else d_out.reshape(-1, D).contiguous().to(x2.dtype)
+        if d_out_lp is not None:
+            d_out_lp = d_out_lp.reshape(-1, D).contiguous().to(torch.bfloat16)
+        dx, dy, dscale = _capi.ext().add_rmsnorm_bwd(d_out, x2, y2 if ctx.has_y else None,
+                                                     scale.contiguous(), rstd, d_out_lp)
+        return (dx.view(ctx.shape), dy.view(ctx.shape) if ctx.has_y else None,
+                dscale.to(scale.dtype), None)
+
+
+class _SwiGLUPackedFn(torch.autograd.Function):
+
+    @staticmethod
+    def forward(ctx, gv):
+        shape = gv.shape
+        gv2 = gv.reshape(-1, shape[-1])
+        ctx.save_for_backward(gv2)
+        ctx.shape = shape
+        return _capi.ext().swiglu_packed_fwd(gv2).view(*shape[:-1], shape[-1] // 2)
+
+    @staticmethod
+    def backward(ctx, dh):
+        (gv2,) = ctx.saved_tensors
+        dh2 = dh.reshape(gv2.shape[0], -1).contiguous().to(gv2.dtype)
+        return _capi.ext().swiglu_packed_bwd(dh2, gv2).view(ctx.shape)
 
 
 class _SwiGLUFn(torch.autograd.Function):
@@ -164,6 +220,19 @@ def wo_add_rms_norm(x: Tensor, msg: Tensor, weight: Tensor, scale: Tensor, eps: 
     sc = scale.to(x.dtype).contiguous()
     out, _ = _capi.ext().wo_add_rmsnorm_fwd(m2, w2, x2, sc, float(eps))
     return out.view(x.shape)
+
+
+def add_rms_norm_lp(x: Tensor, y: Optional[Tensor], scale: Tensor, eps: float):
+    """``(rms_norm(x + y), rms_norm(x + y).to(bf16))`` for an fp32 stream,
+    both from one kernel; gradients flow through both."""
+    if scale.dtype != x.dtype:
+        scale = scale.to(x.dtype)
+    return _AddRMSNormLPFn.apply(x, y, scale, eps)
+
+
+def swiglu_packed(gv: Tensor) -> Tensor:
+    """``silu(g) * v`` for ``g, v = gv.chunk(2, -1)``, without splitting gv."""
+    return _SwiGLUPackedFn.apply(gv)
 
 
 def swiglu(g: Tensor, v: Tensor) -> Tensor:

@@ -499,6 +499,7 @@ static int check_norm(const bozo_add_rmsnorm_args* a) {
   if (a->x_dtype != BOZO_DT_F32 && a->x_dtype != BOZO_DT_BF16) return BOZO_ERR_BAD_DTYPE;
   if (a->y && a->y_dtype != BOZO_DT_F32 && a->y_dtype != BOZO_DT_BF16) return BOZO_ERR_BAD_DTYPE;
   if (a->y && a->x_dtype == BOZO_DT_BF16 && a->y_dtype != BOZO_DT_BF16) return BOZO_ERR_UNSUPPORTED;
+  if ((a->out_lp || a->d_out_lp) && a->x_dtype != BOZO_DT_F32) return BOZO_ERR_UNSUPPORTED;
   if (!a->x || !a->scale || !a->rstd) return BOZO_ERR_NULL;
   return BOZO_OK;
 }
@@ -509,6 +510,7 @@ static NormP norm_params(const bozo_add_rmsnorm_args* a) {
   p.x = a->x; p.x_dt = a->x_dtype; p.y = a->y; p.y_dt = a->y_dtype; p.scale = a->scale;
   p.out = a->out; p.rstd = a->rstd; p.dout = a->d_out; p.dx = a->dx; p.dy = a->dy;
   p.dscale = a->d_scale; p.part = static_cast<float*>(a->workspace);
+  p.out_lp = a->out_lp; p.dout_lp = a->d_out_lp;
   return p;
 }
 
@@ -568,6 +570,9 @@ static int check_swiglu(const bozo_swiglu_args* a) {
   if (!a) return BOZO_ERR_NULL;
   if (a->n <= 0 || a->n % 4 != 0) return BOZO_ERR_BAD_SHAPE;
   if (a->dtype != BOZO_DT_F32 && a->dtype != BOZO_DT_BF16) return BOZO_ERR_BAD_DTYPE;
+  if (a->width < 0 || a->width % 4 != 0 || a->width > 0x7fffffff) return BOZO_ERR_BAD_SHAPE;
+  if (a->width > 0 && (a->n % a->width != 0 || a->row_stride < a->width || a->row_stride % 4 != 0))
+    return BOZO_ERR_BAD_SHAPE;
   if (!a->gate || !a->value) return BOZO_ERR_NULL;
   return BOZO_OK;
 }
@@ -579,8 +584,8 @@ int bozo_swiglu_fwd(const bozo_swiglu_args* a, void* stream) {
   DeviceRestore restore;
   cudaError_t e = bind_device(a->gate, restore);
   if (e != cudaSuccess) return cuda_fail(e);
-  e = launch_swiglu(a->gate, a->value, a->out, nullptr, nullptr, nullptr, a->n, a->dtype, num_sms(),
-                    static_cast<cudaStream_t>(stream));
+  e = launch_swiglu(a->gate, a->value, a->out, nullptr, nullptr, nullptr, a->n, (int)a->width,
+                    a->row_stride, a->dtype, num_sms(), static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
 }
 
@@ -591,8 +596,8 @@ int bozo_swiglu_bwd(const bozo_swiglu_args* a, void* stream) {
   DeviceRestore restore;
   cudaError_t e = bind_device(a->gate, restore);
   if (e != cudaSuccess) return cuda_fail(e);
-  e = launch_swiglu(a->gate, a->value, nullptr, a->d_out, a->d_gate, a->d_value, a->n, a->dtype,
-                    num_sms(), static_cast<cudaStream_t>(stream));
+  e = launch_swiglu(a->gate, a->value, nullptr, a->d_out, a->d_gate, a->d_value, a->n, (int)a->width,
+                    a->row_stride, a->dtype, num_sms(), static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
 }
 

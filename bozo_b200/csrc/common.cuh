@@ -147,6 +147,8 @@ struct NormP {
   void* dy;
   void* dscale;
   float* part;  // backward: [blocks][D] partial sums of dscale
+  void* out_lp;         // forward: bf16 copy of out, or null (fp32 x only)
+  const void* dout_lp;  // backward: bf16 cotangent of out_lp, or null
 };
 int norm_partial_blocks(long long N, int sms);
 bool norm_width_ok(int D);
@@ -155,8 +157,9 @@ cudaError_t launch_add_rmsnorm(const NormP& p, bool backward, cudaStream_t st);
 // for a width (0 = unsupported) and the launch
 int wo_norm_cluster(int width, bool x_bf16);
 cudaError_t launch_wo_norm(const bozo_wo_add_rmsnorm_args& a, int* err, cudaStream_t st);
+// width 0: flat tensors; else g/v/dg/dv rows of `width` elements `stride` apart
 cudaError_t launch_swiglu(const void* g, const void* v, void* h, const void* dh, void* dg, void* dv,
-                          long long n, int dt, int sms, cudaStream_t st);
+                          long long n, int width, long long stride, int dt, int sms, cudaStream_t st);
 
 // Cross-entropy from the logits (xent.cu).
 bool xent_shape_ok(int V, int dt);

@@ -287,29 +287,35 @@ std::vector<at::Tensor> graph_bias(const at::Tensor& ctx_content, const at::Tens
   return {out, stats};
 }
 
-// add + RMSNorm forward: x [N, D] (+ y [N, D]) → (out [N, D] in x's dtype, rstd [N] fp32).
+// add + RMSNorm forward: x [N, D] (+ y [N, D]) → (out [N, D] in x's dtype, rstd [N] fp32,
+// and with want_lp a bf16 copy of out, else an undefined tensor).
 std::vector<at::Tensor> add_rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& y,
-                                        const at::Tensor& scale, double eps) {
+                                        const at::Tensor& scale, double eps, bool want_lp) {
   const c10::cuda::CUDAGuard guard(x.device());
-  at::Tensor out = at::empty_like(x);
+  at::Tensor out = at::empty_like(x), out_lp;
   at::Tensor rstd = at::empty({x.size(0)}, x.options().dtype(at::kFloat));
   bozo_add_rmsnorm_args a{};
+  if (want_lp) {
+    out_lp = at::empty_like(x, x.options().dtype(at::kBFloat16));
+    a.out_lp = out_lp.data_ptr();
+  }
   a.rows = x.size(0); a.width = (int32_t)x.size(1); a.eps = (float)eps;
   a.x = x.data_ptr(); a.x_dtype = dtype_code(x.scalar_type());
   if (y && y->defined()) { a.y = y->data_ptr(); a.y_dtype = dtype_code(y->scalar_type()); }
   a.scale = scale.data_ptr(); a.out = out.data_ptr(); a.rstd = rstd.data_ptr<float>();
   check(bozo_add_rmsnorm_fwd(&a, at::cuda::getCurrentCUDAStream(x.device().index()).stream()),
         "bozo_add_rmsnorm_fwd");
-  return {out, rstd};
+  return {out, rstd, out_lp};
 }
 
 // add + RMSNorm backward → (dx, dy (undefined without y), dscale).
 std::vector<at::Tensor> add_rmsnorm_bwd(const at::Tensor& d_out, const at::Tensor& x,
                                         const c10::optional<at::Tensor>& y, const at::Tensor& scale,
-                                        const at::Tensor& rstd) {
+                                        const at::Tensor& rstd, const c10::optional<at::Tensor>& d_out_lp) {
   const c10::cuda::CUDAGuard guard(x.device());
   at::Tensor dx = at::empty_like(x), dy, dscale = at::empty_like(scale);
   bozo_add_rmsnorm_args a{};
+  if (d_out_lp && d_out_lp->defined()) a.d_out_lp = d_out_lp->data_ptr();
   a.rows = x.size(0); a.width = (int32_t)x.size(1);
   a.x = x.data_ptr(); a.x_dtype = dtype_code(x.scalar_type());
   if (y && y->defined()) {
@@ -344,6 +350,39 @@ std::vector<at::Tensor> wo_add_rmsnorm_fwd(const at::Tensor& msg, const at::Tens
   check(bozo_wo_add_rmsnorm_fwd(&a, at::cuda::getCurrentCUDAStream(x.device().index()).stream()),
         "bozo_wo_add_rmsnorm_fwd");
   return {out, rstd};
+}
+
+// SwiGLU over packed rows gv [N, 2F] = [gate | value] (one GEMM's output):
+// forward → h [N, F]; backward → d_gv [N, 2F] in the same packed layout.
+at::Tensor swiglu_packed_fwd(const at::Tensor& gv) {
+  const c10::cuda::CUDAGuard guard(gv.device());
+  const int64_t F = gv.size(1) / 2;
+  at::Tensor h = at::empty({gv.size(0), F}, gv.options());
+  bozo_swiglu_args a{};
+  a.n = gv.size(0) * F; a.dtype = dtype_code(gv.scalar_type());
+  a.width = F; a.row_stride = gv.stride(0);
+  a.gate = gv.data_ptr();
+  a.value = static_cast<char*>(gv.data_ptr()) + F * gv.element_size();
+  a.out = h.data_ptr();
+  check(bozo_swiglu_fwd(&a, at::cuda::getCurrentCUDAStream(gv.device().index()).stream()), "bozo_swiglu_fwd");
+  return h;
+}
+
+at::Tensor swiglu_packed_bwd(const at::Tensor& dh, const at::Tensor& gv) {
+  const c10::cuda::CUDAGuard guard(gv.device());
+  const int64_t F = gv.size(1) / 2;
+  at::Tensor dgv = at::empty({gv.size(0), 2 * F}, gv.options());
+  bozo_swiglu_args a{};
+  a.n = gv.size(0) * F; a.dtype = dtype_code(gv.scalar_type());
+  a.width = F; a.row_stride = gv.stride(0);
+  a.gate = gv.data_ptr();
+  a.value = static_cast<char*>(gv.data_ptr()) + F * gv.element_size();
+  a.d_out = dh.data_ptr();
+  a.d_gate = dgv.data_ptr();
+  a.d_value = static_cast<char*>(dgv.data_ptr()) + F * dgv.element_size();
+  TORCH_CHECK(dgv.stride(0) == gv.stride(0), "swiglu_packed_bwd: gv must be contiguous");
+  check(bozo_swiglu_bwd(&a, at::cuda::getCurrentCUDAStream(gv.device().index()).stream()), "bozo_swiglu_bwd");
+  return dgv;
 }
 
 at::Tensor swiglu_fwd(const at::Tensor& g, const at::Tensor& v) {
@@ -532,6 +571,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_fwd", &cross_entropy_fwd, "cross-entropy through bozo_cross_entropy_fwd");
   m.def("cross_entropy_bwd", &cross_entropy_bwd, "its backward through bozo_cross_entropy_bwd");
   m.def("swiglu_bwd", &swiglu_bwd, "its backward through bozo_swiglu_bwd");
+  m.def("swiglu_packed_fwd", &swiglu_packed_fwd, "SwiGLU over packed [gate | value] rows");
+  m.def("swiglu_packed_bwd", &swiglu_packed_bwd, "its backward, packed [d_gate | d_value] rows");
   m.def("tau_aux_fwd", &tau_aux_fwd, "τ-field statistics through bozo_tau_aux_fwd");
   m.def("tau_aux_bwd", &tau_aux_bwd, "τ-field cotangents through bozo_tau_aux_bwd");
   m.def("tau_row_entropy", &tau_row_entropy, "per-row τ entropies through bozo_tau_aux_fwd");

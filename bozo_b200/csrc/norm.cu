@@ -13,10 +13,16 @@
 //   dscale = Σ_rows dout·ŝ
 // — the last as fixed-order per-block partial sums (each lane keeps its own
 // columns' sums across the block's rows) reduced by a second kernel, instead
-// of a column reduction over the whole [N, D] gradient.
+// of a column reduction over the whole [N, D] gradient.  For an fp32 stream
+// under bf16 autocast the forward can also write a bf16 copy of out (the
+// operand of the projections that read it, made once instead of one cast per
+// projection), and the backward then adds that copy's bf16 cotangent to
+// dout as it loads it.
 //
 // SwiGLU: h = silu(g)·v, dg = dh·v·σ(g)·(1 + g·(1 − σ(g))), dv = dh·silu(g),
-// in fp32 per element, one read and one write of each tensor.
+// in fp32 per element, one read and one write of each tensor; g and v may be
+// the two halves of packed [g | v] rows (one GEMM's output), and dg, dv then
+// land in the same packed layout.
 #include <cuda_bf16.h>
 
 #include "bozo_block_ops.h"
@@ -53,7 +59,8 @@ __device__ __forceinline__ float round_to(float v, __nv_bfloat16*) {
 template <typename X, typename Y, int K>
 __global__ void __launch_bounds__(kNormWarps * 32)
     add_rmsnorm_fwd_kernel(const X* __restrict__ x, const Y* __restrict__ y, const X* __restrict__ scale,
-                           X* __restrict__ out, float* __restrict__ rstd_out, long long N, float eps) {
+                           X* __restrict__ out, __nv_bfloat16* __restrict__ out_lp,
+                           float* __restrict__ rstd_out, long long N, float eps) {
   constexpr int D = K * 128;
   const int lane = threadIdx.x & 31;
   float sc[K][4];
@@ -84,13 +91,15 @@ __global__ void __launch_bounds__(kNormWarps * 32)
 #pragma unroll
       for (int i = 0; i < 4; ++i) o[i] = s[k][i] * rstd * sc[k][i];
       store4(out + r * D + 4 * (lane + 32 * k), o);
+      if (out_lp) store4(out_lp + r * D + 4 * (lane + 32 * k), o);
     }
   }
 }
 
 template <typename X, typename Y, int K>
 __global__ void __launch_bounds__(kNormWarps * 32)
-    add_rmsnorm_bwd_kernel(const X* __restrict__ dout, const X* __restrict__ x, const Y* __restrict__ y,
+    add_rmsnorm_bwd_kernel(const X* __restrict__ dout, const __nv_bfloat16* __restrict__ dout_lp,
+                           const X* __restrict__ x, const Y* __restrict__ y,
                            const X* __restrict__ scale, const float* __restrict__ rstd_in,
                            X* __restrict__ dx, Y* __restrict__ dy, float* __restrict__ dscale_part,
                            long long N) {
@@ -118,6 +127,12 @@ __global__ void __launch_bounds__(kNormWarps * 32)
         for (int i = 0; i < 4; ++i) sh[k][i] = round_to(sh[k][i] + yv[i], (X*)nullptr);
       }
       load4(dout + e, dv);
+      if (dout_lp) {
+        float dl[4];
+        load4(dout_lp + e, dl);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dv[i] += dl[i];
+      }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         sh[k][i] *= rstd;
@@ -183,14 +198,23 @@ __global__ void __launch_bounds__(kReduceWarps * 32)
   }
 }
 
+// Offset of element e of h in the gate/value (and their gradients') layout:
+// the same index for flat tensors (width 0), else row e / width at `stride`.
+__device__ __forceinline__ long long gv_off(long long e, int width, long long stride) {
+  if (width == 0) return e;
+  const long long r = e / width;
+  return r * stride + (e - r * width);
+}
+
 template <typename T>
 __global__ void swiglu_fwd_kernel(const T* __restrict__ g, const T* __restrict__ v, T* __restrict__ h,
-                                  long long n) {
+                                  long long n, int width, long long stride) {
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n / 4;
        i += (long long)gridDim.x * blockDim.x) {
     float gv[4], vv[4], o[4];
-    load4(g + 4 * i, gv);
-    load4(v + 4 * i, vv);
+    const long long a = gv_off(4 * i, width, stride);
+    load4(g + a, gv);
+    load4(v + a, vv);
 #pragma unroll
     for (int k = 0; k < 4; ++k) o[k] = gv[k] / (1.f + expf(-gv[k])) * vv[k];
     store4(h + 4 * i, o);
@@ -199,21 +223,23 @@ __global__ void swiglu_fwd_kernel(const T* __restrict__ g, const T* __restrict__
 
 template <typename T>
 __global__ void swiglu_bwd_kernel(const T* __restrict__ dh, const T* __restrict__ g, const T* __restrict__ v,
-                                  T* __restrict__ dg, T* __restrict__ dv, long long n) {
+                                  T* __restrict__ dg, T* __restrict__ dv, long long n, int width,
+                                  long long stride) {
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n / 4;
        i += (long long)gridDim.x * blockDim.x) {
     float d[4], gv[4], vv[4], og[4], ov[4];
+    const long long a = gv_off(4 * i, width, stride);
     load4(dh + 4 * i, d);
-    load4(g + 4 * i, gv);
-    load4(v + 4 * i, vv);
+    load4(g + a, gv);
+    load4(v + a, vv);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const float sig = 1.f / (1.f + expf(-gv[k]));
       ov[k] = d[k] * gv[k] * sig;
       og[k] = d[k] * vv[k] * sig * (1.f + gv[k] * (1.f - sig));
     }
-    store4(dg + 4 * i, og);
-    store4(dv + 4 * i, ov);
+    store4(dg + a, og);
+    store4(dv + a, ov);
   }
 }
 
@@ -230,12 +256,13 @@ cudaError_t fwd_t(const NormP& p, cudaStream_t st) {
   const Y* y = static_cast<const Y*>(p.y);
   const X* sc = static_cast<const X*>(p.scale);
   X* out = static_cast<X*>(p.out);
+  __nv_bfloat16* olp = static_cast<__nv_bfloat16*>(p.out_lp);
   switch (p.D / 128) {
-    case 1: add_rmsnorm_fwd_kernel<X, Y, 1><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, p.rstd, p.N, p.eps); break;
-    case 2: add_rmsnorm_fwd_kernel<X, Y, 2><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, p.rstd, p.N, p.eps); break;
-    case 4: add_rmsnorm_fwd_kernel<X, Y, 4><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, p.rstd, p.N, p.eps); break;
-    case 6: add_rmsnorm_fwd_kernel<X, Y, 6><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, p.rstd, p.N, p.eps); break;
-    case 8: add_rmsnorm_fwd_kernel<X, Y, 8><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, p.rstd, p.N, p.eps); break;
+    case 1: add_rmsnorm_fwd_kernel<X, Y, 1><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, olp, p.rstd, p.N, p.eps); break;
+    case 2: add_rmsnorm_fwd_kernel<X, Y, 2><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, olp, p.rstd, p.N, p.eps); break;
+    case 4: add_rmsnorm_fwd_kernel<X, Y, 4><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, olp, p.rstd, p.N, p.eps); break;
+    case 6: add_rmsnorm_fwd_kernel<X, Y, 6><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, olp, p.rstd, p.N, p.eps); break;
+    case 8: add_rmsnorm_fwd_kernel<X, Y, 8><<<grid, kNormWarps * 32, 0, st>>>(x, y, sc, out, olp, p.rstd, p.N, p.eps); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -245,17 +272,18 @@ template <typename X, typename Y>
 cudaError_t bwd_t(const NormP& p, cudaStream_t st) {
   const int grid = norm_grid(p.N, p.sms);
   const X* dout = static_cast<const X*>(p.dout);
+  const __nv_bfloat16* dlp = static_cast<const __nv_bfloat16*>(p.dout_lp);
   const X* x = static_cast<const X*>(p.x);
   const Y* y = static_cast<const Y*>(p.y);
   const X* sc = static_cast<const X*>(p.scale);
   X* dx = static_cast<X*>(p.dx);
   Y* dy = static_cast<Y*>(p.dy);
   switch (p.D / 128) {
-    case 1: add_rmsnorm_bwd_kernel<X, Y, 1><<<grid, kNormWarps * 32, 0, st>>>(dout, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
-    case 2: add_rmsnorm_bwd_kernel<X, Y, 2><<<grid, kNormWarps * 32, 0, st>>>(dout, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
-    case 4: add_rmsnorm_bwd_kernel<X, Y, 4><<<grid, kNormWarps * 32, 0, st>>>(dout, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
-    case 6: add_rmsnorm_bwd_kernel<X, Y, 6><<<grid, kNormWarps * 32, 0, st>>>(dout, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
-    case 8: add_rmsnorm_bwd_kernel<X, Y, 8><<<grid, kNormWarps * 32, 0, st>>>(dout, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
+    case 1: add_rmsnorm_bwd_kernel<X, Y, 1><<<grid, kNormWarps * 32, 0, st>>>(dout, dlp, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
+    case 2: add_rmsnorm_bwd_kernel<X, Y, 2><<<grid, kNormWarps * 32, 0, st>>>(dout, dlp, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
+    case 4: add_rmsnorm_bwd_kernel<X, Y, 4><<<grid, kNormWarps * 32, 0, st>>>(dout, dlp, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
+    case 6: add_rmsnorm_bwd_kernel<X, Y, 6><<<grid, kNormWarps * 32, 0, st>>>(dout, dlp, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
+    case 8: add_rmsnorm_bwd_kernel<X, Y, 8><<<grid, kNormWarps * 32, 0, st>>>(dout, dlp, x, y, sc, p.rstd, dx, dy, p.part, p.N); break;
     default: return cudaErrorInvalidValue;
   }
   cudaError_t e = cudaGetLastError();
@@ -288,16 +316,23 @@ cudaError_t launch_add_rmsnorm(const NormP& p, bool backward, cudaStream_t st) {
 }
 
 cudaError_t launch_swiglu(const void* g, const void* v, void* h, const void* dh, void* dg, void* dv,
-                          long long n, int dt, int sms, cudaStream_t st) {
+                          long long n, int width, long long stride, int dt, int sms, cudaStream_t st) {
   const long long want = (n / 4 + 255) / 256;
   const int grid = (int)(want < (long long)sms * 8 ? (want < 1 ? 1 : want) : (long long)sms * 8);
   if (dt == BOZO_DT_BF16) {
     using T = __nv_bfloat16;
-    if (dh) swiglu_bwd_kernel<T><<<grid, 256, 0, st>>>((const T*)dh, (const T*)g, (const T*)v, (T*)dg, (T*)dv, n);
-    else swiglu_fwd_kernel<T><<<grid, 256, 0, st>>>((const T*)g, (const T*)v, (T*)h, n);
+    if (dh)
+      swiglu_bwd_kernel<T><<<grid, 256, 0, st>>>((const T*)dh, (const T*)g, (const T*)v, (T*)dg, (T*)dv, n,
+                                                  width, stride);
+    else
+      swiglu_fwd_kernel<T><<<grid, 256, 0, st>>>((const T*)g, (const T*)v, (T*)h, n, width, stride);
   } else {
-    if (dh) swiglu_bwd_kernel<float><<<grid, 256, 0, st>>>((const float*)dh, (const float*)g, (const float*)v, (float*)dg, (float*)dv, n);
-    else swiglu_fwd_kernel<float><<<grid, 256, 0, st>>>((const float*)g, (const float*)v, (float*)h, n);
+    if (dh)
+      swiglu_bwd_kernel<float><<<grid, 256, 0, st>>>((const float*)dh, (const float*)g, (const float*)v,
+                                                      (float*)dg, (float*)dv, n, width, stride);
+    else
+      swiglu_fwd_kernel<float><<<grid, 256, 0, st>>>((const float*)g, (const float*)v, (float*)h, n, width,
+                                                      stride);
   }
   return cudaGetLastError();
 }

@@ -115,6 +115,20 @@ class RMSNorm(nn.Module):
             return block_ops.add_rms_norm(x, y, self.scale, self.eps)
         return self(x + y)
 
+    def forward_lin(self, x, y=None):
+        """``(out, lin)``: ``out = self(x + y)`` and the operand the
+        projections that read it take.  For an fp32 stream under bf16 autocast
+        ``lin`` is out rounded to bf16 by the same kernel (autocast would cast
+        it once per projection; its gradient returns into the kernel too);
+        otherwise ``lin`` is out."""
+        from . import block_ops
+        if (x.is_cuda and x.dtype == torch.float32 and torch.is_autocast_enabled("cuda")
+                and torch.get_autocast_dtype("cuda") == torch.bfloat16
+                and block_ops.norm_applies(x, y)):
+            return block_ops.add_rms_norm_lp(x, y, self.scale, self.eps)
+        out = self(x) if y is None else self.add_forward(x, y)
+        return out, out
+
     def wo_add_forward(self, x, msg, wo: nn.Linear, dropout: nn.Dropout):
         """``self(x + dropout(wo(msg)))``: without gradients and with an
         inactive dropout, one tensor-core kernel for the projection, the add
@@ -155,9 +169,21 @@ class MultiHeadCausalTensionLayer(nn.Module):
         self.tension_fn: Callable = ops.tension
 
     def project(self, x):
-        """q, k, v ``[B, T, H, HD]`` of ``x [B, T, D]`` (model.py:196-199)."""
+        """q, k, v ``[B, T, H, HD]`` of ``x [B, T, D]`` (model.py:196-199).  On
+        GPUs the projections run as one GEMM over the concatenated weights
+        (q, k, v are views of its output; the input gradient is one GEMM that
+        sums the three in its accumulator)."""
         B, T, D = x.shape
         H, HD = self.num_heads, self.head_dim
+        if x.is_cuda:
+            if self.rope_enabled:
+                w = torch.cat([self.wq.weight, self.wk.weight, self.wv.weight])
+                q, k, v = F.linear(x, w).split(D, dim=-1)
+                return q.view(B, T, H, HD), k.view(B, T, H, HD), v.view(B, T, H, HD)
+            w = torch.cat([self.wq.weight, self.wkv.weight])
+            q, kv = F.linear(x, w).split([D, 2 * D], dim=-1)
+            k, v = kv.view(B, T, H, 2 * HD).split(HD, dim=-1)
+            return q.view(B, T, H, HD), k, v
         q = self.wq(x).view(B, T, H, HD)
         if self.rope_enabled:
             k = self.wk(x).view(B, T, H, HD)
@@ -167,29 +193,42 @@ class MultiHeadCausalTensionLayer(nn.Module):
             k, v = kv.split(HD, dim=-1)
         return q, k, v
 
-    def forward(self, x, return_tensions: bool = False, tau_bias=None):
+    def forward(self, x, return_tensions: bool = False, tau_bias=None, x_lin=None,
+                want_lin: bool = False):
+        """``x_lin``: the operand the projections read (``RMSNorm.forward_lin``;
+        default x).  ``want_lin``: the output is the pair ``(out, lin)`` of
+        ``RMSNorm.forward_lin`` instead of out."""
         B, T, D = x.shape
-        q, k, v = self.project(x)
+        q, k, v = self.project(x if x_lin is None else x_lin)
         rope = 10_000.0 if self.rope_enabled else None
+        tau = None
         if self.global_layer:
             res = self.tension_fn(q, k, v, window=None, scale=self.scale, rope_base=rope,
                                   rope_len=self.max_seq_len, bias=tau_bias,
                                   return_tau=return_tensions, normalize="mass",
                                   tau_window=self.local_window)
             msg, tau = res if return_tensions else (res, None)
-            out = self.norm.wo_add_forward(x, msg.reshape(B, T, D), self.wo, self.dropout)
-            return (out, tau) if return_tensions else out
-        if return_tensions:
+            drop_first = False
+        elif return_tensions:
             msg, tau = self.tension_fn(q, k, v, window=self.window, scale=self.scale,
                                        rope_base=rope, rope_len=self.max_seq_len,
                                        bias=tau_bias, return_tau=True, normalize="mass")
-            out = self.norm.wo_add_forward(x, msg.reshape(B, T, D), self.wo, self.dropout)
-            return out, tau
-        msg = self.tension_fn(q, k, v, window=self.window, scale=self.scale, rope_base=rope,
-                              rope_len=self.max_seq_len, bias=tau_bias, normalize="count")
-        if self.dropout.training and self.dropout.p > 0.0:  # dropout before wo here
-            return self.norm.add_forward(x, self.wo(self.dropout(msg).reshape(B, T, D)))
-        return self.norm.wo_add_forward(x, msg.reshape(B, T, D), self.wo, self.dropout)
+            drop_first = False
+        else:
+            msg = self.tension_fn(q, k, v, window=self.window, scale=self.scale, rope_base=rope,
+                                  rope_len=self.max_seq_len, bias=tau_bias, normalize="count")
+            drop_first = True  # model.py:261-263: dropout on msg, before wo
+        out = self._residual(x, msg.reshape(B, T, D), drop_first, want_lin)
+        return (out, tau) if return_tensions else out
+
+    def _residual(self, x, msg, drop_first: bool, want_lin: bool):
+        """norm(x + wo(msg)) with the branch's dropout placement."""
+        if want_lin:
+            y = self.wo(self.dropout(msg)) if drop_first else self.dropout(self.wo(msg))
+            return self.norm.forward_lin(x, y)
+        if drop_first and self.dropout.training and self.dropout.p > 0.0:
+            return self.norm.add_forward(x, self.wo(self.dropout(msg)))
+        return self.norm.wo_add_forward(x, msg, self.wo, self.dropout)
 
 
 class OscillatoryModulation(nn.Module):
@@ -221,10 +260,22 @@ class TensionFFN(nn.Module):
         self.norm = RMSNorm(cfg.dim)
         self.dropout = nn.Dropout(cfg.dropout)
 
-    def forward(self, x):
+    def forward(self, x, x_lin=None):
+        """``x_lin``: the operand the gate/value projections read (default x).
+        On GPUs they run as one GEMM over the concatenated weights and SwiGLU
+        reads its packed ``[g | v]`` rows."""
         from . import block_ops
-        g, v = self.gate(x), self.val(x)
-        h = block_ops.swiglu(g, v) if block_ops.swiglu_applies(g, v) else F.silu(g) * v
+        inp = x if x_lin is None else x_lin
+        if inp.is_cuda:
+            gv = F.linear(inp, torch.cat([self.gate.weight, self.val.weight]))
+            if block_ops.swiglu_packed_applies(gv):
+                h = block_ops.swiglu_packed(gv)
+            else:
+                g, v = gv.chunk(2, dim=-1)
+                h = F.silu(g) * v
+        else:
+            g, v = self.gate(inp), self.val(inp)
+            h = block_ops.swiglu(g, v) if block_ops.swiglu_applies(g, v) else F.silu(g) * v
         return self.norm.add_forward(x, self.dropout(self.proj(h)))
 
 
@@ -244,11 +295,16 @@ class TensionBlock(nn.Module):
         return self.oscillate(x) if self.oscillate is not None else x
 
     def forward(self, x, return_tensions: bool = False, tau_bias=None):
-        h = self.pre_norm(x)
-        if return_tensions:
-            h, tau = self.tension(h, return_tensions=True, tau_bias=tau_bias)
-            return self.ffn(self._osc(h)), tau
-        return self.ffn(self._osc(self.tension(h, tau_bias=tau_bias)))
+        h, h_lin = self.pre_norm.forward_lin(x)
+        # the FFN's projections read a bf16 copy of the layer output unless the
+        # oscillation sits between them
+        want = self.oscillate is None
+        res = self.tension(h, return_tensions=return_tensions, tau_bias=tau_bias, x_lin=h_lin,
+                           want_lin=want)
+        out, tau = res if return_tensions else (res, None)
+        o, o_lin = out if want else (self._osc(out), None)
+        y = self.ffn(o, x_lin=o_lin)
+        return (y, tau) if return_tensions else y
 
 
 class TensionLM(nn.Module):
@@ -310,8 +366,8 @@ class TensionLM(nn.Module):
                 tensions.append(tau)
             else:
                 x = block(x, tau_bias=bias)
-        hidden = self.final_norm(x)
-        logits = self.lm_head(hidden)
+        hidden, hidden_lin = self.final_norm.forward_lin(x)
+        logits = self.lm_head(hidden_lin)
         if return_all:
             return logits, hidden, tensions
         return logits

@@ -52,6 +52,12 @@ typedef struct {
   void* d_scale;          /* backward: [width], x's dtype */
   void* workspace;        /* backward: bozo_add_rmsnorm_workspace() bytes */
   size_t workspace_bytes;
+  /* Optional, fp32 x only: the forward also writes out rounded to bf16 here
+   * (what bf16 autocast would cast out to for the projections that read it,
+   * made once), and the backward adds this bf16 cotangent of that copy to
+   * d_out.  NULL: not used. */
+  void* out_lp;           /* forward: [rows, width] bf16 */
+  const void* d_out_lp;   /* backward: [rows, width] bf16 */
 } bozo_add_rmsnorm_args;
 
 size_t bozo_add_rmsnorm_workspace(const bozo_add_rmsnorm_args* args);
@@ -67,6 +73,13 @@ typedef struct {
   const void* d_out;      /* backward */
   void* d_gate;
   void* d_value;
+  /* 0: gate/value/d_gate/d_value are flat like out.  Otherwise out holds
+   * rows of `width` elements (n / width rows, width a multiple of 4) and the
+   * other four hold rows of `width` elements `row_stride` elements apart
+   * (row_stride a multiple of 4) — e.g. the two halves of one GEMM's packed
+   * [gate | value] rows: value = gate + width, row_stride = 2·width. */
+  int64_t width;
+  int64_t row_stride;
 } bozo_swiglu_args;
 
 int bozo_swiglu_fwd(const bozo_swiglu_args* args, void* stream);

@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol():
     assert set(declared) == set(_capi.EXPORTED)
     for name in declared:
         assert hasattr(lib, name), name
-    assert lib.bozo_tension_abi_version() == 5
+    assert lib.bozo_tension_abi_version() == 6
     assert _capi.status_string(0) == "ok"
 
 
@@ -75,11 +75,13 @@ int main(void) {
   O(bozo_tension_decode_args, tau_dtype);
   S(bozo_add_rmsnorm_args); O(bozo_add_rmsnorm_args, eps); O(bozo_add_rmsnorm_args, y_dtype);
   O(bozo_add_rmsnorm_args, scale); O(bozo_add_rmsnorm_args, d_scale);
-  O(bozo_add_rmsnorm_args, workspace_bytes);
+  O(bozo_add_rmsnorm_args, workspace_bytes); O(bozo_add_rmsnorm_args, out_lp);
+  O(bozo_add_rmsnorm_args, d_out_lp);
   S(bozo_wo_add_rmsnorm_args); O(bozo_wo_add_rmsnorm_args, eps); O(bozo_wo_add_rmsnorm_args, msg);
   O(bozo_wo_add_rmsnorm_args, x_dtype); O(bozo_wo_add_rmsnorm_args, scale);
   O(bozo_wo_add_rmsnorm_args, rstd);
   S(bozo_swiglu_args); O(bozo_swiglu_args, gate); O(bozo_swiglu_args, d_value);
+  O(bozo_swiglu_args, width); O(bozo_swiglu_args, row_stride);
   S(bozo_cross_entropy_args); O(bozo_cross_entropy_args, logits_dtype);
   O(bozo_cross_entropy_args, targets); O(bozo_cross_entropy_args, d_logits);
   S(bozo_graph_bias_args); O(bozo_graph_bias_args, alpha); O(bozo_graph_bias_args, ctx_content);

@@ -212,3 +212,48 @@ def test_wo_norm_gating_on_cpu(monkeypatch):
         assert block_ops._wo_width_ok(D, f32) and block_ops._wo_width_ok(D, bf), D
     assert block_ops._wo_width_ok(2048, bf) and not block_ops._wo_width_ok(2048, f32)
     assert not block_ops._wo_width_ok(96, f32) and not block_ops._wo_width_ok(4096, bf)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("D", [768, 1024])
+@pytest.mark.parametrize("with_y", [False, True])
+def test_add_rms_norm_lp_is_the_norm_and_its_bf16_copy(D, with_y):
+    g = torch.Generator().manual_seed(D + with_y)
+    dev = torch.device("cuda:0")
+    x = (torch.randn(2, 333, D, generator=g) * 2).to(dev)
+    y = torch.randn(2, 333, D, generator=g).to(dev, torch.bfloat16) if with_y else None
+    scale = (1 + 0.1 * torch.randn(D, generator=g)).to(dev)
+    d_out = torch.randn(2, 333, D, generator=g).to(dev)
+    d_lp = torch.randn(2, 333, D, generator=g).to(dev, torch.bfloat16)
+    leaves = [t.clone().requires_grad_(True) if t is not None else None for t in (x, y, scale)]
+    ref_leaves = [t.clone().requires_grad_(True) if t is not None else None for t in (x, y, scale)]
+    out, out_lp = block_ops.add_rms_norm_lp(leaves[0], leaves[1], leaves[2], 1e-6)
+    ref = block_ops.add_rms_norm(ref_leaves[0], ref_leaves[1], ref_leaves[2], 1e-6)
+    assert torch.equal(out, ref)
+    assert out_lp.dtype == torch.bfloat16 and torch.equal(out_lp, ref.to(torch.bfloat16))
+    torch.autograd.backward((out, out_lp), (d_out, d_lp))
+    ref.backward(d_out + d_lp.float())
+    for a, b in zip(leaves, ref_leaves):
+        if a is not None:
+            assert torch.equal(a.grad, b.grad)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_swiglu_packed_matches_two_tensor_swiglu(dtype):
+    g = torch.Generator().manual_seed(3)
+    dev = torch.device("cuda:0")
+    gv = torch.randn(4, 100, 2 * 2304, generator=g).to(dev, dtype)
+    dh = torch.randn(4, 100, 2304, generator=g).to(dev, dtype)
+    a = gv.clone().requires_grad_(True)
+    gg, vv = (t.clone().requires_grad_(True) for t in gv.chunk(2, dim=-1))
+    h = block_ops.swiglu_packed(a)
+    ref = block_ops.swiglu(gg.contiguous(), vv.contiguous())
+    assert torch.equal(h, ref)
+    h.backward(dh)
+    ref.backward(dh)
+    assert torch.equal(a.grad, torch.cat([gg.grad, vv.grad], dim=-1))
+
+
+def test_packed_swiglu_gating_on_cpu():
+    assert not block_ops.swiglu_packed_applies(torch.randn(4, 16))

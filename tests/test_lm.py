@@ -151,6 +151,15 @@ def test_harness_bf16_autocast_tensor_core_path(golden_lm):
     assert abs(float(loss.detach()) - float(case["loss"])) < 2e-2
     for i, t in enumerate(tensions):
         assert np.abs(t.detach().float().cpu().numpy() - case[f"tau{i}"]).max() < 3e-2
+    # gradients through the packed projections and the norms' bf16 side
+    # outputs (their cotangents summed in the norm backward) against the
+    # reference model's fp32 gradients, to bf16 accuracy
+    params = dict(m.named_parameters())
+    for k in case:
+        if k.startswith("grad."):
+            got = params[k[5:]].grad.detach().float().cpu().numpy()
+            scale = np.abs(case[k]).max()
+            assert np.abs(got - case[k]).max() <= 5e-2 * scale, k
 
 
 # ───────────────────────── DDP over gloo (CPU) ─────────────────────────
