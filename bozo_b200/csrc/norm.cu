@@ -169,9 +169,9 @@ __global__ void __launch_bounds__(kNormWarps * 32)
 
 // dscale[c] = Σ_blocks part[b][c] in a fixed order (deterministic): one CTA
 // per 32 columns, lane = column (each warp reads whole 128-byte rows), warp w
-// sums blocks w, w + 8, … in four interleaved chains, then the eight warp
-// sums are added in warp order.
-constexpr int kReduceWarps = 8;
+// sums blocks w, w + 32, … in four interleaved chains, then the 32 warp sums
+// are added in warp order.
+constexpr int kReduceWarps = 32;
 template <typename X>
 __global__ void __launch_bounds__(kReduceWarps * 32)
     dscale_reduce_kernel(const float* __restrict__ part, int nblk, int D, X* __restrict__ dscale) {
