@@ -259,19 +259,20 @@ def run_ours(args, rank, world, local_rank):
 
     # ── e2e: public API, pinned host buffers in, results out, every step ──
     # Step i copies its inputs in on a copy stream (into one of two device
-    # input sets), runs fwd+bwd on the compute stream and reads out, results
-    # back on a second copy stream; stream events order the three, so step
-    # i+1's upload overlaps step i's compute and read-out (PCIe is full duplex).
+    # input sets) while the compute stream runs step i−1's fwd+bwd and reads
+    # its results back; stream events order them, so each upload overlaps the
+    # previous step's compute and read-out (the link is full duplex).  The
+    # read-out is queued on the compute stream itself: the results' memory is
+    # then free for the next step as soon as their copies are, with no
+    # cross-stream hold on the allocator's blocks.
     hq, hk, hv, hdo = [x.pin_memory() for x in (hq, hk, hv, hdo)]
     outs_h = [[torch.empty(B, T, H, HD, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
               for _ in range(2)]
     ins_d = [[torch.empty(B, T, H, HD, dtype=torch.bfloat16, device=dev) for _ in range(4)]
              for _ in range(2)]
-    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    s_in = torch.cuda.Stream(dev)
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_used = [torch.cuda.Event() for _ in range(2)]   # compute done reading input set
-    ev_done = [torch.cuda.Event() for _ in range(2)]   # compute results ready
-    ev_out = [torch.cuda.Event() for _ in range(2)]    # read-out of host set finished
 
     def e2e_step(i):
         sl = i & 1
@@ -285,15 +286,8 @@ def run_ours(args, rank, world, local_rank):
         qq, kk, vv, dd = [x.detach().requires_grad_(j < 3) for j, x in enumerate(ins_d[sl])]
         out, gq, gk, gv = step(W_HEAD, qq, kk, vv, dd)
         ev_used[sl].record(stream)
-        ev_done[sl].record(stream)
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(ev_done[sl])
-            if i >= 2:
-                s_out.wait_event(ev_out[sl])
-            for dst, src in zip(outs_h[sl], (out, gq, gk, gv)):
-                src.record_stream(s_out)
-                dst.copy_(src.detach(), non_blocking=True)
-            ev_out[sl].record(s_out)
+        for dst, src in zip(outs_h[sl], (out, gq, gk, gv)):
+            dst.copy_(src.detach(), non_blocking=True)
 
     for i in range(args.warmup):
         e2e_step(i)
@@ -304,7 +298,6 @@ def run_ours(args, rank, world, local_rank):
     s_in.wait_stream(stream)
     for i in range(args.steps):
         e2e_step(i)
-    stream.wait_stream(s_out)
     s1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = maxred(s0.elapsed_time(s1)) / args.steps
