@@ -94,6 +94,21 @@ def preset_350m_prefill(**over) -> TensionConfig:
     return TensionConfig(**cfg)
 
 
+def _packed_weight(owner: nn.Module, name: str, weights):
+    """``torch.cat(weights)`` — the weight of one GEMM standing for several
+    projections.  Without autograd (prefill, decoding, evaluation) the
+    concatenation is kept on ``owner`` until one of the weights changes
+    (storage or version counter), so a decode step does not re-copy it."""
+    if torch.is_grad_enabled() and any(w.requires_grad for w in weights):
+        return torch.cat(weights)
+    key = tuple((w.data_ptr(), w._version, w.dtype) for w in weights)
+    cached = owner.__dict__.get(name)
+    if cached is None or cached[0] != key:
+        cached = (key, torch.cat([w.detach() for w in weights]))
+        owner.__dict__[name] = cached
+    return cached[1]
+
+
 class RMSNorm(nn.Module):
     """model.py:86-98."""
 
@@ -177,10 +192,10 @@ class MultiHeadCausalTensionLayer(nn.Module):
         H, HD = self.num_heads, self.head_dim
         if x.is_cuda:
             if self.rope_enabled:
-                w = torch.cat([self.wq.weight, self.wk.weight, self.wv.weight])
+                w = _packed_weight(self, "_qkv_cat", (self.wq.weight, self.wk.weight, self.wv.weight))
                 q, k, v = F.linear(x, w).split(D, dim=-1)
                 return q.view(B, T, H, HD), k.view(B, T, H, HD), v.view(B, T, H, HD)
-            w = torch.cat([self.wq.weight, self.wkv.weight])
+            w = _packed_weight(self, "_qkv_cat", (self.wq.weight, self.wkv.weight))
             q, kv = F.linear(x, w).split([D, 2 * D], dim=-1)
             k, v = kv.view(B, T, H, 2 * HD).split(HD, dim=-1)
             return q.view(B, T, H, HD), k, v
@@ -267,7 +282,7 @@ class TensionFFN(nn.Module):
         from . import block_ops
         inp = x if x_lin is None else x_lin
         if inp.is_cuda:
-            gv = F.linear(inp, torch.cat([self.gate.weight, self.val.weight]))
+            gv = F.linear(inp, _packed_weight(self, "_gv_cat", (self.gate.weight, self.val.weight)))
             if block_ops.swiglu_packed_applies(gv):
                 h = block_ops.swiglu_packed(gv)
             else:
