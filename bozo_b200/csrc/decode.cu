@@ -128,12 +128,18 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(DecodeP p) {
 // ─────────────── vector path: caches of one dtype E, HD ∈ {32, 64, 128} ───────────────
 // Steps 2 and 4 with whole-row vector loads: G = HD·sizeof(E)/16 lanes share
 // one cached key row (one 16-byte load each), so a warp scores 32/G keys per
-// load and two key groups are in flight per iteration; for the values each
+// load and four key groups are in flight per iteration; for the values each
 // warp accumulates Σ τ·v over its share of the keys with each lane holding
-// HD/32 consecutive dimensions (coalesced row loads, 4 keys in flight), and
-// the 8 warps' partial sums are added in shared memory.
-constexpr int kFastThreads = 256;
-constexpr int kFastWarps = kFastThreads / 32;
+// HD/32 consecutive dimensions (coalesced row loads, 8 keys in flight), and
+// the warps' partial sums are added in shared memory.  The ring slot of each
+// key comes from one division per CTA and a conditional wrap, and the
+// sigmoid runs once per key over all threads after the dot products (not in
+// one lane of G).  At B16 H12 with 1001 cached keys this took the kernel
+// from 33.7 to 17.3 µs (16 warps per CTA for long caches: two CTAs per SM
+// fit in the register file, so all 192 CTAs run in one wave; 32 warps gave
+// 21.4 µs), and a 64-key window from 5.5 to 4.8 µs.
+constexpr int kFastWarps = 8;
+constexpr int kWideWarps = 16;
 
 template <typename E> struct DecVec;
 template <> struct DecVec<float> { static constexpr int n = 4; };
@@ -163,15 +169,15 @@ __device__ __forceinline__ void dec_load(const E* p, float* x) {
   for (int k = 0; k < N; ++k) x[k] = dec_f(e[k]);
 }
 
-template <typename E, int HD>
-__global__ void __launch_bounds__(kFastThreads) decode_kernel_vec(DecodeP p) {
+template <typename E, int HD, int kW>
+__global__ void __launch_bounds__(kW * 32) decode_kernel_vec(DecodeP p) {
   constexpr int NV = DecVec<E>::n, G = HD / NV, KPW = 32 / G, DPL = HD / 32;
   static_assert(HD % NV == 0 && G <= 32 && (G & (G - 1)) == 0, "lanes per key");
   extern __shared__ float sm[];
   float* sq = sm;                      // rotated q [HD]
   float* part = sm + HD;               // per-warp Σ τ·v [warps][HD]
-  float* stau = part + kFastWarps * HD;  // τ per key [n]
-  __shared__ float red[kFastWarps];
+  float* stau = part + kW * HD;  // τ per key [n]
+  __shared__ float red[kW];
   const int b = blockIdx.x / p.H, h = blockIdx.x - b * p.H;
   const int half = HD / 2;
   const int t = __ldg(p.pos);
@@ -210,55 +216,70 @@ __global__ void __launch_bounds__(kFastThreads) decode_kernel_vec(DecodeP p) {
   const bool local = p.mode == BOZO_MODE_LOCAL;
   const int n = local ? min(t, p.W) : min(t + 1, p.C);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane % G, sub = lane / G;
+  // ring slot of key j (0 = the newest key): one division per CTA, then a
+  // conditional wrap (j < n ≤ C, so at most one)
+  const int s_top = max(local ? t - 1 : t, 0) % p.C;
+  const long long row0 = ((long long)b * p.C * p.H + h) * HD, rstride = (long long)p.H * HD;
   auto key_row = [&](int j) {
-    const int s = local ? t - 1 - j : t - j;
-    return (((long long)b * p.C + (s % p.C)) * p.H + h) * HD;
+    int s = s_top - j;
+    s += s < 0 ? p.C : 0;
+    return row0 + s * rstride;
   };
-  // 2. scores: keys j = j0 + sub, two groups per iteration
+  // 2. scores (scaled dot products) into stau: keys j = j0 + sub, four
+  // groups per iteration
   float qv[NV];
 #pragma unroll
   for (int k = 0; k < NV; ++k) qv[k] = sq[g * NV + k];
-  constexpr int kStep = kFastWarps * KPW;
-  for (int j0 = warp * KPW; j0 < n; j0 += 2 * kStep) {
-    const int ja = j0 + sub, jb = j0 + kStep + sub;
-    float xa[NV], xb[NV];
-    if (ja < n) dec_load<E, NV>(kc + key_row(ja) + g * NV, xa);
-    else
+  constexpr int kStep = kW * KPW;
+  constexpr int kGroups = 4;  // key groups in flight per iteration
+  for (int j0 = warp * KPW; j0 < n; j0 += kGroups * kStep) {
+    float x[kGroups][NV];
 #pragma unroll
-      for (int k = 0; k < NV; ++k) xa[k] = 0.f;
-    if (jb < n) dec_load<E, NV>(kc + key_row(jb) + g * NV, xb);
-    else
+    for (int u = 0; u < kGroups; ++u) {
+      const int jj = j0 + u * kStep + sub;
+      if (jj < n) {
+        dec_load<E, NV>(kc + key_row(jj) + g * NV, x[u]);
+      } else {
 #pragma unroll
-      for (int k = 0; k < NV; ++k) xb[k] = 0.f;
-    float da = 0.f, db = 0.f;
-#pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      da = fmaf(qv[k], xa[k], da);
-      db = fmaf(qv[k], xb[k], db);
+        for (int k = 0; k < NV; ++k) x[u][k] = 0.f;
+      }
     }
+    float d[kGroups];
 #pragma unroll
-    for (int o = G / 2; o > 0; o >>= 1) {
-      da += __shfl_xor_sync(0xffffffffu, da, o);
-      db += __shfl_xor_sync(0xffffffffu, db, o);
+    for (int u = 0; u < kGroups; ++u) {
+      d[u] = 0.f;
+#pragma unroll
+      for (int k = 0; k < NV; ++k) d[u] = fmaf(qv[k], x[u][k], d[u]);
+#pragma unroll
+      for (int o = G / 2; o > 0; o >>= 1) d[u] += __shfl_xor_sync(0xffffffffu, d[u], o);
     }
     if (g == 0) {
-      if (ja < n) stau[ja] = sigmoid_exact(da * p.inv_scale);
-      if (jb < n) stau[jb] = sigmoid_exact(db * p.inv_scale);
+#pragma unroll
+      for (int u = 0; u < kGroups; ++u) {
+        const int jj = j0 + u * kStep + sub;
+        if (jj < n) stau[jj] = d[u] * p.inv_scale;
+      }
     }
   }
   __syncthreads();
 
-  // 3. normaliser
+  // 3. τ = σ(score), one key per thread (not one lane in G), and the
+  // normaliser
+  float m = 0.f;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const float tau = sigmoid_exact(stau[j]);
+    stau[j] = tau;
+    m += tau;
+  }
+  __syncthreads();
   float den = 1.f;
   if (p.norm == BOZO_NORM_MASS) {
-    float m = 0.f;
-    for (int j = threadIdx.x; j < n; j += blockDim.x) m += stau[j];
     m = warp_sum(m);
     if (lane == 0) red[warp] = m;
     __syncthreads();
     m = 0.f;
 #pragma unroll
-    for (int w = 0; w < kFastWarps; ++w) m += red[w];
+    for (int w = 0; w < kW; ++w) m += red[w];
     den = fmaxf(m, kMassEps);
   } else if (p.norm == BOZO_NORM_COUNT) {
     den = (float)max(n, 1);
@@ -268,20 +289,21 @@ __global__ void __launch_bounds__(kFastThreads) decode_kernel_vec(DecodeP p) {
   float acc[DPL];
 #pragma unroll
   for (int k = 0; k < DPL; ++k) acc[k] = 0.f;
+  constexpr int kRowsInFlight = 8;
   int j = warp;
-  for (; j + 3 * kFastWarps < n; j += 4 * kFastWarps) {
-    float v0[DPL], v1[DPL], v2[DPL], v3[DPL];
-    dec_load<E, DPL>(vc + key_row(j) + lane * DPL, v0);
-    dec_load<E, DPL>(vc + key_row(j + kFastWarps) + lane * DPL, v1);
-    dec_load<E, DPL>(vc + key_row(j + 2 * kFastWarps) + lane * DPL, v2);
-    dec_load<E, DPL>(vc + key_row(j + 3 * kFastWarps) + lane * DPL, v3);
-    const float t0 = stau[j], t1 = stau[j + kFastWarps], t2 = stau[j + 2 * kFastWarps],
-                t3 = stau[j + 3 * kFastWarps];
+  for (; j + (kRowsInFlight - 1) * kW < n; j += kRowsInFlight * kW) {
+    float v[kRowsInFlight][DPL];
 #pragma unroll
-    for (int k = 0; k < DPL; ++k)
-      acc[k] = fmaf(t3, v3[k], fmaf(t2, v2[k], fmaf(t1, v1[k], fmaf(t0, v0[k], acc[k]))));
+    for (int r = 0; r < kRowsInFlight; ++r)
+      dec_load<E, DPL>(vc + key_row(j + r * kW) + lane * DPL, v[r]);
+#pragma unroll
+    for (int r = 0; r < kRowsInFlight; ++r) {
+      const float tr = stau[j + r * kW];
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) acc[k] = fmaf(tr, v[r][k], acc[k]);
+    }
   }
-  for (; j < n; j += kFastWarps) {
+  for (; j < n; j += kW) {
     float v0[DPL];
     dec_load<E, DPL>(vc + key_row(j) + lane * DPL, v0);
     const float t0 = stau[j];
@@ -296,7 +318,7 @@ __global__ void __launch_bounds__(kFastThreads) decode_kernel_vec(DecodeP p) {
   for (int d = threadIdx.x; d < HD; d += blockDim.x) {
     float o = 0.f;
 #pragma unroll
-    for (int w = 0; w < kFastWarps; ++w) o += part[w * HD + d];
+    for (int w = 0; w < kW; ++w) o += part[w * HD + d];
     stf(p.out, oo + d, p.out_dt, o * inv_den);
   }
   if (p.tau) {
@@ -310,18 +332,23 @@ __global__ void __launch_bounds__(kFastThreads) decode_kernel_vec(DecodeP p) {
 
 template <typename E>
 cudaError_t launch_vec(const DecodeP& p, size_t smem, cudaStream_t st) {
+  // a long cache (global layers, wide windows) gets 32 warps per (b, h):
+  // four times the loads in flight per step of its short dependent chain
+  const bool wide = (p.mode == BOZO_MODE_GLOBAL ? p.C : p.W) > 256;
+  const int threads = (wide ? kWideWarps : kFastWarps) * 32;
   auto go = [&](auto kern) {
     if (smem > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
     }
-    kern<<<p.B * p.H, kFastThreads, smem, st>>>(p);
+    kern<<<p.B * p.H, threads, smem, st>>>(p);
     return cudaGetLastError();
   };
   switch (p.HD) {
-    case 32: return go(decode_kernel_vec<E, 32>);
-    case 64: return go(decode_kernel_vec<E, 64>);
-    default: return go(decode_kernel_vec<E, 128>);
+    case 32: return wide ? go(decode_kernel_vec<E, 32, kWideWarps>) : go(decode_kernel_vec<E, 32, kFastWarps>);
+    case 64: return wide ? go(decode_kernel_vec<E, 64, kWideWarps>) : go(decode_kernel_vec<E, 64, kFastWarps>);
+    default:
+      return wide ? go(decode_kernel_vec<E, 128, kWideWarps>) : go(decode_kernel_vec<E, 128, kFastWarps>);
   }
 }
 
@@ -336,7 +363,7 @@ bool vec_path_ok(const DecodeP& p) {
 
 size_t decode_smem_bytes(const DecodeP& p) {
   const int n = p.mode == BOZO_MODE_LOCAL ? p.W : p.C;
-  if (vec_path_ok(p)) return (size_t)(p.HD * (1 + kFastWarps) + n) * sizeof(float);
+  if (vec_path_ok(p)) return (size_t)(p.HD * (1 + kWideWarps) + n) * sizeof(float);
   return (size_t)(p.HD + n) * sizeof(float);
 }
 
