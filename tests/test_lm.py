@@ -230,3 +230,21 @@ def test_ddp_step_equals_averaged_half_batch_gradients(tmp_path):
     for k in r0:
         torch.testing.assert_close(r0[k], ref[k], rtol=1e-5, atol=1e-6, msg=k)
     assert not math.isnan(float(sum(v.float().sum() for v in r0.values())))
+
+
+def test_packed_weight_cache_follows_the_weights():
+    """Without autograd the concatenated projection weight is reused until a
+    weight changes; with autograd it is built fresh (and differentiable)."""
+    lin = torch.nn.Linear(4, 4, bias=False)
+    owner = torch.nn.Module()
+    ws = (lin.weight, lin.weight)
+    with torch.no_grad():
+        a = lm._packed_weight(owner, "_cat", ws)
+        b = lm._packed_weight(owner, "_cat", ws)
+        assert a is b and torch.equal(a, torch.cat(ws))
+        lin.weight.add_(1.0)  # in-place update bumps the version counter
+        c = lm._packed_weight(owner, "_cat", ws)
+        assert c is not a and torch.equal(c, torch.cat(ws))
+    d = lm._packed_weight(owner, "_cat", ws)
+    assert d.requires_grad and d is not c
+    assert "_cat" not in owner.state_dict()
