@@ -293,7 +293,9 @@ int bozo_tension_fwd(const bozo_tension_fwd_args* a, void* stream) {
   return BOZO_OK;
 }
 
-size_t bozo_tension_bwd_workspace(const bozo_tension_bwd_args* a) {
+// The workspace every backward needs (coefficient planes, a bf16 copy of an
+// fp32 cotangent); the key-tile path's optional dSᵀ scratch follows it.
+static size_t bwd_base_bytes(const bozo_tension_bwd_args* a) {
   if (!a || a->B <= 0 || a->T <= 0 || a->H <= 0) return 0;
   // three per-query-row coefficient planes (five with a per-row τ
   // cotangent); rows padded to a multiple of 128 so a 128-row slice starts
@@ -306,6 +308,18 @@ size_t bozo_tension_bwd_workspace(const bozo_tension_bwd_args* a) {
   if (a->d_out.dtype == BOZO_DT_F32 && a->q.dtype == BOZO_DT_BF16 && a->HD > 0)
     bytes += round256((size_t)a->B * a->T * a->H * a->HD * 2);
   return bytes;
+}
+
+// The dSᵀ scratch of the key-tile backward (global block, windows > 128,
+// bf16 HD 64): with it the dQ pass multiplies stored dSᵀ tiles by K instead
+// of recomputing S, dP and the element math.
+static size_t bwd_ds_bytes(const bozo_tension_bwd_args* a) {
+  if (!a || a->HD != 64 || a->q.dtype != BOZO_DT_BF16 || a->path == BOZO_PATH_SIMT) return 0;
+  return round256(tc_global_ds_bytes(a->B, a->T, a->H, a->mode, a->window));
+}
+
+size_t bozo_tension_bwd_workspace(const bozo_tension_bwd_args* a) {
+  return bwd_base_bytes(a) + bwd_ds_bytes(a);
 }
 
 int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
@@ -324,7 +338,7 @@ int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
   for (int i = 0; i < 3; ++i)
     if (!dtype_ok(a->grad_dtype[i])) return BOZO_ERR_BAD_DTYPE;
   if (a->d_tau && !dtype_ok(a->d_tau_dtype)) return BOZO_ERR_BAD_DTYPE;
-  const size_t need = bozo_tension_bwd_workspace(a);
+  const size_t need = bwd_base_bytes(a);
   if (need && (!a->workspace || a->workspace_bytes < need)) return BOZO_ERR_WORKSPACE;
 
   DeviceRestore restore;
@@ -353,6 +367,9 @@ int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
   p.coef = static_cast<float*>(a->workspace);
   if (a->d_out.dtype == BOZO_DT_F32 && a->q.dtype == BOZO_DT_BF16)
     p.dout_lp = static_cast<char*>(a->workspace) + round256(rows * sizeof(float)) * (a->aux_row ? 5 : 3);
+  // the dSᵀ scratch when the caller's workspace holds it (else dQ recomputes)
+  const size_t ds = bwd_ds_bytes(a);
+  if (ds && a->workspace_bytes >= need + ds) p.ds_scratch = static_cast<char*>(a->workspace) + need;
   p.err = error_word(&e);
   if (!p.err) return cuda_fail(e);
 
@@ -380,7 +397,7 @@ int bozo_tension_bwd(const bozo_tension_bwd_args* a, void* stream) {
 int bozo_tension_bwd_noalloc(const bozo_tension_bwd_args* a, void* stream) {
   if (!a) return BOZO_ERR_NULL;
   if (!a->q.ptr) return BOZO_ERR_NULL;
-  if (bozo_tension_bwd_workspace(a) > (size_t)BOZO_NOALLOC_SCRATCH_BYTES)
+  if (bwd_base_bytes(a) > (size_t)BOZO_NOALLOC_SCRATCH_BYTES)
     return BOZO_ERR_SCRATCH_LIMIT;
   // the scratch address is per device: take it with the data's device current
   DeviceRestore restore;

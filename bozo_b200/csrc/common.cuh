@@ -68,6 +68,7 @@ struct BwdP {
   float* beta;   // [B,H,T] workspace
   float* coef;   // [3][B·H, Tpad] workspace (tensor-core path)
   void* dout_lp;  // workspace room for a bf16 copy of an fp32 dO (tensor-core path) or null
+  void* ds_scratch;  // key-tile path: dSᵀ tiles stored by DKV for the dQ pass, or null
   int qk_rotated;  // q, k are RoPE-rotated already
   const float* aux_row;  // [3][B·H·T] per-row τ cotangent (a1, a0, inv_d) or null
   int* err;

@@ -21,6 +21,9 @@ bool tc_global_fwd_eligible(const FwdP& p);
 cudaError_t launch_tc_global_fwd(const FwdP& p, cudaStream_t st, int* launches);
 bool tc_global_bwd_eligible(const BwdP& p);
 cudaError_t launch_tc_global_bwd(const BwdP& p, cudaStream_t st, int* launches);
+// Bytes of the dSᵀ scratch that lets the key-tile backward skip recomputing
+// S and dP for dQ (0 when the key-tile kernels do not serve the shape).
+size_t tc_global_ds_bytes(int B, int T, int H, int mode, int W);
 
 // Bounded-wait self-test kernel (wait_selftest.cu): one wait on an mbarrier
 // nothing arrives on, limited to limit_ns; result (device int[4] or null).

@@ -26,8 +26,13 @@
 // double-buffered in shared memory, and the accumulators double-buffered in
 // TMEM per unit, so the MMA of sub-step n+1 overlaps the epilogue of n and a
 // unit's output overlaps the next unit.  dQ is computed per query tile by its
-// own kernel (recomputing S and dP) so no partial sums leave an SM and no
-// atomics are needed.  Units are dealt to persistent CTAs heaviest first.
+// own kernel so no partial sums leave an SM and no atomics are needed.  When
+// the caller's workspace has room for it, DKV also stores each dSᵀ tile it
+// formed (bf16, [128 keys × 64 queries], by TMA from the tile the dK MMA
+// reads) and the dQ kernel is a pure MMA pass over them (role DQS):
+//   DQS   (none)          K_i, dSᵀ(i,j) halves   —                      dQ += dS·K_h
+// instead of recomputing S, dP and the element math (role DQ).  Units are
+// dealt to persistent CTAs heaviest first.
 //
 // Warps: 0 TMA; 1 MMA (one thread); 2,3,12,13 output (TMEM accumulators →
 // bf16 tile in the dead outer slot → TMA store); 4-11 epilogue.  Every
@@ -51,15 +56,17 @@ constexpr int kCoefBytes = 3 * kTile * 4;   // α/2, α·c, β·c of 128 query r
 constexpr int kThreads = 14 * 32;
 constexpr int kErrG = 0x300;
 
-enum Role : int { kFwd = 0, kDKV = 1, kDQ = 2 };
+enum Role : int { kFwd = 0, kDKV = 1, kDQ = 2, kDQS = 3 };
 
 template <int R>
 struct Traits {
-  static constexpr int kOuterTiles = R == kFwd ? 1 : 2;
+  // DQS keeps one outer slot per unit only as the dQ staging tile
+  static constexpr int kOuterTiles = (R == kFwd || R == kDQS) ? 1 : 2;
   static constexpr bool kOuterCoef = R == kDQ;
   static constexpr bool kInnerCoef = R == kDKV;
   static constexpr int kInnerStages = R == kDKV ? 2 : 3;
-  static constexpr int kEpiTiles = R == kDKV ? 2 : 1;  // bf16 tiles per sub-step
+  static constexpr int kInnerTiles = R == kDQS ? 3 : 2;  // K_i (+ V_i | Q_j, dO_j | dSᵀ halves)
+  static constexpr int kEpiTiles = R == kDKV ? 2 : (R == kDQS ? 0 : 1);  // bf16 tiles per sub-step
   static constexpr int kAccCols = R == kDKV ? 128 : 64;
 };
 
@@ -75,8 +82,16 @@ struct GlobTC {
   const __nv_bfloat16* dtau;  // DKV/DQ: its cotangent
   float* row_mass;            // FWD: [B,H,T]
   const float* coef;          // DKV/DQ: [3][B·H, tpad]
+  int ds_store;               // DKV: store every dSᵀ tile for DQS
+  int dsD;                    // dSᵀ tiles per (b·h, key tile): the longest inner range
   int* err;
 };
+
+// Index of the first of the two dSᵀ query-half tiles of key tile i and query
+// tile j of head bh in the dense scratch [B·H][nT][dsD][2][128][64] (bf16).
+__device__ __forceinline__ int ds_tile(int bh, int i, int j, int nT, int dsD) {
+  return ((bh * nT + i) * dsD + (j - i)) * 2;
+}
 
 struct __align__(8) GBars {
   uint64_t outer_full[2], outer_empty[2];
@@ -99,7 +114,7 @@ __host__ __device__ inline GLayout glayout() {
   L.ocoef = L.outer + 2 * Tr::kOuterTiles * kTileBytes;
   L.inner = L.ocoef + (Tr::kOuterCoef ? 2 * kCoefBytes : 0);
   L.inner = (L.inner + 1023) & ~1023u;
-  L.icoef = L.inner + Tr::kInnerStages * 2 * kTileBytes;
+  L.icoef = L.inner + Tr::kInnerStages * Tr::kInnerTiles * kTileBytes;
   L.epi = L.icoef + (Tr::kInnerCoef ? Tr::kInnerStages * kCoefBytes : 0);
   L.epi = (L.epi + 1023) & ~1023u;
   L.mass = L.epi + 2 * Tr::kEpiTiles * kTileBytes;
@@ -132,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_global_kernel(const __grid_constant__ CUtensorMap tmo0, const __grid_constant__ CUtensorMap tmo1,
                      const __grid_constant__ CUtensorMap tmi0, const __grid_constant__ CUtensorMap tmi1,
                      const __grid_constant__ CUtensorMap tmout0, const __grid_constant__ CUtensorMap tmout1,
-                     const GlobTC p) {
+                     const __grid_constant__ CUtensorMap tmds, const GlobTC p) {
   using Tr = Traits<R>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -157,7 +172,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar->s_full[s], 1);
       mbar_init(&bar->s_free[s], 8);
       mbar_init(&bar->p_full[s], 8);
-      mbar_init(&bar->p_free[s], 1);
+      // DKV storing dSᵀ: the MMA thread also arrives once the tile's store
+      // has read the buffer
+      mbar_init(&bar->p_free[s], (R == kDKV && p.ds_store) ? 2 : 1);
       mbar_init(&bar->acc_full[s], 1);
       mbar_init(&bar->acc_free[s], 4);
       mbar_init(&bar->mass_ready[s], 8);
@@ -182,9 +199,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ─────────────────────────── TMA producer ───────────────────────────
     if (lane == 0) {
-      prefetch_tmap(&tmo0); prefetch_tmap(&tmi0); prefetch_tmap(&tmi1); prefetch_tmap(&tmout0);
+      if (R != kDQS) prefetch_tmap(&tmo0);
+      prefetch_tmap(&tmi0); prefetch_tmap(&tmi1); prefetch_tmap(&tmout0);
       if (Tr::kOuterTiles == 2) prefetch_tmap(&tmo1);
       if (R == kDKV) prefetch_tmap(&tmout1);
+      if (R == kDQS) prefetch_tmap(&tmds);
       const long long plane = (long long)BH * p.tpad;
       bool ok = true;
       int ni = 0;
@@ -193,6 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         unit_of(R, k, BH, nT, p.local, p.W, bh, ot, fi, nin);
         const int b = bh / H, h = bh % H;
         const int os = m & 1;
+        if (R != kDQS) {  // DQS has no outer operand (its outer slot is staging only)
         if (m >= 2) ok = mbar_wait(&bar->outer_empty[os], ((m >> 1) - 1) & 1, err, kErrG | 1);
         if (!ok) break;
         uint8_t* o = sOuter + os * Tr::kOuterTiles * kTileBytes;
@@ -200,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                               Tr::kOuterTiles * kTileBytes + (Tr::kOuterCoef ? kCoefBytes : 0));
         tma_load_4d(o, &tmo0, &bar->outer_full[os], 0, h, ot * kTile, b);
         if (Tr::kOuterTiles == 2) tma_load_4d(o + kTileBytes, &tmo1, &bar->outer_full[os], 0, h, ot * kTile, b);
+        }
         if (Tr::kOuterCoef) {
           const long long off = (long long)bh * p.tpad + ot * kTile;
 #pragma unroll
@@ -212,10 +233,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int st = ni % kStages;
           if (ni >= kStages) ok = mbar_wait(&bar->inner_empty[st], ((ni / kStages) - 1) & 1, err, kErrG | 2);
           if (!ok) break;
-          uint8_t* in = sInner + st * 2 * kTileBytes;
-          mbar_arrive_expect_tx(&bar->inner_full[st], 2 * kTileBytes + (Tr::kInnerCoef ? kCoefBytes : 0));
+          uint8_t* in = sInner + st * Tr::kInnerTiles * kTileBytes;
+          mbar_arrive_expect_tx(&bar->inner_full[st],
+                                Tr::kInnerTiles * kTileBytes + (Tr::kInnerCoef ? kCoefBytes : 0));
           tma_load_4d(in, &tmi0, &bar->inner_full[st], 0, h, it * kTile, b);
-          tma_load_4d(in + kTileBytes, &tmi1, &bar->inner_full[st], 0, h, it * kTile, b);
+          if (R == kDQS) {  // the two dSᵀ query halves of (key tile it, query tile ot)
+            const int t0 = ds_tile(bh, it, ot, nT, p.dsD);
+            tma_load_2d(in + kTileBytes, &tmds, &bar->inner_full[st], 0, t0 * kTile);
+            tma_load_2d(in + 2 * kTileBytes, &tmds, &bar->inner_full[st], 0, (t0 + 1) * kTile);
+          } else {
+            tma_load_4d(in + kTileBytes, &tmi1, &bar->inner_full[st], 0, h, it * kTile, b);
+          }
           if (Tr::kInnerCoef) {
             const long long off = (long long)bh * p.tpad + it * kTile;
 #pragma unroll
@@ -236,22 +264,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dOuter = sdesc_sw128(smem_u32(sOuter), 16, 1024);
       const uint64_t dInner = sdesc_sw128(smem_u32(sInner), 16, 1024);
       const uint64_t dEpi = sdesc_sw128(smem_u32(sEpi), 16, 1024);
+      // DQS: both dSᵀ query halves of a stage as the MN-major A operand of
+      // dQ (query blocks one tile apart), K_i as the MN-major B operand
+      const uint32_t id_q = idesc_bf16(128, kHD, true, true);
+      const uint64_t dDSmn = sdesc_sw128(smem_u32(sInner) + kTileBytes, kTileBytes, 1024);
       bool ok = true;
 
       // The CTA's sub-steps in order (the order the epilogue walks): unit m,
       // inner tile x of it (ring load ni, stage st), 64-row half hh.
       struct GSub {
-        int n, m, ni, st, hh;
+        int n, m, ni, st, hh, bh, ot, x;
         bool unit_first, last;
       };
-      int gk = blockIdx.x, gm = 0, gx = 0, ghh = 0, gn = 0, gni = 0, gnin = 0;
+      int gk = blockIdx.x, gm = 0, gx = 0, ghh = 0, gn = 0, gni = 0, gnin = 0, gbh = 0, got = 0;
       bool in_unit = false;
       auto next_sub = [&](GSub& s) -> bool {
         for (;;) {
           if (!in_unit) {
             if (gk >= p.units) return false;
-            int bh, ot, fi;
-            unit_of(R, gk, BH, nT, p.local, p.W, bh, ot, fi, gnin);
+            int fi;
+            unit_of(R, gk, BH, nT, p.local, p.W, gbh, got, fi, gnin);
             gx = 0;
             ghh = 0;
             in_unit = true;
@@ -262,6 +294,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             s.ni = gni;
             s.st = gni % kStages;
             s.hh = ghh;
+            s.bh = gbh;
+            s.ot = got;
+            s.x = gx;
             s.unit_first = gx == 0 && ghh == 0;
             s.last = gx == gnin - 1 && ghh == 1;
             if (++ghh == 2) {
@@ -332,6 +367,41 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         mma_commit(&bar->p_free[b]);
+        if (R == kDKV && p.ds_store) {
+          // this sub-step's dSᵀ tile (the epilogue's second tile, fenced for
+          // the async proxy before p_full) to the scratch, for DQS; the
+          // buffer's second p_free arrival comes once the store has read it,
+          // checked one sub-step later so the wait rarely blocks
+          const int t = ds_tile(c.bh, c.ot, c.ot + c.x, nT, p.dsD) + c.hh;
+          tma_store_2d(&tmds, sEpi + (b * 2 + 1) * kTileBytes, 0, t * kTile);
+          bulk_commit_group();
+          if (c.n >= 1) {
+            bulk_wait_group_read1();
+            mbar_arrive(&bar->p_free[(c.n - 1) & 1]);
+          }
+        }
+        if (c.hh == 1) mma_commit(&bar->inner_empty[c.st]);
+        if (c.last) mma_commit(&bar->acc_full[ub]);
+      };
+
+      // DQS: dQ += dS·K_h straight from the stored dSᵀ halves (no producers,
+      // no element math)
+      auto consumers_dqs = [&](const GSub& c) {
+        const int ub = c.m & 1;
+        if (c.hh == 0) ok = mbar_wait(&bar->inner_full[c.st], (c.ni / kStages) & 1, err, kErrG | 6);
+        if (ok && c.unit_first && c.m >= 2)
+          ok = mbar_wait(&bar->acc_free[ub], ((c.m >> 1) - 1) & 1, err, kErrG | 4);
+        if (!ok) return;
+        tc_fence_after();
+        const uint64_t k0 = dInner + (uint64_t)(c.st * Tr::kInnerTiles) * kTD;
+        const uint64_t ds = dDSmn + (uint64_t)(c.st * Tr::kInnerTiles) * kTD;
+        const uint32_t acc_col = tbase + 256 + ub * Tr::kAccCols;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t rows = (uint64_t)(64 * c.hh + 16 * kk) * 8;  // key rows, 16 B units
+          const uint32_t acc = (c.unit_first && kk == 0) ? 0u : 1u;
+          mma_bf16(acc_col, ds + rows, k0 + rows, id_q, acc);
+        }
         if (c.hh == 1) mma_commit(&bar->inner_empty[c.st]);
         if (c.last) mma_commit(&bar->acc_full[ub]);
       };
@@ -343,15 +413,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the loop, read their B tile with a corrupted layout (every 16-byte
       // column chunk of the product equal to the first) whenever the wait
       // before them ran out of line.
-      GSub cur{}, prev{};
-      bool have_prev = false;
-      while (ok) {
-        const bool more = next_sub(cur);
-        if (more) producers(cur);
-        if (ok && have_prev) consumers(prev);
-        if (!more) break;
-        prev = cur;
-        have_prev = true;
+      if constexpr (R == kDQS) {
+        GSub cur{};
+        while (ok && next_sub(cur)) consumers_dqs(cur);
+      } else {
+        GSub cur{}, prev{};
+        bool have_prev = false;
+        while (ok) {
+          const bool more = next_sub(cur);
+          if (more) producers(cur);
+          if (ok && have_prev) consumers(prev);
+          if (!more) break;
+          prev = cur;
+          have_prev = true;
+        }
+        if (R == kDKV && p.ds_store) bulk_wait_group0();  // the dSᵀ stores have landed
       }
     }
   } else if (warp < 4 || warp >= 12) {
@@ -370,6 +446,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ub = m & 1, os = m & 1;
       ok = mbar_wait(&bar->acc_full[ub], (m >> 1) & 1, err, kErrG | 8);
       if (R == kFwd && ok) ok = mbar_wait(&bar->mass_ready[ub], (m >> 1) & 1, err, kErrG | 9);
+      // DQS loads nothing into its outer slots: the staging slot is free
+      // again once the store from it two units back has read it
+      if (R == kDQS && ok && m >= 2) ok = mbar_wait(&bar->outer_empty[os], ((m >> 1) - 1) & 1, err, kErrG | 16);
       if (!ok) break;
       __syncwarp();
       tc_fence_after();
@@ -472,7 +551,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t epi = smem_u32(sEpi);
     bool ok = true;
     int n = 0, ni = 0;
-    for (int k = blockIdx.x, m = 0; k < p.units && ok; k += G, ++m) {
+    // (DQS has no element math: its epilogue warps only reach the final sync)
+    for (int k = blockIdx.x, m = 0; R != kDQS && k < p.units && ok; k += G, ++m) {
       int bh, ot, fi, nin;
       unit_of(R, k, BH, nT, p.local, p.W, bh, ot, fi, nin);
       const int b = bh / H, h = bh % H;
@@ -706,7 +786,7 @@ cudaError_t launch_g(const CUtensorMap* m, const GlobTC& a, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int grid = std::min(num_sms(), a.units);
-  kern<<<grid, kThreads, smem, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], a);
+  kern<<<grid, kThreads, smem, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], m[6], a);
   return cudaGetLastError();
 }
 
@@ -720,7 +800,22 @@ cudaError_t launch_role(const CUtensorMap* m, const GlobTC& a, bool bias, bool e
 
 bool out_ok(const void* ptr) { return ptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
 
+// Longest inner range of a DKV unit: every query tile for the global block,
+// the band's tiles for a local window.
+int ds_depth(int nT, int mode, int W) {
+  return mode == BOZO_MODE_GLOBAL ? nT : std::min(nT, (kTile - 1 + W) / kTile + 1);
+}
+
 }  // namespace
+
+size_t tc_global_ds_bytes(int B, int T, int H, int mode, int W) {
+  if (B <= 0 || T <= 0 || H <= 0) return 0;
+  if (mode == BOZO_MODE_LOCAL && W <= 128) return 0;  // the band kernels serve it
+  const int nT = (T + kTile - 1) / kTile;
+  const long long tiles = (long long)B * H * nT * ds_depth(nT, mode, W) * 2;
+  if (tiles * kTile > 0x7fffffffLL) return 0;  // beyond a tensor map's row coordinate
+  return (size_t)tiles * kTileBytes;
+}
 
 bool tc_global_fwd_eligible(const FwdP& p) {
   if (p.HD != kHD || (p.mode == BOZO_MODE_LOCAL && p.W < 1)) return false;
@@ -765,7 +860,7 @@ cudaError_t launch_tc_global_fwd(const FwdP& p, cudaStream_t st, int* launches) 
     e = cudaMemsetAsync(p.tau, 0, (size_t)p.B * p.T * p.H * p.W * sizeof(__nv_bfloat16), st);
     if (e != cudaSuccess) return e;
   }
-  CUtensorMap m[6];
+  CUtensorMap m[7];
   if (!make_tmap_bthd(&m[0], qp, qs[0], qs[1], qs[2], p.B, p.T, p.H, kTile) ||
       !make_tmap_bthd(&m[2], kp, ks[0], ks[1], ks[2], p.B, p.T, p.H, kTile) ||
       !make_tmap_bthd(&m[3], p.v.p, p.v.sb, p.v.st, p.v.sh, p.B, p.T, p.H, kTile) ||
@@ -773,6 +868,7 @@ cudaError_t launch_tc_global_fwd(const FwdP& p, cudaStream_t st, int* launches) 
     return cudaErrorInvalidValue;
   m[1] = m[0];
   m[5] = m[4];
+  m[6] = m[0];  // unused
   *launches += 1;
   return launch_role<kFwd>(m, a, p.bias != nullptr, p.tau != nullptr, st);
 }
@@ -827,12 +923,25 @@ cudaError_t launch_tc_global_bwd(const BwdP& p, cudaStream_t st, int* launches) 
       !make_tmap_bthd(&mdv, p.dv, ob, ot, oh, p.B, p.T, p.H, kTile))
     return cudaErrorInvalidValue;
   const bool bias = p.bias != nullptr, dt = p.dtau != nullptr;
-  {
-    const CUtensorMap m[6] = {mk, mv, mq, mdo, mdk, mdv};
-    if ((e = launch_role<kDKV>(m, a, bias, dt, st)) != cudaSuccess) return e;
+  // with room for the dSᵀ scratch, DKV stores its dSᵀ tiles and the dQ pass
+  // multiplies them by K (DQS); otherwise the dQ pass recomputes S and dP (DQ)
+  CUtensorMap mds = mq;
+  if (p.ds_scratch) {
+    a.dsD = ds_depth(a.nT, p.mode, p.W);
+    const long long rows = (long long)a.BH * a.nT * a.dsD * 2 * kTile;
+    if (!make_tmap_2d(&mds, p.ds_scratch, false, kHD, (uint64_t)rows, kHD * 2, kHD, kTile))
+      return cudaErrorInvalidValue;
+    a.ds_store = 1;
   }
   {
-    const CUtensorMap m[6] = {mq, mdo, mk, mv, mdq, mdq};
+    const CUtensorMap m[7] = {mk, mv, mq, mdo, mdk, mdv, mds};
+    if ((e = launch_role<kDKV>(m, a, bias, dt, st)) != cudaSuccess) return e;
+  }
+  if (p.ds_scratch) {
+    const CUtensorMap m[7] = {mq, mq, mk, mk, mdq, mdq, mds};
+    if ((e = launch_g<kDQS, false, false>(m, a, st)) != cudaSuccess) return e;
+  } else {
+    const CUtensorMap m[7] = {mq, mdo, mk, mv, mdq, mdq, mds};
     if ((e = launch_role<kDQ>(m, a, bias, dt, st)) != cudaSuccess) return e;
   }
   *launches = 3;

@@ -214,8 +214,13 @@ int bozo_tension_fwd_needs_lp(const bozo_tension_fwd_args* args);
  * (a cudaStream_t, NULL = legacy default stream). */
 int bozo_tension_fwd(const bozo_tension_fwd_args* args, void* stream);
 
-/* Device scratch the backward needs for these arguments (bytes, 256-aligned
- * size; 0 is possible). */
+/* Device scratch the backward uses for these arguments (bytes, 256-aligned
+ * size; 0 is possible).  For the key-tile kernels (global block, windows
+ * wider than 128, bf16 HD 64) it includes a dSᵀ scratch of
+ * 2·B·H·nT·D·16 KiB (nT = ceil(T/128); D = nT for the global block, else
+ * min(nT, floor((W+127)/128)+1)) that spares the dQ pass recomputing the
+ * scores; a workspace of only the rest (what bozo_tension_bwd_noalloc
+ * checks) still works, with that recomputation. */
 size_t bozo_tension_bwd_workspace(const bozo_tension_bwd_args* args);
 
 /* Backward: writes dq, dk, dv. */

@@ -93,6 +93,11 @@ CASES = [
          norm=_capi.NORM_MASS, rope_base=10000.0, tau=False, path=_capi.PATH_TCGEN05),
     dict(B=1, T=300, H=3, HD=64, dtype=torch.bfloat16, mode=_capi.MODE_LOCAL, window=100,
          norm=_capi.NORM_COUNT, rope_base=10000.0, tau=True, path=_capi.PATH_TCGEN05),
+    # key-tile tensor-core path, global block: the ordinary call has room for
+    # the dSᵀ scratch (dQ from stored dSᵀ tiles), the no-alloc call does not
+    # (dQ recomputes the scores) — the two dQ passes must agree
+    dict(B=1, T=300, H=2, HD=64, dtype=torch.bfloat16, mode=_capi.MODE_GLOBAL, window=64,
+         norm=_capi.NORM_MASS, rope_base=10000.0, tau=False, path=_capi.PATH_TCGEN05),
     # CUDA-core path: fp32, local and global, τ cotangent
     dict(B=2, T=200, H=2, HD=32, dtype=torch.float32, mode=_capi.MODE_LOCAL, window=37,
          norm=_capi.NORM_NONE, rope_base=None, tau=True, path=_capi.PATH_SIMT),
