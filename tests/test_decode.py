@@ -4,7 +4,8 @@
   caches reproduces, row by row, the float64 oracle of the sequence operator
   (local W ∈ {16, 64} with τ-mass / count / raw normalisation, global with
   τ-mass) — outputs and the exported τ rows; a global ring shorter than the
-  sequence keeps the last ``capacity`` keys.
+  sequence keeps the last ``capacity`` keys; caches over 256 keys (the
+  16-warp kernel) match too, wrapped or not.
 * GPU, model: after a prefill, each decode step's logits equal the last row
   of a full forward of the harness over the same ids (plain forward: local
   count normalisation; export mode: the ``return_all`` forward, incl. its τ
@@ -110,6 +111,34 @@ def test_global_ring_keeps_last_capacity_keys():
         tau = torch.sigmoid(torch.einsum("bhd,bshd->bhs", qr[:, t], kr[:, s0:t + 1]) / SCALE)
         ref[:, t] = torch.einsum("bhs,bshd->bhd", tau, vv[:, s0:t + 1]) / tau.sum(-1, keepdim=True)
     assert_close(out, ref, torch.float32, "sliding global out")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_long_caches_take_the_wide_kernel(dtype):
+    """Caches over 256 keys (global layers, wide windows) run 16 warps per
+    (b, h): global without and with the ring wrapping, and a local window of
+    300."""
+    T, HD = 420, 64
+    q, k, v = _seq(1, T, 2, HD, dtype, seed=5)
+    cos, sin = orc.rope_tables(HD, T, 10_000.0, torch.float64)
+    qr, kr, vv = orc.rope(q.double(), cos, sin), orc.rope(k.double(), cos, sin), v.double()
+    out, _ = _decode_all(q, k, v, mode=_capi.MODE_GLOBAL, W=0, norm=_capi.NORM_MASS, cap=T, tw=0)
+    ref, _, _ = orc.global_tension(qr, kr, vv, SCALE)
+    assert_close(out, ref, dtype, "global 420-key cache out")
+    C = 300
+    out, _ = _decode_all(q, k, v, mode=_capi.MODE_GLOBAL, W=0, norm=_capi.NORM_MASS, cap=C, tw=0)
+    ref = torch.zeros(1, T, 2, HD, dtype=torch.float64)
+    for t in range(T):
+        s0 = max(0, t - C + 1)
+        tau = torch.sigmoid(torch.einsum("bhd,bshd->bhs", qr[:, t], kr[:, s0:t + 1]) / SCALE)
+        ref[:, t] = torch.einsum("bhs,bshd->bhd", tau, vv[:, s0:t + 1]) / tau.sum(-1, keepdim=True)
+    assert_close(out, ref, dtype, "global ring of 300 out")
+    out, tau = _decode_all(q, k, v, mode=_capi.MODE_LOCAL, W=300, norm=_capi.NORM_MASS, cap=301, tw=300)
+    ref_out, ref_tau = orc.fused_reference(*(x.double() for x in (q, k, v)), window=300, scale=SCALE,
+                                           normalize="mass")
+    assert_close(out, ref_out, dtype, "local W300 out")
+    assert_close(tau, ref_tau, dtype, "local W300 τ rows")
 
 
 CFGS = {
