@@ -938,7 +938,11 @@ def main():
         tau_consumer = run_tau_consumer(local_rank)
         torch.cuda.empty_cache()
         from bozo_b200 import lm as _lm
-        train13 = run_train(args, rank, world, local_rank, cfg=_lm.preset_13m(), batch=32,
+        # the 13.5M step is ≈ 8 ms and host-launch heavy: more steps for a
+        # stable figure (same warm-up rule)
+        a13 = argparse.Namespace(**vars(args))
+        a13.train_steps, a13.train_warmup = max(args.train_steps, 30), max(args.train_warmup, 5)
+        train13 = run_train(a13, rank, world, local_rank, cfg=_lm.preset_13m(), batch=32,
                             seq=512, variants=("aux_on",))
         torch.cuda.empty_cache()
         one_m = {"gpu": run_1m_gpu(local_rank)}
@@ -998,7 +1002,8 @@ def main():
         train13_obj = {
             "metric": "13.5M TensionLM train tokens/s (whole job)",
             "value": round(tok13 / (ms13 * 1e-3), 1), "unit": "tokens/s",
-            "ms_per_step": round(ms13, 3), "steps": args.train_steps, "n_gpus": n,
+            "ms_per_step": round(ms13, 3), "steps": max(args.train_steps, 30),
+            "warmup": max(args.train_warmup, 5), "n_gpus": n,
             "e2e": {"value": round(tok13 / (e2e13 * 1e-3), 1), "unit": "tokens/s",
                     "ms_per_step": round(e2e13, 3), "h2d_bytes_per_step": 32 * 513 * 8,
                     "d2h_bytes_per_step": 4},
