@@ -213,13 +213,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int b = bh / H, h = bh % H;
         const int os = m & 1;
         if (R != kDQS) {  // DQS has no outer operand (its outer slot is staging only)
-        if (m >= 2) ok = mbar_wait(&bar->outer_empty[os], ((m >> 1) - 1) & 1, err, kErrG | 1);
-        if (!ok) break;
-        uint8_t* o = sOuter + os * Tr::kOuterTiles * kTileBytes;
-        mbar_arrive_expect_tx(&bar->outer_full[os],
-                              Tr::kOuterTiles * kTileBytes + (Tr::kOuterCoef ? kCoefBytes : 0));
-        tma_load_4d(o, &tmo0, &bar->outer_full[os], 0, h, ot * kTile, b);
-        if (Tr::kOuterTiles == 2) tma_load_4d(o + kTileBytes, &tmo1, &bar->outer_full[os], 0, h, ot * kTile, b);
+          if (m >= 2) ok = mbar_wait(&bar->outer_empty[os], ((m >> 1) - 1) & 1, err, kErrG | 1);
+          if (!ok) break;
+          uint8_t* o = sOuter + os * Tr::kOuterTiles * kTileBytes;
+          mbar_arrive_expect_tx(&bar->outer_full[os],
+                                Tr::kOuterTiles * kTileBytes + (Tr::kOuterCoef ? kCoefBytes : 0));
+          tma_load_4d(o, &tmo0, &bar->outer_full[os], 0, h, ot * kTile, b);
+          if (Tr::kOuterTiles == 2)
+            tma_load_4d(o + kTileBytes, &tmo1, &bar->outer_full[os], 0, h, ot * kTile, b);
         }
         if (Tr::kOuterCoef) {
           const long long off = (long long)bh * p.tpad + ot * kTile;
