@@ -316,9 +316,13 @@ def run_train(args, rank, world, local_rank, cfg=None, batch=TRAIN_B, seq=TRAIN_
     operator in every tension layer, CE + train.py's default aux losses
     (w_closure 0.01, w_diversity 0.02, which put τ export and its cotangent
     in the loop; ``aux_off`` drops them), global-norm clip, fused AdamW; DDP
-    over NCCL when world > 1 (fp32 gradient all-reduce in 64 MB buckets).  Uniform random
+    over NCCL when world > 1 (fp32 gradient all-reduce in 64 MB buckets,
+    averaged inside the all-reduce).  Each timed step is one replay of the
+    whole optimiser step recorded as a CUDA graph (``lm.GraphedTrainStep``);
+    the same step run eagerly is timed beside it (aux_on).  Uniform random
     token ids from a per-rank seed, random init.  Returns
-    ({variant: (ms_per_step max over ranks, e2e ms_per_step)}, params)."""
+    ({variant: (ms_per_step max over ranks, e2e ms_per_step, eager ms_per_step)},
+    params)."""
     import torch.distributed as dist
     from bozo_b200 import lm
     dev = torch.device("cuda", local_rank)
@@ -326,7 +330,7 @@ def run_train(args, rank, world, local_rank, cfg=None, batch=TRAIN_B, seq=TRAIN_
     cfg = cfg or lm.preset_117m()
     base = lm.TensionLM(cfg).to(dev)
     model = lm.wrap_ddp(base) if (world > 1 and ddp) else base
-    opt = lm.make_optimizer(base, fused=True)
+    opt = lm.make_optimizer(base, fused=True, capturable=True)
     g = torch.Generator().manual_seed(4242 + rank)
     ids_h = torch.randint(0, cfg.vocab_size, (batch, seq + 1), generator=g).pin_memory()
     ids = ids_h.to(dev)
@@ -345,36 +349,43 @@ def run_train(args, rank, world, local_rank, cfg=None, batch=TRAIN_B, seq=TRAIN_
         if world > 1:
             dist.barrier()
 
-    out = {}
-    weights = {"aux_on": lm.TrainWeights(), "aux_off": lm.TrainWeights(0.0, 0.0, 0.0, 0.0)}
-    for name in variants:
-        w = weights[name]
-        for _ in range(args.train_warmup):
-            lm.train_step(model, base, opt, inputs, targets, weights=w)
+    def timed(fn, k):
         torch.cuda.synchronize()
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.train_steps):
-            lm.train_step(model, base, opt, inputs, targets, weights=w)
+        for _ in range(k):
+            fn()
         e1.record(stream)
         torch.cuda.synchronize()
-        ms = maxred(e0.elapsed_time(e1)) / args.train_steps
+        return maxred(e0.elapsed_time(e1)) / k
+
+    out = {}
+    weights = {"aux_on": lm.TrainWeights(), "aux_off": lm.TrainWeights(0.0, 0.0, 0.0, 0.0)}
+    for name in variants:
+        w = weights[name]
+        eager = None
+        if name == "aux_on":
+            for _ in range(args.train_warmup):
+                lm.train_step(model, base, opt, inputs, targets, weights=w)
+            eager = timed(lambda: lm.train_step(model, base, opt, inputs, targets, weights=w),
+                          args.train_steps)
+        # the graph's own warm-up steps run eagerly first (11 under DDP)
+        step = lm.GraphedTrainStep(model, base, opt, ids, weights=w)
+        for _ in range(args.train_warmup):
+            step()
+        ms = timed(step, args.train_steps)
         e2e = None
         if name == "aux_on":
             # end to end: token ids copied in from pinned host memory and the
             # loss read back every step
-            barrier()
-            e0.record(stream)
-            for _ in range(args.train_steps):
-                idd = ids_h.to(dev, non_blocking=True)
-                loss = lm.train_step(model, base, opt, idd[:, :-1], idd[:, 1:], weights=w)
-                loss_h.copy_(loss, non_blocking=True)
-            e1.record(stream)
-            torch.cuda.synchronize()
-            e2e = maxred(e0.elapsed_time(e1)) / args.train_steps
-        out[name] = (ms, e2e)
+            def e2e_step():
+                loss_h.copy_(step(ids_h), non_blocking=True)
+            e2e = timed(e2e_step, args.train_steps)
+        step.release()  # before any process-group teardown: it holds NCCL calls
+        del step
+        out[name] = (ms, e2e, eager)
         barrier()
     params = base.num_params
     del model, base, opt
@@ -932,8 +943,8 @@ def main():
         tau_consumer = run_tau_consumer(local_rank)
         torch.cuda.empty_cache()
         from bozo_b200 import lm as _lm
-        # the 13.5M step is ≈ 8 ms and host-launch heavy: more steps for a
-        # stable figure (same warm-up rule)
+        # the 13.5M step is ≈ 6 ms: more steps for a stable figure (same
+        # warm-up rule)
         a13 = argparse.Namespace(**vars(args))
         a13.train_steps, a13.train_warmup = max(args.train_steps, 30), max(args.train_warmup, 5)
         train13 = run_train(a13, rank, world, local_rank, cfg=_lm.preset_13m(), batch=32,
@@ -965,14 +976,15 @@ def main():
     if train is not None:
         n = args.gpus
         tok = n * TRAIN_B * TRAIN_T
-        ms_on, e2e_on = train["aux_on"]
-        ms_off, _ = train["aux_off"]
+        ms_on, e2e_on, eager_on = train["aux_on"]
+        ms_off, _, _ = train["aux_off"]
         flop_tok = 6 * n_params + 12 * 64 * 12 * (9 * 64 + 3 * (TRAIN_T + 1) / 2)
         tflops = tok * flop_tok / (ms_on * 1e-3) / 1e12
         train_obj = {
             "metric": "117M TensionLM train tokens/s (whole job)",
             "value": round(tok / (ms_on * 1e-3), 1), "unit": "tokens/s",
-            "ms_per_step": round(ms_on, 3), "steps": args.train_steps,
+            "ms_per_step": round(ms_on, 3), "eager_ms_per_step": round(eager_on, 3),
+            "steps": args.train_steps,
             "warmup": args.train_warmup, "n_gpus": n,
             "aux_losses": "on (train.py defaults w_closure 0.01, w_diversity 0.02)",
             "aux_off": {"value": round(tok / (ms_off * 1e-3), 1), "unit": "tokens/s",
@@ -990,8 +1002,12 @@ def main():
                        "vocab": 32768, "W": 64, "global_every": 4, "seq_len": TRAIN_T,
                        "per_gpu_batch": TRAIN_B, "global_batch": TRAIN_B * n,
                        "dtype": "bf16 autocast, fp32 master weights", "optimizer": "AdamW (fused)",
+                       "execution": ("whole optimiser step replayed as one CUDA graph "
+                                     "(lm.GraphedTrainStep); eager_ms_per_step: the same step "
+                                     "launched op by op"),
                        "parallelism": f"ddp{n}" if n > 1 else "single GPU",
-                       "gradient_allreduce": ("NCCL, fp32, 64 MB buckets overlapped with the "
+                       "gradient_allreduce": ("NCCL, fp32, averaged in the all-reduce, 64 MB "
+                                              "buckets overlapped with the "
                                               "backward (static graph)") if n > 1 else None,
                        "data": "uniform random token ids, random init"},
             "tau_consumer": tau_consumer,
@@ -999,12 +1015,13 @@ def main():
     train13_obj = None
     if train13 is not None:
         n = args.gpus
-        (ms13, e2e13), p13 = train13[0]["aux_on"], train13[1]
+        (ms13, e2e13, eager13), p13 = train13[0]["aux_on"], train13[1]
         tok13 = n * 32 * 512
         train13_obj = {
             "metric": "13.5M TensionLM train tokens/s (whole job)",
             "value": round(tok13 / (ms13 * 1e-3), 1), "unit": "tokens/s",
-            "ms_per_step": round(ms13, 3), "steps": max(args.train_steps, 30),
+            "ms_per_step": round(ms13, 3), "eager_ms_per_step": round(eager13, 3),
+            "steps": max(args.train_steps, 30),
             "warmup": max(args.train_warmup, 5), "n_gpus": n,
             "e2e": {"value": round(tok13 / (e2e13 * 1e-3), 1), "unit": "tokens/s",
                     "ms_per_step": round(e2e13, 3), "h2d_bytes_per_step": 32 * 513 * 8,
@@ -1014,6 +1031,7 @@ def main():
                        "W": 64, "global_every": 4, "seq_len": 512, "per_gpu_batch": 32,
                        "dtype": "bf16 autocast, fp32 master weights",
                        "aux_losses": "on (train.py defaults)", "optimizer": "AdamW (fused)",
+                       "execution": "whole optimiser step replayed as one CUDA graph",
                        "parallelism": f"ddp{n}" if n > 1 else "single GPU",
                        "data": "uniform random token ids, random init"},
         }

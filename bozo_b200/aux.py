@@ -58,13 +58,14 @@ class _TauStatsFn(torch.autograd.Function):
         rows = [i for i, sl in enumerate(ctx.slots) if sl is not None]
         mats = [i for i, sl in enumerate(ctx.slots) if sl is None]
         if rows:
-            coef = _capi.ext().tau_aux_rowcoef([taus[i] for i in rows], d_stats[rows].contiguous())
+            coef = _capi.ext().tau_aux_rowcoef([taus[i] for i in rows],
+                                               _take(d_stats, rows).contiguous())
             for j, i in enumerate(rows):
                 ctx.slots[i].add(coef[j])
         if mats:
             sub = mats if len(mats) < len(taus) else None
             dts = _capi.ext().tau_aux_bwd([taus[i] for i in mats],
-                                          d_stats[sub].contiguous() if sub else d_stats)
+                                          _take(d_stats, sub).contiguous() if sub else d_stats)
             for j, i in enumerate(mats):
                 grads[i] = dts[j]
         return (None, *grads)
@@ -103,6 +104,24 @@ def _consistency_applies(shape: torch.Size) -> bool:
     return min(W - 2, 4) + 1 < T
 
 
+_index_cache: Dict[tuple, Tensor] = {}
+
+
+def _take(col: Tensor, idx: List[int]) -> Tensor:
+    """``col[idx]`` without copying a host index list to the device on every
+    call (a pageable copy per loss term, and one a CUDA graph cannot hold): a
+    slice when ``idx`` is a contiguous run, else an index tensor made once
+    per (device, idx)."""
+    idx = list(idx)
+    if idx == list(range(idx[0], idx[0] + len(idx))):
+        return col[idx[0]:idx[0] + len(idx)]
+    key = (col.device, tuple(idx))
+    ix = _index_cache.get(key)
+    if ix is None:
+        ix = _index_cache[key] = torch.tensor(idx, dtype=torch.long, device=col.device)
+    return col.index_select(0, ix)
+
+
 def tension_aux_losses(all_tensions: Sequence[Tensor], window_groups: Optional[dict] = None,
                        grad_consistency: bool = True) -> Tuple[Tensor, Tensor, Tensor]:
     """(diversity, consistency, entropy) of model.py:498-611 for the per-layer
@@ -129,13 +148,13 @@ def tension_aux_losses(all_tensions: Sequence[Tensor], window_groups: Optional[d
     for W, idx in groups.items():
         # every field of a group has N = B·T·H rows, so the mean of the
         # per-layer means is the mean over the stacked rows
-        ent = stats[idx, 0].mean()
+        ent = _take(stats[:, 0], idx).mean()
         div = div + torch.relu(math.log(W) - ent)
     div = div / max(len(groups), 1)
     # consistency (model.py:548-577): average over the layers that apply
     live = [i for i, t in enumerate(all_tensions) if _consistency_applies(t.shape)]
     cons_col = stats[:, 1] if grad_consistency else stats[:, 1].detach()
-    cons = cons_col[live].sum() / max(len(live), 1) if live else stats.new_zeros(())
+    cons = _take(cons_col, live).sum() / max(len(live), 1) if live else stats.new_zeros(())
     # entropy regulariser (model.py:597-611): average over all layers
     ent_loss = stats[:, 2].sum() / len(all_tensions)
     return div, cons, ent_loss

@@ -22,6 +22,7 @@ from dataclasses import dataclass
 from typing import Callable, Optional
 
 import torch
+import torch.distributed as dist
 import torch.nn as nn
 import torch.nn.functional as F
 
@@ -482,37 +483,67 @@ class TrainWeights:
                                    self.w_entropy))
 
 
+def _avg_allreduce_hook(process_group, bucket):
+    """DDP communication hook: one NCCL all-reduce with the AVG operator per
+    gradient bucket.  Without a hook DDP divides every gradient by the world
+    size as it becomes ready — one elementwise kernel per parameter on the
+    compute stream (130 launches, 0.32 ms of device time per 117M step on
+    B200) — while NCCL applies the 1/N inside the all-reduce."""
+    group = process_group if process_group is not None else dist.group.WORLD
+    fut = dist.all_reduce(bucket.buffer(), op=dist.ReduceOp.AVG, group=group,
+                          async_op=True).get_future()
+    return fut.then(lambda f: f.value()[0])
+
+
 def wrap_ddp(model: nn.Module, compress: bool = False, bucket_cap_mb: float = 64.0):
     """train.py:789-797: DDP with static graph, no buffer broadcast; gradients
     are bucketed and all-reduced (NCCL on GPUs) while the backward runs, in
-    64 MB buckets (DDP's default is 25 MB).  ``compress`` all-reduces the
-    buckets in bf16 (the reference all-reduces fp32).  Measured on two B200s
-    (117M model, batch 16 x 1024 per GPU, ms per step, max over ranks):
-    fp32 25 MB 27.30, fp32 64 MB 27.16, fp32 128 MB 27.24, bf16 25 MB 31.14,
-    bf16 64 MB 27.45, bf16 128 MB 27.80, no DDP 25.88 — over NVLink the
-    casts of the compression hook cost more than the halved bytes save, so
-    it is off by default."""
+    64 MB buckets (DDP's default is 25 MB), averaged inside the all-reduce
+    (``_avg_allreduce_hook``) on NCCL.  ``compress`` all-reduces the buckets
+    in bf16 (the reference all-reduces fp32).  Measured on two B200s (117M
+    model, batch 16 x 1024 per GPU, ms per step, max over ranks, before the
+    averaging hook): fp32 25 MB 27.30, fp32 64 MB 27.16, fp32 128 MB 27.24,
+    bf16 25 MB 31.14, bf16 64 MB 27.45, bf16 128 MB 27.80, no DDP 25.88 —
+    over NVLink the casts of the compression hook cost more than the halved
+    bytes save, so it is off by default."""
     from torch.nn.parallel import DistributedDataParallel as DDP
     dev = next(model.parameters()).device
-    ddp = DDP(model, device_ids=[dev.index] if dev.type == "cuda" else None,
-              find_unused_parameters=False, broadcast_buffers=False, static_graph=True,
-              gradient_as_bucket_view=True, bucket_cap_mb=bucket_cap_mb)
+
+    def make():
+        return DDP(model, device_ids=[dev.index] if dev.type == "cuda" else None,
+                   find_unused_parameters=False, broadcast_buffers=False, static_graph=True,
+                   gradient_as_bucket_view=True, bucket_cap_mb=bucket_cap_mb)
+    if dev.type == "cuda":
+        # set up on a side stream, as a CUDA graph that records the step
+        # (GraphedTrainStep) requires of DDP
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            ddp = make()
+        torch.cuda.current_stream(dev).wait_stream(side)
+    else:
+        ddp = make()
     if compress and dev.type == "cuda":
         # gradients cross NVLink as bf16 (half the bytes of the fp32 all-reduce);
         # the averaged result is written back in fp32 before the optimiser step
         from torch.distributed.algorithms.ddp_comm_hooks import default_hooks
         ddp.register_comm_hook(state=None, hook=default_hooks.bf16_compress_hook)
+    elif dev.type == "cuda" and dist.get_backend() == "nccl":
+        ddp.register_comm_hook(state=None, hook=_avg_allreduce_hook)
     return ddp
 
 
 def make_optimizer(model: nn.Module, lr: float = 3e-4, weight_decay: float = 0.10,
-                   fused: Optional[bool] = None):
-    """train.py:893-901: AdamW, decay on ≥2-D parameters, betas (0.9, 0.95)."""
+                   fused: Optional[bool] = None, capturable: bool = False):
+    """train.py:893-901: AdamW, decay on ≥2-D parameters, betas (0.9, 0.95).
+    ``capturable``: step counts kept on the device, so the step can be
+    recorded in a CUDA graph (``GraphedTrainStep``)."""
     decay = [p for p in model.parameters() if p.requires_grad and p.dim() >= 2]
     nodecay = [p for p in model.parameters() if p.requires_grad and p.dim() < 2]
     return torch.optim.AdamW([{"params": decay, "weight_decay": weight_decay},
                               {"params": nodecay, "weight_decay": 0.0}],
-                             lr=lr, betas=(0.9, 0.95), eps=1e-8, fused=fused)
+                             lr=lr, betas=(0.9, 0.95), eps=1e-8, fused=fused,
+                             capturable=capturable)
 
 
 def train_step(model, base_model: TensionLM, optimizer, inputs, targets,
@@ -558,3 +589,65 @@ def train_step(model, base_model: TensionLM, optimizer, inputs, targets,
         from .ops import check_device_error
         check_device_error(inputs.device)
     return loss.detach()
+
+
+class GraphedTrainStep:
+    """``train_step`` recorded once as a CUDA graph and replayed per batch.
+
+    The step (autocast forward, CE + aux losses, backward — with DDP's
+    bucketed NCCL all-reduces when ``model`` is wrapped — global-norm clip,
+    AdamW) launches several hundred kernels; eager, the host's launch and
+    autograd work leaves the GPU idle between the short ones (one B200: the
+    13.5M step 7.9 → 5.9 ms, the 117M step 19.9 → 19.5 ms).  Replay runs the
+    same kernels on the same buffers and leaves bit-identical parameters:
+    token ids are copied into a static ``[batch, seq + 1]`` buffer, and
+    ``loss`` is the static result tensor of the recorded step.
+
+    Requirements: a capturable optimiser (``make_optimizer(capturable=True)``),
+    fixed shapes, a learning rate that does not change between steps.  The
+    first ``warmup`` steps run eagerly on a side stream (DDP needs at least
+    11 before its buckets are final).  Release the graph (``release()``)
+    before destroying a process group whose all-reduces it holds."""
+
+    def __init__(self, model, base_model: TensionLM, optimizer, ids: torch.Tensor,
+                 weights: Optional[TrainWeights] = None, clip_grad: float = 1.0,
+                 warmup: Optional[int] = None):
+        if not ids.is_cuda:
+            raise RuntimeError("GraphedTrainStep: token ids must be a CUDA tensor")
+        if not all(g.get("capturable", False) for g in optimizer.param_groups):
+            raise ValueError("GraphedTrainStep: the optimiser must be capturable")
+        from torch.nn.parallel import DistributedDataParallel as DDP
+        if warmup is None:
+            warmup = 11 if isinstance(model, DDP) else 3
+        self.device = ids.device
+        self.ids = ids.detach().clone()
+        inputs, targets = self.ids[:, :-1], self.ids[:, 1:]
+        args = (model, base_model, optimizer, inputs, targets, weights, clip_grad)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                train_step(*args)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        optimizer.zero_grad(set_to_none=True)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.loss = train_step(*args)
+
+    def __call__(self, ids: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One optimiser step on ``ids`` (copied into the static buffer; the
+        previous batch again when None).  Returns the static loss tensor
+        (not synchronised; the next replay overwrites it)."""
+        if self.graph is None:
+            raise RuntimeError("GraphedTrainStep: released")
+        if ids is not None:
+            self.ids.copy_(ids, non_blocking=True)
+        self.graph.replay()
+        from .ops import check_device_error
+        check_device_error(self.device)
+        return self.loss
+
+    def release(self) -> None:
+        """Drop the graph (and with it any NCCL calls it recorded)."""
+        self.graph = None
+

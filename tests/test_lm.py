@@ -162,6 +162,37 @@ def test_harness_bf16_autocast_tensor_core_path(golden_lm):
             assert np.abs(got - case[k]).max() <= 5e-2 * scale, k
 
 
+@pytest.mark.gpu
+def test_graphed_train_step_matches_eager():
+    """``GraphedTrainStep`` (the step recorded as a CUDA graph, replayed per
+    batch) leaves exactly the parameters and losses of the eager steps,
+    including a batch copied in from pinned host memory."""
+    dev = torch.device("cuda:0")
+    cfg = lm.TensionConfig(**CFGS["rope_global"])
+    g = torch.Generator().manual_seed(11)
+    batches = [torch.randint(0, cfg.vocab_size, (2, 193), generator=g) for _ in range(2)]
+    ids0 = batches[0].to(dev)
+    ids1 = batches[1].pin_memory()
+
+    def build():
+        torch.manual_seed(0)
+        base = lm.TensionLM(cfg).to(dev)
+        return base, lm.make_optimizer(base, fused=True, capturable=True)
+
+    base_e, opt_e = build()
+    losses_e = []
+    for ids in [ids0] * 5 + [ids1.to(dev)] * 2:
+        losses_e.append(float(lm.train_step(base_e, base_e, opt_e, ids[:, :-1], ids[:, 1:])))
+    base_g, opt_g = build()
+    step = lm.GraphedTrainStep(base_g, base_g, opt_g, ids0, warmup=3)  # steps 1-3 eagerly
+    losses_g = [float(step()), float(step())]
+    losses_g += [float(step(ids1)), float(step())]
+    step.release()
+    assert losses_g == losses_e[3:]
+    for (name, pe), pg in zip(base_e.named_parameters(), base_g.parameters()):
+        assert torch.equal(pe, pg), name
+
+
 # ───────────────────────── DDP over gloo (CPU) ─────────────────────────
 
 TINY = dict(vocab_size=53, dim=32, num_layers=2, num_heads=2, window=4, ffn_mult=2,
