@@ -755,9 +755,11 @@ def run_prefill(args, rank, world, local_rank):
     """350M TensionLM inference prefill with τ export:
     bf16 weights, no grad, every layer returns τ (local [B,T,H,W], global
     the exported window), batch 4 per GPU (32 over 8 GPUs), T 2048, random
-    init, uniform token ids.  Pure replicas: no collective.  Returns
-    (ms per forward max over ranks, e2e ms with token ids in and every
-    layer's τ read back to pinned host memory, params, τ bytes)."""
+    init, uniform token ids.  Pure replicas: no collective.  The timed
+    forward is a CUDA-graph replay (``lm.GraphedForward``); the eager
+    forward is timed beside it.  Returns (ms per forward max over ranks, e2e
+    ms with token ids in and every layer's τ read back to pinned host
+    memory, params, τ bytes, eager ms per forward)."""
     import torch.distributed as dist
     from bozo_b200 import lm
     dev = torch.device("cuda", local_rank)
@@ -782,64 +784,65 @@ def run_prefill(args, rank, world, local_rank):
 
     _, _, taus = fwd(ids)
     tau_bytes = sum(t.numel() * t.element_size() for t in taus)
-    taus_h = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in taus]
     del taus
+
+    def timed(fn, k):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(k):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return maxred(e0.elapsed_time(e1)) / k
+
     for _ in range(args.train_warmup):
         fwd(ids)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.train_steps):
-        fwd(ids)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = maxred(e0.elapsed_time(e1)) / args.train_steps
-    if world > 1:
-        dist.barrier()
+    eager = timed(lambda: fwd(ids), args.train_steps)
+    # the forward replayed as a CUDA graph: two copies with their own static
+    # outputs, so one copy's τ can be read out while the other runs
+    graphed = lm.GraphedForward(model, ids, copies=2)
+    for _ in range(args.train_warmup):
+        graphed()
+    ms = timed(graphed, args.train_steps)
     # end to end: token ids in from pinned memory, every layer's τ out to
-    # pinned memory each forward.  Forward i's τ read-out runs on a copy stream
-    # while forward i+1 computes (two pinned τ sets); its τ tensors stay
-    # referenced until the compute stream has waited for those copies, so the
-    # allocator reuses their memory only after them.
-    taus_hs = [taus_h, [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in taus_h]]
+    # pinned memory each forward.  Forward i's τ read-out runs on a copy
+    # stream while forward i+1 computes on the other graph copy; a copy is
+    # replayed again only after the read-out of its previous τ finished.
+    taus_hs = [[torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in graphed.slots[c][2][2]]
+               for c in range(2)]
     s_out = torch.cuda.Stream(dev)
     ev_done = [torch.cuda.Event() for _ in range(2)]
     ev_out = [torch.cuda.Event() for _ in range(2)]
+    used = [False, False]
+    count = [0]
 
     def e2e_run(n):
-        held = [None, None]
-        for i in range(n):
-            sl = i & 1
-            if held[sl] is not None:
+        for _ in range(n):
+            sl = count[0] & 1
+            count[0] += 1
+            if used[sl]:
                 stream.wait_event(ev_out[sl])
-                held[sl] = None
-            x = ids_h.to(dev, non_blocking=True)
-            _, _, taus_i = fwd(x)
+            _, _, taus_i = graphed(ids_h, copy=sl)
             ev_done[sl].record(stream)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev_done[sl])
                 for dst, src in zip(taus_hs[sl], taus_i):
                     dst.copy_(src, non_blocking=True)
                 ev_out[sl].record(s_out)
-            held[sl] = taus_i
+            used[sl] = True
         stream.wait_stream(s_out)
 
-    e2e_run(3)  # untimed: the allocator settles on two forwards' τ in flight
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0.record(stream)
-    e2e_run(args.train_steps)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e = maxred(e0.elapsed_time(e1)) / args.train_steps
+    e2e_run(2)  # untimed
+    e2e = timed(lambda: e2e_run(args.train_steps), 1) / args.train_steps
     params = model.num_params
     del model
     torch.cuda.empty_cache()
-    return ms, e2e, params, tau_bytes
+    del graphed
+    return ms, e2e, params, tau_bytes, eager
 
 
 def cpu_baseline(budget_s=12.0):
@@ -1044,12 +1047,13 @@ def main():
     prefill_obj = None
     if prefill is not None:
         n = args.gpus
-        ms_p, e2e_p, p_params, tau_bytes = prefill
+        ms_p, e2e_p, p_params, tau_bytes, eager_p = prefill
         tok = n * PREFILL_B * PREFILL_T
         prefill_obj = {
             "metric": "350M TensionLM prefill tokens/s with tau export (whole job)",
             "value": round(tok / (ms_p * 1e-3), 1), "unit": "tokens/s",
-            "ms_per_step": round(ms_p, 3), "steps": args.train_steps, "n_gpus": n,
+            "ms_per_step": round(ms_p, 3), "eager_ms_per_step": round(eager_p, 3),
+            "steps": args.train_steps, "n_gpus": n,
             "model_tflops": round(tok * 2 * p_params / (ms_p * 1e-3) / 1e12, 1),
             "e2e": {"value": round(tok / (e2e_p * 1e-3), 1), "unit": "tokens/s",
                     "ms_per_step": round(e2e_p, 3),
@@ -1061,6 +1065,9 @@ def main():
                        "vocab": 32768, "W": 128, "global_every": 3, "seq_len": PREFILL_T,
                        "per_gpu_batch": PREFILL_B, "global_batch": PREFILL_B * n,
                        "dtype": "bf16 weights, no grad", "tau_bytes_per_gpu": tau_bytes,
+                       "execution": ("forward replayed as a CUDA graph (lm.GraphedForward, two "
+                                     "copies so one copy's tau read-out overlaps the next "
+                                     "forward); eager_ms_per_step: launched op by op"),
                        "parallelism": f"batch-sharded replicas x{n}",
                        "data": "uniform random token ids, random init"},
         }

@@ -193,6 +193,30 @@ def test_graphed_train_step_matches_eager():
         assert torch.equal(pe, pg), name
 
 
+@pytest.mark.gpu
+def test_graphed_forward_matches_eager():
+    """``GraphedForward`` (the no-grad forward replayed as CUDA graphs, two
+    copies with their own outputs) returns exactly the eager forward's
+    logits and τ fields for each batch it is given."""
+    dev = torch.device("cuda:0")
+    cfg = lm.TensionConfig(**CFGS["rope_global"])
+    torch.manual_seed(0)
+    model = lm.TensionLM(cfg).to(dev, torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(5)
+    b0, b1 = (torch.randint(0, cfg.vocab_size, (2, 192), generator=g).to(dev) for _ in range(2))
+    with torch.no_grad():
+        ref0, ref1 = model(b0, return_all=True), model(b1, return_all=True)
+    fw = lm.GraphedForward(model, b0, copies=2)
+    out0 = fw(copy=0)
+    out1 = fw(b1, copy=1)
+    torch.cuda.synchronize()
+    for ref, out in ((ref0, out0), (ref1, out1)):
+        assert torch.equal(ref[0], out[0])
+        assert len(ref[2]) == len(out[2])
+        for a, b in zip(ref[2], out[2]):
+            assert torch.equal(a, b)
+
+
 # ───────────────────────── DDP over gloo (CPU) ─────────────────────────
 
 TINY = dict(vocab_size=53, dim=32, num_layers=2, num_heads=2, window=4, ffn_mult=2,
