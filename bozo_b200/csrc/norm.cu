@@ -243,6 +243,66 @@ __global__ void swiglu_bwd_kernel(const T* __restrict__ dh, const T* __restrict_
   }
 }
 
+// bf16 SwiGLU, 8 elements (16 bytes) per thread and step.  Chunk c of h is
+// row c / w8, columns 8·(c mod w8) … +7 of the gate/value layout (a flat
+// tensor is one row: w8 = chunks, stride unused); a 32-bit division per 8
+// elements instead of a 64-bit one per 4.  σ(g) = 1/(1 + e^−g) with the
+// hardware exponential and a correctly rounded reciprocal (e^−g = ∞ gives
+// σ = 0); the products round once more, to bf16, on the way out.
+__device__ __forceinline__ void unpack8(uint4 q, float* f) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    f[2 * k] = __uint_as_float(w[k] << 16);
+    f[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+  }
+}
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
+    w[k] = *reinterpret_cast<const uint32_t*>(&b);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+__device__ __forceinline__ float sigmoid_fast(float x) { return __frcp_rn(1.f + __expf(-x)); }
+
+__global__ void swiglu_fwd_bf16x8(const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ v,
+                                  __nv_bfloat16* __restrict__ h, int chunks, int w8, long long stride) {
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < chunks; c += gridDim.x * blockDim.x) {
+    const int row = c / w8;
+    const long long a = (long long)row * stride + 8 * (c - row * w8);
+    float gf[8], vf[8], o[8];
+    unpack8(__ldg(reinterpret_cast<const uint4*>(g + a)), gf);
+    unpack8(__ldg(reinterpret_cast<const uint4*>(v + a)), vf);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = gf[k] * sigmoid_fast(gf[k]) * vf[k];
+    reinterpret_cast<uint4*>(h)[c] = pack8(o);
+  }
+}
+
+__global__ void swiglu_bwd_bf16x8(const __nv_bfloat16* __restrict__ dh, const __nv_bfloat16* __restrict__ g,
+                                  const __nv_bfloat16* __restrict__ v, __nv_bfloat16* __restrict__ dg,
+                                  __nv_bfloat16* __restrict__ dv, int chunks, int w8, long long stride) {
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < chunks; c += gridDim.x * blockDim.x) {
+    const int row = c / w8;
+    const long long a = (long long)row * stride + 8 * (c - row * w8);
+    float d[8], gf[8], vf[8], og[8], ov[8];
+    unpack8(__ldg(reinterpret_cast<const uint4*>(dh) + c), d);
+    unpack8(__ldg(reinterpret_cast<const uint4*>(g + a)), gf);
+    unpack8(__ldg(reinterpret_cast<const uint4*>(v + a)), vf);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float sig = sigmoid_fast(gf[k]);
+      ov[k] = d[k] * gf[k] * sig;
+      og[k] = d[k] * vf[k] * sig * (1.f + gf[k] * (1.f - sig));
+    }
+    *reinterpret_cast<uint4*>(dg + a) = pack8(og);
+    *reinterpret_cast<uint4*>(dv + a) = pack8(ov);
+  }
+}
+
 int norm_grid(long long N, int sms) {
   const long long want = (N + kNormWarps - 1) / kNormWarps;
   const long long cap = (long long)sms * 4;
@@ -321,6 +381,20 @@ cudaError_t launch_swiglu(const void* g, const void* v, void* h, const void* dh,
   const int grid = (int)(want < (long long)sms * 8 ? (want < 1 ? 1 : want) : (long long)sms * 8);
   if (dt == BOZO_DT_BF16) {
     using T = __nv_bfloat16;
+    auto a16 = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    if (n % 8 == 0 && n / 8 <= 0x7fffffffLL && width % 8 == 0 && stride % 8 == 0 && a16(g) && a16(v) &&
+        a16(h) && a16(dh) && a16(dg) && a16(dv)) {
+      const int chunks = (int)(n / 8);
+      const int w8 = width ? width / 8 : chunks;
+      const long long want8 = (chunks + 255) / 256;
+      const int grid8 = (int)(want8 < (long long)sms * 8 ? (want8 < 1 ? 1 : want8) : (long long)sms * 8);
+      if (dh)
+        swiglu_bwd_bf16x8<<<grid8, 256, 0, st>>>((const T*)dh, (const T*)g, (const T*)v, (T*)dg, (T*)dv,
+                                                 chunks, w8, stride);
+      else
+        swiglu_fwd_bf16x8<<<grid8, 256, 0, st>>>((const T*)g, (const T*)v, (T*)h, chunks, w8, stride);
+      return cudaGetLastError();
+    }
     if (dh)
       swiglu_bwd_kernel<T><<<grid, 256, 0, st>>>((const T*)dh, (const T*)g, (const T*)v, (T*)dg, (T*)dv, n,
                                                   width, stride);
