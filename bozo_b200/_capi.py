@@ -36,6 +36,7 @@ EXPORTED = (
     "bozo_cross_entropy_fwd", "bozo_cross_entropy_bwd",
     "bozo_tension_error_async", "bozo_tension_wait_selftest", "bozo_tension_fwd_needs_lp",
     "bozo_wo_add_rmsnorm_fwd", "bozo_wo_add_rmsnorm_supported",
+    "bozo_embedding_bwd",
 )
 TAU_AUX_MAX_LAYERS = 64  # BOZO_TAU_AUX_MAX_LAYERS
 
@@ -115,6 +116,14 @@ class SwiGLUArgs(C.Structure):
         ("n", C.c_int64), ("dtype", C.c_int32), ("gate", C.c_void_p), ("value", C.c_void_p),
         ("out", C.c_void_p), ("d_out", C.c_void_p), ("d_gate", C.c_void_p), ("d_value", C.c_void_p),
         ("width", C.c_int64), ("row_stride", C.c_int64),
+    ]
+
+
+class EmbeddingBwdArgs(C.Structure):
+    _fields_ = [
+        ("n", C.c_int64), ("dim", C.c_int32), ("vocab", C.c_int32), ("sorted_ids", C.c_void_p),
+        ("order", C.c_void_p), ("d_out", C.c_void_p), ("d_weight", C.c_void_p),
+        ("scratch", C.c_void_p),
     ]
 
 

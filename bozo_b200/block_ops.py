@@ -27,6 +27,10 @@ and backward, as autograd functions.
 * ``swiglu(g, v)`` = ``silu(g) * v`` (model.py:328-329): one pass each way;
   ``swiglu_packed(gv)`` takes one GEMM's packed ``[g | v]`` rows and returns
   the cotangent in that layout.
+* ``embedding(ids, weight)`` = ``F.embedding`` (the token embedding, tied
+  to the output head) whose weight gradient is one pass over the sorted ids
+  — every vocabulary row written once, each the sum of its tokens' rows in
+  position order — instead of the framework's sort-and-scatter kernels.
 * ``cross_entropy(logits, targets)`` = ``F.cross_entropy`` (train.py:920,
   mean over targets ≠ −100) from the logits in their own dtype: one pass
   for the per-row logsumexp, one for the gradient, no fp32 copy.
@@ -47,7 +51,7 @@ from . import _capi
 
 __all__ = ["add_rms_norm", "add_rms_norm_lp", "swiglu", "swiglu_packed", "cross_entropy",
            "norm_applies", "swiglu_applies", "swiglu_packed_applies", "xent_applies",
-           "wo_add_rms_norm", "wo_norm_applies"]
+           "wo_add_rms_norm", "wo_norm_applies", "embedding", "embedding_applies"]
 
 _WIDTHS = {128, 256, 512, 768, 1024}
 _DTYPES = (torch.float32, torch.bfloat16)
@@ -266,3 +270,33 @@ class _CrossEntropyFn(torch.autograd.Function):
 def cross_entropy(logits: Tensor, targets: Tensor) -> Tensor:
     """Mean cross-entropy of ``logits [R, V]`` against ``targets [R]`` (fp32)."""
     return _CrossEntropyFn.apply(logits, targets)
+
+
+def embedding_applies(ids: Tensor, weight: Tensor) -> bool:
+    return (weight.is_cuda and weight.dim() == 2 and weight.dtype == torch.float32
+            and weight.shape[1] % 4 == 0 and ids.device == weight.device
+            and ids.dtype in (torch.long, torch.int) and 0 < ids.numel() < 2 ** 31)
+
+
+class _EmbeddingFn(torch.autograd.Function):
+
+    @staticmethod
+    def forward(ctx, ids, weight):
+        ctx.save_for_backward(ids)
+        ctx.vocab = weight.shape[0]
+        return torch.nn.functional.embedding(ids, weight)
+
+    @staticmethod
+    def backward(ctx, d_out):
+        (ids,) = ctx.saved_tensors
+        # stable: equal ids keep increasing positions, the order the rows are summed in
+        keys, order = torch.sort(ids.reshape(-1).to(torch.int32), stable=True)
+        dim = d_out.shape[-1]
+        dw = _capi.ext().embedding_bwd(keys, order, d_out.reshape(-1, dim).float().contiguous(),
+                                       ctx.vocab)
+        return None, dw
+
+
+def embedding(ids: Tensor, weight: Tensor) -> Tensor:
+    """``weight[ids]`` with the weight gradient of ``bozo_embedding_bwd``."""
+    return _EmbeddingFn.apply(ids, weight)

@@ -618,6 +618,20 @@ int bozo_swiglu_bwd(const bozo_swiglu_args* a, void* stream) {
   return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
 }
 
+int bozo_embedding_bwd(const bozo_embedding_bwd_args* a, void* stream) {
+  if (!a) return BOZO_ERR_NULL;
+  if (a->n <= 0 || a->n > 0x7fffffffLL || a->vocab <= 0 || a->dim <= 0 || a->dim % 4 != 0)
+    return BOZO_ERR_BAD_SHAPE;
+  if (!a->sorted_ids || !a->order || !a->d_out || !a->d_weight || !a->scratch) return BOZO_ERR_NULL;
+  if ((reinterpret_cast<uintptr_t>(a->d_out) & 15) || (reinterpret_cast<uintptr_t>(a->d_weight) & 15))
+    return BOZO_ERR_ALIGNMENT;
+  DeviceRestore restore;
+  cudaError_t e = bind_device(a->d_out, restore);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = launch_embedding_bwd(*a, num_sms(), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BOZO_OK : cuda_fail(e);
+}
+
 static int check_xent(const bozo_cross_entropy_args* a) {
   if (!a) return BOZO_ERR_NULL;
   if (a->rows <= 0 || a->rows > 0x7fffffffLL) return BOZO_ERR_BAD_SHAPE;

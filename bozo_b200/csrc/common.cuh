@@ -162,6 +162,9 @@ cudaError_t launch_wo_norm(const bozo_wo_add_rmsnorm_args& a, int* err, cudaStre
 cudaError_t launch_swiglu(const void* g, const void* v, void* h, const void* dh, void* dg, void* dv,
                           long long n, int width, long long stride, int dt, int sms, cudaStream_t st);
 
+// Token-embedding weight gradient (embed.cu).
+cudaError_t launch_embedding_bwd(const bozo_embedding_bwd_args& a, int sms, cudaStream_t st);
+
 // Cross-entropy from the logits (xent.cu).
 bool xent_shape_ok(int V, int dt);
 cudaError_t launch_xent(const bozo_cross_entropy_args& a, bool backward, cudaStream_t st);

@@ -406,6 +406,29 @@ std::vector<at::Tensor> swiglu_bwd(const at::Tensor& dh, const at::Tensor& g, co
   return {dg, dv};
 }
 
+// Token-embedding weight gradient from the stably sorted ids (int32) and
+// their positions (int64): [vocab, dim] fp32, every row written.
+at::Tensor embedding_bwd(const at::Tensor& sorted_ids, const at::Tensor& order, const at::Tensor& d_out,
+                         int64_t vocab) {
+  const c10::cuda::CUDAGuard guard(d_out.device());
+  TORCH_CHECK(sorted_ids.scalar_type() == at::kInt && order.scalar_type() == at::kLong,
+              "embedding_bwd: int32 keys and int64 positions");
+  TORCH_CHECK(d_out.scalar_type() == at::kFloat && d_out.dim() == 2 && d_out.is_contiguous(),
+              "embedding_bwd: d_out must be contiguous fp32 [n, dim]");
+  TORCH_CHECK(sorted_ids.is_contiguous() && order.is_contiguous() && sorted_ids.numel() == d_out.size(0) &&
+              order.numel() == d_out.size(0), "embedding_bwd: one key and one position per d_out row");
+  at::Tensor dw = at::empty({vocab, d_out.size(1)}, d_out.options());
+  at::Tensor scratch = at::empty({2 * vocab}, d_out.options().dtype(at::kInt));
+  bozo_embedding_bwd_args a{};
+  a.n = d_out.size(0); a.dim = (int32_t)d_out.size(1); a.vocab = (int32_t)vocab;
+  a.sorted_ids = sorted_ids.data_ptr<int32_t>(); a.order = order.data_ptr<int64_t>();
+  a.d_out = d_out.data_ptr<float>(); a.d_weight = dw.data_ptr<float>();
+  a.scratch = scratch.data_ptr<int32_t>();
+  check(bozo_embedding_bwd(&a, at::cuda::getCurrentCUDAStream(d_out.device().index()).stream()),
+        "bozo_embedding_bwd");
+  return dw;
+}
+
 // Cross-entropy: forward → (row_loss, row_lse); backward → d_logits.
 std::vector<at::Tensor> cross_entropy_fwd(const at::Tensor& logits, const at::Tensor& targets) {
   const c10::cuda::CUDAGuard guard(logits.device());
@@ -567,6 +590,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("add_rmsnorm_bwd", &add_rmsnorm_bwd, "its backward through bozo_add_rmsnorm_bwd");
   m.def("wo_add_rmsnorm_fwd", &wo_add_rmsnorm_fwd,
         "wo projection + residual add + RMSNorm through bozo_wo_add_rmsnorm_fwd");
+  m.def("embedding_bwd", &embedding_bwd, "token-embedding weight gradient through bozo_embedding_bwd");
   m.def("swiglu_fwd", &swiglu_fwd, "SwiGLU through bozo_swiglu_fwd");
   m.def("cross_entropy_fwd", &cross_entropy_fwd, "cross-entropy through bozo_cross_entropy_fwd");
   m.def("cross_entropy_bwd", &cross_entropy_bwd, "its backward through bozo_cross_entropy_bwd");

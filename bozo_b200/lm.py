@@ -370,7 +370,12 @@ class TensionLM(nn.Module):
         B, T = input_ids.shape
         assert T <= self.cfg.max_seq_len, \
             f"Sequence length {T} exceeds max_seq_len {self.cfg.max_seq_len}"
-        x = self.embedding(input_ids)
+        from . import block_ops
+        w = self.embedding.weight
+        if w.requires_grad and torch.is_grad_enabled() and block_ops.embedding_applies(input_ids, w):
+            x = block_ops.embedding(input_ids, w)  # fused weight gradient
+        else:
+            x = self.embedding(input_ids)
         if self.pos_embedding is not None:
             x = x + self.pos_embedding(self.pos_buf[:, :T])
         x = self.emb_drop(x)

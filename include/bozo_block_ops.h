@@ -137,6 +137,29 @@ typedef struct {
 int bozo_cross_entropy_fwd(const bozo_cross_entropy_args* args, void* stream);
 int bozo_cross_entropy_bwd(const bozo_cross_entropy_args* args, void* stream);
 
+/* Gradient of a token-embedding lookup (out[p] = weight[ids[p]]) with
+ * respect to the weight: d_weight[v] = Σ of d_out[p] over the positions p
+ * with ids[p] = v, summed in increasing p (the same result on every call),
+ * and zero rows for tokens that do not occur.  Replaces the weight gradient
+ * of nn.Embedding (model.py's tok_emb, tied to the output head).  The caller
+ * sorts the n ids stably: sorted_ids ascending (int32), order their positions
+ * (int64) — e.g. torch.sort(ids.int(), stable=True).  Ids outside [0, vocab)
+ * contribute nothing.  d_out [n, dim] and d_weight [vocab, dim] fp32
+ * contiguous, 16-byte aligned, dim a multiple of 4; scratch holds
+ * 2·vocab int32 (run bounds). */
+typedef struct {
+  int64_t n;              /* positions */
+  int32_t dim;
+  int32_t vocab;
+  const int32_t* sorted_ids;
+  const int64_t* order;
+  const float* d_out;
+  float* d_weight;        /* written in full */
+  int32_t* scratch;       /* [2·vocab] int32 */
+} bozo_embedding_bwd_args;
+
+int bozo_embedding_bwd(const bozo_embedding_bwd_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

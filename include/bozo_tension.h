@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define BOZO_TENSION_ABI_VERSION 6
+#define BOZO_TENSION_ABI_VERSION 7
 
 typedef enum {
   BOZO_OK = 0,

@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol():
     assert set(declared) == set(_capi.EXPORTED)
     for name in declared:
         assert hasattr(lib, name), name
-    assert lib.bozo_tension_abi_version() == 6
+    assert lib.bozo_tension_abi_version() == 7
     assert _capi.status_string(0) == "ok"
 
 
@@ -82,6 +82,8 @@ int main(void) {
   O(bozo_wo_add_rmsnorm_args, rstd);
   S(bozo_swiglu_args); O(bozo_swiglu_args, gate); O(bozo_swiglu_args, d_value);
   O(bozo_swiglu_args, width); O(bozo_swiglu_args, row_stride);
+  S(bozo_embedding_bwd_args); O(bozo_embedding_bwd_args, vocab); O(bozo_embedding_bwd_args, sorted_ids);
+  O(bozo_embedding_bwd_args, d_weight); O(bozo_embedding_bwd_args, scratch);
   S(bozo_cross_entropy_args); O(bozo_cross_entropy_args, logits_dtype);
   O(bozo_cross_entropy_args, targets); O(bozo_cross_entropy_args, d_logits);
   S(bozo_graph_bias_args); O(bozo_graph_bias_args, alpha); O(bozo_graph_bias_args, ctx_content);
@@ -111,6 +113,7 @@ def test_struct_layout_matches_header():
              "bozo_swiglu_args": _capi.SwiGLUArgs,
              "bozo_wo_add_rmsnorm_args": _capi.WoAddRMSNormArgs,
              "bozo_cross_entropy_args": _capi.CrossEntropyArgs,
+             "bozo_embedding_bwd_args": _capi.EmbeddingBwdArgs,
              "bozo_tau_aux_fwd_args": _capi.TauAuxFwdArgs,
              "bozo_tau_aux_bwd_args": _capi.TauAuxBwdArgs}
     for line in filter(None, lines):

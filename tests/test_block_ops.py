@@ -257,3 +257,33 @@ def test_swiglu_packed_matches_two_tensor_swiglu(dtype):
 
 def test_packed_swiglu_gating_on_cpu():
     assert not block_ops.swiglu_packed_applies(torch.randn(4, 16))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("V,D,n", [(32768, 768, 16384), (97, 1040, 600), (50, 36, 257)])
+def test_embedding_weight_grad_matches_framework(V, D, n):
+    """The fused embedding's weight gradient equals the framework's (sums of
+    the same fp32 rows, possibly in another order), absent tokens get exact
+    zero rows, and two calls give identical bits."""
+    dev = torch.device("cuda:0")
+    g = torch.Generator().manual_seed(V + D)
+    ids = torch.randint(0, max(V // 2, 1), (n,), generator=g).to(dev)  # repeats, absent upper half
+    w = torch.randn(V, D, generator=g).to(dev)
+    dy = torch.randn(n, D, generator=g).to(dev)
+    a = w.clone().requires_grad_(True)
+    b = w.clone().requires_grad_(True)
+    out = block_ops.embedding(ids, a)
+    ref = F.embedding(ids, b)
+    assert torch.equal(out, ref)
+    (ga,) = torch.autograd.grad(out, a, dy)
+    (gb,) = torch.autograd.grad(ref, b, dy)
+    torch.testing.assert_close(ga, gb, rtol=1e-5, atol=1e-5)
+    absent = torch.ones(V, dtype=torch.bool, device=dev)
+    absent[ids] = False
+    assert torch.count_nonzero(ga[absent]) == 0
+    (ga2,) = torch.autograd.grad(block_ops.embedding(ids, a), a, dy)
+    assert torch.equal(ga, ga2)
+
+
+def test_embedding_gating_on_cpu():
+    assert not block_ops.embedding_applies(torch.zeros(4, dtype=torch.long), torch.randn(8, 4))
