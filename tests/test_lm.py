@@ -287,6 +287,53 @@ def test_ddp_step_equals_averaged_half_batch_gradients(tmp_path):
     assert not math.isnan(float(sum(v.float().sum() for v in r0.values())))
 
 
+def _graphed_ddp_worker(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        cfg = lm.TensionConfig(**CFGS["rope_global"])
+        g = torch.Generator().manual_seed(23 + rank)
+        ids = torch.randint(0, cfg.vocab_size, (2, 193), generator=g).to(dev)
+        finals = []
+        for graphed in (False, True):
+            torch.manual_seed(0)
+            base = lm.TensionLM(cfg).to(dev)
+            model = lm.wrap_ddp(base)
+            opt = lm.make_optimizer(base, fused=True, capturable=True)
+            if graphed:
+                step = lm.GraphedTrainStep(model, base, opt, ids)  # 11 eager warm-up steps
+                for _ in range(2):
+                    step()
+                step.release()
+            else:
+                for _ in range(13):
+                    lm.train_step(model, base, opt, ids[:, :-1], ids[:, 1:])
+            torch.cuda.synchronize()
+            finals.append({k: v.detach().cpu().clone() for k, v in base.state_dict().items()})
+            del model
+        torch.save(finals, os.path.join(out_dir, f"rank{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_graphed_ddp_step_matches_eager_ddp(tmp_path):
+    """The DDP step the multi-GPU bench replays — NCCL all-reduces with the
+    averaging hook recorded inside ``GraphedTrainStep`` — leaves exactly the
+    parameters of the same number of eager DDP steps (one NCCL rank here; the
+    bench's two- and eight-rank runs use the same code)."""
+    mp.start_processes(_graphed_ddp_worker, args=(1, _free_port(), str(tmp_path)), nprocs=1,
+                       join=True, start_method="spawn")
+    eager, graphed = torch.load(tmp_path / "rank0.pt")
+    for k in eager:
+        assert torch.equal(eager[k], graphed[k]), k
+
+
 def test_packed_weight_cache_follows_the_weights():
     """Without autograd the concatenated projection weight is reused until a
     weight changes; with autograd it is built fresh (and differentiable)."""
